@@ -1,0 +1,154 @@
+/*
+ * jxrng: B200 (sm_100a) kernels for jaxR's threefry2x32 random-bits path.
+ *
+ * A plain C ABI: pointers, sizes and status codes, no C++ or torch types, so the
+ * R `.Call` shim, an XLA typed-FFI handler or Python ctypes can bind it alike.
+ *
+ * Conventions
+ *  - Every entry point returns JXR_OK (0) or a status code; jxr_last_error()
+ *    returns a message for the last failure on the calling host thread.
+ *  - Arrays named `keys`, `out`, `x` ... are DEVICE pointers on the current
+ *    CUDA device, owned by the caller.  Work is enqueued on `stream` (a
+ *    cudaStream_t; NULL = the legacy default stream) and is asynchronous unless
+ *    the entry point says otherwise.
+ *  - A key is two uint32 words (k0, k1); `keys` holds `nkeys` keys, key j at
+ *    keys[2j], keys[2j+1].  Key-batched entry points write one row per key
+ *    (row-major, key-major), which is what vmap over a key batch produces.
+ *  - Requests are given by `size`, the element count of one key's full request
+ *    (the product of its shape), and the range [begin, begin + count) of it to
+ *    produce.  Elements are in C order, exactly as the reference's outputs, so
+ *    a caller can shard a request over devices by element range and each
+ *    device writes its own slab; begin = 0, count = size is the whole request.
+ *  - layout selects jax_threefry_partitionable: JXR_LAYOUT_PARTITIONABLE (the
+ *    reference's default) or JXR_LAYOUT_ORIGINAL.
+ *
+ * Reference interfaces replaced (paths within the jaxR project):
+ *  - threefry2x32_p and its lowering           R/prng.R:48-99
+ *  - prng_threefry_2x32 (hash of counts)        R/prng.R:101-120
+ *  - prng_threefry_seed                         R/prng.R:159-170
+ *  - prng_threefry_split (both layouts)         R/prng.R:172-191
+ *  - prng_threefry_fold_in                      R/prng.R:193-194
+ *  - prng_threefry_random_bits (both layouts)   R/prng.R:201-262
+ *  - rnd_uniform                                R/random.R:287-304
+ *  - rnd_normal_real / lax_erf_inv              R/random.R:501-508, R/lax.R:222
+ *  - rnd_bernoulli (mode "low")                 R/random.R:655-666
+ * The reference reaches these through .Call(jaxr_compile/jaxr_execute)
+ * (src/pjrt.cpp:255, :725) on the XLA CPU plugin; INTEGRATION.md shows the
+ * .Call shim that binds this ABI instead.
+ */
+#ifndef JXRNG_H
+#define JXRNG_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JXR_ABI_VERSION 1
+
+/* status codes */
+enum {
+  JXR_OK = 0,
+  JXR_ERR_INVALID_ARGUMENT = 1, /* bad size, range, dtype, layout, bit width, pointer */
+  JXR_ERR_NOT_IMPLEMENTED = 2,  /* e.g. a request of more than 2^64 elements */
+  JXR_ERR_CUDA = 3,             /* a CUDA runtime call failed; message has the CUDA error */
+  JXR_ERR_NO_DEVICE = 4         /* no sm_100 device is current */
+};
+
+/* layouts: the value of jax_threefry_partitionable */
+enum { JXR_LAYOUT_ORIGINAL = 0, JXR_LAYOUT_PARTITIONABLE = 1 };
+
+/* floating dtypes (16-bit results are stored as their raw bits) */
+enum { JXR_F32 = 0, JXR_F64 = 1, JXR_F16 = 2, JXR_BF16 = 3 };
+
+/* flags for jxr_uniform: the reference's recorded samples (tests/testthat/
+ * test-random.R:43, :160) are those of a fused floats*(maxval-minval)+minval;
+ * this flag asks for a separately rounded multiply and add instead. */
+enum { JXR_FLAG_UNFUSED_MUL_ADD = 1 };
+
+/* ABI version (JXR_ABI_VERSION) and the last error of this host thread. */
+int jxr_abi_version(void);
+const char* jxr_last_error(void);
+
+/* Seeds to keys on the host (R/prng.R:159-170 after R/prng.R:504-519): with x64
+ * off an R number wraps to int32 and k0 is 0; with x64 on k0 is the high word.
+ * keys_out: HOST uint32[2 * n]. */
+int jxr_seed(const int64_t* seeds, int64_t n, int x64, uint32_t* keys_out);
+
+/* threefry2x32_p on n broadcast elements (R/prng.R:88-99). */
+int jxr_threefry2x32(const uint32_t* k0, const uint32_t* k1, const uint32_t* c0,
+                     const uint32_t* c1, uint32_t* x0, uint32_t* x1, int64_t n,
+                     void* stream);
+
+/* prng_threefry_2x32(key, count) for each of nkeys keys over one uint32 count
+ * vector of n elements, with odd-n zero padding (R/prng.R:101-120).
+ * out: uint32[nkeys][n]. */
+int jxr_threefry_2x32(const uint32_t* keys, int64_t nkeys, const uint32_t* count, int64_t n,
+                      uint32_t* out, void* stream);
+
+/* random_split of each key into num keys (R/prng.R:172-191).
+ * out: uint32[nkeys][num][2]. */
+int jxr_split(const uint32_t* keys, int64_t nkeys, int64_t num, int layout, uint32_t* out,
+              void* stream);
+
+/* random_fold_in (R/prng.R:193-194): out key i = fold_in(keys[i or 0], data[i or 0]),
+ * n = max(nkeys, ndata); nkeys and ndata are each n or 1. out: uint32[n][2]. */
+int jxr_fold_in(const uint32_t* keys, int64_t nkeys, const uint32_t* data, int64_t ndata,
+                uint32_t* out, void* stream);
+
+/* random_bits (R/prng.R:201-262): bit_width 8, 16, 32 or 64; out holds
+ * uint{bit_width}[nkeys][count], elements [begin, begin+count) of each key's
+ * size-element request. */
+int jxr_random_bits(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                    uint64_t count, int layout, int bit_width, void* out, void* stream);
+
+/* random_uniform (R/random.R:287-304) in dtype with scalar bounds given as double
+ * and converted to dtype first. out: dtype[nkeys][count]. */
+int jxr_uniform(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                uint64_t count, int layout, int dtype, double minval, double maxval,
+                uint32_t flags, void* out, void* stream);
+
+/* random_normal for a real dtype (R/random.R:501-508): sqrt(2) * erf_inv(u) with u
+ * uniform on [nextafter(-1, 0), 1). out: dtype[nkeys][count]. */
+int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+               uint64_t count, int layout, int dtype, void* out, void* stream);
+
+/* random_bernoulli, mode "low" (R/random.R:655-666): uniform(dtype(p)) < p.
+ * out: uint8 (0/1)[nkeys][count]. */
+int jxr_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                  uint64_t count, int layout, int p_dtype, double p, uint8_t* out,
+                  void* stream);
+
+/* random_normal(key, shape, dtype) and random_bernoulli(key, p, shape) of the SAME
+ * key and shape in one pass: both draw the same bits, so the cipher runs once.
+ * normal_out: dtype[nkeys][count]; bern_out: uint8[nkeys][count]. */
+int jxr_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                         uint64_t count, int layout, int dtype, double p, void* normal_out,
+                         uint8_t* bern_out, void* stream);
+
+/* The sampler transforms alone, applied element-wise to caller-provided random
+ * bits (the second half of rnd_uniform / rnd_normal_real, R/random.R:297-304,
+ * :505-507): bits are uint32 for F32, uint64 for F64, uint16 for F16 and uint8
+ * for BF16, as rnd_bits draws them. */
+int jxr_uniform_from_bits(const void* bits, int64_t n, int dtype, double minval,
+                          double maxval, uint32_t flags, void* out, void* stream);
+int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void* stream);
+
+/* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
+ * element-wise for F32 or F64. */
+int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);
+
+/* random_bits into HOST memory: generates on the current device in chunks into a
+ * device staging buffer that the call allocates and frees, and copies each chunk
+ * to host_out while the next one is generated.  Synchronous: returns when
+ * host_out holds the result.  host_out should be pinned (cudaHostAlloc or
+ * cudaHostRegister) for full PCIe bandwidth. */
+int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size,
+                         uint64_t begin, uint64_t count, int layout, int bit_width,
+                         void* host_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JXRNG_H */

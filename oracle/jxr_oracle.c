@@ -1,0 +1,452 @@
+/*
+ * CPU oracle for the threefry2x32 random-bits path of jaxR.
+ *
+ * TEST INFRASTRUCTURE ONLY: the checker for tests/, __graft_entry__.smoke()
+ * and the CPU baseline leg of bench.py.  Nothing in the product links or calls
+ * it.  Compiled with -ffp-contract=off so that every float operation below is
+ * rounded exactly as written; fused multiply-adds appear only where fmaf/fma
+ * is called explicitly.
+ *
+ * Reference lines cited are paths within the jaxR project.
+ */
+#include "jxr_oracle.h"
+
+#include <math.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static int g_threads = 0;
+
+void orc_set_threads(int n) { g_threads = n; }
+
+int orc_get_threads(void) {
+#ifdef _OPENMP
+  return g_threads > 0 ? g_threads : omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* ---- the cipher ------------------------------------------------------------------------ */
+
+static inline uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+/* R/prng.R:51-86: key schedule ks = (k0, k1, k0^k1^0x1BD11BDA); x = (c0+ks0, c1+ks1);
+ * five steps of four rounds (x0 += x1; x1 = rotl(x1, r); x1 ^= x0) with the rotation
+ * sets (13,15,26,6) and (17,29,16,24) alternating, each step followed by the injection
+ * x0 += ks[(i+1)%3], x1 += ks[(i+2)%3] + (i+1). */
+static inline void tf(uint32_t k0, uint32_t k1, uint32_t c0, uint32_t c1, uint32_t* o0,
+                      uint32_t* o1) {
+  static const int rot[2][4] = {{13, 15, 26, 6}, {17, 29, 16, 24}};
+  const uint32_t ks[3] = {k0, k1, k0 ^ k1 ^ 0x1BD11BDAu};
+  uint32_t x0 = c0 + ks[0], x1 = c1 + ks[1];
+  for (int i = 0; i < 5; ++i) {
+    const int* r = rot[i & 1];
+    for (int j = 0; j < 4; ++j) {
+      x0 += x1;
+      x1 = rotl32(x1, r[j]);
+      x1 ^= x0;
+    }
+    x0 += ks[(i + 1) % 3];
+    x1 += ks[(i + 2) % 3] + (uint32_t)(i + 1);
+  }
+  *o0 = x0;
+  *o1 = x1;
+}
+
+void orc_threefry2x32(uint32_t k0, uint32_t k1, uint32_t c0, uint32_t c1, uint32_t out[2]) {
+  tf(k0, k1, c0, c1, &out[0], &out[1]);
+}
+
+void orc_threefry2x32_arr(const uint32_t* k0, const uint32_t* k1, const uint32_t* c0,
+                          const uint32_t* c1, uint32_t* x0, uint32_t* x1, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) tf(k0[i], k1[i], c0[i], c1[i], &x0[i], &x1[i]);
+}
+
+/* R/prng.R:102-120: pad odd n with one zero; block j hashes (flat[j], flat[half+j]);
+ * the output is [x0 of all blocks, x1 of all blocks] cut to n. */
+void orc_threefry_2x32(const uint32_t key[2], const uint32_t* count, int64_t n, uint32_t* out) {
+  const int64_t half = (n + 1) / 2;
+  for (int64_t j = 0; j < half; ++j) {
+    uint32_t a, b;
+    tf(key[0], key[1], count[j], half + j < n ? count[half + j] : 0u, &a, &b);
+    out[j] = a;
+    if (half + j < n) out[half + j] = b;
+  }
+}
+
+/* Word g of threefry_2x32(key, iota(n)) without materialising the iota. */
+static inline uint32_t iota_hash_word(const uint32_t key[2], uint64_t n, uint64_t g) {
+  const uint64_t half = (n + 1) / 2;
+  uint32_t a, b;
+  if (g < half) {
+    tf(key[0], key[1], (uint32_t)g, half + g < n ? (uint32_t)(half + g) : 0u, &a, &b);
+    return a;
+  }
+  tf(key[0], key[1], (uint32_t)(g - half), (uint32_t)g, &a, &b);
+  return b;
+}
+
+/* ---- seed / split / fold_in ------------------------------------------------------------ */
+
+/* R/prng.R:160-170 with the int64 -> int32 wrap of R/prng.R:505-514: k1 is the seed
+ * shifted right (logically) by 32, which is 0 for an int32 seed, k2 its low word. */
+void orc_seed(int64_t seed, int x64, uint32_t out[2]) {
+  if (x64) {
+    out[0] = (uint32_t)((uint64_t)seed >> 32);
+    out[1] = (uint32_t)(uint64_t)seed;
+  } else {
+    out[0] = 0u;
+    out[1] = (uint32_t)(uint64_t)seed;
+  }
+}
+
+/* Key s of split_original(key, num) (R/prng.R:173-177): threefry_2x32(key, iota(2 num))
+ * reshaped to (num, 2). */
+static inline void split_original_key(const uint32_t key[2], uint64_t num, uint64_t s,
+                                      uint32_t out[2]) {
+  out[0] = iota_hash_word(key, 2 * num, 2 * s);
+  out[1] = iota_hash_word(key, 2 * num, 2 * s + 1);
+}
+
+/* R/prng.R:180-191. */
+void orc_split(const uint32_t key[2], int64_t num, int partitionable, uint32_t* out) {
+  for (int64_t j = 0; j < num; ++j) {
+    if (partitionable) {
+      tf(key[0], key[1], (uint32_t)((uint64_t)j >> 32), (uint32_t)j, &out[2 * j],
+         &out[2 * j + 1]);
+    } else {
+      split_original_key(key, (uint64_t)num, (uint64_t)j, &out[2 * j]);
+    }
+  }
+}
+
+/* R/prng.R:194: threefry_2x32(key, seed(data)) with seed(uint32 d) = (0, d), one block. */
+void orc_fold_in(const uint32_t key[2], uint32_t data, uint32_t out[2]) {
+  tf(key[0], key[1], 0u, data, &out[0], &out[1]);
+}
+
+/* ---- random bits ----------------------------------------------------------------------- */
+
+/* Word g of the original-layout stream of max_count uint32 words (R/prng.R:230-245):
+ * below 2^32-1 words one hash of iota(max_count); otherwise the key is split into
+ * nblocks+1 keys, each hashing iota(2^32-1) except the last, which hashes iota(rem). */
+static inline uint32_t original_word(const uint32_t key[2], uint64_t max_count, uint64_t g) {
+  const uint64_t U = 0xFFFFFFFFull;
+  const uint64_t nblocks = max_count / U, rem = max_count % U;
+  if (nblocks == 0) return iota_hash_word(key, max_count, g);
+  const uint64_t s = g / U, local = g % U;
+  uint32_t sk[2];
+  split_original_key(key, nblocks + 1, s, sk);
+  return iota_hash_word(sk, s < nblocks ? U : rem, local);
+}
+
+uint64_t orc_bits_at(const uint32_t key[2], int bit_width, uint64_t size, int partitionable,
+                     uint64_t i) {
+  if (partitionable) {
+    /* R/prng.R:213-227 with the C-order iota split into (hi, lo) words (R/prng.R:130-148). */
+    uint32_t x0, x1;
+    tf(key[0], key[1], (uint32_t)(i >> 32), (uint32_t)i, &x0, &x1);
+    if (bit_width == 64) return ((uint64_t)x0 << 32) | x1;
+    const uint32_t x = x0 ^ x1;
+    if (bit_width == 32) return x;
+    if (bit_width == 16) return (uint16_t)x;
+    return (uint8_t)x;
+  }
+  /* R/prng.R:246-261 */
+  if (bit_width == 64) {
+    const uint64_t mc = 2 * size;
+    return ((uint64_t)original_word(key, mc, i) << 32) | original_word(key, mc, size + i);
+  }
+  if (bit_width == 32) return original_word(key, size, i);
+  const uint64_t per = 32 / (uint64_t)bit_width;
+  const uint64_t mc = ((uint64_t)bit_width * size + 31) / 32;
+  const uint32_t w = original_word(key, mc, i / per);
+  const uint32_t v = w >> (bit_width * (int)(i % per));
+  return bit_width == 16 ? (uint16_t)v : (uint8_t)v;
+}
+
+/* Bulk partitionable 32-bit words, written so that the compiler vectorises it. */
+__attribute__((target_clones("avx512f", "avx2", "default"))) static void bulk_part32(
+    uint32_t k0, uint32_t k1, uint64_t begin, uint64_t count, uint32_t* out) {
+  const uint32_t ks2 = k0 ^ k1 ^ 0x1BD11BDAu;
+  for (uint64_t t = 0; t < count; ++t) {
+    const uint64_t i = begin + t;
+    uint32_t x0 = (uint32_t)(i >> 32) + k0, x1 = (uint32_t)i + k1;
+#define ORC_R(r) x0 += x1; x1 = rotl32(x1, r); x1 ^= x0;
+    ORC_R(13) ORC_R(15) ORC_R(26) ORC_R(6)  x0 += k1;  x1 += ks2 + 1u;
+    ORC_R(17) ORC_R(29) ORC_R(16) ORC_R(24) x0 += ks2; x1 += k0 + 2u;
+    ORC_R(13) ORC_R(15) ORC_R(26) ORC_R(6)  x0 += k0;  x1 += k1 + 3u;
+    ORC_R(17) ORC_R(29) ORC_R(16) ORC_R(24) x0 += k1;  x1 += ks2 + 4u;
+    ORC_R(13) ORC_R(15) ORC_R(26) ORC_R(6)  x0 += ks2; x1 += k0 + 5u;
+#undef ORC_R
+    out[t] = x0 ^ x1;
+  }
+}
+
+#ifdef _OPENMP
+#define ORC_PAR_FOR _Pragma("omp parallel for schedule(static) num_threads(orc_get_threads())")
+#else
+#define ORC_PAR_FOR
+#endif
+
+int orc_random_bits(const uint32_t key[2], int bit_width, uint64_t size, int partitionable,
+                    uint64_t begin, uint64_t count, void* out) {
+  if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64) return 1;
+  if (begin > size || count > size - begin) return 2;
+  if (partitionable && bit_width == 32) {
+    const int64_t chunk = 1 << 16;
+    const int64_t nchunks = (int64_t)((count + chunk - 1) / chunk);
+    uint32_t* o = (uint32_t*)out;
+    ORC_PAR_FOR
+    for (int64_t c = 0; c < nchunks; ++c) {
+      const uint64_t s = (uint64_t)c * chunk;
+      const uint64_t n = count - s < (uint64_t)chunk ? count - s : (uint64_t)chunk;
+      bulk_part32(key[0], key[1], begin + s, n, o + s);
+    }
+    return 0;
+  }
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t) {
+    const uint64_t v = orc_bits_at(key, bit_width, size, partitionable, begin + (uint64_t)t);
+    switch (bit_width) {
+      case 64: ((uint64_t*)out)[t] = v; break;
+      case 32: ((uint32_t*)out)[t] = (uint32_t)v; break;
+      case 16: ((uint16_t*)out)[t] = (uint16_t)v; break;
+      default: ((uint8_t*)out)[t] = (uint8_t)v; break;
+    }
+  }
+  return 0;
+}
+
+/* ---- 16-bit float helpers -------------------------------------------------------------- */
+
+static inline float bits_f32(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
+static inline uint32_t f32_bits(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
+static inline double bits_f64(uint64_t b) { double d; memcpy(&d, &b, 8); return d; }
+
+/* float -> 16-bit float with round to nearest even.  man = mantissa bits kept (10 for
+ * float16, 7 for bfloat16), ebias/emax describe the target exponent. */
+static uint16_t f32_to_half_bits(float f, int bf16) {
+  const uint32_t b = f32_bits(f);
+  if (bf16) {
+    if ((b & 0x7F800000u) == 0x7F800000u && (b & 0x007FFFFFu)) return (uint16_t)((b >> 16) | 0x40);
+    const uint32_t lsb = (b >> 16) & 1u;
+    return (uint16_t)((b + 0x7FFFu + lsb) >> 16);
+  }
+  const _Float16 h = (_Float16)f;
+  uint16_t r;
+  memcpy(&r, &h, 2);
+  return r;
+}
+
+static float half_bits_to_f32(uint16_t h, int bf16) {
+  if (bf16) return bits_f32((uint32_t)h << 16);
+  _Float16 v;
+  memcpy(&v, &h, 2);
+  return (float)v;
+}
+
+/* double -> float rounded to odd, so that a following round to a 16-bit float is a
+ * single correct rounding of the double. */
+static float f64_to_f32_odd(double x) {
+  float f = (float)x;
+  if (isfinite(x) && (double)f != x) {
+    if (fabs((double)f) > fabs(x)) f = nextafterf(f, 0.0f);
+    f = bits_f32(f32_bits(f) | 1u);
+  }
+  return f;
+}
+
+/* One rounding to the 16-bit type of a float computed exactly or with one rounding
+ * (f32 has more than 2p+2 bits for both 16-bit types, so double rounding is harmless
+ * for a single +, -, *). */
+static inline float rh(float f, int bf16) { return half_bits_to_f32(f32_to_half_bits(f, bf16), bf16); }
+
+/* ---- erf_inv --------------------------------------------------------------------------- */
+
+/* Giles (2011), single precision: two polynomials in w = -log(1 - x^2), split at w = 5. */
+static const float GS_LT5[9] = {2.81022636e-08f, 3.43273939e-07f, -3.5233877e-06f,
+                                -4.39150654e-06f, 0.00021858087f, -0.00125372503f,
+                                -0.00417768164f, 0.246640727f, 1.50140941f};
+static const float GS_GE5[9] = {-0.000200214257f, 0.000100950558f, 0.00134934322f,
+                                -0.00367342844f, 0.00573950773f, -0.0076224613f,
+                                0.00943887047f, 1.00167406f, 2.83297682f};
+
+float orc_erfinv_f32(float x, int fma) {
+  /* log1p of the rounded float -(x*x), correctly rounded to float (through double). */
+  const float w0 = -(float)log1p((double)(-(x * x)));
+  const int lt = w0 < 5.0f;
+  const float* c = lt ? GS_LT5 : GS_GE5;
+  const float w = lt ? w0 - 2.5f : sqrtf(w0) - 3.0f;
+  float p = c[0];
+  for (int i = 1; i < 9; ++i) p = fma ? fmaf(p, w, c[i]) : c[i] + p * w;
+  if (fabsf(x) == 1.0f) return x * INFINITY;
+  return p * x;
+}
+
+/* Giles (2011), double precision: three polynomials split at w = 6.25 and w = 16. */
+static const double GD_LT625[23] = {
+    -3.6444120640178196996e-21, -1.685059138182016589e-19, 1.2858480715256400167e-18,
+    1.115787767802518096e-17,   -1.333171662854620906e-16, 2.0972767875968561637e-17,
+    6.6376381343583238325e-15,  -4.0545662729752068639e-14, -8.1519341976054721522e-14,
+    2.6335093153082322977e-12,  -1.2975133253453532498e-11, -5.4154120542946279317e-11,
+    1.051212273321532285e-09,   -4.1126339803469836976e-09, -2.9070369957882005086e-08,
+    4.2347877827932403518e-07,  -1.3654692000834678645e-06, -1.3882523362786468719e-05,
+    0.0001867342080340571352,   -0.00074070253416626697512, -0.0060336708714301490533,
+    0.24015818242558961693,     1.6536545626831027356};
+static const double GD_LT16[19] = {
+    2.2137376921775787049e-09,  9.0756561938885390979e-08,  -2.7517406297064545428e-07,
+    1.8239629214389227755e-08,  1.5027403968909827627e-06,  -4.013867526981545969e-06,
+    2.9234449089955446044e-06,  1.2475304481671778723e-05,  -4.7318229009055733981e-05,
+    6.8284851459573175448e-05,  2.4031110387097893999e-05,  -0.0003550375203628474796,
+    0.00095328937973738049703,  -0.0016882755560235047313, 0.0024914420961078508066,
+    -0.0037512085075692412107, 0.005370914553590063617,   1.0052589676941592334,
+    3.0838856104922207635};
+static const double GD_GE16[17] = {
+    -2.7109920616438573243e-11, -2.5556418169965252055e-10, 1.5076572693500548083e-09,
+    -3.7894654401267369937e-09, 7.6157012080783393804e-09,  -1.4960026627149240478e-08,
+    2.9147953450901080826e-08,  -6.7711997758452339498e-08, 2.2900482228026654717e-07,
+    -9.9298272942317002539e-07, 4.5260625972231537039e-06,  -1.9681778105531670567e-05,
+    7.5995277030017761139e-05,  -0.00021503011930044477347, -0.00013871931833623122026,
+    1.0103004648645343977,      4.8499064014085844221};
+
+double orc_erfinv_f64(double x, int fma_) {
+  const double w0 = -log1p(-(x * x));
+  const double* c;
+  int n;
+  double w;
+  if (w0 < 6.25) {
+    c = GD_LT625; n = 23; w = w0 - 3.125;
+  } else if (w0 < 16.0) {
+    c = GD_LT16; n = 19; w = sqrt(w0) - 3.25;
+  } else {
+    c = GD_GE16; n = 17; w = sqrt(w0) - 5.0;
+  }
+  double p = c[0];
+  for (int i = 1; i < n; ++i) p = fma_ ? fma(p, w, c[i]) : c[i] + p * w;
+  if (fabs(x) == 1.0) return x * INFINITY;
+  return p * x;
+}
+
+/* ---- samplers -------------------------------------------------------------------------- */
+
+static inline double xla_max(double a, double b) {
+  if (isnan(a) || isnan(b)) return NAN;
+  return a > b ? a : b;
+}
+
+/* R/random.R:288-304: bits >> (nbits - nmant) | bits(1.0), bitcast, - 1, then
+ * floats * (maxval - minval) + minval and max(minval, .), all in the target dtype. */
+double orc_uniform_at(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
+                      double minval, double maxval, int mul_add_fma, uint64_t i) {
+  switch (dtype) {
+    case ORC_F32: {
+      const uint32_t b = (uint32_t)orc_bits_at(key, 32, size, partitionable, i);
+      const float f = bits_f32((b >> 9) | 0x3F800000u) - 1.0f;
+      const float mn = (float)minval, mx = (float)maxval;
+      const float d = mx - mn;
+      const float r = mul_add_fma ? fmaf(f, d, mn) : f * d + mn;
+      return (float)xla_max(mn, r);
+    }
+    case ORC_F64: {
+      const uint64_t b = orc_bits_at(key, 64, size, partitionable, i);
+      const double f = bits_f64((b >> 12) | 0x3FF0000000000000ull) - 1.0;
+      const double d = maxval - minval;
+      const double r = mul_add_fma ? fma(f, d, minval) : f * d + minval;
+      return xla_max(minval, r);
+    }
+    case ORC_F16:
+    case ORC_BF16: {
+      const int bf = dtype == ORC_BF16;
+      /* float16: 16 random bits, shift 6, one = 0x3C00; bfloat16: 8 random bits
+       * widened to 16, shift 1, one = 0x3F80 (nmant < 8 uses 8-bit draws). */
+      const uint32_t b = (uint32_t)orc_bits_at(key, bf ? 8 : 16, size, partitionable, i);
+      const uint16_t fb = bf ? (uint16_t)((b >> 1) | 0x3F80u) : (uint16_t)((b >> 6) | 0x3C00u);
+      const float f = rh(half_bits_to_f32(fb, bf) - 1.0f, bf);
+      const float mn = rh(f64_to_f32_odd(minval), bf), mx = rh(f64_to_f32_odd(maxval), bf);
+      const float d = rh(mx - mn, bf);
+      /* fused: the exact f * d + mn (22-bit product, in double) rounded once */
+      const float r = mul_add_fma ? rh(f64_to_f32_odd((double)f * (double)d + (double)mn), bf)
+                                  : rh(rh(f * d, bf) + mn, bf);
+      return xla_max(mn, r);
+    }
+  }
+  return NAN;
+}
+
+/* R/random.R:502-508: u = uniform(lo = nextafter(-1, 0), hi = 1), sqrt(2) * erf_inv(u). */
+double orc_normal_at(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
+                     int erfinv_fma, uint64_t i) {
+  switch (dtype) {
+    case ORC_F32: {
+      const float u = (float)orc_uniform_at(key, ORC_F32, size, partitionable,
+                                            -1.0 + 0x1p-24, 1.0, 0, i);
+      return (float)1.41421356237309504880 * orc_erfinv_f32(u, erfinv_fma);
+    }
+    case ORC_F64: {
+      const double u = orc_uniform_at(key, ORC_F64, size, partitionable, -1.0 + 0x1p-53, 1.0,
+                                      0, i);
+      return 1.41421356237309504880 * orc_erfinv_f64(u, erfinv_fma);
+    }
+    case ORC_F16:
+    case ORC_BF16: {
+      const int bf = dtype == ORC_BF16;
+      const double lo = bf ? -1.0 + 0x1p-8 : -1.0 + 0x1p-11;
+      const float u = (float)orc_uniform_at(key, dtype, size, partitionable, lo, 1.0, 0, i);
+      /* erf_inv of a 16-bit float is evaluated in float32 and rounded back. */
+      const float e = rh(orc_erfinv_f32(u, erfinv_fma), bf);
+      return rh(rh((float)1.41421356237309504880, bf) * e, bf);
+    }
+  }
+  return NAN;
+}
+
+static void store_float(void* out, int dtype, int64_t t, double v) {
+  switch (dtype) {
+    case ORC_F32: ((float*)out)[t] = (float)v; break;
+    case ORC_F64: ((double*)out)[t] = v; break;
+    default: ((uint16_t*)out)[t] = f32_to_half_bits((float)v, dtype == ORC_BF16); break;
+  }
+}
+
+int orc_uniform(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
+                double minval, double maxval, int mul_add_fma, uint64_t begin,
+                uint64_t count, void* out) {
+  if (dtype < ORC_F32 || dtype > ORC_BF16) return 1;
+  if (begin > size || count > size - begin) return 2;
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t)
+    store_float(out, dtype, t,
+                orc_uniform_at(key, dtype, size, partitionable, minval, maxval, mul_add_fma,
+                               begin + (uint64_t)t));
+  return 0;
+}
+
+int orc_normal(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
+               int erfinv_fma, uint64_t begin, uint64_t count, void* out) {
+  if (dtype < ORC_F32 || dtype > ORC_BF16) return 1;
+  if (begin > size || count > size - begin) return 2;
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t)
+    store_float(out, dtype, t,
+                orc_normal_at(key, dtype, size, partitionable, erfinv_fma, begin + (uint64_t)t));
+  return 0;
+}
+
+/* R/random.R:656-666, mode "low": uniform(key, shape, dtype(p)) < p. */
+int orc_bernoulli(const uint32_t key[2], int p_dtype, double p, uint64_t size,
+                  int partitionable, uint64_t begin, uint64_t count, uint8_t* out) {
+  if (p_dtype < ORC_F32 || p_dtype > ORC_BF16) return 1;
+  if (begin > size || count > size - begin) return 2;
+  double pc = p;
+  if (p_dtype == ORC_F32) pc = (float)p;
+  if (p_dtype == ORC_F16 || p_dtype == ORC_BF16) pc = rh(f64_to_f32_odd(p), p_dtype == ORC_BF16);
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t)
+    out[t] = orc_uniform_at(key, p_dtype, size, partitionable, 0.0, 1.0, 0,
+                            begin + (uint64_t)t) < pc;
+  return 0;
+}

@@ -1,0 +1,189 @@
+"""ctypes binding of the CPU oracle (oracle/jxr_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the CPU
+baseline leg of bench.py, as the checker.  The product package (jaxr_b200) never
+imports it.  Build with `make -C oracle`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+F32, F64, F16, BF16 = 0, 1, 2, 3
+DTYPE_CODE = {"float32": F32, "float64": F64, "float16": F16, "bfloat16": BF16}
+NP_FLOAT = {F32: np.float32, F64: np.float64, F16: np.uint16, BF16: np.uint16}
+NP_BITS = {8: np.uint8, 16: np.uint16, 32: np.uint32, 64: np.uint64}
+
+_lib = None
+
+
+def build():
+    import subprocess
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        u32p = ctypes.POINTER(ctypes.c_uint32)
+        vp = ctypes.c_void_p
+        u64, i64, i32, dbl = ctypes.c_uint64, ctypes.c_int64, ctypes.c_int, ctypes.c_double
+        L.orc_threefry2x32.argtypes = [ctypes.c_uint32] * 4 + [u32p]
+        L.orc_threefry_2x32.argtypes = [u32p, u32p, i64, u32p]
+        L.orc_seed.argtypes = [i64, i32, u32p]
+        L.orc_split.argtypes = [u32p, i64, i32, u32p]
+        L.orc_fold_in.argtypes = [u32p, ctypes.c_uint32, u32p]
+        L.orc_bits_at.argtypes = [u32p, i32, u64, i32, u64]
+        L.orc_bits_at.restype = u64
+        L.orc_random_bits.argtypes = [u32p, i32, u64, i32, u64, u64, vp]
+        L.orc_erfinv_f32.argtypes = [ctypes.c_float, i32]
+        L.orc_erfinv_f32.restype = ctypes.c_float
+        L.orc_erfinv_f64.argtypes = [dbl, i32]
+        L.orc_erfinv_f64.restype = dbl
+        L.orc_uniform.argtypes = [u32p, i32, u64, i32, dbl, dbl, i32, u64, u64, vp]
+        L.orc_normal.argtypes = [u32p, i32, u64, i32, i32, u64, u64, vp]
+        L.orc_bernoulli.argtypes = [u32p, i32, dbl, u64, i32, u64, u64, vp]
+        L.orc_uniform_at.argtypes = [u32p, i32, u64, i32, dbl, dbl, i32, u64]
+        L.orc_uniform_at.restype = dbl
+        L.orc_normal_at.argtypes = [u32p, i32, u64, i32, i32, u64]
+        L.orc_normal_at.restype = dbl
+        L.orc_set_threads.argtypes = [i32]
+        L.orc_get_threads.restype = i32
+        _lib = L
+    return _lib
+
+
+def _key(key):
+    k = (ctypes.c_uint32 * 2)(int(key[0]) & 0xFFFFFFFF, int(key[1]) & 0xFFFFFFFF)
+    return k
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def threefry2x32(k0, k1, c0, c1):
+    out = (ctypes.c_uint32 * 2)()
+    lib().orc_threefry2x32(k0, k1, c0, c1, out)
+    return int(out[0]), int(out[1])
+
+
+def threefry_2x32(key, count):
+    count = np.ascontiguousarray(count, dtype=np.uint32)
+    out = np.empty_like(count)
+    lib().orc_threefry_2x32(_key(key), count.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)),
+                            count.size, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    return out
+
+
+def seed(s, x64=False):
+    out = (ctypes.c_uint32 * 2)()
+    lib().orc_seed(int(s), int(bool(x64)), out)
+    return np.array([out[0], out[1]], dtype=np.uint32)
+
+
+def split(key, num, partitionable=True):
+    out = np.empty((int(num), 2), dtype=np.uint32)
+    lib().orc_split(_key(key), int(num), int(bool(partitionable)),
+                    out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    return out
+
+
+def fold_in(key, data):
+    out = (ctypes.c_uint32 * 2)()
+    lib().orc_fold_in(_key(key), int(data) & 0xFFFFFFFF, out)
+    return np.array([out[0], out[1]], dtype=np.uint32)
+
+
+def random_bits(key, bit_width, size, partitionable=True, begin=0, count=None):
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=NP_BITS[bit_width])
+    rc = lib().orc_random_bits(_key(key), bit_width, int(size), int(bool(partitionable)),
+                               int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_random_bits failed ({rc})")
+    return out
+
+
+def bits_at(key, bit_width, size, partitionable, idx):
+    L = lib()
+    k = _key(key)
+    return np.array([L.orc_bits_at(k, bit_width, int(size), int(bool(partitionable)), int(i))
+                     for i in idx], dtype=NP_BITS[bit_width])
+
+
+def erfinv(x, dtype="float32", fma=True):
+    L = lib()
+    if dtype == "float32":
+        return np.array([L.orc_erfinv_f32(float(v), int(fma)) for v in
+                         np.asarray(x, dtype=np.float32).ravel()], dtype=np.float32)
+    return np.array([L.orc_erfinv_f64(float(v), int(fma)) for v in
+                     np.asarray(x, dtype=np.float64).ravel()], dtype=np.float64)
+
+
+def uniform(key, dtype, size, partitionable=True, minval=0.0, maxval=1.0, fma=True, begin=0,
+            count=None):
+    code = DTYPE_CODE[dtype]
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=NP_FLOAT[code])
+    rc = lib().orc_uniform(_key(key), code, int(size), int(bool(partitionable)), float(minval),
+                           float(maxval), int(fma), int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_uniform failed ({rc})")
+    return out
+
+
+def normal(key, dtype, size, partitionable=True, fma=True, begin=0, count=None):
+    code = DTYPE_CODE[dtype]
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=NP_FLOAT[code])
+    rc = lib().orc_normal(_key(key), code, int(size), int(bool(partitionable)), int(fma),
+                          int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_normal failed ({rc})")
+    return out
+
+
+def bernoulli(key, p_dtype, p, size, partitionable=True, begin=0, count=None):
+    code = DTYPE_CODE[p_dtype]
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=np.uint8)
+    rc = lib().orc_bernoulli(_key(key), code, float(p), int(size), int(bool(partitionable)),
+                             int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_bernoulli failed ({rc})")
+    return out
+
+
+def uniform_at(key, dtype, size, partitionable, minval, maxval, fma, idx):
+    L = lib()
+    k = _key(key)
+    code = DTYPE_CODE[dtype]
+    return np.array([L.orc_uniform_at(k, code, int(size), int(bool(partitionable)),
+                                      float(minval), float(maxval), int(fma), int(i))
+                     for i in idx])
+
+
+def normal_at(key, dtype, size, partitionable, fma, idx):
+    L = lib()
+    k = _key(key)
+    code = DTYPE_CODE[dtype]
+    return np.array([L.orc_normal_at(k, code, int(size), int(bool(partitionable)), int(fma),
+                                     int(i)) for i in idx])
+
+
+def set_threads(n):
+    lib().orc_set_threads(int(n))
+
+
+def get_threads():
+    return int(lib().orc_get_threads())
