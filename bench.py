@@ -1,0 +1,330 @@
+#!/usr/bin/env python
+"""Threefry 32-bit words/s on B200: random_bits(random_key(123), (2^34,)) uint32.
+
+The workload is the bulk-bits request (64 GiB of uint32, jax_threefry_partitionable
+layout, 32-bit mode), split by contiguous counter range over the N GPUs of one node:
+rank r writes elements [r 2^34/N, (r+1) 2^34/N) into its own HBM with no
+communication.  A step is one pass of that request; value = 2^34 words / the max over
+ranks of the device time per step.
+
+    python bench.py [--gpus N --steps K --warmup W]      # our kernels
+    python bench.py --impl reference                      # the CPU implementation
+
+For N > 1 launch one process per GPU with torch.distributed.run.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TOTAL = 1 << 34          # words per step (the 2^34-word request)
+SEED = 123
+METRIC = "threefry 32-bit words/s (device-timed) at 1/2/4/8 B200; % of INT-pipe roofline"
+OPS_PER_BLOCK = 100      # the metric's integer-op count per 64-bit cipher block
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+TRAFFIC = os.path.join(ROOT, "profiles", "traffic.json")
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def config_block(args, world, e2e_words=None):
+    c = {"workload": "random_bits(random_key(123L), shape=(2^34,)) uint32, "
+                     "jax_threefry_partitionable, x32",
+         "request_words": TOTAL, "per_gpu_words": TOTAL // world, "sharding": "contiguous counter range",
+         "parallelism": f"counter-range x{world}", "l2": "outputs larger than L2 (no flush needed)"}
+    if e2e_words:
+        c["e2e_words_per_gpu"] = e2e_words
+    return c
+
+
+# ---- clocks during the timed region ------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.path = f"/tmp/jxr_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.dev)], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for ln in open(self.path):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        mhz = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---- the CPU implementation (oracle port, all host threads) -------------------------------------
+
+def cpu_words_per_s(min_seconds=3.0, sample=1 << 27):
+    """Bulk partitionable uint32 bits of the same request on the host cores: the first
+    `sample` words of the 2^34-word request, repeated until min_seconds have passed."""
+    import numpy as np
+    from oracle import oracle as orc
+    key = orc.seed(SEED)
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    out = np.empty(sample, dtype=np.uint32)
+    lib = orc.lib()
+    import ctypes
+    k = (ctypes.c_uint32 * 2)(int(key[0]), int(key[1]))
+    lib.orc_random_bits(k, 32, TOTAL, 1, 0, sample, out.ctypes.data_as(ctypes.c_void_p))  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        lib.orc_random_bits(k, 32, TOTAL, 1, reps * sample % TOTAL, sample,
+                            out.ctypes.data_as(ctypes.c_void_p))
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_seconds:
+            break
+    return reps * sample / dt, threads, f"first {reps} x 2^{sample.bit_length() - 1} words of the request"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: F401
+    from oracle import oracle as orc
+    orc.build()
+    vals = []
+    for _ in range(args.warmup):
+        cpu_words_per_s(min_seconds=0.5)
+    sample_desc, threads = "", 1
+    for _ in range(args.steps):
+        v, threads, sample_desc = cpu_words_per_s(min_seconds=1.0)
+        vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "words/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": TOTAL / value * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u32", "data": "synthetic (seeds only)",
+        "config": config_block(args, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "words/s", "cores": threads, "kind": "port",
+                         "sample": sample_desc + " per step; the reference (R + XLA CPU PJRT "
+                                   "plugin) cannot run here, so its C restatement runs, "
+                                   "OpenMP over all host threads"},
+        "e2e": {"value": value, "unit": "words/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- our kernels ---------------------------------------------------------------------------------
+
+def probe_peak(torch, nat, dev, iters=2000):
+    """Blocks/s of the register-resident cipher (the integer-pipe ceiling), best of 3."""
+    import ctypes
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    best = 0.0
+    for cps in (4, 8):
+        sink = torch.empty(sms * cps * 256, dtype=torch.int32, device=dev)
+        blocks = ctypes.c_uint64(0)
+        st = torch.cuda.current_stream().cuda_stream
+        nat.call("jxr_probe_cipher", 10, cps, sink.data_ptr(), ctypes.byref(blocks), st)
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            nat.call("jxr_probe_cipher", iters, cps, sink.data_ptr(), ctypes.byref(blocks), st)
+            e1.record()
+            e1.synchronize()
+            best = max(best, blocks.value / (e0.elapsed_time(e1) * 1e-3))
+    return best
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import jaxr_b200 as jr
+    from jaxr_b200 import _native as nat
+    from jaxr_b200 import build as jb
+    from jaxr_b200.shard import random_bits_shard, random_bits_to_host, shard_range
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    jb.build()
+    nat.lib()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    key = jr.random_key(SEED)
+    lo, hi = shard_range(TOTAL, rank, world)
+    out = torch.empty(hi - lo, dtype=torch.uint32, device=dev)
+
+    def step():
+        random_bits_shard(key, (TOTAL,), rank, world, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.25)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    ms_max = max_over_ranks(ms)
+    value = TOTAL / (ms_max * 1e-3)
+
+    # roofline of the kernel on this GPU: cipher blocks/s against the register-resident
+    # cipher's ceiling, and output bytes/s against measured HBM bandwidth
+    peak_blocks = probe_peak(torch, nat, dev)
+    my_blocks = (hi - lo) / (ms * 1e-3)
+    hbm_peak = None
+    try:
+        hbm_peak = json.load(open(PEAKS))["hbm_gbs"]
+    except (OSError, ValueError, KeyError):
+        pass
+    traffic = None
+    try:
+        tr = json.load(open(TRAFFIC))["bits_u32"]
+        traffic = tr["dram_bytes_per_word"] * (hi - lo)
+    except (OSError, ValueError, KeyError):
+        pass
+    roofline = {
+        "bound": "int", "unit": "Tops/s",
+        "achieved": my_blocks * OPS_PER_BLOCK / 1e12,
+        "peak": peak_blocks * OPS_PER_BLOCK / 1e12,
+        "frac": my_blocks / peak_blocks,
+        "ops_per_block": OPS_PER_BLOCK,
+        "peak_source": "measured: jxr_probe_cipher (threefry20 in registers, no memory), this GPU",
+        "traffic": traffic,
+        "hbm": {"achieved": my_blocks * 4 / 1e9, "peak": hbm_peak, "unit": "GB/s",
+                "frac": (my_blocks * 4 / 1e9 / hbm_peak) if hbm_peak else None,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+    }
+
+    # end to end through the public API with a host buffer: key in, bits out to pinned
+    # host memory, chunked generation overlapped with the copies
+    e2e = None
+    e2e_words = None
+    if not args.no_e2e:
+        e2e_words = min(hi - lo, args.e2e_words)
+        host = torch.empty(e2e_words, dtype=torch.uint32, pin_memory=True)
+        random_bits_to_host(key, (e2e_words,), out=host)  # warm
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            random_bits_to_host(key, (e2e_words,), out=host)
+        dt = max_over_ranks((time.perf_counter() - t0) / args.e2e_steps)
+        e2e = {"value": e2e_words * world / dt, "unit": "words/s", "h2d_bytes_per_step": 8,
+               "d2h_bytes_per_step": e2e_words * 4 * world,
+               "note": "random_bits_to_host of 2^%d words per GPU per step into pinned host "
+                       "memory; the key goes host->device and every word device->host inside "
+                       "the timed region" % (e2e_words.bit_length() - 1)}
+        del host
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, sample = cpu_words_per_s()
+        cpu = {"value": v, "unit": "words/s", "cores": threads, "kind": "port",
+               "sample": sample + " (C restatement of the reference, OpenMP)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "words/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
+            "data": "synthetic (seeds only; the request is generated from random_key(123))",
+            "config": config_block(args, world, e2e_words),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": args.steps, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    del out
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-words", type=int, default=1 << 30)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("note: warmup raised to 3")
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

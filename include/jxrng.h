@@ -135,6 +135,18 @@ int jxr_uniform_from_bits(const void* bits, int64_t n, int dtype, double minval,
                           double maxval, uint32_t flags, void* out, void* stream);
 int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void* stream);
 
+/* Array-valued parameters, applied to unit draws u = uniform(key, shape, dtype, 0, 1)
+ * (which are the unit floats themselves), all arrays of n elements of dtype:
+ *  - uniform with per-element bounds (R/random.R:297-303, bounds broadcast by the
+ *    caller): out = max(minval, u * (maxval - minval) + minval);
+ *  - bernoulli with per-element p (R/random.R:656-666): mode "low" (u_hi == NULL)
+ *    out = u_lo < p; mode "high" out = u_hi * 2^-nmant < p - u_lo, where u_lo and
+ *    u_hi are the two halves of uniform(key, (2, shape)).  out: uint8 0/1. */
+int jxr_uniform_affine(const void* unit, const void* minval, const void* maxval, int64_t n,
+                       int dtype, uint32_t flags, void* out, void* stream);
+int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p, int64_t n,
+                               int dtype, uint8_t* out, void* stream);
+
 /* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
  * element-wise for F32 or F64. */
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);
@@ -147,6 +159,14 @@ int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);
 int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size,
                          uint64_t begin, uint64_t count, int layout, int bit_width,
                          void* host_out);
+
+/* Throughput probe: launches (number of SMs) x ctas_per_sm CTAs of 256 threads that
+ * each push 8 register-resident blocks through `iters` threefry20 passes (no counters,
+ * loads or stores) and returns in *blocks_out the number of cipher blocks that launch
+ * computes; sink needs (number of SMs) x ctas_per_sm x 256 uint32.  Timing it gives the
+ * cipher's integer-pipe ceiling on this GPU (the roofline of the bits kernels). */
+int jxr_probe_cipher(uint64_t iters, int ctas_per_sm, uint32_t* sink, uint64_t* blocks_out,
+                     void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,1031 @@
+// jxrng: sm_100a kernels and the C ABI (include/jxrng.h) for jaxR's threefry2x32
+// random-bits path.
+//
+// Two cipher kernels cover every request:
+//   k_blocks  one cipher block per output element.  Counters are either the (hi, lo)
+//             words of the element's C-order index (the partitionable layout,
+//             R/prng.R:212-227, any bit width) or (i, size + i) (the original layout's
+//             64-bit draws, R/prng.R:246-251).
+//   k_words   the original layout's hash of iota(n) (R/prng.R:101-120, :229-262):
+//             block j hashes (j, half + j) and yields words j and half + j, each
+//             unpacked into 32 / W elements of W bits.
+// Both fuse the sampler transform (samplers.cuh) into the same pass, keep each
+// thread's blocks in registers, and write 16-byte vector stores that a warp
+// issues as one contiguous 512-byte segment.  Grids are persistent: one wave of
+// resident CTAs (a multiple of the SM count) strides over the work.
+#include "jxrng.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "samplers.cuh"
+#include "threefry.cuh"
+
+namespace jxr {
+namespace {
+
+constexpr int kThreads = 256;
+
+__host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+#define JXR_CUDA(expr)                                                                   \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess) return fail(JXR_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+};
+
+int device_info(DeviceInfo* info) {
+  static DeviceInfo cache[64];
+  int dev = 0;
+  JXR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(JXR_ERR_NO_DEVICE, "device index %d out of range", dev);
+  if (cache[dev].sms == 0) {
+    int sms = 0, major = 0;
+    JXR_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    JXR_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    cache[dev].major = major;
+    cache[dev].sms = sms;
+  }
+  *info = cache[dev];
+  if (info->major != 10)
+    return fail(JXR_ERR_NO_DEVICE, "device %d has compute capability %d.x; this library is built for sm_100a",
+                dev, info->major);
+  return JXR_OK;
+}
+
+// ---- cipher output -> draw ----------------------------------------------------------------
+
+// kBits == -1 stores the key pair (x0, x1) itself (split); otherwise W-bit draws:
+// 64 bits are x0 << 32 | x1 (R/prng.R:220-224), narrower ones x0 ^ x1 truncated
+// (R/prng.R:225-226).
+template <int kBits>
+struct Draw;
+template <> struct Draw<64> {
+  __device__ static uint64_t get(uint32_t x0, uint32_t x1) { return ((uint64_t)x0 << 32) | x1; }
+};
+template <> struct Draw<32> {
+  __device__ static uint32_t get(uint32_t x0, uint32_t x1) { return x0 ^ x1; }
+};
+template <> struct Draw<16> {
+  __device__ static uint16_t get(uint32_t x0, uint32_t x1) { return (uint16_t)(x0 ^ x1); }
+};
+template <> struct Draw<8> {
+  __device__ static uint8_t get(uint32_t x0, uint32_t x1) { return (uint8_t)(x0 ^ x1); }
+};
+
+struct OpKeyPair {
+  static constexpr int kBits = -1;
+  using Out = uint64_t;  // little-endian: (x0, x1) in memory
+};
+
+template <class Op>
+__device__ __forceinline__ typename Op::Out apply(const Op& op, uint32_t x0, uint32_t x1) {
+  if constexpr (Op::kBits == -1) return ((uint64_t)x1 << 32) | x0;
+  else return op(Draw<Op::kBits>::get(x0, x1));
+}
+
+// 16 bytes of outputs, stored as one vector
+template <class T>
+union Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  T v[N];
+  uint4 u;
+};
+
+// ---- k_blocks: one block per output -----------------------------------------------------
+
+enum { kCtrIndex = 0, kCtrPair = 1 };
+
+template <class Out>
+__host__ __device__ constexpr int groups_for() {
+  // blocks in flight per thread: G groups of 16 / sizeof(Out) outputs
+  return sizeof(Out) >= 8 ? 4 : (sizeof(Out) == 4 ? 2 : 1);
+}
+
+template <class Op, int kCtr, bool kOneKey>
+__global__ void __launch_bounds__(kThreads)
+    k_blocks(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin, uint64_t count,
+             uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, Op op,
+             typename Op::Out* __restrict__ out) {
+  using Out = typename Op::Out;
+  constexpr int V = 16 / sizeof(Out);
+  constexpr int G = groups_for<Out>();
+  constexpr int N = G * V;
+
+  KeySchedule s1;
+  if (kOneKey) s1 = make_schedule(__ldg(keys), __ldg(keys + 1));
+
+  const uint64_t stride = (uint64_t)gridDim.x * (kThreads * G);
+  for (uint64_t base = (uint64_t)blockIdx.x * (kThreads * G); base < nchunks; base += stride) {
+    uint64_t row[G], pos[G];
+    KeySchedule s[G];
+    uint32_t x0[N], x1[N];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
+      if (kOneKey) {
+        row[g] = 0;
+        pos[g] = c * V;
+        s[g] = s1;
+      } else {
+        const uint64_t cc = c < nchunks ? c : nchunks - 1;
+        row[g] = cc / chunks_per_row;
+        pos[g] = (cc - row[g] * chunks_per_row) * V;
+        s[g] = make_schedule(__ldg(keys + 2 * row[g]), __ldg(keys + 2 * row[g] + 1));
+      }
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const uint64_t i = begin + pos[g] + v;  // element index within the request
+        if (kCtr == kCtrIndex) {
+          x0[g * V + v] = (uint32_t)(i >> 32);
+          x1[g * V + v] = (uint32_t)i;
+        } else {
+          x0[g * V + v] = (uint32_t)i;
+          x1[g * V + v] = (uint32_t)(size + i);
+        }
+      }
+    }
+    if (kOneKey) {
+      threefry20<N>(s1, x0, x1);
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        uint32_t (&a0)[V] = *reinterpret_cast<uint32_t(*)[V]>(&x0[g * V]);
+        uint32_t (&a1)[V] = *reinterpret_cast<uint32_t(*)[V]>(&x1[g * V]);
+        threefry20<V>(s[g], a0, a1);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
+      if (c >= nchunks) continue;
+      Vec16<Out> r;
+#pragma unroll
+      for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g * V + v], x1[g * V + v]);
+      Out* dst = out + row[g] * count + pos[g];
+      if (vec_ok && pos[g] + V <= count) {
+        *reinterpret_cast<uint4*>(dst) = r.u;
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (pos[g] + v < count) dst[v] = r.v[v];
+      }
+    }
+  }
+}
+
+template <class K>
+int resident_grid(K kernel, uint64_t work_ctas, int* grid) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int per_sm = 0;
+  JXR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0));
+  if (per_sm < 1) per_sm = 1;
+  const uint64_t wave = (uint64_t)di.sms * (uint64_t)per_sm;
+  *grid = (int)std::min<uint64_t>(std::max<uint64_t>(work_ctas, 1), wave);
+  return JXR_OK;
+}
+
+template <class Op, int kCtr>
+int launch_blocks(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                  uint64_t count, const Op& op, void* out, cudaStream_t st) {
+  using Out = typename Op::Out;
+  constexpr int V = 16 / sizeof(Out);
+  constexpr int G = groups_for<Out>();
+  if (count == 0 || nkeys == 0) return JXR_OK;
+  const uint64_t cpr = (count + V - 1) / V;
+  if (cpr > ~0ull / (uint64_t)nkeys) return fail(JXR_ERR_INVALID_ARGUMENT, "request too large");
+  const uint64_t nchunks = cpr * (uint64_t)nkeys;
+  const int vec_ok = ((uintptr_t)out % 16 == 0) && (nkeys == 1 || (count * sizeof(Out)) % 16 == 0);
+  const uint64_t ctas = (nchunks + kThreads * G - 1) / (kThreads * G);
+  int grid = 0, rc;
+  if (nkeys == 1) {
+    auto k = k_blocks<Op, kCtr, true>;
+    if ((rc = resident_grid(k, ctas, &grid))) return rc;
+    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, (Out*)out);
+  } else {
+    auto k = k_blocks<Op, kCtr, false>;
+    if ((rc = resident_grid(k, ctas, &grid))) return rc;
+    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, (Out*)out);
+  }
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+// ---- k_words: the original layout's hash of iota(nwords) --------------------------------
+
+template <class Op>
+__host__ __device__ constexpr int words_per_thread() {
+  // enough blocks that one slab chunk is a whole number of 16-byte vectors (>= 4 blocks)
+  constexpr int per = Op::kBits > 0 ? 32 / Op::kBits : 1;
+  constexpr int b = 16 / (per * (int)sizeof(typename Op::Out));
+  return b > 4 ? b : 4;
+}
+
+// Word w (0 <= w < nwords) holds elements [w * per, w * per + per) of the request, in
+// little-endian W-bit pieces (R/prng.R:252-260).  Block j hashes counts (j, half + j),
+// the second count being the zero pad when half + j == nwords (R/prng.R:112-116).
+template <class Op>
+__global__ void __launch_bounds__(kThreads)
+    k_words(const uint32_t* __restrict__ keys, uint64_t nwords, uint64_t half, uint64_t jlo,
+            uint64_t jhi, uint64_t units_per_row, uint64_t nunits, uint64_t begin, uint64_t count,
+            Op op, typename Op::Out* __restrict__ out) {
+  using Out = typename Op::Out;
+  constexpr int B = words_per_thread<Op>();
+  constexpr int W = Op::kBits;
+  constexpr int per = 32 / W;
+  const uint64_t end = begin + count;
+  const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+  for (uint64_t u = (uint64_t)blockIdx.x * kThreads + threadIdx.x; u < nunits; u += stride) {
+    const uint64_t row = u / units_per_row;
+    const uint64_t j0 = jlo + (u - row * units_per_row) * B;
+    const KeySchedule s = make_schedule(__ldg(keys + 2 * row), __ldg(keys + 2 * row + 1));
+    uint32_t x0[B], x1[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const uint64_t j = j0 + b;
+      x0[b] = (uint32_t)j;
+      x1[b] = half + j < nwords ? (uint32_t)(half + j) : 0u;
+    }
+    threefry20<B>(s, x0, x1);
+    Out* orow = out + row * count;
+#pragma unroll
+    for (int slab = 0; slab < 2; ++slab) {
+      const uint64_t w0 = slab == 0 ? j0 : half + j0;  // first word of this slab chunk
+      // words of this slab that exist: slab 0 needs j < half, slab 1 half + j < nwords
+      const uint64_t wlim = slab == 0 ? umin(half, jhi) : umin(nwords, half + jhi);
+      const uint64_t e0 = w0 * per;  // first element
+      Vec16<Out> r[(B * per + Vec16<Out>::N - 1) / Vec16<Out>::N];
+      Out* rv = &r[0].v[0];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const uint32_t word = slab == 0 ? x0[b] : x1[b];
+#pragma unroll
+        for (int q = 0; q < per; ++q) {
+          if constexpr (W == 32) rv[b * per + q] = op(word);
+          else rv[b * per + q] = op((typename Op::Bits)(word >> (W * q)));
+        }
+      }
+      constexpr int NE = B * per;
+      const bool all_in = w0 + B <= wlim && e0 >= begin && e0 + NE <= end;
+      Out* dst = orow + (e0 - begin);
+      if (all_in && ((uintptr_t)dst % 16) == 0) {
+#pragma unroll
+        for (int k = 0; k < (NE * (int)sizeof(Out)) / 16; ++k)
+          reinterpret_cast<uint4*>(dst)[k] = r[k].u;
+      } else {
+#pragma unroll
+        for (int k = 0; k < NE; ++k) {
+          const uint64_t e = e0 + k;
+          if (w0 + k / per < wlim && e >= begin && e < end) orow[e - begin] = rv[k];
+        }
+      }
+    }
+  }
+}
+
+template <class Op>
+int launch_words(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                 uint64_t count, const Op& op, void* out, cudaStream_t st) {
+  using Out = typename Op::Out;
+  constexpr int B = words_per_thread<Op>();
+  constexpr int per = 32 / Op::kBits;
+  if (count == 0 || nkeys == 0) return JXR_OK;
+  const uint64_t nwords = (size + per - 1) / per;
+  if (nwords >= 0xFFFFFFFFull)
+    return fail(JXR_ERR_NOT_IMPLEMENTED,
+                "original-layout requests of 2^32-1 or more 32-bit words (key splitting, "
+                "R/prng.R:236-245) are not supported");
+  const uint64_t half = (nwords + 1) / 2;
+  const uint64_t wb = begin / per, we = (begin + count + per - 1) / per;
+  // blocks whose first word (j) or second word (half + j) falls in [wb, we)
+  uint64_t r1lo = wb, r1hi = std::min(we, half);
+  uint64_t r2lo = (std::max(wb, half)) - half, r2hi = we > half ? we - half : 0;
+  struct Range { uint64_t lo, hi; } ranges[2];
+  int nr = 0;
+  if (r1lo < r1hi) ranges[nr++] = {r1lo, r1hi};
+  if (r2lo < r2hi) {
+    if (nr && r2lo <= ranges[0].hi && r2hi >= ranges[0].lo) {
+      ranges[0].lo = std::min(ranges[0].lo, r2lo);
+      ranges[0].hi = std::max(ranges[0].hi, r2hi);
+    } else {
+      ranges[nr++] = {r2lo, r2hi};
+    }
+  }
+  for (int k = 0; k < nr; ++k) {
+    const uint64_t upr = (ranges[k].hi - ranges[k].lo + B - 1) / B;
+    const uint64_t nunits = upr * (uint64_t)nkeys;
+    int grid = 0, rc;
+    auto kern = k_words<Op>;
+    if ((rc = resident_grid(kern, (nunits + kThreads - 1) / kThreads, &grid))) return rc;
+    kern<<<grid, kThreads, 0, st>>>(keys, nwords, half, ranges[k].lo, ranges[k].hi, upr, nunits,
+                                    begin, count, op, (Out*)out);
+    JXR_CUDA(cudaGetLastError());
+  }
+  return JXR_OK;
+}
+
+// ---- dispatch by layout -------------------------------------------------------------------
+
+// Ops drawing W <= 32 bits: partitionable -> k_blocks, original -> k_words.
+// Ops drawing 64 bits: k_blocks with index counters or (i, size + i) pairs.
+template <class Op>
+int launch_op(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
+              int layout, const Op& op, void* out, cudaStream_t st) {
+  if (layout == JXR_LAYOUT_PARTITIONABLE)
+    return launch_blocks<Op, kCtrIndex>(keys, nkeys, size, begin, count, op, out, st);
+  if constexpr (Op::kBits == 64) {
+    if (size >= 0x7FFFFFFFull)
+      return fail(JXR_ERR_NOT_IMPLEMENTED,
+                  "original-layout 64-bit requests of 2^31-1 or more elements (key splitting, "
+                  "R/prng.R:236-245) are not supported");
+    return launch_blocks<Op, kCtrPair>(keys, nkeys, size, begin, count, op, out, st);
+  } else {
+    return launch_words<Op>(keys, nkeys, size, begin, count, op, out, st);
+  }
+}
+
+int check_request(const void* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
+                  int layout, const void* out) {
+  if (nkeys < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "nkeys must be >= 0, got %lld", (long long)nkeys);
+  if (layout != JXR_LAYOUT_ORIGINAL && layout != JXR_LAYOUT_PARTITIONABLE)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "layout must be 0 (original) or 1 (partitionable), got %d", layout);
+  if (begin > size || count > size - begin)
+    return fail(JXR_ERR_INVALID_ARGUMENT,
+                "range [%llu, %llu + %llu) is outside a request of %llu elements",
+                (unsigned long long)begin, (unsigned long long)begin, (unsigned long long)count,
+                (unsigned long long)size);
+  if (count && nkeys && (!keys || !out)) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  return JXR_OK;
+}
+
+int check_dtype(int dtype) {
+  if (dtype < JXR_F32 || dtype > JXR_BF16)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "dtype must be 0 (f32), 1 (f64), 2 (f16) or 3 (bf16), got %d", dtype);
+  return JXR_OK;
+}
+
+// host-side conversion of a double bound to a 16-bit float value (round to nearest even)
+float to_half_value(double x, bool bf) {
+  // round to odd into float, then to nearest even at 16 bits: one correct rounding
+  float f = (float)x;
+  if (std::isfinite(x) && (double)f != x) {
+    if (std::fabs((double)f) > std::fabs(x)) f = std::nextafter(f, 0.0f);
+    uint32_t b;
+    std::memcpy(&b, &f, 4);
+    b |= 1u;
+    std::memcpy(&f, &b, 4);
+  }
+  uint32_t b;
+  std::memcpy(&b, &f, 4);
+  uint32_t hb;
+  if (bf) {
+    if ((b & 0x7F800000u) == 0x7F800000u && (b & 0x7FFFFFu)) hb = (b >> 16) | 0x40u;
+    else hb = (b + 0x7FFFu + ((b >> 16) & 1u)) >> 16;
+    uint32_t r = hb << 16;
+    float out;
+    std::memcpy(&out, &r, 4);
+    return out;
+  }
+  const __half h = __float2half_rn(f);
+  return __half2float(h);
+}
+
+// ---- small kernels --------------------------------------------------------------------------
+
+__global__ void k_threefry2x32_elem(const uint32_t* __restrict__ k0, const uint32_t* __restrict__ k1,
+                                    const uint32_t* __restrict__ c0, const uint32_t* __restrict__ c1,
+                                    uint32_t* __restrict__ x0, uint32_t* __restrict__ x1, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const KeySchedule s = make_schedule(k0[i], k1[i]);
+    uint32_t a[1] = {c0[i]}, b[1] = {c1[i]};
+    threefry20<1>(s, a, b);
+    x0[i] = a[0];
+    x1[i] = b[0];
+  }
+}
+
+__global__ void k_hash_counts(const uint32_t* __restrict__ keys, int64_t nkeys,
+                              const uint32_t* __restrict__ cnt, int64_t n, uint32_t* __restrict__ out) {
+  const int64_t half = (n + 1) / 2;
+  const int64_t total = half * nkeys;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = t / half, j = t - row * half;
+    const KeySchedule s = make_schedule(keys[2 * row], keys[2 * row + 1]);
+    uint32_t a[1] = {cnt[j]}, b[1] = {half + j < n ? cnt[half + j] : 0u};
+    threefry20<1>(s, a, b);
+    out[row * n + j] = a[0];
+    if (half + j < n) out[row * n + half + j] = b[0];
+  }
+}
+
+__global__ void k_fold_in(const uint32_t* __restrict__ keys, int64_t nkeys,
+                          const uint32_t* __restrict__ data, int64_t ndata, uint32_t* __restrict__ out,
+                          int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t kk = nkeys == 1 ? 0 : i, dd = ndata == 1 ? 0 : i;
+    const KeySchedule s = make_schedule(keys[2 * kk], keys[2 * kk + 1]);
+    uint32_t a[1] = {0u}, b[1] = {data[dd]};
+    threefry20<1>(s, a, b);
+    out[2 * i] = a[0];
+    out[2 * i + 1] = b[0];
+  }
+}
+
+template <class Op>
+__global__ void k_from_bits(const typename Op::Bits* __restrict__ bits, int64_t n, Op op,
+                            typename Op::Out* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = op(bits[i]);
+}
+
+template <class Op>
+int launch_from_bits(const void* bits, int64_t n, const Op& op, void* out, cudaStream_t st,
+                     int grid) {
+  k_from_bits<Op><<<grid, 256, 0, st>>>((const typename Op::Bits*)bits, n, op,
+                                        (typename Op::Out*)out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+__global__ void k_erfinv_f32(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = erfinv_f32(x[i]);
+}
+__global__ void k_erfinv_f64(const double* __restrict__ x, int64_t n, double* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = erfinv_f64(x[i]);
+}
+
+// ---- element-wise helpers for array-valued parameters ------------------------------------
+
+// uniform with per-element bounds from the unit draw u = uniform(0, 1) (which is the unit
+// float itself): max(minval, u * (maxval - minval) + minval), R/random.R:297-303.
+template <class T, bool kFused>
+__global__ void k_affine(const T* __restrict__ u, const T* __restrict__ mn, const T* __restrict__ mx,
+                         int64_t n, T* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const T lo = mn[i];
+    T r;
+    if constexpr (sizeof(T) == 4) {
+      const T d = __fsub_rn(mx[i], lo);
+      r = kFused ? __fmaf_rn(u[i], d, lo) : __fadd_rn(__fmul_rn(u[i], d), lo);
+    } else {
+      const T d = __dsub_rn(mx[i], lo);
+      r = kFused ? __fma_rn(u[i], d, lo) : __dadd_rn(__dmul_rn(u[i], d), lo);
+    }
+    out[i] = xla_max(lo, r);
+  }
+}
+
+template <bool BF, bool kFused>
+__global__ void k_affine_h(const uint16_t* __restrict__ u, const uint16_t* __restrict__ mn,
+                           const uint16_t* __restrict__ mx, int64_t n, uint16_t* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float f = h2f<BF>(u[i]), lo = h2f<BF>(mn[i]);
+    const float d = rh<BF>(__fsub_rn(h2f<BF>(mx[i]), lo));
+    float r;
+    if (kFused) r = h2f<BF>(d2h<BF>(__fma_rn((double)f, (double)d, (double)lo)));
+    else r = rh<BF>(__fadd_rn(rh<BF>(__fmul_rn(f, d)), lo));
+    out[i] = f2h<BF>(xla_max(lo, r));
+  }
+}
+
+// bernoulli from unit draws (R/random.R:656-666): mode "low" u < p; mode "high"
+// u_hi * 2^-nmant < p - u_lo, all in the dtype of p.
+template <class T>
+__global__ void k_bern_unit(const T* __restrict__ ulo, const T* __restrict__ uhi,
+                            const T* __restrict__ p, int64_t n, T scale, uint8_t* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (uhi == nullptr) {
+      out[i] = ulo[i] < p[i];
+    } else if constexpr (sizeof(T) == 4) {
+      out[i] = __fmul_rn(uhi[i], scale) < __fsub_rn(p[i], ulo[i]);
+    } else {
+      out[i] = __dmul_rn(uhi[i], scale) < __dsub_rn(p[i], ulo[i]);
+    }
+  }
+}
+
+template <bool BF>
+__global__ void k_bern_unit_h(const uint16_t* __restrict__ ulo, const uint16_t* __restrict__ uhi,
+                              const uint16_t* __restrict__ p, int64_t n, float scale,
+                              uint8_t* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float pv = h2f<BF>(p[i]), lo = h2f<BF>(ulo[i]);
+    if (uhi == nullptr) out[i] = lo < pv;
+    else out[i] = rh<BF>(__fmul_rn(h2f<BF>(uhi[i]), scale)) < rh<BF>(__fsub_rn(pv, lo));
+  }
+}
+
+int small_grid(int64_t n, int* grid) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int64_t want = (n + 255) / 256;
+  *grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)di.sms * 8));
+  return JXR_OK;
+}
+
+// ---- fused normal + bernoulli (same key and shape: one cipher pass, two outputs) ---------
+
+template <class OpN, class OpB, int kCtr, bool kOneKey>
+__global__ void __launch_bounds__(kThreads)
+    k_normal_bernoulli(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
+                       uint64_t count, uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, OpN opn,
+                       OpB opb, typename OpN::Out* __restrict__ nout, uint8_t* __restrict__ bout) {
+  using Out = typename OpN::Out;
+  constexpr int V = 16 / sizeof(Out);
+  const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+  for (uint64_t c = (uint64_t)blockIdx.x * kThreads + threadIdx.x; c < nchunks; c += stride) {
+    const uint64_t row = kOneKey ? 0 : c / chunks_per_row;
+    const uint64_t pos = (c - row * chunks_per_row) * V;
+    const KeySchedule s = make_schedule(__ldg(keys + 2 * row), __ldg(keys + 2 * row + 1));
+    uint32_t x0[V], x1[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const uint64_t i = begin + pos + v;
+      x0[v] = kCtr == kCtrIndex ? (uint32_t)(i >> 32) : (uint32_t)i;
+      x1[v] = kCtr == kCtrIndex ? (uint32_t)i : (uint32_t)(size + i);
+    }
+    threefry20<V>(s, x0, x1);
+    Vec16<Out> r;
+    uint8_t bb[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const auto bits = Draw<OpN::kBits>::get(x0[v], x1[v]);
+      r.v[v] = opn(bits);
+      bb[v] = opb(bits);
+    }
+    Out* dst = nout + row * count + pos;
+    uint8_t* bdst = bout + row * count + pos;
+    if (vec_ok && pos + V <= count) {
+      *reinterpret_cast<uint4*>(dst) = r.u;
+#pragma unroll
+      for (int v = 0; v < V; ++v) bdst[v] = bb[v];
+    } else {
+#pragma unroll
+      for (int v = 0; v < V; ++v)
+        if (pos + v < count) { dst[v] = r.v[v]; bdst[v] = bb[v]; }
+    }
+  }
+}
+
+template <class OpN, class OpB>
+int launch_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                            uint64_t count, int layout, const OpN& opn, const OpB& opb, void* nout,
+                            uint8_t* bout, cudaStream_t st) {
+  using Out = typename OpN::Out;
+  constexpr int V = 16 / sizeof(Out);
+  if (count == 0 || nkeys == 0) return JXR_OK;
+  const uint64_t cpr = (count + V - 1) / V;
+  const uint64_t nchunks = cpr * (uint64_t)nkeys;
+  const int vec_ok = ((uintptr_t)nout % 16 == 0) && (nkeys == 1 || (count * sizeof(Out)) % 16 == 0);
+  const uint64_t ctas = (nchunks + kThreads - 1) / kThreads;
+  int grid = 0, rc;
+#define JXR_NB_LAUNCH(CTR, ONE)                                                              \
+  {                                                                                          \
+    auto k = k_normal_bernoulli<OpN, OpB, CTR, ONE>;                                         \
+    if ((rc = resident_grid(k, ctas, &grid))) return rc;                                     \
+    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, opn, opb,   \
+                                 (Out*)nout, bout);                                          \
+  }
+  if (layout == JXR_LAYOUT_PARTITIONABLE) {
+    if (nkeys == 1) JXR_NB_LAUNCH(kCtrIndex, true) else JXR_NB_LAUNCH(kCtrIndex, false)
+  } else {
+    if (nkeys == 1) JXR_NB_LAUNCH(kCtrPair, true) else JXR_NB_LAUNCH(kCtrPair, false)
+  }
+#undef JXR_NB_LAUNCH
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+
+// ---- throughput probe: the cipher alone, in registers ----------------------------------------
+
+// Each thread advances 8 independent blocks through `iters` full threefry20 passes, with
+// no counters, loads or stores: the integer-pipe ceiling of the cipher on this GPU, used
+// as the roofline denominator.  The xor of the final words is stored so the work stays.
+__global__ void __launch_bounds__(kThreads) k_probe_cipher(uint64_t iters, uint32_t* sink) {
+  const uint32_t t = blockIdx.x * kThreads + threadIdx.x;
+  const KeySchedule s = make_schedule(t * 0x9E3779B9u, t ^ 0x85EBCA6Bu);
+  uint32_t x0[8], x1[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { x0[j] = t + j; x1[j] = ~t * (j + 1); }
+  for (uint64_t i = 0; i < iters; ++i) threefry20<8>(s, x0, x1);
+  uint32_t acc = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc ^= x0[j] ^ x1[j];
+  sink[t] = acc;
+}
+}  // namespace
+}  // namespace jxr
+
+// ==== C ABI ==================================================================================
+
+using namespace jxr;
+
+extern "C" {
+
+int jxr_abi_version(void) { return JXR_ABI_VERSION; }
+
+const char* jxr_last_error(void) { return g_error.c_str(); }
+
+int jxr_seed(const int64_t* seeds, int64_t n, int x64, uint32_t* keys_out) {
+  if (n < 0 || (n && (!seeds || !keys_out))) return fail(JXR_ERR_INVALID_ARGUMENT, "bad seed arrays");
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t s = (uint64_t)seeds[i];
+    keys_out[2 * i] = x64 ? (uint32_t)(s >> 32) : 0u;
+    keys_out[2 * i + 1] = (uint32_t)s;
+  }
+  return JXR_OK;
+}
+
+int jxr_threefry2x32(const uint32_t* k0, const uint32_t* k1, const uint32_t* c0, const uint32_t* c1,
+                     uint32_t* x0, uint32_t* x1, int64_t n, void* stream) {
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (n == 0) return JXR_OK;
+  if (!k0 || !k1 || !c0 || !c1 || !x0 || !x1) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  k_threefry2x32_elem<<<grid, 256, 0, (cudaStream_t)stream>>>(k0, k1, c0, c1, x0, x1, n);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_threefry_2x32(const uint32_t* keys, int64_t nkeys, const uint32_t* count, int64_t n,
+                      uint32_t* out, void* stream) {
+  if (nkeys < 0 || n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
+  if (n > 0xFFFFFFFFll) return fail(JXR_ERR_INVALID_ARGUMENT, "count vector longer than 2^32");
+  if (!nkeys || !n) return JXR_OK;
+  if (!keys || !count || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(((n + 1) / 2) * nkeys, &grid))) return rc;
+  k_hash_counts<<<grid, 256, 0, (cudaStream_t)stream>>>(keys, nkeys, count, n, out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_split(const uint32_t* keys, int64_t nkeys, int64_t num, int layout, uint32_t* out,
+              void* stream) {
+  if (num < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "num must be >= 0");
+  int rc = check_request(keys, nkeys, (uint64_t)num, 0, (uint64_t)num, layout, out);
+  if (rc) return rc;
+  if (layout == JXR_LAYOUT_PARTITIONABLE)  // key j = threefry(key, (hi(j), lo(j)))
+    return launch_blocks<OpKeyPair, kCtrIndex>(keys, nkeys, (uint64_t)num, 0, (uint64_t)num,
+                                               OpKeyPair{}, out, (cudaStream_t)stream);
+  // original: threefry_2x32(key, iota(2 num)) reshaped to (num, 2)
+  return launch_words<OpBits<32>>(keys, nkeys, 2 * (uint64_t)num, 0, 2 * (uint64_t)num,
+                                  OpBits<32>{}, out, (cudaStream_t)stream);
+}
+
+int jxr_fold_in(const uint32_t* keys, int64_t nkeys, const uint32_t* data, int64_t ndata,
+                uint32_t* out, void* stream) {
+  if (nkeys < 0 || ndata < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
+  if (nkeys != ndata && nkeys != 1 && ndata != 1)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "nkeys (%lld) and ndata (%lld) do not broadcast",
+                (long long)nkeys, (long long)ndata);
+  const int64_t n = (nkeys == 0 || ndata == 0) ? 0 : std::max(nkeys, ndata);
+  if (!n) return JXR_OK;
+  if (!keys || !data || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  k_fold_in<<<grid, 256, 0, (cudaStream_t)stream>>>(keys, nkeys, data, ndata, out, n);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_random_bits(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                    uint64_t count, int layout, int bit_width, void* out, void* stream) {
+  int rc = check_request(keys, nkeys, size, begin, count, layout, out);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (bit_width) {
+    case 8: return launch_op(keys, nkeys, size, begin, count, layout, OpBits<8>{}, out, st);
+    case 16: return launch_op(keys, nkeys, size, begin, count, layout, OpBits<16>{}, out, st);
+    case 32: return launch_op(keys, nkeys, size, begin, count, layout, OpBits<32>{}, out, st);
+    case 64: return launch_op(keys, nkeys, size, begin, count, layout, OpBits<64>{}, out, st);
+  }
+  return fail(JXR_ERR_INVALID_ARGUMENT, "requires 8-, 16-, 32- or 64-bit field width, got %d", bit_width);
+}
+
+int jxr_uniform(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
+                int layout, int dtype, double minval, double maxval, uint32_t flags, void* out,
+                void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool unfused = flags & JXR_FLAG_UNFUSED_MUL_ADD;
+  switch (dtype) {
+    case JXR_F32: {
+      const float mn = (float)minval, mx = (float)maxval, d = mx - mn;
+      if (unfused) return launch_op(keys, nkeys, size, begin, count, layout, OpUniformF32<false>{mn, d}, out, st);
+      return launch_op(keys, nkeys, size, begin, count, layout, OpUniformF32<true>{mn, d}, out, st);
+    }
+    case JXR_F64: {
+      const double d = maxval - minval;
+      if (unfused) return launch_op(keys, nkeys, size, begin, count, layout, OpUniformF64<false>{minval, d}, out, st);
+      return launch_op(keys, nkeys, size, begin, count, layout, OpUniformF64<true>{minval, d}, out, st);
+    }
+    case JXR_F16: {
+      const float mn = to_half_value(minval, false), mx = to_half_value(maxval, false);
+      const float d = to_half_value((double)mx - (double)mn, false);
+      if (unfused) return launch_op(keys, nkeys, size, begin, count, layout, OpUniformH<false, false>{mn, d}, out, st);
+      return launch_op(keys, nkeys, size, begin, count, layout, OpUniformH<false, true>{mn, d}, out, st);
+    }
+    default: {
+      const float mn = to_half_value(minval, true), mx = to_half_value(maxval, true);
+      const float d = to_half_value((double)mx - (double)mn, true);
+      if (unfused) return launch_op(keys, nkeys, size, begin, count, layout, OpUniformH<true, false>{mn, d}, out, st);
+      return launch_op(keys, nkeys, size, begin, count, layout, OpUniformH<true, true>{mn, d}, out, st);
+    }
+  }
+}
+
+int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
+               int layout, int dtype, void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case JXR_F32: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32{}, out, st);
+    case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF64{}, out, st);
+    case JXR_F16: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<false>{}, out, st);
+    default: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<true>{}, out, st);
+  }
+}
+
+int jxr_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                  uint64_t count, int layout, int p_dtype, double p, uint8_t* out, void* stream) {
+  int rc = check_dtype(p_dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (p_dtype) {
+    case JXR_F32: return launch_op(keys, nkeys, size, begin, count, layout, OpBernoulliF32{(float)p}, out, st);
+    case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpBernoulliF64{p}, out, st);
+    case JXR_F16: return launch_op(keys, nkeys, size, begin, count, layout, OpBernoulliH<false>{to_half_value(p, false)}, out, st);
+    default: return launch_op(keys, nkeys, size, begin, count, layout, OpBernoulliH<true>{to_half_value(p, true)}, out, st);
+  }
+}
+
+int jxr_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                         uint64_t count, int layout, int dtype, double p, void* normal_out,
+                         uint8_t* bern_out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, normal_out))) return rc;
+  if (count && nkeys && !bern_out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == JXR_F64) {
+    if (layout == JXR_LAYOUT_ORIGINAL && size >= 0x7FFFFFFFull)
+      return fail(JXR_ERR_NOT_IMPLEMENTED, "original-layout 64-bit requests of 2^31-1 or more elements are not supported");
+    return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout, OpNormalF64{},
+                                   OpBernoulliF64{p}, normal_out, bern_out, st);
+  }
+  if (dtype == JXR_F32 && layout == JXR_LAYOUT_PARTITIONABLE)
+    return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout, OpNormalF32{},
+                                   OpBernoulliF32{(float)p}, normal_out, bern_out, st);
+  // other dtypes and layouts: the two samplers one after the other (same results)
+  if ((rc = jxr_normal(keys, nkeys, size, begin, count, layout, dtype, normal_out, stream))) return rc;
+  return jxr_bernoulli(keys, nkeys, size, begin, count, layout, dtype, p, bern_out, stream);
+}
+
+int jxr_uniform_from_bits(const void* bits, int64_t n, int dtype, double minval, double maxval,
+                          uint32_t flags, void* out, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!bits || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool unfused = flags & JXR_FLAG_UNFUSED_MUL_ADD;
+if (dtype == JXR_F32) {
+    const float mn = (float)minval, d = (float)maxval - mn;
+    if (unfused) return launch_from_bits(bits, n, OpUniformF32<false>{mn, d}, out, st, grid);
+    return launch_from_bits(bits, n, OpUniformF32<true>{mn, d}, out, st, grid);
+  }
+  if (dtype == JXR_F64) {
+    const double d = maxval - minval;
+    if (unfused) return launch_from_bits(bits, n, OpUniformF64<false>{minval, d}, out, st, grid);
+    return launch_from_bits(bits, n, OpUniformF64<true>{minval, d}, out, st, grid);
+  }
+  const bool bf = dtype == JXR_BF16;
+  const float mn = to_half_value(minval, bf), mx = to_half_value(maxval, bf);
+  const float d = to_half_value((double)mx - (double)mn, bf);
+  if (bf) {
+    if (unfused) return launch_from_bits(bits, n, OpUniformH<true, false>{mn, d}, out, st, grid);
+    return launch_from_bits(bits, n, OpUniformH<true, true>{mn, d}, out, st, grid);
+  }
+  if (unfused) return launch_from_bits(bits, n, OpUniformH<false, false>{mn, d}, out, st, grid);
+  return launch_from_bits(bits, n, OpUniformH<false, true>{mn, d}, out, st, grid);
+}
+
+int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!bits || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case JXR_F32: return launch_from_bits(bits, n, OpNormalF32{}, out, st, grid);
+    case JXR_F64: return launch_from_bits(bits, n, OpNormalF64{}, out, st, grid);
+    case JXR_F16: return launch_from_bits(bits, n, OpNormalH<false>{}, out, st, grid);
+    default: return launch_from_bits(bits, n, OpNormalH<true>{}, out, st, grid);
+  }
+}
+
+int jxr_uniform_affine(const void* unit, const void* minval, const void* maxval, int64_t n,
+                       int dtype, uint32_t flags, void* out, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!unit || !minval || !maxval || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool f = !(flags & JXR_FLAG_UNFUSED_MUL_ADD);
+  using U16 = const uint16_t*;
+  switch (dtype) {
+    case JXR_F32:
+      if (f) k_affine<float, true><<<grid, 256, 0, st>>>((const float*)unit, (const float*)minval, (const float*)maxval, n, (float*)out);
+      else k_affine<float, false><<<grid, 256, 0, st>>>((const float*)unit, (const float*)minval, (const float*)maxval, n, (float*)out);
+      break;
+    case JXR_F64:
+      if (f) k_affine<double, true><<<grid, 256, 0, st>>>((const double*)unit, (const double*)minval, (const double*)maxval, n, (double*)out);
+      else k_affine<double, false><<<grid, 256, 0, st>>>((const double*)unit, (const double*)minval, (const double*)maxval, n, (double*)out);
+      break;
+    case JXR_F16:
+      if (f) k_affine_h<false, true><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
+      else k_affine_h<false, false><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
+      break;
+    default:
+      if (f) k_affine_h<true, true><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
+      else k_affine_h<true, false><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
+  }
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p, int64_t n,
+                               int dtype, uint8_t* out, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!u_lo || !p || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  using U16 = const uint16_t*;
+  switch (dtype) {
+    case JXR_F32:
+      k_bern_unit<float><<<grid, 256, 0, st>>>((const float*)u_lo, (const float*)u_hi, (const float*)p, n, 0x1p-23f, out);
+      break;
+    case JXR_F64:
+      k_bern_unit<double><<<grid, 256, 0, st>>>((const double*)u_lo, (const double*)u_hi, (const double*)p, n, 0x1p-52, out);
+      break;
+    case JXR_F16:
+      k_bern_unit_h<false><<<grid, 256, 0, st>>>((U16)u_lo, (U16)u_hi, (U16)p, n, 0x1p-10f, out);
+      break;
+    default:
+      k_bern_unit_h<true><<<grid, 256, 0, st>>>((U16)u_lo, (U16)u_hi, (U16)p, n, 0x1p-7f, out);
+  }
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream) {
+  if (dtype != JXR_F32 && dtype != JXR_F64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "erf_inv supports dtype 0 (f32) or 1 (f64), got %d", dtype);
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!x || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  if (dtype == JXR_F32)
+    k_erfinv_f32<<<grid, 256, 0, (cudaStream_t)stream>>>((const float*)x, n, (float*)out);
+  else
+    k_erfinv_f64<<<grid, 256, 0, (cudaStream_t)stream>>>((const double*)x, n, (double*)out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size, uint64_t begin,
+                         uint64_t count, int layout, int bit_width, void* host_out) {
+  int rc = check_request(keys_host, nkeys, size, begin, count, layout, host_out);
+  if (rc) return rc;
+  if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "requires 8-, 16-, 32- or 64-bit field width, got %d", bit_width);
+  if (!count || !nkeys) return JXR_OK;
+  const size_t esz = (size_t)bit_width / 8;
+  // chunks of up to 64 MiB per key row, two staging buffers, generate and copy overlapped
+  const uint64_t chunk = std::min<uint64_t>(count, (64ull << 20) / esz);
+  cudaStream_t gen = nullptr, cpy = nullptr;
+  cudaEvent_t done[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
+  uint32_t* dkeys = nullptr;
+  void* stage[2] = {nullptr, nullptr};
+  int status = JXR_OK;
+  auto check = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && status == JXR_OK) status = fail(JXR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    return e == cudaSuccess;
+  };
+  if (check(cudaStreamCreateWithFlags(&gen, cudaStreamNonBlocking), "cudaStreamCreate") &&
+      check(cudaStreamCreateWithFlags(&cpy, cudaStreamNonBlocking), "cudaStreamCreate") &&
+      check(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming), "cudaEventCreate") &&
+      check(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming), "cudaEventCreate") &&
+      check(cudaEventCreateWithFlags(&freed[0], cudaEventDisableTiming), "cudaEventCreate") &&
+      check(cudaEventCreateWithFlags(&freed[1], cudaEventDisableTiming), "cudaEventCreate") &&
+      check(cudaMalloc(&dkeys, 8 * (size_t)nkeys), "cudaMalloc") &&
+      check(cudaMalloc(&stage[0], chunk * esz), "cudaMalloc") &&
+      check(cudaMalloc(&stage[1], chunk * esz), "cudaMalloc") &&
+      check(cudaMemcpyAsync(dkeys, keys_host, 8 * (size_t)nkeys, cudaMemcpyHostToDevice, gen),
+            "cudaMemcpyAsync")) {
+    int buf = 0;
+    bool first[2] = {true, true};
+    for (int64_t r = 0; r < nkeys && status == JXR_OK; ++r) {
+      for (uint64_t off = 0; off < count && status == JXR_OK; off += chunk) {
+        const uint64_t n = std::min(chunk, count - off);
+        if (!first[buf]) check(cudaStreamWaitEvent(gen, freed[buf], 0), "cudaStreamWaitEvent");
+        first[buf] = false;
+        int rc2 = jxr_random_bits(dkeys + 2 * r, 1, size, begin + off, n, layout, bit_width,
+                                  stage[buf], gen);
+        if (rc2) { status = rc2; break; }
+        check(cudaEventRecord(done[buf], gen), "cudaEventRecord");
+        check(cudaStreamWaitEvent(cpy, done[buf], 0), "cudaStreamWaitEvent");
+        char* dst = (char*)host_out + ((uint64_t)r * count + off) * esz;
+        check(cudaMemcpyAsync(dst, stage[buf], n * esz, cudaMemcpyDeviceToHost, cpy), "cudaMemcpyAsync");
+        check(cudaEventRecord(freed[buf], cpy), "cudaEventRecord");
+        buf ^= 1;
+      }
+    }
+  }
+  if (cpy) check(cudaStreamSynchronize(cpy), "cudaStreamSynchronize");
+  if (gen) check(cudaStreamSynchronize(gen), "cudaStreamSynchronize");
+  for (int b = 0; b < 2; ++b) {
+    if (stage[b]) cudaFree(stage[b]);
+    if (done[b]) cudaEventDestroy(done[b]);
+    if (freed[b]) cudaEventDestroy(freed[b]);
+  }
+  if (dkeys) cudaFree(dkeys);
+  if (gen) cudaStreamDestroy(gen);
+  if (cpy) cudaStreamDestroy(cpy);
+  return status;
+}
+
+int jxr_probe_cipher(uint64_t iters, int ctas_per_sm, uint32_t* sink, uint64_t* blocks_out,
+                     void* stream) {
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (ctas_per_sm < 1 || ctas_per_sm > 8)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "ctas_per_sm must be in [1, 8], got %d", ctas_per_sm);
+  if (!sink || !blocks_out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  const int grid = di.sms * ctas_per_sm;
+  k_probe_cipher<<<grid, kThreads, 0, (cudaStream_t)stream>>>(iters, sink);
+  JXR_CUDA(cudaGetLastError());
+  *blocks_out = (uint64_t)grid * kThreads * 8ull * iters;
+  return JXR_OK;
+}
+
+}  // extern "C"
+

@@ -1,0 +1,295 @@
+// Bits -> float transforms of jaxR's samplers, fused into the cipher kernels.
+//
+//   uniform   R/random.R:287-304  bits >> (nbits - nmant) | bits(1.0), bitcast, - 1,
+//                                 floats * (maxval - minval) + minval, max(minval, .)
+//   normal    R/random.R:501-508  sqrt(2) * erf_inv(uniform(nextafter(-1, 0), 1))
+//   bernoulli R/random.R:655-666  uniform(dtype(p)) < p
+//   erf_inv   R/lax.R:222 lowered to chlo.erf_inv (R/lax_special.R:1327-1331): M. Giles,
+//             "Approximating the erfinv function", GPU Computing Gems Jade (2011), with
+//             w = -log1p(-x*x) and erf_inv(+-1) = +-inf.
+//
+// Every float operation is an explicitly rounded intrinsic (__fmul_rn, __fadd_rn,
+// __fmaf_rn ...), so compiler contraction cannot change a result.  Where the
+// reference's recorded samples show fused multiply-adds (the uniform's affine map,
+// test-random.R:43 and :160; the erf_inv Horner steps), __fmaf_rn/__fma_rn is used.
+// The float32 erf_inv takes log1p of the rounded float -(x*x) in double precision
+// and rounds it to float: the correctly rounded value, which reproduces every
+// float32 normal the reference recorded.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace jxr {
+
+// lax_max(a, b) as XLA's CPU code computes it: NaN-propagating, `a` on ties.
+__device__ __forceinline__ float xla_max(float a, float b) { return (a >= b || a != a) ? a : b; }
+__device__ __forceinline__ double xla_max(double a, double b) {
+  return (a >= b || a != a) ? a : b;
+}
+
+// ---- erf_inv --------------------------------------------------------------------------
+
+__device__ __forceinline__ float erfinv_f32(float x) {
+  const float y = -__fmul_rn(x, x);
+  const float w0 = -__double2float_rn(log1p((double)y));
+  float p, w;
+  if (w0 < 5.0f) {
+    w = __fsub_rn(w0, 2.5f);
+    p = 2.81022636e-08f;
+    p = __fmaf_rn(p, w, 3.43273939e-07f);
+    p = __fmaf_rn(p, w, -3.5233877e-06f);
+    p = __fmaf_rn(p, w, -4.39150654e-06f);
+    p = __fmaf_rn(p, w, 0.00021858087f);
+    p = __fmaf_rn(p, w, -0.00125372503f);
+    p = __fmaf_rn(p, w, -0.00417768164f);
+    p = __fmaf_rn(p, w, 0.246640727f);
+    p = __fmaf_rn(p, w, 1.50140941f);
+  } else {
+    w = __fsub_rn(__fsqrt_rn(w0), 3.0f);
+    p = -0.000200214257f;
+    p = __fmaf_rn(p, w, 0.000100950558f);
+    p = __fmaf_rn(p, w, 0.00134934322f);
+    p = __fmaf_rn(p, w, -0.00367342844f);
+    p = __fmaf_rn(p, w, 0.00573950773f);
+    p = __fmaf_rn(p, w, -0.0076224613f);
+    p = __fmaf_rn(p, w, 0.00943887047f);
+    p = __fmaf_rn(p, w, 1.00167406f);
+    p = __fmaf_rn(p, w, 2.83297682f);
+  }
+  if (fabsf(x) == 1.0f) return __fmul_rn(x, __int_as_float(0x7F800000));
+  return __fmul_rn(p, x);
+}
+
+__device__ __forceinline__ double erfinv_f64(double x) {
+  const double w0 = -log1p(-__dmul_rn(x, x));
+  double p, w;
+  if (w0 < 6.25) {
+    w = __dsub_rn(w0, 3.125);
+    p = -3.6444120640178196996e-21;
+    p = __fma_rn(p, w, -1.685059138182016589e-19);
+    p = __fma_rn(p, w, 1.2858480715256400167e-18);
+    p = __fma_rn(p, w, 1.115787767802518096e-17);
+    p = __fma_rn(p, w, -1.333171662854620906e-16);
+    p = __fma_rn(p, w, 2.0972767875968561637e-17);
+    p = __fma_rn(p, w, 6.6376381343583238325e-15);
+    p = __fma_rn(p, w, -4.0545662729752068639e-14);
+    p = __fma_rn(p, w, -8.1519341976054721522e-14);
+    p = __fma_rn(p, w, 2.6335093153082322977e-12);
+    p = __fma_rn(p, w, -1.2975133253453532498e-11);
+    p = __fma_rn(p, w, -5.4154120542946279317e-11);
+    p = __fma_rn(p, w, 1.051212273321532285e-09);
+    p = __fma_rn(p, w, -4.1126339803469836976e-09);
+    p = __fma_rn(p, w, -2.9070369957882005086e-08);
+    p = __fma_rn(p, w, 4.2347877827932403518e-07);
+    p = __fma_rn(p, w, -1.3654692000834678645e-06);
+    p = __fma_rn(p, w, -1.3882523362786468719e-05);
+    p = __fma_rn(p, w, 0.0001867342080340571352);
+    p = __fma_rn(p, w, -0.00074070253416626697512);
+    p = __fma_rn(p, w, -0.0060336708714301490533);
+    p = __fma_rn(p, w, 0.24015818242558961693);
+    p = __fma_rn(p, w, 1.6536545626831027356);
+  } else if (w0 < 16.0) {
+    w = __dsub_rn(__dsqrt_rn(w0), 3.25);
+    p = 2.2137376921775787049e-09;
+    p = __fma_rn(p, w, 9.0756561938885390979e-08);
+    p = __fma_rn(p, w, -2.7517406297064545428e-07);
+    p = __fma_rn(p, w, 1.8239629214389227755e-08);
+    p = __fma_rn(p, w, 1.5027403968909827627e-06);
+    p = __fma_rn(p, w, -4.013867526981545969e-06);
+    p = __fma_rn(p, w, 2.9234449089955446044e-06);
+    p = __fma_rn(p, w, 1.2475304481671778723e-05);
+    p = __fma_rn(p, w, -4.7318229009055733981e-05);
+    p = __fma_rn(p, w, 6.8284851459573175448e-05);
+    p = __fma_rn(p, w, 2.4031110387097893999e-05);
+    p = __fma_rn(p, w, -0.0003550375203628474796);
+    p = __fma_rn(p, w, 0.00095328937973738049703);
+    p = __fma_rn(p, w, -0.0016882755560235047313);
+    p = __fma_rn(p, w, 0.0024914420961078508066);
+    p = __fma_rn(p, w, -0.0037512085075692412107);
+    p = __fma_rn(p, w, 0.005370914553590063617);
+    p = __fma_rn(p, w, 1.0052589676941592334);
+    p = __fma_rn(p, w, 3.0838856104922207635);
+  } else {
+    w = __dsub_rn(__dsqrt_rn(w0), 5.0);
+    p = -2.7109920616438573243e-11;
+    p = __fma_rn(p, w, -2.5556418169965252055e-10);
+    p = __fma_rn(p, w, 1.5076572693500548083e-09);
+    p = __fma_rn(p, w, -3.7894654401267369937e-09);
+    p = __fma_rn(p, w, 7.6157012080783393804e-09);
+    p = __fma_rn(p, w, -1.4960026627149240478e-08);
+    p = __fma_rn(p, w, 2.9147953450901080826e-08);
+    p = __fma_rn(p, w, -6.7711997758452339498e-08);
+    p = __fma_rn(p, w, 2.2900482228026654717e-07);
+    p = __fma_rn(p, w, -9.9298272942317002539e-07);
+    p = __fma_rn(p, w, 4.5260625972231537039e-06);
+    p = __fma_rn(p, w, -1.9681778105531670567e-05);
+    p = __fma_rn(p, w, 7.5995277030017761139e-05);
+    p = __fma_rn(p, w, -0.00021503011930044477347);
+    p = __fma_rn(p, w, -0.00013871931833623122026);
+    p = __fma_rn(p, w, 1.0103004648645343977);
+    p = __fma_rn(p, w, 4.8499064014085844221);
+  }
+  if (fabs(x) == 1.0) return __dmul_rn(x, __longlong_as_double(0x7FF0000000000000ll));
+  return __dmul_rn(p, x);
+}
+
+// ---- 16-bit float helpers (raw bits in, raw bits out, arithmetic exact then rounded once) -
+
+template <bool BF>
+__device__ __forceinline__ float h2f(uint16_t h) {
+  if constexpr (BF) return __uint_as_float((uint32_t)h << 16);
+  else return __half2float(__ushort_as_half(h));
+}
+template <bool BF>
+__device__ __forceinline__ uint16_t f2h(float f) {
+  if constexpr (BF) return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  else return __half_as_ushort(__float2half_rn(f));
+}
+template <bool BF>
+__device__ __forceinline__ uint16_t d2h(double d) {
+  if constexpr (BF) return __bfloat16_as_ushort(__double2bfloat16(d));
+  else return __half_as_ushort(__double2half(d));
+}
+// round a float that is exact (or rounded once to float) to the 16-bit type and back
+template <bool BF>
+__device__ __forceinline__ float rh(float f) { return h2f<BF>(f2h<BF>(f)); }
+
+// ---- the transforms ---------------------------------------------------------------------
+// Each has Bits (the unsigned draw it consumes: 32, 64, 16 or 8 bits), Out (what it
+// stores) and operator()(Bits) -> Out.
+
+template <int W> struct UintOf;
+template <> struct UintOf<8> { using T = uint8_t; };
+template <> struct UintOf<16> { using T = uint16_t; };
+template <> struct UintOf<32> { using T = uint32_t; };
+template <> struct UintOf<64> { using T = uint64_t; };
+
+template <int W>
+struct OpBits {
+  static constexpr int kBits = W;
+  using Bits = typename UintOf<W>::T;
+  using Out = Bits;
+  __device__ __forceinline__ Out operator()(Bits b) const { return b; }
+};
+
+__device__ __forceinline__ float unit_f32(uint32_t b) {
+  return __fsub_rn(__uint_as_float((b >> 9) | 0x3F800000u), 1.0f);
+}
+__device__ __forceinline__ double unit_f64(uint64_t b) {
+  return __dsub_rn(__longlong_as_double((long long)((b >> 12) | 0x3FF0000000000000ull)), 1.0);
+}
+// float16 draws 16 bits: shift 6, one = 0x3C00; bfloat16 has nmant = 7 < 8 and draws
+// 8 bits, widened to 16: shift 1, one = 0x3F80.
+template <bool BF>
+__device__ __forceinline__ float unit_h(uint32_t b) {
+  const uint16_t fb = BF ? (uint16_t)((b >> 1) | 0x3F80u) : (uint16_t)((b >> 6) | 0x3C00u);
+  return __fsub_rn(h2f<BF>(fb), 1.0f);  // exact: the result is a 16-bit float in [0, 1)
+}
+
+template <bool kFused>
+struct OpUniformF32 {
+  static constexpr int kBits = 32;
+  using Bits = uint32_t;
+  using Out = float;
+  float mn, d;  // minval and maxval - minval, in float32
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float f = unit_f32(b);
+    const float r = kFused ? __fmaf_rn(f, d, mn) : __fadd_rn(__fmul_rn(f, d), mn);
+    return xla_max(mn, r);
+  }
+};
+
+template <bool kFused>
+struct OpUniformF64 {
+  static constexpr int kBits = 64;
+  using Bits = uint64_t;
+  using Out = double;
+  double mn, d;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const double f = unit_f64(b);
+    const double r = kFused ? __fma_rn(f, d, mn) : __dadd_rn(__dmul_rn(f, d), mn);
+    return xla_max(mn, r);
+  }
+};
+
+template <bool BF, bool kFused>
+struct OpUniformH {
+  static constexpr int kBits = BF ? 8 : 16;
+  using Bits = typename UintOf<kBits>::T;
+  using Out = uint16_t;
+  float mn, d;  // values of 16-bit floats
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float f = unit_h<BF>(b);
+    float r;
+    if (kFused) r = h2f<BF>(d2h<BF>(__fma_rn((double)f, (double)d, (double)mn)));
+    else r = rh<BF>(__fadd_rn(rh<BF>(__fmul_rn(f, d)), mn));
+    return f2h<BF>(xla_max(mn, r));
+  }
+};
+
+// u = uniform(nextafter(-1, 0), 1): maxval - minval rounds to exactly 2 in every dtype,
+// so u = 2 f + lo is exact and the fused and unfused forms agree.
+struct OpNormalF32 {
+  static constexpr int kBits = 32;
+  using Bits = uint32_t;
+  using Out = float;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float lo = -0x1.fffffep-1f;  // -1 + 2^-24
+    const float u = xla_max(lo, __fmaf_rn(unit_f32(b), 2.0f, lo));
+    return __fmul_rn(1.41421354f, erfinv_f32(u));
+  }
+};
+
+struct OpNormalF64 {
+  static constexpr int kBits = 64;
+  using Bits = uint64_t;
+  using Out = double;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const double lo = -0x1.fffffffffffffp-1;  // -1 + 2^-53
+    const double u = xla_max(lo, __fma_rn(unit_f64(b), 2.0, lo));
+    return __dmul_rn(1.4142135623730951, erfinv_f64(u));
+  }
+};
+
+// erf_inv of a 16-bit float is evaluated in float32 and rounded back.
+template <bool BF>
+struct OpNormalH {
+  static constexpr int kBits = BF ? 8 : 16;
+  using Bits = typename UintOf<kBits>::T;
+  using Out = uint16_t;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float lo = BF ? -0x1.fep-1f : -0x1.ffcp-1f;  // -1 + 2^-8, -1 + 2^-11
+    const float u = xla_max(lo, rh<BF>(__fmaf_rn(unit_h<BF>(b), 2.0f, lo)));
+    const float e = rh<BF>(erfinv_f32(u));
+    return f2h<BF>(__fmul_rn(rh<BF>(1.41421354f), e));
+  }
+};
+
+// uniform(key, shape, dtype(p), 0, 1) is the unit float itself (f * 1 + 0 = f and
+// max(0, f) = f), so the draw is unit(bits) < p in dtype(p).
+struct OpBernoulliF32 {
+  static constexpr int kBits = 32;
+  using Bits = uint32_t;
+  using Out = uint8_t;
+  float p;
+  __device__ __forceinline__ Out operator()(Bits b) const { return unit_f32(b) < p; }
+};
+struct OpBernoulliF64 {
+  static constexpr int kBits = 64;
+  using Bits = uint64_t;
+  using Out = uint8_t;
+  double p;
+  __device__ __forceinline__ Out operator()(Bits b) const { return unit_f64(b) < p; }
+};
+template <bool BF>
+struct OpBernoulliH {
+  static constexpr int kBits = BF ? 8 : 16;
+  using Bits = typename UintOf<kBits>::T;
+  using Out = uint8_t;
+  float p;  // value of a 16-bit float
+  __device__ __forceinline__ Out operator()(Bits b) const { return unit_h<BF>(b) < p; }
+};
+
+}  // namespace jxr

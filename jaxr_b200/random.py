@@ -1,0 +1,864 @@
+"""jax.random's threefry path with jaxR's interface, on sm_100a kernels.
+
+Host-side mirror of the reference's R API (R/random.R, R/prng.R): same function
+names, argument meanings, defaults, dtype rules and error messages/classes.  Arrays
+are torch tensors on the current CUDA device (torch is plumbing here: device memory
+and streams); every value is computed by libjxrng (include/jxrng.h).  There is no
+CPU path.
+
+Shapes are C order, as in the reference; uint32/uint64 results are torch.uint32 /
+torch.uint64 tensors, bool results torch.bool.
+"""
+
+from __future__ import annotations
+
+import math
+import numbers
+import warnings
+
+import numpy as np
+import torch
+
+from . import _native as nat
+from . import config as cfg
+from .errors import (JaxNotImplementedError, JaxOverflowError, JaxTypeError, JaxValueError)
+
+# ---- dtypes -------------------------------------------------------------------------------
+
+_TORCH = {
+    "bool": torch.bool, "uint8": torch.uint8, "uint16": torch.uint16, "uint32": torch.uint32,
+    "uint64": torch.uint64, "int8": torch.int8, "int16": torch.int16, "int32": torch.int32,
+    "int64": torch.int64, "float16": torch.float16, "bfloat16": torch.bfloat16,
+    "float32": torch.float32, "float64": torch.float64, "complex64": torch.complex64,
+    "complex128": torch.complex128,
+}
+_NAME = {v: k for k, v in _TORCH.items()}
+_BITS = {"uint8": 8, "uint16": 16, "uint32": 32, "uint64": 64, "int8": 8, "int16": 16,
+         "int32": 32, "int64": 64, "float16": 16, "bfloat16": 16, "float32": 32, "float64": 64,
+         "bool": 8, "complex64": 64, "complex128": 128}
+_FLOAT_CODE = {"float32": nat.F32, "float64": nat.F64, "float16": nat.F16, "bfloat16": nat.BF16}
+_NMANT = {"float32": 23, "float64": 52, "float16": 10, "bfloat16": 7}
+
+
+def default_uint():
+    return "uint64" if cfg.x64_enabled() else "uint32"
+
+
+def default_float():
+    return "float64" if cfg.x64_enabled() else "float32"
+
+
+def default_int():
+    return "int64" if cfg.x64_enabled() else "int32"
+
+
+def canonicalize_dtype(dt):
+    """A dtype name (or torch/numpy dtype, or 'float'/'int'/'uint'), canonicalised for the
+    x64 setting as the reference's dtype() does (64-bit types become 32-bit with x64 off)."""
+    if isinstance(dt, torch.dtype):
+        name = _NAME[dt]
+    elif isinstance(dt, np.dtype) or (isinstance(dt, type) and issubclass(dt, np.generic)):
+        name = np.dtype(dt).name
+    else:
+        name = str(dt)
+    alias = {"float": default_float(), "float_": default_float(), "double": default_float(),
+             "numeric": default_float(), "int": default_int(), "integer": default_int(),
+             "uint": default_uint(), "complex": "complex128" if cfg.x64_enabled() else "complex64",
+             "logical": "bool", "bool_": "bool"}
+    name = alias.get(name, name)
+    if name not in _TORCH:
+        raise JaxTypeError(f"Unsupported dtype {dt}")
+    if not cfg.x64_enabled():
+        name = {"uint64": "uint32", "int64": "int32", "float64": "float32",
+                "complex128": "complex64"}.get(name, name)
+    return name
+
+
+def dtype(x):
+    """dtype name of an array, key array or scalar (the reference's jaxR::dtype)."""
+    if isinstance(x, PRNGKeyArray):
+        return x.dtype
+    if isinstance(x, torch.Tensor):
+        return _NAME[x.dtype]
+    if isinstance(x, np.ndarray):
+        return canonicalize_dtype(x.dtype)
+    if isinstance(x, bool):
+        return "bool"
+    if isinstance(x, numbers.Integral):
+        return default_int()
+    if isinstance(x, numbers.Real):
+        return default_float()
+    raise JaxTypeError(f"no dtype for {type(x).__name__}")
+
+
+def _is_unsigned(dt):
+    return dt.startswith("uint")
+
+
+def _is_float(dt):
+    return dt in _FLOAT_CODE
+
+
+def _device():
+    if not torch.cuda.is_available():
+        raise RuntimeError("no CUDA device: the threefry kernels run on an sm_100 GPU and "
+                           "there is no CPU path")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _stream():
+    return ctypes_stream(torch.cuda.current_stream())
+
+
+def ctypes_stream(s):
+    return s.cuda_stream
+
+
+def _ptr(t):
+    return t.data_ptr()
+
+
+def shape_str(s):
+    """The reference's prng_shape_str: (5,), (2, 3), ()."""
+    s = tuple(int(v) for v in s)
+    if len(s) == 1:
+        return f"({s[0]},)"
+    return "(" + ", ".join(str(v) for v in s) + ")"
+
+
+def canon_shape(shape):
+    """Shape argument to a tuple of non-negative ints (R/lax_shape.R:16-28)."""
+    if shape is None:
+        return ()
+    if isinstance(shape, torch.Tensor):
+        shape = shape.tolist()
+    if isinstance(shape, numbers.Integral):
+        shape = (shape,)
+    try:
+        out = tuple(shape)
+    except TypeError:
+        raise JaxTypeError(f"Shapes must be 1D sequences of concrete values of integer type, "
+                           f"got {shape!r}.")
+    for v in out:
+        if not isinstance(v, numbers.Integral) and not (isinstance(v, float) and v == int(v)):
+            raise JaxTypeError(f"Shapes must be 1D sequences of concrete values of integer type, "
+                               f"got {shape_str(out)}.")
+        if v < 0:
+            raise JaxTypeError(f"Shapes must be 1D sequences of concrete values of integer type, "
+                               f"got {shape_str(out)}.")
+    return tuple(int(v) for v in out)
+
+
+def _size(shape):
+    return math.prod(shape) if shape else 1
+
+
+# ---- vmap batching --------------------------------------------------------------------------
+
+class _Batched:
+    """A value inside vmap: `value` carries `nb` leading batch axes that the function body
+    does not see (R/batching.R:4-50 for the reference's batch trace)."""
+
+    __slots__ = ("value", "nb")
+
+    def __init__(self, value, nb):
+        self.value = value
+        self.nb = nb
+
+    @property
+    def batch_shape(self):
+        v = self.value
+        s = v.shape if isinstance(v, PRNGKeyArray) else tuple(v.shape)
+        return tuple(s[:self.nb])
+
+    @property
+    def shape(self):
+        v = self.value
+        s = v.shape if isinstance(v, PRNGKeyArray) else tuple(v.shape)
+        return tuple(s[self.nb:])
+
+    def __repr__(self):
+        return f"Batched({self.value!r}, batch axes={self.nb})"
+
+
+def _unbatch(x):
+    if isinstance(x, _Batched):
+        return x.value, x.nb
+    return x, 0
+
+
+def _rebatch(x, nb):
+    return _Batched(x, nb) if nb else x
+
+
+def vmap(fun, in_axes=0, out_axes=0):
+    """Vectorise `fun` over the leading axis of its arguments (R/batching.R).
+
+    Inside `fun`, key arrays, raw keys, seeds and fold_in data carry the batch; the
+    random functions run one key-batched kernel launch for the whole batch, which is
+    what the reference's batching rule for threefry2x32 (lax_broadcast_batcher,
+    R/prng.R:99) amounts to.  in_axes is 0 (batch every argument), None, or a
+    sequence of 0/None per argument; out_axes must be 0.
+    """
+    if out_axes != 0:
+        raise JaxValueError("vmap: only out_axes = 0 is supported")
+
+    def wrapped(*args):
+        axes = in_axes if isinstance(in_axes, (list, tuple)) else [in_axes] * len(args)
+        if len(axes) != len(args):
+            raise JaxValueError("vmap in_axes must have one entry per argument")
+        level = 1 + max([a.nb for a in args if isinstance(a, _Batched)], default=0)
+        sizes = set()
+        bargs = []
+        for a, ax in zip(args, axes):
+            if ax is None:
+                bargs.append(a)
+                continue
+            if ax != 0:
+                raise JaxValueError("vmap: in_axes must be 0 or None")
+            v, nb = _unbatch(a)
+            if isinstance(v, (numbers.Number, np.generic)) or (
+                    not isinstance(v, PRNGKeyArray) and not isinstance(v, torch.Tensor)):
+                v = torch.as_tensor(np.asarray(v))
+            vs = v.shape if isinstance(v, PRNGKeyArray) else tuple(v.shape)
+            if len(vs) <= nb:
+                raise JaxValueError("vmap was requested to map its argument along axis 0, "
+                                    "which implies that its rank should be at least 1, but is only 0")
+            sizes.add(vs[nb])
+            bargs.append(_Batched(v, nb + 1))
+        if len(sizes) > 1:
+            raise JaxValueError(f"vmap got inconsistent sizes for the mapped axis: {sorted(sizes)}")
+        out = fun(*bargs)
+        size = sizes.pop() if sizes else None
+        return _vmap_out(out, level, size)
+
+    return wrapped
+
+
+def _vmap_out(out, level, size):
+    if isinstance(out, (list, tuple)):
+        return type(out)(_vmap_out(o, level, size) for o in out)
+    if isinstance(out, _Batched):
+        if out.nb != level:
+            raise JaxValueError("vmap: output batched at an unexpected level")
+        return _rebatch(out.value, level - 1)
+    # an output that does not depend on the mapped arguments is broadcast
+    if size is None:
+        return out
+    if isinstance(out, PRNGKeyArray):
+        return PRNGKeyArray(out.data.unsqueeze(0).expand((size,) + tuple(out.data.shape)).contiguous(),
+                            out.impl)
+    t = torch.as_tensor(out)
+    return t.unsqueeze(0).expand((size,) + tuple(t.shape)).contiguous()
+
+
+# ---- key arrays (R/prng.R:455-584) ----------------------------------------------------------
+
+_IMPLS = {"threefry2x32": "fry", "rbg": "rbg", "unsafe_rbg": "urbg"}
+
+
+class PRNGKeyArray:
+    """A typed key array (jax_key_threefry2x32): uint32 key data of shape (*shape, 2)."""
+
+    __slots__ = ("data", "impl")
+
+    def __init__(self, data, impl="threefry2x32"):
+        self.data = data
+        self.impl = impl
+
+    @property
+    def shape(self):
+        return tuple(self.data.shape[:-1])
+
+    @property
+    def ndim(self):
+        return len(self.shape)
+
+    @property
+    def dtype(self):
+        return f"key<{_IMPLS[self.impl]}>"
+
+    def __len__(self):
+        if not self.shape:
+            raise JaxTypeError("len() of unsized object")
+        return self.shape[0]
+
+    def __getitem__(self, idx):
+        if not isinstance(idx, tuple):
+            idx = (idx,)
+        if len(idx) > self.ndim:
+            raise IndexError("too many indices for key array")
+        return PRNGKeyArray(self.data[idx], self.impl)
+
+    def __iter__(self):
+        if not self.shape:
+            raise JaxTypeError("iteration over a 0-d key array")
+        return iter([PRNGKeyArray(self.data[i], self.impl) for i in range(self.shape[0])])
+
+    def as_list(self):
+        return list(iter(self))
+
+    def __repr__(self):
+        return f"Array({shape_str(self.shape)}, dtype={self.dtype}) overlaying:\n{self.data!r}"
+
+
+def _resolve_impl(spec):
+    """R/prng.R:444-453; only threefry2x32 has kernels here."""
+    if spec is None:
+        spec = cfg.jax_config("jax_default_prng_impl")
+    if not isinstance(spec, str):
+        raise JaxTypeError(f"unrecognized type {type(spec).__name__} for specifying PRNG "
+                           "implementation.")
+    name = spec
+    for impl, tag in _IMPLS.items():
+        if spec == f"key<{tag}>":
+            name = impl
+    if name not in _IMPLS:
+        names = ", ".join(f'"{n}"' for n in _IMPLS)
+        raise JaxValueError(f'unrecognized PRNG implementation "{spec}". Did you mean one of: '
+                            f"{names}?")
+    if name != "threefry2x32":
+        raise JaxNotImplementedError(
+            f'PRNG implementation "{name}" (XLA RngBitGenerator) is not provided: these kernels '
+            "implement threefry2x32")
+    return name
+
+
+def _as_uint32_data(x):
+    """Raw key data to a uint32 device tensor, checked as _check_prng_key_data
+    (R/prng.R:478-492)."""
+    if isinstance(x, torch.Tensor):
+        t = x
+        dt = _NAME[t.dtype]
+    else:
+        arr = np.asarray(x)
+        if arr.dtype.kind == "f":
+            dt = default_float()
+        elif arr.dtype.kind in "iu":
+            dt = canonicalize_dtype(arr.dtype) if arr.dtype != np.uint32 else "uint32"
+            if arr.dtype.kind == "i" and arr.dtype != np.int64:
+                dt = canonicalize_dtype(arr.dtype)
+        elif arr.dtype.kind == "b":
+            dt = "bool"
+        else:
+            raise JaxTypeError(f"unexpected PRNG key type {type(x).__name__}")
+        t = None
+    shape = tuple(t.shape) if t is not None else np.asarray(x).shape
+    if len(shape) < 1:
+        raise JaxTypeError("JAX encountered invalid PRNG key data: expected key_data.ndim >= 1; "
+                           f"got ndim={len(shape)}")
+    if shape[-1] != 2:
+        raise JaxTypeError("JAX encountered invalid PRNG key data: expected key_data.shape to end "
+                           f"with (2,); got shape={shape_str(shape)} for impl=threefry2x32")
+    if dt != "uint32":
+        raise JaxTypeError("JAX encountered invalid PRNG key data: expected key_data.dtype = "
+                           f"uint32; got dtype={dt}")
+    if t is None:
+        t = torch.from_numpy(np.ascontiguousarray(np.asarray(x), dtype=np.uint32))
+    return t
+
+
+def _legacy_check():
+    msg = ("Legacy uint32 key array passed as key to jax.random function. Please create keys "
+           "using jax.random.key(). If use of a raw key array was intended, set "
+           'jax_legacy_prng_key="allow".')
+    mode = cfg.legacy_key_mode()
+    if mode == "error":
+        raise JaxValueError(msg)
+    if mode == "warn":
+        warnings.warn(msg, stacklevel=4)
+
+
+def _check_key(name, key, allow_batched=False):
+    """R/random.R:55-77: (typed key, wrapped, batch axes)."""
+    key, nb = _unbatch(key)
+    if isinstance(key, PRNGKeyArray):
+        k, wrapped = key, False
+    elif isinstance(key, (torch.Tensor, np.ndarray, list, tuple, numbers.Number)) and not isinstance(key, str):
+        _legacy_check()
+        k, wrapped = PRNGKeyArray(_as_uint32_data(key)), True
+    else:
+        raise JaxTypeError(f"unexpected PRNG key type {type(key).__name__}")
+    per_shape = k.shape[nb:]
+    if not allow_batched and per_shape:
+        raw = tuple(k.data.shape[nb:]) if wrapped else per_shape
+        raise JaxValueError(f"{name} accepts a single key, but was given a key array of shape "
+                            f"{shape_str(raw)} != (). Use jax.vmap for batching.")
+    return k, wrapped, nb
+
+
+def _return_keys(wrapped, key):
+    return key.data if wrapped else key
+
+
+def _layout():
+    return nat.LAYOUT_PARTITIONABLE if cfg.partitionable() else nat.LAYOUT_ORIGINAL
+
+
+# ---- seeds (R/prng.R:159-170, :501-519) --------------------------------------------------------
+
+def _seed_words(seed):
+    """(k0, k1) uint32 numpy arrays of the keys of integer seeds (R/prng.R:159-170).
+
+    An R number (here a Python/numpy number) is an int64 that wraps to int32 with x64
+    off (R/prng.R:505-514); an integer array keeps its width, canonicalised for x64.
+    jax_random_seed_offset is added first (R/prng.R:516-517).  k0 is the seed shifted
+    right by 32, which is 0 for 32-bit seeds; k1 is its low word.
+    """
+    x64 = cfg.x64_enabled()
+    off = int(cfg.jax_config("jax_random_seed_offset") or 0)
+    if isinstance(seed, torch.Tensor):
+        dt = _NAME[seed.dtype]
+        if not dt.startswith(("int", "uint")):
+            raise JaxTypeError(f"PRNG key seed must be an integer; got {seed.tolist()}")
+        wide = _BITS[dt] == 64 and x64
+        vals = [int(v) + off for v in np.asarray(seed.detach().cpu().reshape(-1).tolist(),
+                                                 dtype=object)]
+        shape = tuple(seed.shape)
+    else:
+        arr = np.asarray(seed)
+        if arr.dtype.kind == "f":
+            if not np.all(arr == np.round(arr)):
+                raise JaxTypeError(f"PRNG key seed must be an integer; got {seed}")
+        elif arr.dtype.kind not in "iu":
+            raise JaxTypeError(f"PRNG key seed must be an integer; got {seed}")
+        wide = x64
+        vals = [int(v) + off for v in arr.reshape(-1).tolist()]
+        shape = arr.shape
+    mod = 1 << (64 if wide else 32)
+    v = np.array([x % mod for x in vals], dtype=np.uint64).reshape(shape)
+    k0 = (v >> np.uint64(32)).astype(np.uint32)
+    k1 = (v & np.uint64(0xFFFFFFFF)).astype(np.uint32)
+    return k0, k1
+
+
+def _keys_from_seeds(seed):
+    k0, k1 = _seed_words(seed)
+    data = np.stack([k0, k1], axis=-1).astype(np.uint32)
+    return torch.from_numpy(np.ascontiguousarray(data)).to(_device())
+
+
+def _key_ctor(ctor, seed, impl_spec):
+    impl = _resolve_impl(impl_spec)
+    s, nb = _unbatch(seed)
+    if isinstance(s, PRNGKeyArray):
+        raise JaxTypeError(f"{ctor} accepts a scalar seed, but was given a PRNG key.")
+    sshape = tuple(s.shape) if isinstance(s, (torch.Tensor, np.ndarray)) else np.shape(s)
+    if len(sshape) > nb:
+        raise JaxTypeError(f"{ctor} accepts a scalar seed, but was given an array of shape "
+                           f"{shape_str(sshape[nb:])} != (). Use jax.vmap for batching")
+    if not isinstance(s, (torch.Tensor, np.ndarray, numbers.Number)):
+        raise JaxTypeError(f"PRNG key seed must be an integer; got {s!r}")
+    return _rebatch(PRNGKeyArray(_keys_from_seeds(s), impl), nb)
+
+
+def random_key(seed, impl=None, dtype=None):
+    """A typed key from an integer seed (R/random.R:169-189)."""
+    if dtype is not None:
+        if impl is not None:
+            raise JaxValueError("Cannot specify both `impl` and `dtype` arguments to "
+                                "jax.random.key")
+        impl = dtype
+    return _key_ctor("key", seed, impl)
+
+
+def random_PRNGKey(seed, impl=None):
+    """A legacy raw key: uint32 data of shape (2,) (R/random.R:191-193)."""
+    k = _key_ctor("PRNGKey", seed, impl)
+    kv, nb = _unbatch(k)
+    return _rebatch(kv.data, nb)
+
+
+def random_key_data(keys):
+    k, _, nb = _check_key("key_data", keys, allow_batched=True)
+    return _rebatch(k.data, nb)
+
+
+def random_key_impl(keys):
+    k, _, _ = _check_key("key_impl", keys, allow_batched=True)
+    return k.impl
+
+
+def random_key_dtype(impl_spec=None):
+    if impl_spec is not None and impl_spec not in _IMPLS and not str(impl_spec).startswith("key<"):
+        _resolve_impl(impl_spec)
+    name = impl_spec if impl_spec in _IMPLS else (impl_spec and next(
+        (n for n, t in _IMPLS.items() if impl_spec == f"key<{t}>"), None))
+    if name is None:
+        name = cfg.jax_config("jax_default_prng_impl")
+    return f"key<{_IMPLS[name]}>"
+
+
+def random_wrap_key_data(key_bits_array, impl=None, dtype=None):
+    if dtype is not None:
+        if impl is not None:
+            raise JaxValueError("Cannot specify both `impl` and `dtype` arguments to "
+                                "jax.random.wrap_key_data")
+        impl = dtype
+    name = _resolve_impl(impl)
+    kb, nb = _unbatch(key_bits_array)
+    return _rebatch(PRNGKeyArray(_as_uint32_data(kb), name), nb)
+
+
+def random_clone(key):
+    if not isinstance(key, PRNGKeyArray):
+        return key
+    return PRNGKeyArray(key.data.clone(), key.impl)
+
+
+def random_Key(x):
+    return x
+
+
+# ---- kernels on flat key batches -------------------------------------------------------------
+
+def _flat_keys(k):
+    """Key data as a contiguous (nkeys, 2) uint32 tensor on the current device."""
+    return k.data.to(_device()).reshape(-1, 2).contiguous()
+
+
+def _k_split(kd, shape, layout):
+    n = kd.shape[0]
+    num = _size(shape)
+    out = torch.empty((n, num, 2), dtype=torch.uint32, device=kd.device)
+    nat.call("jxr_split", _ptr(kd), n, num, layout, _ptr(out), _stream())
+    return out
+
+
+def _k_fold_in(kd, data):
+    n = max(kd.shape[0], data.shape[0])
+    out = torch.empty((n, 2), dtype=torch.uint32, device=kd.device)
+    nat.call("jxr_fold_in", _ptr(kd), kd.shape[0], _ptr(data), data.shape[0], _ptr(out), _stream())
+    return out
+
+
+def _check_size(size, layout):
+    if size >= 1 << 64:
+        raise JaxNotImplementedError("random bits array of size exceeding 2 ** 64")
+
+
+def _k_bits(kd, size, bit_width, layout):
+    _check_size(size, layout)
+    out = torch.empty((kd.shape[0], size), dtype=_TORCH[f"uint{bit_width}"], device=kd.device)
+    nat.call("jxr_random_bits", _ptr(kd), kd.shape[0], size, 0, size, layout, bit_width,
+             _ptr(out), _stream())
+    return out
+
+
+def _float_storage(dt):
+    return torch.uint16 if dt in ("float16", "bfloat16") else _TORCH[dt]
+
+
+def _as_float_view(t, dt):
+    return t.view(_TORCH[dt]) if dt in ("float16", "bfloat16") else t
+
+
+def _k_uniform(kd, size, dt, mn, mx, layout, flags=0):
+    _check_size(size, layout)
+    out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    nat.call("jxr_uniform", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
+             float(mn), float(mx), flags, _ptr(out), _stream())
+    return _as_float_view(out, dt)
+
+
+def _k_normal(kd, size, dt, layout):
+    _check_size(size, layout)
+    out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    nat.call("jxr_normal", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
+             _ptr(out), _stream())
+    return _as_float_view(out, dt)
+
+
+def _k_bernoulli(kd, size, dt, p, layout):
+    _check_size(size, layout)
+    out = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
+    nat.call("jxr_bernoulli", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
+             float(p), _ptr(out), _stream())
+    return out.view(torch.bool)
+
+
+# ---- threefry primitives (R/prng.R:88-120) ----------------------------------------------------
+
+def _u32_tensor(x, what):
+    if isinstance(x, torch.Tensor):
+        return x
+    return torch.as_tensor(np.asarray(x))
+
+
+def threefry2x32(key1, key2, x1, x2):
+    """The threefry2x32 primitive: uint32 arrays broadcast to one shape -> (x0, x1)
+    (R/prng.R:88-99)."""
+    args = [_u32_tensor(a, "arg") for a in (key1, key2, x1, x2)]
+    if any(a.dtype != torch.uint32 for a in args):
+        raise JaxTypeError("Arguments to threefry2x32 must have uint32 type, got "
+                           + ", ".join(f"{_NAME[a.dtype]}{list(a.shape)}" for a in args))
+    shape = torch.broadcast_shapes(*[a.shape for a in args])
+    dev = _device()
+    flat = [a.to(dev).broadcast_to(shape).contiguous().reshape(-1) for a in args]
+    n = flat[0].numel()
+    o0 = torch.empty(n, dtype=torch.uint32, device=dev)
+    o1 = torch.empty(n, dtype=torch.uint32, device=dev)
+    nat.call("jxr_threefry2x32", *[_ptr(f) for f in flat], _ptr(o0), _ptr(o1), n, _stream())
+    return o0.reshape(shape), o1.reshape(shape)
+
+
+def threefry_2x32(keypair, count):
+    """prng_threefry_2x32: the Threefry-2x32 hash of a uint32 `count` array
+    (R/prng.R:101-120)."""
+    if isinstance(keypair, (list, tuple)) and len(keypair) == 2:
+        k = [_u32_tensor(v, "key") for v in keypair]
+    else:
+        kt = _u32_tensor(keypair, "key")
+        k = [kt[0], kt[1]]
+    c = _u32_tensor(count, "count")
+    dts = [_NAME[t.dtype] for t in (k[0], k[1], c)]
+    if any(d != "uint32" for d in dts):
+        raise JaxTypeError(f"threefry_2x32 requires uint32 arguments, got [{', '.join(dts)}]")
+    dev = _device()
+    kd = torch.stack([k[0].reshape(()), k[1].reshape(())]).to(dev).reshape(1, 2).contiguous()
+    flat = c.to(dev).contiguous().reshape(-1)
+    out = torch.empty_like(flat)
+    nat.call("jxr_threefry_2x32", _ptr(kd), 1, _ptr(flat), flat.numel(), _ptr(out), _stream())
+    return out.reshape(c.shape)
+
+
+# ---- split / fold_in / bits (R/random.R:195-276) ---------------------------------------------
+
+def random_split(key, num=2):
+    """Split a key into `num` (an int or a shape) new keys (R/random.R:209-213)."""
+    k, wrapped, nb = _check_key("split", key)
+    shape = canon_shape(num)
+    bshape = k.shape[:nb]
+    out = _k_split(_flat_keys(k), shape, _layout()).reshape(bshape + shape + (2,))
+    return _rebatch(_return_keys(wrapped, PRNGKeyArray(out, k.impl)), nb)
+
+
+def _fold_data(data):
+    d, nb = _unbatch(data)
+    if isinstance(d, (torch.Tensor, np.ndarray)):
+        dshape = tuple(d.shape)
+        if len(dshape) > nb:
+            raise JaxTypeError(f"fold_in accepts a scalar, but was given an array of shape "
+                               f"{shape_str(dshape[nb:])} != (). Use jax.vmap for batching.")
+        t = torch.as_tensor(d) if not isinstance(d, torch.Tensor) else d
+        if t.dtype == torch.uint32:
+            vals = t.reshape(-1)
+        else:
+            if t.dtype.is_floating_point:
+                t = t.to(torch.int64)
+            vals = (t.to(torch.int64).reshape(-1) & 0xFFFFFFFF).to(torch.uint32)
+        return vals.to(_device()).contiguous(), dshape[:nb], nb
+    if isinstance(d, (list, tuple)):
+        raise JaxTypeError(f"fold_in accepts a scalar, but was given an array of shape "
+                           f"{shape_str(np.shape(d))} != (). Use jax.vmap for batching.")
+    if isinstance(d, numbers.Number):
+        if not float(d) == int(d):
+            raise JaxTypeError(f"fold_in data must be an integer; got {d}")
+        v = int(d)
+        if v < 0 or v >= 1 << 32:
+            raise JaxOverflowError(f"Python integer {v} out of bounds for uint32")
+        return torch.tensor([v], dtype=torch.uint32).to(_device()), (), 0
+    raise JaxTypeError(f"fold_in data must be an integer; got {type(d).__name__}")
+
+
+def random_fold_in(key, data):
+    """Fold a 32-bit integer into a key (R/random.R:195-206)."""
+    k, wrapped, knb = _check_key("fold_in", key)
+    dvals, dbshape, dnb = _fold_data(data)
+    kd = _flat_keys(k)
+    kbshape = k.shape[:knb]
+    nb = max(knb, dnb)
+    if knb and dnb and kbshape != dbshape:
+        raise JaxValueError("fold_in: key and data batch shapes differ")
+    bshape = kbshape if knb >= dnb else dbshape
+    out = _k_fold_in(kd, dvals).reshape(bshape + (2,))
+    return _rebatch(_return_keys(wrapped, PRNGKeyArray(out, k.impl)), nb)
+
+
+def random_bits(key, shape=(), dtype=None):
+    """Uniform random bits of an unsigned dtype (R/random.R:269-276)."""
+    k, _, nb = _check_key("bits", key)
+    dt = default_uint() if dtype is None else canonicalize_dtype(dtype)
+    if not _is_unsigned(dt):
+        raise JaxValueError(f"dtype argument to `bits` must be an unsigned int dtype, got {dt}")
+    shape = canon_shape(shape)
+    out = _k_bits(_flat_keys(k), _size(shape), _BITS[dt], _layout())
+    return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
+
+
+# ---- uniform / normal / bernoulli (R/random.R:278-304, :466-508, :643-666) -------------------
+
+def _float_dtype(name, dt, kind="a float"):
+    d = canonicalize_dtype(dt if dt is not None else "float")
+    ok = d in _FLOAT_CODE or (kind == "a float or complex" and d.startswith("complex"))
+    if not ok:
+        raise JaxValueError(f"dtype argument to `{name}` must be {kind} dtype, got {d}")
+    return d
+
+
+def _param(x, dt):
+    """A bound or probability: a Python number (scalar) or an array converted to dt."""
+    x, nb = _unbatch(x)
+    if nb:
+        raise JaxNotImplementedError("batched sampler parameters are not supported")
+    if isinstance(x, numbers.Number) and not isinstance(x, bool):
+        return float(x), None
+    t = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x, dtype=np.float64))
+    if t.ndim == 0:
+        return float(t.item()), None
+    return None, t
+
+
+def _broadcast_param(t, shape, dt, name):
+    try:
+        b = torch.broadcast_shapes(tuple(t.shape), shape)
+    except RuntimeError:
+        b = None
+    if b != tuple(shape):
+        raise JaxValueError(
+            f"{name} parameter shapes must be broadcast-compatible with shape argument, and the "
+            "result of broadcasting the shapes must equal the shape argument, but got result "
+            f"{shape_str(b or t.shape)} for shape argument {shape_str(shape)}.")
+    # convert in double then to the dtype (one rounding), as lax_convert_element_type
+    t64 = t.to(torch.float64).to(_device())
+    conv = t64.to(_TORCH[dt])
+    return conv.broadcast_to(shape).contiguous()
+
+
+def _raw16(t, dt):
+    return t.view(torch.uint16) if dt in ("float16", "bfloat16") else t
+
+
+def random_uniform(key, shape=(), dtype=None, minval=0.0, maxval=1.0):
+    """Uniform floats in [minval, maxval) (R/random.R:278-304)."""
+    k, _, nb = _check_key("uniform", key)
+    dt = _float_dtype("uniform", dtype)
+    shape = canon_shape(shape)
+    size = _size(shape)
+    kd = _flat_keys(k)
+    mn_s, mn_t = _param(minval, dt)
+    mx_s, mx_t = _param(maxval, dt)
+    if mn_t is None and mx_t is None:
+        out = _k_uniform(kd, size, dt, mn_s, mx_s, _layout())
+    else:
+        unit = _k_uniform(kd, size, dt, 0.0, 1.0, _layout())
+        mn = _broadcast_param(mn_t if mn_t is not None else torch.tensor(mn_s), shape, dt, "uniform")
+        mx = _broadcast_param(mx_t if mx_t is not None else torch.tensor(mx_s), shape, dt, "uniform")
+        out = torch.empty_like(unit)
+        n = size
+        for r in range(unit.shape[0] if n else 0):
+            nat.call("jxr_uniform_affine", _ptr(_raw16(unit[r], dt)), _ptr(_raw16(mn, dt)),
+                     _ptr(_raw16(mx, dt)), n, _FLOAT_CODE[dt], 0, _ptr(_raw16(out[r], dt)),
+                     _stream())
+    return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
+
+
+def random_normal(key, shape=(), dtype=None):
+    """Standard normal floats: sqrt(2) * erf_inv(u), u uniform in (-1, 1)
+    (R/random.R:482-508)."""
+    k, _, nb = _check_key("normal", key)
+    dt = _float_dtype("normal", dtype, kind="a float or complex")
+    shape = canon_shape(shape)
+    size = _size(shape)
+    bshape = k.shape[:nb]
+    if dt.startswith("complex"):
+        return _rebatch(_complex_normal(k, bshape, shape, dt), nb)
+    out = _k_normal(_flat_keys(k), size, dt, _layout())
+    return _rebatch(out.reshape(bshape + shape), nb)
+
+
+def _complex_normal(k, bshape, shape, dt):
+    """(re + i im) / sqrt(2) with re, im normals of the two halves of split(key)
+    (R/random.R:489-499)."""
+    real = "float32" if dt == "complex64" else "float64"
+    kd = _flat_keys(k)
+    halves = _k_split(kd, (2,), _layout())  # (n, 2, 2)
+    size = _size(shape)
+    re = _k_normal(halves[:, 0].contiguous(), size, real, _layout())
+    im = _k_normal(halves[:, 1].contiguous(), size, real, _layout())
+    # complex / complex(sqrt 2, 0): each part divided by sqrt(2) in the real dtype
+    s = torch.tensor(math.sqrt(2), dtype=_TORCH[real], device=re.device)
+    z = torch.complex(re / s, im / s)
+    return z.reshape(bshape + shape)
+
+
+def random_bernoulli(key, p=0.5, shape=None, mode="low"):
+    """Bernoulli draws uniform(dtype(p)) < p (R/random.R:643-666)."""
+    if shape is not None:
+        shape = canon_shape(shape)
+    if mode not in ("high", "low"):
+        raise JaxValueError(f"got mode='{mode}', expected 'high' or 'low'")
+    k, _, nb = _check_key("bernoulli", key)
+    pv, pnb = _unbatch(p)
+    if isinstance(pv, bool) or (isinstance(pv, numbers.Integral)):
+        raise JaxTypeError(f"bernoulli probability `p` must have a floating dtype, got "
+                           f"{default_int()}.")
+    if isinstance(pv, torch.Tensor):
+        dt = _NAME[pv.dtype]
+    elif isinstance(pv, np.ndarray):
+        dt = canonicalize_dtype(pv.dtype)
+    elif isinstance(pv, (list, tuple)):
+        arr = np.asarray(pv)
+        dt = default_float() if arr.dtype.kind == "f" else canonicalize_dtype(arr.dtype)
+    else:
+        dt = default_float()  # an R number: weak float of the default width
+    if not _is_float(dt):
+        raise JaxTypeError(f"bernoulli probability `p` must have a floating dtype, got {dt}.")
+    p_s, p_t = _param(p, dt)
+    if shape is None:
+        shape = () if p_t is None else tuple(p_t.shape)
+    size = _size(shape)
+    kd = _flat_keys(k)
+    bshape = k.shape[:nb]
+    layout = _layout()
+    if mode == "low" and p_t is None:
+        out = _k_bernoulli(kd, size, dt, p_s, layout)
+        return _rebatch(out.reshape(bshape + shape), nb)
+    pt = _broadcast_param(p_t if p_t is not None else torch.tensor(p_s), shape, dt, "bernoulli")
+    n = size
+    if mode == "low":
+        u = _k_uniform(kd, size, dt, 0.0, 1.0, layout)
+        lo, hi = u, None
+    else:
+        u = _k_uniform(kd, 2 * size, dt, 0.0, 1.0, layout).reshape(kd.shape[0], 2, size)
+        lo, hi = u[:, 0], u[:, 1]
+    out = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
+    for r in range(kd.shape[0] if n else 0):
+        lo_r = _raw16(lo[r].contiguous(), dt)
+        hi_r = _raw16(hi[r].contiguous(), dt) if hi is not None else None
+        nat.call("jxr_bernoulli_from_uniform", _ptr(lo_r), _ptr(hi_r) if hi_r is not None else None,
+                 _ptr(_raw16(pt, dt)), n, _FLOAT_CODE[dt], _ptr(out[r]), _stream())
+    return _rebatch(out.view(torch.bool).reshape(bshape + shape), nb)
+
+
+def random_normal_bernoulli(key, p=0.5, shape=(), dtype=None):
+    """(random_normal(key, shape, dtype), random_bernoulli(key, p, shape)) of one key in a
+    single cipher pass; p is a Python float converted to dtype."""
+    k, _, nb = _check_key("normal", key)
+    dt = _float_dtype("normal", dtype)
+    shape = canon_shape(shape)
+    size = _size(shape)
+    kd = _flat_keys(k)
+    layout = _layout()
+    _check_size(size, layout)
+    nout = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    bout = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
+    nat.call("jxr_normal_bernoulli", _ptr(kd), kd.shape[0], size, 0, size, layout,
+             _FLOAT_CODE[dt], float(p), _ptr(nout), _ptr(bout), _stream())
+    bshape = k.shape[:nb]
+    return (_rebatch(_as_float_view(nout, dt).reshape(bshape + shape), nb),
+            _rebatch(bout.view(torch.bool).reshape(bshape + shape), nb))
+
+
+# ---- erf_inv (R/lax.R:222) ---------------------------------------------------------------------
+
+def lax_erf_inv(x):
+    """Element-wise inverse error function for float32/float64 arrays."""
+    t = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x, dtype=default_float()))
+    dt = _NAME[t.dtype]
+    if dt not in ("float32", "float64"):
+        raise JaxTypeError(f"erf_inv does not accept dtype {dt}")
+    src = t.to(_device()).contiguous()
+    out = torch.empty_like(src)
+    nat.call("jxr_erf_inv", _ptr(src), src.numel(), _FLOAT_CODE[dt], _ptr(out), _stream())
+    return out

@@ -1,0 +1,93 @@
+"""Requests split by contiguous counter range over the GPUs of one node.
+
+Every element of a threefry request depends only on (key, element index), so device
+r of G produces elements [r*size/G, (r+1)*size/G) of the C-order result with no
+communication (the partitionable layout; for the original layout the same element
+range is produced from the blocks that feed it).  `gather_to` assembles the whole
+array on one device when a caller asks for it, over NVLink through NCCL.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+from . import config as cfg
+from .random import (_TORCH, _BITS, _check_key, _flat_keys, _layout, _ptr, _size, _stream,
+                     canon_shape, canonicalize_dtype, default_uint)
+from .errors import JaxValueError
+
+
+def shard_range(size, rank, world):
+    """[begin, end) of `rank`'s slab of a size-element request over `world` devices."""
+    if world < 1 or not 0 <= rank < world:
+        raise JaxValueError(f"bad rank {rank} of world {world}")
+    return size * rank // world, size * (rank + 1) // world
+
+
+def random_bits_shard(key, shape, rank, world, dtype=None, out=None):
+    """This device's slab of random_bits(key, shape, dtype): a 1-D tensor of the elements
+    [begin, end) of the flattened C-order result (see shard_range)."""
+    k, _, nb = _check_key("bits", key)
+    if nb:
+        raise JaxValueError("random_bits_shard takes a single key")
+    dt = default_uint() if dtype is None else canonicalize_dtype(dtype)
+    size = _size(canon_shape(shape))
+    lo, hi = shard_range(size, rank, world)
+    n = hi - lo
+    if out is None:
+        out = torch.empty(n, dtype=_TORCH[dt], device=k.data.device)
+    elif out.numel() != n or out.dtype != _TORCH[dt] or not out.is_contiguous():
+        raise JaxValueError(f"out must be a contiguous {dt} tensor of {n} elements")
+    nat.call("jxr_random_bits", _ptr(_flat_keys(k)), 1, size, lo, n, _layout(), _BITS[dt],
+             _ptr(out), _stream())
+    return out
+
+
+def random_bits_to_host(key, shape, dtype=None, out=None):
+    """random_bits(key, shape, dtype) written into host memory (pinned `out`, allocated if
+    not given): generated on the current device in chunks, each copied to the host while
+    the next is generated.  Returns the host tensor of `shape`."""
+    k, _, nb = _check_key("bits", key)
+    if nb:
+        raise JaxValueError("random_bits_to_host takes a single key")
+    dt = default_uint() if dtype is None else canonicalize_dtype(dtype)
+    shape = canon_shape(shape)
+    size = _size(shape)
+    if out is None:
+        out = torch.empty(size, dtype=_TORCH[dt], pin_memory=True)
+    keys_host = k.data.reshape(-1, 2).cpu().contiguous()
+    nat.call("jxr_random_bits_host", _ptr(keys_host), 1, size, 0, size, _layout(), _BITS[dt],
+             _ptr(out))
+    return out.reshape(shape)
+
+
+def gather_to(local, root, group=None):
+    """Assemble the slabs of all ranks (rank order) on rank `root` with NCCL; returns the
+    whole flattened array on root and None elsewhere.  Every rank passes its slab; slabs
+    may differ in length by one element (shard_range)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n = torch.tensor([local.numel()], device=local.device, dtype=torch.int64)
+    sizes = [torch.empty_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n, group=group)
+    sizes = [int(s.item()) for s in sizes]
+    view = local.view(torch.int32) if local.element_size() == 4 else local.view(torch.uint8)
+    if rank == root:
+        total = sum(sizes) * local.element_size() // view.element_size()
+        whole = torch.empty(total, dtype=view.dtype, device=local.device)
+        parts = list(torch.split(whole, [s * local.element_size() // view.element_size()
+                                         for s in sizes]))
+        ops = []
+        for r in range(world):
+            if r == root:
+                parts[r].copy_(view)
+            else:
+                ops.append(dist.P2POp(dist.irecv, parts[r], r, group=group))
+        for w in dist.batch_isend_irecv(ops) if ops else []:
+            w.wait()
+        return whole.view(local.dtype)
+    for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, view, root, group=group)]):
+        w.wait()
+    return None

@@ -17,6 +17,12 @@
 #include <omp.h>
 #endif
 
+#ifdef _OPENMP
+#define ORC_PAR_FOR _Pragma("omp parallel for schedule(static) num_threads(orc_get_threads())")
+#else
+#define ORC_PAR_FOR
+#endif
+
 static int g_threads = 0;
 
 void orc_set_threads(int n) { g_threads = n; }
@@ -186,11 +192,6 @@ __attribute__((target_clones("avx512f", "avx2", "default"))) static void bulk_pa
   }
 }
 
-#ifdef _OPENMP
-#define ORC_PAR_FOR _Pragma("omp parallel for schedule(static) num_threads(orc_get_threads())")
-#else
-#define ORC_PAR_FOR
-#endif
 
 int orc_random_bits(const uint32_t key[2], int bit_width, uint64_t size, int partitionable,
                     uint64_t begin, uint64_t count, void* out) {
@@ -329,6 +330,14 @@ double orc_erfinv_f64(double x, int fma_) {
   for (int i = 1; i < n; ++i) p = fma_ ? fma(p, w, c[i]) : c[i] + p * w;
   if (fabs(x) == 1.0) return x * INFINITY;
   return p * x;
+}
+
+void orc_erfinv_arr(const void* x, int64_t n, int dtype, int fma_, void* out) {
+  ORC_PAR_FOR
+  for (int64_t i = 0; i < n; ++i) {
+    if (dtype == ORC_F32) ((float*)out)[i] = orc_erfinv_f32(((const float*)x)[i], fma_);
+    else ((double*)out)[i] = orc_erfinv_f64(((const double*)x)[i], fma_);
+  }
 }
 
 /* ---- samplers -------------------------------------------------------------------------- */

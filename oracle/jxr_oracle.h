@@ -61,6 +61,7 @@ int orc_random_bits(const uint32_t key[2], int bit_width, uint64_t size, int par
  * emits chlo.erf_inv).  fma selects a fused Horner evaluation. */
 float orc_erfinv_f32(float x, int fma);
 double orc_erfinv_f64(double x, int fma);
+void orc_erfinv_arr(const void* x, int64_t n, int dtype, int fma, void* out);
 
 /* Samplers (R/random.R:288-304, :502-508, :656-666).  dtype is an ORC_ code;
  * 16-bit results are returned as their raw bits in a uint16_t array.

@@ -49,6 +49,7 @@ def lib():
         L.orc_erfinv_f32.restype = ctypes.c_float
         L.orc_erfinv_f64.argtypes = [dbl, i32]
         L.orc_erfinv_f64.restype = dbl
+        L.orc_erfinv_arr.argtypes = [vp, i64, i32, i32, vp]
         L.orc_uniform.argtypes = [u32p, i32, u64, i32, dbl, dbl, i32, u64, u64, vp]
         L.orc_normal.argtypes = [u32p, i32, u64, i32, i32, u64, u64, vp]
         L.orc_bernoulli.argtypes = [u32p, i32, dbl, u64, i32, u64, u64, vp]
@@ -122,12 +123,10 @@ def bits_at(key, bit_width, size, partitionable, idx):
 
 
 def erfinv(x, dtype="float32", fma=True):
-    L = lib()
-    if dtype == "float32":
-        return np.array([L.orc_erfinv_f32(float(v), int(fma)) for v in
-                         np.asarray(x, dtype=np.float32).ravel()], dtype=np.float32)
-    return np.array([L.orc_erfinv_f64(float(v), int(fma)) for v in
-                     np.asarray(x, dtype=np.float64).ravel()], dtype=np.float64)
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32 if dtype == "float32" else np.float64))
+    out = np.empty_like(a)
+    lib().orc_erfinv_arr(_ptr(a), a.size, F32 if dtype == "float32" else F64, int(fma), _ptr(out))
+    return out.ravel()
 
 
 def uniform(key, dtype, size, partitionable=True, minval=0.0, maxval=1.0, fma=True, begin=0,

@@ -1,0 +1,91 @@
+"""Replays golden cases through the product's public API (jaxr_b200), on the GPU."""
+
+from __future__ import annotations
+
+import contextlib
+
+import numpy as np
+import torch
+
+import jaxr_b200 as jr
+from jaxr_b200 import random as jrr
+
+
+def to_np(t):
+    if isinstance(t, jr.PRNGKeyArray):
+        t = t.data
+    t = t.detach().cpu()
+    if t.dtype in (torch.float16, torch.bfloat16):
+        return t.float().numpy()
+    return t.numpy()
+
+
+@contextlib.contextmanager
+def flags(x64=False, partitionable=True):
+    with jr.with_jax_config("jax_enable_x64", x64), \
+            jr.with_jax_config("jax_threefry_partitionable", partitionable):
+        yield
+
+
+class ProductBackend:
+    """The interface of golden_cases.OracleBackend on jaxr_b200 (raw uint32 keys)."""
+
+    def __init__(self, x64=False, partitionable=True):
+        self.x64 = x64
+        self.part = partitionable
+
+    def _ctx(self, part=None):
+        return flags(self.x64, self.part if part is None else part)
+
+    def threefry_2x32(self, key, count):
+        k = torch.tensor(np.asarray(key, dtype=np.uint32))
+        c = torch.tensor(np.asarray(count, dtype=np.uint32))
+        return to_np(jr.threefry_2x32(k, c))
+
+    def seed(self, s, x64):
+        with flags(x64, self.part):
+            return to_np(jr.random_PRNGKey(s))
+
+    def fold_in(self, key, data):
+        with self._ctx():
+            return to_np(jr.random_fold_in(torch.tensor(np.asarray(key, np.uint32)), int(data)))
+
+    def split(self, key, n, part):
+        with self._ctx(part):
+            return to_np(jr.random_split(torch.tensor(np.asarray(key, np.uint32)), n))
+
+    def bits(self, key, bw, n, part):
+        with flags(bw == 64 or self.x64, part):
+            return to_np(jr.random_bits(torch.tensor(np.asarray(key, np.uint32)), (n,), f"uint{bw}"))
+
+    def uniform(self, key, dt, n, part, mn, mx):
+        with flags(dt == "float64" or self.x64, part):
+            out = jr.random_uniform(torch.tensor(np.asarray(key, np.uint32)), (n,), dt, mn, mx)
+        return _raw(out, dt)
+
+    def uniform_array_bounds(self, key, dt, shape, part, mn, mx):
+        with flags(dt == "float64" or self.x64, part):
+            out = jr.random_uniform(torch.tensor(np.asarray(key, np.uint32)), shape, dt,
+                                    np.asarray(mn, dtype=np.float64), np.asarray(mx, dtype=np.float64))
+        return _raw(out, dt)
+
+    def normal(self, key, dt, n, part):
+        with flags(dt == "float64" or self.x64, part):
+            out = jr.random_normal(torch.tensor(np.asarray(key, np.uint32)), (n,), dt)
+        return _raw(out, dt)
+
+    def bernoulli(self, key, dt, p, n, part):
+        with flags(dt == "float64" or self.x64, part):
+            pt = torch.tensor(p, dtype=jrr._TORCH[dt])
+            return to_np(jr.random_bernoulli(torch.tensor(np.asarray(key, np.uint32)), pt, (n,)))
+
+    def erfinv(self, xs, dt):
+        with flags(dt == "float64", self.part):
+            return to_np(jr.lax_erf_inv(torch.tensor(np.asarray(xs))))
+
+
+def _raw(out, dt):
+    """16-bit floats as their raw bits (as the oracle returns them)."""
+    if dt in ("float16", "bfloat16"):
+        return out.detach().cpu().view(torch.uint16).numpy()
+    return to_np(out)

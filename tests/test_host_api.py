@@ -1,0 +1,150 @@
+"""Host-side behaviour of the public API that needs no GPU: argument checks and error
+messages/classes (tests/testthat/test-prng.R:260-279, test-random.R:382-407), dtype
+canonicalisation, seeds and shard ranges."""
+
+import numpy as np
+import pytest
+import torch
+
+import jaxr_b200 as jr
+from jaxr_b200 import random as jrr
+from jaxr_b200.shard import shard_range
+
+U32 = torch.uint32
+
+
+def raw(*shape):
+    return torch.zeros(shape, dtype=U32)
+
+
+def test_key_errors_follow_reference():
+    # test-prng.R:263-279
+    with pytest.raises(jr.JaxValueError, match=r"split accepts a single key, but was given a key "
+                                               r"array of shape \(2, 2\)"):
+        jr.random_split(raw(2, 2))
+    with pytest.raises(jr.JaxValueError, match="uniform accepts a single key"):
+        jr.random_uniform(jr.PRNGKeyArray(raw(2, 2)))
+    with pytest.raises(jr.JaxTypeError, match="expected key_data.dtype = uint32; got dtype=float32"):
+        jr.random_split(np.array([0.0, 0.0]))
+    with pytest.raises(jr.JaxTypeError, match=r"expected key_data.shape to end with \(2,\)"):
+        jr.random_split(raw(3))
+    with pytest.raises(jr.JaxTypeError, match="expected key_data.ndim >= 1"):
+        jr.random_split(torch.zeros((), dtype=U32))
+    with pytest.raises(jr.JaxTypeError, match="unexpected PRNG key type"):
+        jr.random_split("a")
+    with pytest.raises(jr.JaxTypeError, match=r"key accepts a scalar seed, but was given an array "
+                                              r"of shape \(2,\)"):
+        jr.random_key([1, 2])
+    with pytest.raises(jr.JaxTypeError, match="accepts a scalar seed, but was given a PRNG key"):
+        jr.random_PRNGKey(jr.PRNGKeyArray(raw(2)))
+    with pytest.raises(jr.JaxTypeError, match="PRNG key seed must be an integer"):
+        jr.random_key(0.5)
+    with pytest.raises(jr.JaxValueError, match="Cannot specify both"):
+        jr.random_key(0, impl="rbg", dtype="rbg")
+    with pytest.raises(jr.JaxTypeError, match="fold_in accepts a scalar"):
+        jr.random_fold_in(raw(2), np.array([1, 2]))
+    with pytest.raises(jr.JaxOverflowError, match="out of bounds for uint32"):
+        jr.random_fold_in(raw(2), -1)
+    with pytest.raises(jr.JaxValueError, match="must be an unsigned int dtype"):
+        jr.random_bits(raw(2), 3, "int32")
+    with pytest.raises(jr.JaxTypeError, match="iteration over a 0-d key array"):
+        list(jr.PRNGKeyArray(raw(2)))
+    with pytest.raises(jr.JaxValueError, match="unrecognized PRNG implementation"):
+        jr.random_key(0, impl="philox")
+
+
+def test_sampler_argument_errors():
+    # test-random.R:385-390
+    k = raw(2)
+    with pytest.raises(jr.JaxValueError, match="dtype argument to `uniform` must be a float dtype"):
+        jr.random_uniform(k, 3, dtype="int32")
+    with pytest.raises(jr.JaxValueError, match="must be a float or complex dtype"):
+        jr.random_normal(k, 3, dtype="int32")
+    with pytest.raises(jr.JaxTypeError, match="bernoulli probability `p` must have a floating dtype"):
+        jr.random_bernoulli(k, 1)
+    with pytest.raises(jr.JaxValueError, match="expected 'high' or 'low'"):
+        jr.random_bernoulli(k, 0.5, mode="mid")
+    with pytest.raises(jr.JaxTypeError, match="Shapes must be 1D sequences"):
+        jr.random_normal(k, -1)
+
+
+def test_errors_are_builtin_classes_too():
+    with pytest.raises(ValueError):
+        jr.random_bits(raw(2), 3, "int32")
+    with pytest.raises(TypeError):
+        jr.random_key(0.5)
+    with pytest.raises(OverflowError):
+        jr.random_fold_in(raw(2), 2 ** 32)
+
+
+def test_dtype_canonicalisation():
+    assert jr.canonicalize_dtype("uint64") == "uint32"
+    assert jr.canonicalize_dtype("float") == "float32"
+    with jr.with_jax_config("jax_enable_x64", True):
+        assert jr.canonicalize_dtype("uint64") == "uint64"
+        assert jr.canonicalize_dtype("float") == "float64"
+        assert jrr.default_uint() == "uint64"
+    assert jr.random_key_dtype() == "key<fry>"
+    assert jr.random_key_dtype("rbg") == "key<rbg>"
+
+
+def test_seed_words_match_reference_keys():
+    # test-prng.R:27-30 and :118-119
+    def words(s, x64):
+        with jr.with_jax_config("jax_enable_x64", x64):
+            k0, k1 = jrr._seed_words(s)
+        return [int(k0), int(k1)]
+    assert words(0, False) == [0, 0]
+    assert words(42, False) == [0, 42]
+    assert words(-1, False) == [0, 4294967295]
+    assert words(2 ** 40 + 5, False) == [0, 5]
+    assert words(-1, True) == [4294967295, 4294967295]
+    assert words(2 ** 40 + 5, True) == [256, 5]
+    # integer arrays keep their width: a 32-bit seed has k0 = 0 even with x64
+    with jr.with_jax_config("jax_enable_x64", True):
+        k0, k1 = jrr._seed_words(torch.tensor([-1, 3], dtype=torch.int32))
+    assert k0.tolist() == [0, 0] and k1.tolist() == [4294967295, 3]
+    with jr.with_jax_config("jax_random_seed_offset", 10):
+        assert words(0, False) == [0, 10]
+
+
+def test_shard_ranges_cover_the_request():
+    size = (1 << 34) + 3
+    for world in (1, 2, 3, 4, 8):
+        spans = [shard_range(size, r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == size
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        lens = [b - a for a, b in spans]
+        assert max(lens) - min(lens) <= 1
+
+
+def test_config_flags():
+    assert jr.jax_config("jax_threefry_partitionable") is True
+    with jr.with_jax_config("jax_threefry_partitionable", False):
+        assert jrr._layout() == 0
+    assert jrr._layout() == 1
+    old = jr.enable_x64(True)
+    try:
+        assert jr.jax_config("jax_enable_x64") is True
+    finally:
+        jr.enable_x64(old)
+    with pytest.raises(jr.JaxValueError):
+        jr.jax_config_update("no_such_option", 1)
+
+
+def test_vmap_argument_checks():
+    with pytest.raises(jr.JaxValueError, match="inconsistent sizes"):
+        jr.vmap(lambda a, b: a)(raw(3, 2), raw(4, 2))
+    with pytest.raises(jr.JaxValueError, match="rank should be at least 1"):
+        jr.vmap(lambda a: a)(torch.tensor(1))
+
+
+def test_key_array_surface():
+    k = jr.PRNGKeyArray(torch.arange(12, dtype=torch.int64).to(U32).reshape(3, 2, 2))
+    assert k.shape == (3, 2) and k.ndim == 2 and len(k) == 3
+    assert k[1].shape == (2,) and k[1, 0].data.tolist() == [4, 5]
+    assert [x.shape for x in k] == [(2,), (2,), (2,)]
+    assert "dtype=key<fry>" in repr(k)
+    assert jr.random_key_impl(k) == "threefry2x32"
+    assert jr.random_key_data(k) is k.data
+    assert jr.random_Key(k) is k
