@@ -151,11 +151,13 @@ int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p
  * element-wise for F32 or F64. */
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);
 
-/* random_bits into HOST memory: generates on the current device in chunks into a
- * device staging buffer that the call allocates and frees, and copies each chunk
- * to host_out while the next one is generated.  Synchronous: returns when
- * host_out holds the result.  host_out should be pinned (cudaHostAlloc or
- * cudaHostRegister) for full PCIe bandwidth. */
+/* random_bits into HOST memory: generates on the current device in 64 MiB chunks into
+ * device staging buffers and copies each chunk to host_out while the next one is
+ * generated.  Synchronous: returns when host_out holds the result.  host_out should be
+ * pinned (cudaHostAlloc or cudaHostRegister) for full PCIe bandwidth.  The staging
+ * buffers (2 x 64 MiB), a device copy of the keys and two streams are created on the
+ * first call on a device and kept for later calls; calls on one device run one at a
+ * time. */
 int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size,
                          uint64_t begin, uint64_t count, int layout, int bit_width,
                          void* host_out);

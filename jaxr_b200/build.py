@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libjxrng.so")
 SOURCES = [os.path.join(CSRC, "jxrng.cu")]
-HEADERS = [os.path.join(CSRC, f) for f in ("threefry.cuh", "samplers.cuh")] + [
+HEADERS = [os.path.join(CSRC, f) for f in ("threefry.cuh", "samplers.cuh", "blocks.cuh")] + [
     os.path.join(ROOT, "include", "jxrng.h")]
 
 NVCC_FLAGS = [

@@ -1,0 +1,207 @@
+// k_blocks: one threefry block per output element, the bulk kernel of the
+// partitionable layout (R/prng.R:212-227) and of the original layout's 64-bit draws
+// (R/prng.R:246-251).
+//
+// Element i of a request hashes the counters
+//   kCtrIndex  (i >> 32, i & 0xFFFFFFFF)   the C-order index split into two words
+//   kCtrPair   (i, size + i)              original layout, 64 bits, size < 2^31
+// and the op turns the cipher words into the stored value (bits, uniform, normal, ...).
+//
+// Work decomposition.  A CTA of 256 threads owns tiles of TILE = 256 * G * V elements,
+// V = 16 / sizeof(Out) so that one thread-group of V elements is one 16-byte store;
+// group g of thread t covers elements [tile + (g * 256 + t) * V, ... + V), so each warp
+// store instruction writes 512 contiguous bytes.  The grid is one resident wave and
+// strides over the tiles.  For a single key the tile's counter words are derived from
+// per-tile uniform values: inside a tile that does not cross a multiple of 2^32 the
+// high word is constant and the low word is base + immediate, so the cipher's integer
+// pipe work is almost all the per-element cost.
+#pragma once
+
+#include <cstdint>
+
+#include "samplers.cuh"
+#include "threefry.cuh"
+
+namespace jxr {
+
+constexpr int kThreads = 256;
+
+// The pipe mix the bulk kernels use: round adds as multiply-adds on the FMA pipe,
+// rotations and xors on the ALU pipe (the fastest mix measured on B200).
+using ProductMix = MixPolicy<0u, 0xFu, false>;
+
+enum { kCtrIndex = 0, kCtrPair = 1 };
+
+// kBits == -1 stores the key pair (x0, x1) itself (split); otherwise W-bit draws:
+// 64 bits are x0 << 32 | x1 (R/prng.R:220-224), narrower ones x0 ^ x1 truncated
+// (R/prng.R:225-226).
+template <int kBits>
+struct Draw;
+template <> struct Draw<64> {
+  __device__ static uint64_t get(uint32_t x0, uint32_t x1) { return ((uint64_t)x0 << 32) | x1; }
+};
+template <> struct Draw<32> {
+  __device__ static uint32_t get(uint32_t x0, uint32_t x1) { return x0 ^ x1; }
+};
+template <> struct Draw<16> {
+  __device__ static uint16_t get(uint32_t x0, uint32_t x1) { return (uint16_t)(x0 ^ x1); }
+};
+template <> struct Draw<8> {
+  __device__ static uint8_t get(uint32_t x0, uint32_t x1) { return (uint8_t)(x0 ^ x1); }
+};
+
+struct OpKeyPair {
+  static constexpr int kBits = -1;
+  using Out = uint64_t;  // little-endian: (x0, x1) in memory
+};
+
+template <class Op>
+__device__ __forceinline__ typename Op::Out apply(const Op& op, uint32_t x0, uint32_t x1) {
+  if constexpr (Op::kBits == -1) return ((uint64_t)x1 << 32) | x0;
+  else return op(Draw<Op::kBits>::get(x0, x1));
+}
+
+// 16 bytes of outputs, stored as one vector
+template <class T>
+union Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  T v[N];
+  uint4 u;
+};
+
+template <class Out>
+__host__ __device__ constexpr int groups_for() {
+  // blocks in flight per thread: G groups of 16 / sizeof(Out) outputs (16 blocks for 4-byte
+  // outputs: 40 registers, 6 CTAs per SM, measured fastest on B200)
+  return sizeof(Out) >= 4 ? 4 : (sizeof(Out) == 2 ? 2 : 1);
+}
+
+__host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
+
+// ---- single key ---------------------------------------------------------------------------
+
+template <class Op, int kCtr, class Mix = ProductMix, int G = groups_for<typename Op::Out>()>
+__global__ void __launch_bounds__(kThreads)
+    k_blocks_1key(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
+                  uint64_t count, int vec_ok, Op op, PipeConsts pc,
+                  typename Op::Out* __restrict__ out) {
+  using Out = typename Op::Out;
+  constexpr int V = 16 / sizeof(Out);
+  constexpr int N = G * V;
+  constexpr uint32_t TILE = (uint32_t)kThreads * G * V;
+  const KeySchedule s = make_schedule(__ldg(keys), __ldg(keys + 1));
+  const uint64_t ntiles = (count + TILE - 1) / TILE;
+  const uint32_t toff = threadIdx.x * V;
+  for (uint64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    const uint64_t p0 = t * TILE;   // first output of the tile
+    const uint64_t e0 = begin + p0; // its element index in the request
+    uint32_t x0[N], x1[N];
+    if (kCtr == kCtrIndex) {
+      const uint32_t lo = (uint32_t)e0;
+      if (lo <= 0xFFFFFFFFu - TILE) {  // the whole tile shares the high word
+        const uint32_t hi = (uint32_t)(e0 >> 32), base = lo + toff;
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            x0[g * V + v] = hi;
+            x1[g * V + v] = base + (uint32_t)(g * kThreads * V + v);
+          }
+      } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            const uint64_t i = e0 + toff + (uint32_t)(g * kThreads * V + v);
+            x0[g * V + v] = (uint32_t)(i >> 32);
+            x1[g * V + v] = (uint32_t)i;
+          }
+      }
+    } else {  // (i, size + i), all below 2^32
+      const uint32_t a = (uint32_t)e0 + toff, b = (uint32_t)(size + e0) + toff;
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          x0[g * V + v] = a + (uint32_t)(g * kThreads * V + v);
+          x1[g * V + v] = b + (uint32_t)(g * kThreads * V + v);
+        }
+    }
+    threefry20<N, Mix>(s, x0, x1, pc);
+    Out* dst = out + p0 + toff;
+    if (vec_ok && p0 + TILE <= count) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        Vec16<Out> r;
+#pragma unroll
+        for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g * V + v], x1[g * V + v]);
+        *reinterpret_cast<uint4*>(dst + g * kThreads * V) = r.u;
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint64_t p = p0 + toff + (uint64_t)g * kThreads * V;
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (p + v < count) out[p + v] = apply(op, x0[g * V + v], x1[g * V + v]);
+      }
+    }
+  }
+}
+
+// ---- key batches (vmap): rows of `count` outputs, one key per row ---------------------------
+
+template <class Op, int kCtr, class Mix = ProductMix>
+__global__ void __launch_bounds__(kThreads)
+    k_blocks_nkey(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
+                  uint64_t count, uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, Op op,
+                  PipeConsts pc, typename Op::Out* __restrict__ out) {
+  using Out = typename Op::Out;
+  constexpr int V = 16 / sizeof(Out);
+  constexpr int G = groups_for<Out>();
+  const uint64_t stride = (uint64_t)gridDim.x * (kThreads * G);
+  for (uint64_t base = (uint64_t)blockIdx.x * (kThreads * G); base < nchunks; base += stride) {
+    uint64_t row[G], pos[G];
+    KeySchedule s[G];
+    uint32_t x0[G][V], x1[G][V];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
+      const uint64_t cc = c < nchunks ? c : nchunks - 1;
+      row[g] = cc / chunks_per_row;
+      pos[g] = (cc - row[g] * chunks_per_row) * V;
+      s[g] = make_schedule(__ldg(keys + 2 * row[g]), __ldg(keys + 2 * row[g] + 1));
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const uint64_t i = begin + pos[g] + v;  // element index within the request
+        if (kCtr == kCtrIndex) {
+          x0[g][v] = (uint32_t)(i >> 32);
+          x1[g][v] = (uint32_t)i;
+        } else {
+          x0[g][v] = (uint32_t)i;
+          x1[g][v] = (uint32_t)(size + i);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) threefry20<V, Mix>(s[g], x0[g], x1[g], pc);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
+      if (c >= nchunks) continue;
+      Vec16<Out> r;
+#pragma unroll
+      for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g][v], x1[g][v]);
+      Out* dst = out + row[g] * count + pos[g];
+      if (vec_ok && pos[g] + V <= count) {
+        *reinterpret_cast<uint4*>(dst) = r.u;
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (pos[g] + v < count) dst[v] = r.v[v];
+      }
+    }
+  }
+}
+
+}  // namespace jxr

@@ -22,18 +22,19 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
+#include "blocks.cuh"
 #include "samplers.cuh"
 #include "threefry.cuh"
 
 namespace jxr {
 namespace {
 
-constexpr int kThreads = 256;
+const PipeConsts kPipe = make_pipe_consts();
 
-__host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
 
 thread_local std::string g_error;
 
@@ -77,126 +78,42 @@ int device_info(DeviceInfo* info) {
   return JXR_OK;
 }
 
-// ---- cipher output -> draw ----------------------------------------------------------------
+// jxr_random_bits_host keeps, per device, two staging buffers of kStageBytes, a device
+// copy of the keys, two non-blocking streams (generate, copy) and their events, created on
+// the first call and reused by later calls (calls on one device are serialised).
+constexpr size_t kStageBytes = 64ull << 20;
 
-// kBits == -1 stores the key pair (x0, x1) itself (split); otherwise W-bit draws:
-// 64 bits are x0 << 32 | x1 (R/prng.R:220-224), narrower ones x0 ^ x1 truncated
-// (R/prng.R:225-226).
-template <int kBits>
-struct Draw;
-template <> struct Draw<64> {
-  __device__ static uint64_t get(uint32_t x0, uint32_t x1) { return ((uint64_t)x0 << 32) | x1; }
-};
-template <> struct Draw<32> {
-  __device__ static uint32_t get(uint32_t x0, uint32_t x1) { return x0 ^ x1; }
-};
-template <> struct Draw<16> {
-  __device__ static uint16_t get(uint32_t x0, uint32_t x1) { return (uint16_t)(x0 ^ x1); }
-};
-template <> struct Draw<8> {
-  __device__ static uint8_t get(uint32_t x0, uint32_t x1) { return (uint8_t)(x0 ^ x1); }
-};
+struct HostCopyCtx {
+  std::mutex mu;
+  bool ready = false;
+  cudaStream_t gen = nullptr, cpy = nullptr;
+  cudaEvent_t done[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
+  void* stage[2] = {nullptr, nullptr};
+  uint32_t* dkeys = nullptr;
+  size_t key_cap = 0;
 
-struct OpKeyPair {
-  static constexpr int kBits = -1;
-  using Out = uint64_t;  // little-endian: (x0, x1) in memory
-};
-
-template <class Op>
-__device__ __forceinline__ typename Op::Out apply(const Op& op, uint32_t x0, uint32_t x1) {
-  if constexpr (Op::kBits == -1) return ((uint64_t)x1 << 32) | x0;
-  else return op(Draw<Op::kBits>::get(x0, x1));
-}
-
-// 16 bytes of outputs, stored as one vector
-template <class T>
-union Vec16 {
-  static constexpr int N = 16 / sizeof(T);
-  T v[N];
-  uint4 u;
-};
-
-// ---- k_blocks: one block per output -----------------------------------------------------
-
-enum { kCtrIndex = 0, kCtrPair = 1 };
-
-template <class Out>
-__host__ __device__ constexpr int groups_for() {
-  // blocks in flight per thread: G groups of 16 / sizeof(Out) outputs
-  return sizeof(Out) >= 8 ? 4 : (sizeof(Out) == 4 ? 2 : 1);
-}
-
-template <class Op, int kCtr, bool kOneKey>
-__global__ void __launch_bounds__(kThreads)
-    k_blocks(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin, uint64_t count,
-             uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, Op op,
-             typename Op::Out* __restrict__ out) {
-  using Out = typename Op::Out;
-  constexpr int V = 16 / sizeof(Out);
-  constexpr int G = groups_for<Out>();
-  constexpr int N = G * V;
-
-  KeySchedule s1;
-  if (kOneKey) s1 = make_schedule(__ldg(keys), __ldg(keys + 1));
-
-  const uint64_t stride = (uint64_t)gridDim.x * (kThreads * G);
-  for (uint64_t base = (uint64_t)blockIdx.x * (kThreads * G); base < nchunks; base += stride) {
-    uint64_t row[G], pos[G];
-    KeySchedule s[G];
-    uint32_t x0[N], x1[N];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
-      if (kOneKey) {
-        row[g] = 0;
-        pos[g] = c * V;
-        s[g] = s1;
-      } else {
-        const uint64_t cc = c < nchunks ? c : nchunks - 1;
-        row[g] = cc / chunks_per_row;
-        pos[g] = (cc - row[g] * chunks_per_row) * V;
-        s[g] = make_schedule(__ldg(keys + 2 * row[g]), __ldg(keys + 2 * row[g] + 1));
+  int ensure(size_t nkeys) {
+    if (!ready) {
+      JXR_CUDA(cudaStreamCreateWithFlags(&gen, cudaStreamNonBlocking));
+      JXR_CUDA(cudaStreamCreateWithFlags(&cpy, cudaStreamNonBlocking));
+      for (int b = 0; b < 2; ++b) {
+        JXR_CUDA(cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming));
+        JXR_CUDA(cudaEventCreateWithFlags(&freed[b], cudaEventDisableTiming));
+        JXR_CUDA(cudaMalloc(&stage[b], kStageBytes));
       }
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const uint64_t i = begin + pos[g] + v;  // element index within the request
-        if (kCtr == kCtrIndex) {
-          x0[g * V + v] = (uint32_t)(i >> 32);
-          x1[g * V + v] = (uint32_t)i;
-        } else {
-          x0[g * V + v] = (uint32_t)i;
-          x1[g * V + v] = (uint32_t)(size + i);
-        }
-      }
+      ready = true;
     }
-    if (kOneKey) {
-      threefry20<N>(s1, x0, x1);
-    } else {
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        uint32_t (&a0)[V] = *reinterpret_cast<uint32_t(*)[V]>(&x0[g * V]);
-        uint32_t (&a1)[V] = *reinterpret_cast<uint32_t(*)[V]>(&x1[g * V]);
-        threefry20<V>(s[g], a0, a1);
-      }
+    if (key_cap < nkeys) {
+      if (dkeys) JXR_CUDA(cudaFree(dkeys));
+      dkeys = nullptr;
+      JXR_CUDA(cudaMalloc(&dkeys, 8 * nkeys));
+      key_cap = nkeys;
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
-      if (c >= nchunks) continue;
-      Vec16<Out> r;
-#pragma unroll
-      for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g * V + v], x1[g * V + v]);
-      Out* dst = out + row[g] * count + pos[g];
-      if (vec_ok && pos[g] + V <= count) {
-        *reinterpret_cast<uint4*>(dst) = r.u;
-      } else {
-#pragma unroll
-        for (int v = 0; v < V; ++v)
-          if (pos[g] + v < count) dst[v] = r.v[v];
-      }
-    }
+    return JXR_OK;
   }
-}
+};
+
+HostCopyCtx g_host_ctx[64];
 
 template <class K>
 int resident_grid(K kernel, uint64_t work_ctas, int* grid) {
@@ -218,20 +135,23 @@ int launch_blocks(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t b
   constexpr int V = 16 / sizeof(Out);
   constexpr int G = groups_for<Out>();
   if (count == 0 || nkeys == 0) return JXR_OK;
-  const uint64_t cpr = (count + V - 1) / V;
-  if (cpr > ~0ull / (uint64_t)nkeys) return fail(JXR_ERR_INVALID_ARGUMENT, "request too large");
-  const uint64_t nchunks = cpr * (uint64_t)nkeys;
-  const int vec_ok = ((uintptr_t)out % 16 == 0) && (nkeys == 1 || (count * sizeof(Out)) % 16 == 0);
-  const uint64_t ctas = (nchunks + kThreads * G - 1) / (kThreads * G);
   int grid = 0, rc;
   if (nkeys == 1) {
-    auto k = k_blocks<Op, kCtr, true>;
-    if ((rc = resident_grid(k, ctas, &grid))) return rc;
-    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, (Out*)out);
+    const int vec_ok = ((uintptr_t)out % 16 == 0);
+    const uint64_t ntiles = (count + (uint64_t)kThreads * G * V - 1) / ((uint64_t)kThreads * G * V);
+    auto k = k_blocks_1key<Op, kCtr>;
+    if ((rc = resident_grid(k, ntiles, &grid))) return rc;
+    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, vec_ok, op, kPipe, (Out*)out);
   } else {
-    auto k = k_blocks<Op, kCtr, false>;
+    const uint64_t cpr = (count + V - 1) / V;
+    if (cpr > ~0ull / (uint64_t)nkeys) return fail(JXR_ERR_INVALID_ARGUMENT, "request too large");
+    const uint64_t nchunks = cpr * (uint64_t)nkeys;
+    const int vec_ok = ((uintptr_t)out % 16 == 0) && (count * sizeof(Out)) % 16 == 0;
+    const uint64_t ctas = (nchunks + kThreads * G - 1) / (kThreads * G);
+    auto k = k_blocks_nkey<Op, kCtr>;
     if ((rc = resident_grid(k, ctas, &grid))) return rc;
-    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, (Out*)out);
+    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, kPipe,
+                                 (Out*)out);
   }
   JXR_CUDA(cudaGetLastError());
   return JXR_OK;
@@ -254,7 +174,7 @@ template <class Op>
 __global__ void __launch_bounds__(kThreads)
     k_words(const uint32_t* __restrict__ keys, uint64_t nwords, uint64_t half, uint64_t jlo,
             uint64_t jhi, uint64_t units_per_row, uint64_t nunits, uint64_t begin, uint64_t count,
-            Op op, typename Op::Out* __restrict__ out) {
+            Op op, PipeConsts pc, typename Op::Out* __restrict__ out) {
   using Out = typename Op::Out;
   constexpr int B = words_per_thread<Op>();
   constexpr int W = Op::kBits;
@@ -272,7 +192,7 @@ __global__ void __launch_bounds__(kThreads)
       x0[b] = (uint32_t)j;
       x1[b] = half + j < nwords ? (uint32_t)(half + j) : 0u;
     }
-    threefry20<B>(s, x0, x1);
+    threefry20<B, ProductMix>(s, x0, x1, pc);
     Out* orow = out + row * count;
 #pragma unroll
     for (int slab = 0; slab < 2; ++slab) {
@@ -344,7 +264,7 @@ int launch_words(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t be
     auto kern = k_words<Op>;
     if ((rc = resident_grid(kern, (nunits + kThreads - 1) / kThreads, &grid))) return rc;
     kern<<<grid, kThreads, 0, st>>>(keys, nwords, half, ranges[k].lo, ranges[k].hi, upr, nunits,
-                                    begin, count, op, (Out*)out);
+                                    begin, count, op, kPipe, (Out*)out);
     JXR_CUDA(cudaGetLastError());
   }
   return JXR_OK;
@@ -568,7 +488,8 @@ template <class OpN, class OpB, int kCtr, bool kOneKey>
 __global__ void __launch_bounds__(kThreads)
     k_normal_bernoulli(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
                        uint64_t count, uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, OpN opn,
-                       OpB opb, typename OpN::Out* __restrict__ nout, uint8_t* __restrict__ bout) {
+                       OpB opb, PipeConsts pc, typename OpN::Out* __restrict__ nout,
+                       uint8_t* __restrict__ bout) {
   using Out = typename OpN::Out;
   constexpr int V = 16 / sizeof(Out);
   const uint64_t stride = (uint64_t)gridDim.x * kThreads;
@@ -583,7 +504,7 @@ __global__ void __launch_bounds__(kThreads)
       x0[v] = kCtr == kCtrIndex ? (uint32_t)(i >> 32) : (uint32_t)i;
       x1[v] = kCtr == kCtrIndex ? (uint32_t)i : (uint32_t)(size + i);
     }
-    threefry20<V>(s, x0, x1);
+    threefry20<V, ProductMix>(s, x0, x1, pc);
     Vec16<Out> r;
     uint8_t bb[V];
 #pragma unroll
@@ -623,7 +544,7 @@ int launch_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, 
     auto k = k_normal_bernoulli<OpN, OpB, CTR, ONE>;                                         \
     if ((rc = resident_grid(k, ctas, &grid))) return rc;                                     \
     k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, opn, opb,   \
-                                 (Out*)nout, bout);                                          \
+                                 kPipe, (Out*)nout, bout);                                   \
   }
   if (layout == JXR_LAYOUT_PARTITIONABLE) {
     if (nkeys == 1) JXR_NB_LAUNCH(kCtrIndex, true) else JXR_NB_LAUNCH(kCtrIndex, false)
@@ -641,13 +562,14 @@ int launch_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, 
 // Each thread advances 8 independent blocks through `iters` full threefry20 passes, with
 // no counters, loads or stores: the integer-pipe ceiling of the cipher on this GPU, used
 // as the roofline denominator.  The xor of the final words is stored so the work stays.
-__global__ void __launch_bounds__(kThreads) k_probe_cipher(uint64_t iters, uint32_t* sink) {
+__global__ void __launch_bounds__(kThreads) k_probe_cipher(uint64_t iters, uint32_t* sink,
+                                                           PipeConsts pc) {
   const uint32_t t = blockIdx.x * kThreads + threadIdx.x;
   const KeySchedule s = make_schedule(t * 0x9E3779B9u, t ^ 0x85EBCA6Bu);
   uint32_t x0[8], x1[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) { x0[j] = t + j; x1[j] = ~t * (j + 1); }
-  for (uint64_t i = 0; i < iters; ++i) threefry20<8>(s, x0, x1);
+  for (uint64_t i = 0; i < iters; ++i) threefry20<8, ProductMix>(s, x0, x1, pc);
   uint32_t acc = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc ^= x0[j] ^ x1[j];
@@ -957,58 +879,42 @@ int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size
   if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64)
     return fail(JXR_ERR_INVALID_ARGUMENT, "requires 8-, 16-, 32- or 64-bit field width, got %d", bit_width);
   if (!count || !nkeys) return JXR_OK;
+  int dev = 0;
+  JXR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(JXR_ERR_NO_DEVICE, "device index %d out of range", dev);
+  HostCopyCtx& cx = g_host_ctx[dev];
+  std::lock_guard<std::mutex> lock(cx.mu);
+  if ((rc = cx.ensure((size_t)nkeys))) return rc;
   const size_t esz = (size_t)bit_width / 8;
-  // chunks of up to 64 MiB per key row, two staging buffers, generate and copy overlapped
-  const uint64_t chunk = std::min<uint64_t>(count, (64ull << 20) / esz);
-  cudaStream_t gen = nullptr, cpy = nullptr;
-  cudaEvent_t done[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
-  uint32_t* dkeys = nullptr;
-  void* stage[2] = {nullptr, nullptr};
+  const uint64_t chunk = kStageBytes / esz;
+  JXR_CUDA(cudaMemcpyAsync(cx.dkeys, keys_host, 8 * (size_t)nkeys, cudaMemcpyHostToDevice, cx.gen));
   int status = JXR_OK;
-  auto check = [&](cudaError_t e, const char* what) {
-    if (e != cudaSuccess && status == JXR_OK) status = fail(JXR_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-    return e == cudaSuccess;
-  };
-  if (check(cudaStreamCreateWithFlags(&gen, cudaStreamNonBlocking), "cudaStreamCreate") &&
-      check(cudaStreamCreateWithFlags(&cpy, cudaStreamNonBlocking), "cudaStreamCreate") &&
-      check(cudaEventCreateWithFlags(&done[0], cudaEventDisableTiming), "cudaEventCreate") &&
-      check(cudaEventCreateWithFlags(&done[1], cudaEventDisableTiming), "cudaEventCreate") &&
-      check(cudaEventCreateWithFlags(&freed[0], cudaEventDisableTiming), "cudaEventCreate") &&
-      check(cudaEventCreateWithFlags(&freed[1], cudaEventDisableTiming), "cudaEventCreate") &&
-      check(cudaMalloc(&dkeys, 8 * (size_t)nkeys), "cudaMalloc") &&
-      check(cudaMalloc(&stage[0], chunk * esz), "cudaMalloc") &&
-      check(cudaMalloc(&stage[1], chunk * esz), "cudaMalloc") &&
-      check(cudaMemcpyAsync(dkeys, keys_host, 8 * (size_t)nkeys, cudaMemcpyHostToDevice, gen),
-            "cudaMemcpyAsync")) {
-    int buf = 0;
-    bool first[2] = {true, true};
-    for (int64_t r = 0; r < nkeys && status == JXR_OK; ++r) {
-      for (uint64_t off = 0; off < count && status == JXR_OK; off += chunk) {
-        const uint64_t n = std::min(chunk, count - off);
-        if (!first[buf]) check(cudaStreamWaitEvent(gen, freed[buf], 0), "cudaStreamWaitEvent");
-        first[buf] = false;
-        int rc2 = jxr_random_bits(dkeys + 2 * r, 1, size, begin + off, n, layout, bit_width,
-                                  stage[buf], gen);
-        if (rc2) { status = rc2; break; }
-        check(cudaEventRecord(done[buf], gen), "cudaEventRecord");
-        check(cudaStreamWaitEvent(cpy, done[buf], 0), "cudaStreamWaitEvent");
-        char* dst = (char*)host_out + ((uint64_t)r * count + off) * esz;
-        check(cudaMemcpyAsync(dst, stage[buf], n * esz, cudaMemcpyDeviceToHost, cpy), "cudaMemcpyAsync");
-        check(cudaEventRecord(freed[buf], cpy), "cudaEventRecord");
-        buf ^= 1;
+  int buf = 0;
+  uint64_t issued = 0;
+  for (int64_t r = 0; r < nkeys && status == JXR_OK; ++r) {
+    for (uint64_t off = 0; off < count && status == JXR_OK; off += chunk, ++issued) {
+      const uint64_t n = std::min(chunk, count - off);
+      // the staging buffer is free once the copy issued two chunks ago has finished
+      if (issued >= 2 && cudaStreamWaitEvent(cx.gen, cx.freed[buf], 0) != cudaSuccess) {
+        status = fail(JXR_ERR_CUDA, "cudaStreamWaitEvent failed");
+        break;
       }
+      if ((status = jxr_random_bits(cx.dkeys + 2 * r, 1, size, begin + off, n, layout, bit_width,
+                                    cx.stage[buf], cx.gen)))
+        break;
+      char* dst = (char*)host_out + ((uint64_t)r * count + off) * esz;
+      cudaError_t e = cudaEventRecord(cx.done[buf], cx.gen);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(cx.cpy, cx.done[buf], 0);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(dst, cx.stage[buf], n * esz, cudaMemcpyDeviceToHost, cx.cpy);
+      if (e == cudaSuccess) e = cudaEventRecord(cx.freed[buf], cx.cpy);
+      if (e != cudaSuccess) status = fail(JXR_ERR_CUDA, "staged copy: %s", cudaGetErrorString(e));
+      buf ^= 1;
     }
   }
-  if (cpy) check(cudaStreamSynchronize(cpy), "cudaStreamSynchronize");
-  if (gen) check(cudaStreamSynchronize(gen), "cudaStreamSynchronize");
-  for (int b = 0; b < 2; ++b) {
-    if (stage[b]) cudaFree(stage[b]);
-    if (done[b]) cudaEventDestroy(done[b]);
-    if (freed[b]) cudaEventDestroy(freed[b]);
-  }
-  if (dkeys) cudaFree(dkeys);
-  if (gen) cudaStreamDestroy(gen);
-  if (cpy) cudaStreamDestroy(cpy);
+  cudaError_t e1 = cudaStreamSynchronize(cx.cpy), e2 = cudaStreamSynchronize(cx.gen);
+  if (status == JXR_OK && (e1 != cudaSuccess || e2 != cudaSuccess))
+    status = fail(JXR_ERR_CUDA, "cudaStreamSynchronize: %s",
+                  cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
   return status;
 }
 
@@ -1021,7 +927,7 @@ int jxr_probe_cipher(uint64_t iters, int ctas_per_sm, uint32_t* sink, uint64_t* 
     return fail(JXR_ERR_INVALID_ARGUMENT, "ctas_per_sm must be in [1, 8], got %d", ctas_per_sm);
   if (!sink || !blocks_out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
   const int grid = di.sms * ctas_per_sm;
-  k_probe_cipher<<<grid, kThreads, 0, (cudaStream_t)stream>>>(iters, sink);
+  k_probe_cipher<<<grid, kThreads, 0, (cudaStream_t)stream>>>(iters, sink, kPipe);
   JXR_CUDA(cudaGetLastError());
   *blocks_out = (uint64_t)grid * kThreads * 8ull * iters;
   return JXR_OK;

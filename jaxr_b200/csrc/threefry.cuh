@@ -9,8 +9,15 @@
 //
 // Everything stays in registers.  The key schedule (including the step counters
 // folded into the x1 injections) is hoisted once per key; N independent blocks
-// are advanced round by round so that a thread has N dependency chains in
-// flight; rotations are single funnel shifts.
+// are advanced round by round so that a thread has N dependency chains in flight.
+//
+// Pipe balance.  The cipher is integer work only: per block 20 rotations, 20 xors and
+// 32 adds.  Bitwise ops and funnel shifts issue to the ALU pipe; integer multiply-adds
+// issue to the FMA pipe, which is otherwise idle here.  An add can be written as a
+// multiply-add by a 1 the compiler cannot see (a kernel parameter), and a rotation as a
+// 32x32->64-bit multiply by 2^r whose two halves, or-ed, are the rotated word; the xor
+// that follows the rotation then takes the or for free in one three-input logic op.
+// MixPolicy selects, per round of a step, which rotations and adds take the FMA pipe.
 #pragma once
 
 #include <cstdint>
@@ -33,43 +40,103 @@ __host__ __device__ __forceinline__ KeySchedule make_schedule(uint32_t k0, uint3
   return s;
 }
 
-__device__ __forceinline__ uint32_t rotl(uint32_t x, int r) { return __funnelshift_l(x, x, r); }
+// Constants passed as kernel parameters so that the compiler emits multiply-adds:
+// one == 1 and pow2[r] == 2^r.  make_pipe_consts() fills them on the host.
+struct PipeConsts {
+  uint32_t one;
+  uint32_t pow2[32];
+};
 
-// Four rounds of one step over N blocks, round-major so the N chains interleave.
-template <int N, int R0, int R1, int R2, int R3>
-__device__ __forceinline__ void four_rounds(uint32_t (&x0)[N], uint32_t (&x1)[N]) {
-#pragma unroll
-  for (int j = 0; j < N; ++j) { x0[j] += x1[j]; x1[j] = rotl(x1[j], R0) ^ x0[j]; }
-#pragma unroll
-  for (int j = 0; j < N; ++j) { x0[j] += x1[j]; x1[j] = rotl(x1[j], R1) ^ x0[j]; }
-#pragma unroll
-  for (int j = 0; j < N; ++j) { x0[j] += x1[j]; x1[j] = rotl(x1[j], R2) ^ x0[j]; }
-#pragma unroll
-  for (int j = 0; j < N; ++j) { x0[j] += x1[j]; x1[j] = rotl(x1[j], R3) ^ x0[j]; }
+inline PipeConsts make_pipe_consts() {
+  PipeConsts c;
+  c.one = 1u;
+  for (int r = 0; r < 32; ++r) c.pow2[r] = 1u << r;
+  return c;
 }
 
-template <int N>
-__device__ __forceinline__ void inject(uint32_t (&x0)[N], uint32_t (&x1)[N], uint32_t a,
-                                       uint32_t b) {
+// kWide: bit j set = round j of every step rotates with a wide multiply (FMA pipe).
+// kMadd: bit j set = the x0 += x1 of round j is a multiply-add (FMA pipe).
+// kMaddInject: the key injections are multiply-adds.
+template <unsigned kWide, unsigned kMadd, bool kMaddInject>
+struct MixPolicy {
+  static constexpr unsigned wide = kWide;
+  static constexpr unsigned madd = kMadd;
+  static constexpr bool madd_inject = kMaddInject;
+};
+
+// Funnel shifts and plain adds, left to the compiler's scheduling (the small kernels).
+using DefaultMix = MixPolicy<0u, 0u, false>;
+
+template <bool kMad>
+__device__ __forceinline__ uint32_t add32(uint32_t a, uint32_t b, const PipeConsts& pc) {
+  if constexpr (kMad) return a * pc.one + b;
+  else return a + b;
+}
+
+// rotl(x1, R) ^ x0
+template <int R, bool kWideRot>
+__device__ __forceinline__ uint32_t rotxor(uint32_t x1, uint32_t x0, const PipeConsts& pc) {
+  if constexpr (kWideRot) {
+    const uint64_t t = (uint64_t)x1 * pc.pow2[R];
+    return ((uint32_t)t | (uint32_t)(t >> 32)) ^ x0;
+  } else {
+    return __funnelshift_l(x1, x1, R) ^ x0;
+  }
+}
+
+template <class Mix, int J, int R, int N>
+__device__ __forceinline__ void round_n(uint32_t (&x0)[N], uint32_t (&x1)[N], const PipeConsts& pc) {
 #pragma unroll
-  for (int j = 0; j < N; ++j) { x0[j] += a; x1[j] += b; }
+  for (int j = 0; j < N; ++j) {
+    x0[j] = add32<((Mix::madd >> J) & 1u) != 0>(x0[j], x1[j], pc);
+    x1[j] = rotxor<R, ((Mix::wide >> J) & 1u) != 0>(x1[j], x0[j], pc);
+  }
+}
+
+// Four rounds of one step over N blocks, round-major so the N chains interleave.
+template <class Mix, int N, int R0, int R1, int R2, int R3>
+__device__ __forceinline__ void four_rounds(uint32_t (&x0)[N], uint32_t (&x1)[N],
+                                            const PipeConsts& pc) {
+  round_n<Mix, 0, R0>(x0, x1, pc);
+  round_n<Mix, 1, R1>(x0, x1, pc);
+  round_n<Mix, 2, R2>(x0, x1, pc);
+  round_n<Mix, 3, R3>(x0, x1, pc);
+}
+
+template <class Mix, int N>
+__device__ __forceinline__ void inject(uint32_t (&x0)[N], uint32_t (&x1)[N], uint32_t a,
+                                       uint32_t b, const PipeConsts& pc) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) {
+    x0[j] = add32<Mix::madd_inject>(x0[j], a, pc);
+    x1[j] = add32<Mix::madd_inject>(x1[j], b, pc);
+  }
 }
 
 // N blocks in place: on entry x0/x1 hold the counters (c0, c1), on exit the cipher words.
+template <int N, class Mix = DefaultMix>
+__device__ __forceinline__ void threefry20(const KeySchedule& s, uint32_t (&x0)[N],
+                                           uint32_t (&x1)[N], const PipeConsts& pc) {
+  inject<Mix, N>(x0, x1, s.k0, s.k1, pc);
+  four_rounds<Mix, N, 13, 15, 26, 6>(x0, x1, pc);
+  inject<Mix, N>(x0, x1, s.a[0], s.b[0], pc);
+  four_rounds<Mix, N, 17, 29, 16, 24>(x0, x1, pc);
+  inject<Mix, N>(x0, x1, s.a[1], s.b[1], pc);
+  four_rounds<Mix, N, 13, 15, 26, 6>(x0, x1, pc);
+  inject<Mix, N>(x0, x1, s.a[2], s.b[2], pc);
+  four_rounds<Mix, N, 17, 29, 16, 24>(x0, x1, pc);
+  inject<Mix, N>(x0, x1, s.a[3], s.b[3], pc);
+  four_rounds<Mix, N, 13, 15, 26, 6>(x0, x1, pc);
+  inject<Mix, N>(x0, x1, s.a[4], s.b[4], pc);
+}
+
+// Plain form for code with no PipeConsts at hand (small kernels): DefaultMix only uses
+// funnel shifts and adds, so the constants are never read.
 template <int N>
 __device__ __forceinline__ void threefry20(const KeySchedule& s, uint32_t (&x0)[N],
                                            uint32_t (&x1)[N]) {
-  inject<N>(x0, x1, s.k0, s.k1);
-  four_rounds<N, 13, 15, 26, 6>(x0, x1);
-  inject<N>(x0, x1, s.a[0], s.b[0]);
-  four_rounds<N, 17, 29, 16, 24>(x0, x1);
-  inject<N>(x0, x1, s.a[1], s.b[1]);
-  four_rounds<N, 13, 15, 26, 6>(x0, x1);
-  inject<N>(x0, x1, s.a[2], s.b[2]);
-  four_rounds<N, 17, 29, 16, 24>(x0, x1);
-  inject<N>(x0, x1, s.a[3], s.b[3]);
-  four_rounds<N, 13, 15, 26, 6>(x0, x1);
-  inject<N>(x0, x1, s.a[4], s.b[4]);
+  PipeConsts unused;
+  threefry20<N, DefaultMix>(s, x0, x1, unused);
 }
 
 }  // namespace jxr
