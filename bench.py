@@ -174,6 +174,112 @@ def probe_peak(torch, nat, dev, iters=2000):
     return best
 
 
+# ---- the other BASELINE workloads (N = 1; not the driver's line) ---------------------------------
+
+WORKLOADS = {
+    "c1": "random_bits(random_key(0L), shape=(2^20,)) uint32, partitionable, x32",
+    "c2": "random_normal(random_key(42L), shape=(8192, 8192)) float32, partitionable",
+    "c2o": "random_normal(random_key(42L), shape=(8192, 8192)) float32, original layout",
+    "c3": "vmap(function(k) random_uniform(k, 1024, minval=-2, maxval=3))(random_split(random_key(7L), 65536)) float32",
+    "c5": "x64: random_normal(random_fold_in(random_key(2024L), 17L), (16384, 16384)) float64 and "
+          "random_bernoulli(same key, 0.3, same shape), one fused pass",
+}
+
+
+def run_workload(args):
+    """One JSON line for a secondary workload: device time per call of the public API,
+    32-bit words of output per second, and the cipher-block rate against the probe."""
+    import torch
+
+    import jaxr_b200 as jr
+    from jaxr_b200 import _native as nat
+    from jaxr_b200 import build as jb
+    jb.build()
+    nat.lib()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    c = args.config
+    flags = {"x64": c == "c5", "part": c != "c2o"}
+    old = (jr.enable_x64(flags["x64"]), jr.jax_config_update("jax_threefry_partitionable", flags["part"]))
+    if c == "c1":
+        key = jr.random_key(0)
+        step = lambda: jr.random_bits(key, (1 << 20,))
+        words, blocks, out_bytes, dt = 1 << 20, 1 << 20, 4 << 20, "u32"
+    elif c in ("c2", "c2o"):
+        key = jr.random_key(42)
+        step = lambda: jr.random_normal(key, (8192, 8192))
+        words, out_bytes, dt = 1 << 26, 4 << 26, "f32"
+        blocks = words if c == "c2" else words // 2
+    elif c == "c3":
+        keys = jr.random_split(jr.random_key(7), 65536)
+        f = jr.vmap(lambda k: jr.random_uniform(k, (1024,), minval=-2, maxval=3))
+        step = lambda: f(keys)
+        words, blocks, out_bytes, dt = 1 << 26, 1 << 26, 4 << 26, "f32"
+    elif c == "c5":
+        key = jr.random_fold_in(jr.random_key(2024), 17)
+        step = lambda: jr.random_normal_bernoulli(key, 0.3, (16384, 16384))
+        words, blocks, out_bytes, dt = 1 << 29, 1 << 28, 9 << 28, "f64"
+    else:
+        raise SystemExit(f"unknown config {c}")
+    small = out_bytes < (1 << 30)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if small else None
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(0)
+    sampler.start()
+    time.sleep(0.25)
+    total = 0.0
+    if small:  # outputs fit in L2: flush it before every timed call
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = step()
+            e1.record()
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+            del r
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        e1.synchronize()
+        total = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    ms = total / args.steps
+    peak_blocks = probe_peak(torch, nat, dev)
+    hbm_peak = None
+    try:
+        hbm_peak = json.load(open(PEAKS))["hbm_gbs"]
+    except (OSError, ValueError, KeyError):
+        pass
+    bps = blocks / (ms * 1e-3)
+    line = {
+        "metric": "threefry 32-bit words/s (device-timed), secondary workload", "value": words / (ms * 1e-3),
+        "unit": "words/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": None, "vs_baseline": None,
+        "dtype": dt, "data": "synthetic (seeds only)",
+        "config": {"workload": WORKLOADS[c], "name": c, "output_bytes": out_bytes,
+                   "cipher_blocks": blocks,
+                   "l2": "flushed (256 MiB write) before every timed call" if small else
+                         "outputs larger than L2"},
+        "roofline": {"bound": "int", "unit": "Tops/s", "achieved": bps * OPS_PER_BLOCK / 1e12,
+                     "peak": peak_blocks * OPS_PER_BLOCK / 1e12, "frac": bps / peak_blocks,
+                     "ops_per_block": OPS_PER_BLOCK,
+                     "hbm": {"achieved": out_bytes / (ms * 1e-3) / 1e9, "peak": hbm_peak,
+                             "unit": "GB/s",
+                             "frac": out_bytes / (ms * 1e-3) / 1e9 / hbm_peak if hbm_peak else None}},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+    jr.enable_x64(old[0])
+    jr.jax_config_update("jax_threefry_partitionable", old[1])
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -313,6 +419,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c4",
+                    help="c4 = the 2^34-word bits request (the benchmark); c1, c2, c2o, c3, c5 = "
+                         "the other workloads, one GPU, one JSON line each; 'all' = every one")
+    ap.add_argument("--words-log2", type=int, default=34,
+                    help="request size 2^k words (34 = the benchmark; smaller only for profiling)")
     ap.add_argument("--e2e-words", type=int, default=1 << 30)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
@@ -321,8 +432,18 @@ def main():
     if args.warmup < 3:
         log("note: warmup raised to 3")
         args.warmup = 3
+    global TOTAL
+    TOTAL = 1 << args.words_log2
     if args.impl == "reference":
         return run_reference(args)
+    if args.config == "all":
+        rc = 0
+        for c in ("c1", "c2", "c2o", "c3", "c5"):
+            args.config = c
+            rc |= run_workload(args)
+        return rc
+    if args.config != "c4":
+        return run_workload(args)
     return run_ours(args)
 
 

@@ -28,7 +28,7 @@ constexpr int kThreads = 256;
 
 // The pipe mix the bulk kernels use: round adds as multiply-adds on the FMA pipe,
 // rotations and xors on the ALU pipe (the fastest mix measured on B200).
-using ProductMix = MixPolicy<0u, 0xFu, false>;
+using ProductMix = MixPolicy<0u, 0xFFFFFu, false>;
 
 enum { kCtrIndex = 0, kCtrPair = 1 };
 
@@ -74,6 +74,12 @@ __host__ __device__ constexpr int groups_for() {
   // blocks in flight per thread: G groups of 16 / sizeof(Out) outputs (16 blocks for 4-byte
   // outputs: 40 registers, 6 CTAs per SM, measured fastest on B200)
   return sizeof(Out) >= 4 ? 4 : (sizeof(Out) == 2 ? 2 : 1);
+}
+
+// groups per thread in the key-batched kernel, which holds one key schedule per group
+template <class Out>
+__host__ __device__ constexpr int groups_nkey() {
+  return sizeof(Out) >= 8 ? 4 : (sizeof(Out) == 4 ? 2 : 1);
 }
 
 __host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
@@ -158,7 +164,7 @@ __global__ void __launch_bounds__(kThreads)
                   PipeConsts pc, typename Op::Out* __restrict__ out) {
   using Out = typename Op::Out;
   constexpr int V = 16 / sizeof(Out);
-  constexpr int G = groups_for<Out>();
+  constexpr int G = groups_nkey<Out>();
   const uint64_t stride = (uint64_t)gridDim.x * (kThreads * G);
   for (uint64_t base = (uint64_t)blockIdx.x * (kThreads * G); base < nchunks; base += stride) {
     uint64_t row[G], pos[G];

@@ -147,7 +147,8 @@ int launch_blocks(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t b
     if (cpr > ~0ull / (uint64_t)nkeys) return fail(JXR_ERR_INVALID_ARGUMENT, "request too large");
     const uint64_t nchunks = cpr * (uint64_t)nkeys;
     const int vec_ok = ((uintptr_t)out % 16 == 0) && (count * sizeof(Out)) % 16 == 0;
-    const uint64_t ctas = (nchunks + kThreads * G - 1) / (kThreads * G);
+    constexpr int GN = groups_nkey<Out>();
+    const uint64_t ctas = (nchunks + kThreads * GN - 1) / (kThreads * GN);
     auto k = k_blocks_nkey<Op, kCtr>;
     if ((rc = resident_grid(k, ctas, &grid))) return rc;
     k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, kPipe,

@@ -17,7 +17,7 @@
 // multiply-add by a 1 the compiler cannot see (a kernel parameter), and a rotation as a
 // 32x32->64-bit multiply by 2^r whose two halves, or-ed, are the rotated word; the xor
 // that follows the rotation then takes the or for free in one three-input logic op.
-// MixPolicy selects, per round of a step, which rotations and adds take the FMA pipe.
+// MixPolicy selects, per round, which rotations and adds take the FMA pipe.
 #pragma once
 
 #include <cstdint>
@@ -54,13 +54,16 @@ inline PipeConsts make_pipe_consts() {
   return c;
 }
 
-// kWide: bit j set = round j of every step rotates with a wide multiply (FMA pipe).
-// kMadd: bit j set = the x0 += x1 of round j is a multiply-add (FMA pipe).
+// Per-round choices, bit q (q = 4 * step + round, 0..19) of each mask:
+//   kWide  rotation as one 32x32->64 multiply (both halves from one instruction)
+//   kPair  rotation as a low and a high 32-bit multiply (two instructions)
+//   kMadd  the x0 += x1 of the round as a multiply-add
 // kMaddInject: the key injections are multiply-adds.
-template <unsigned kWide, unsigned kMadd, bool kMaddInject>
+template <unsigned kWide, unsigned kMadd, bool kMaddInject, unsigned kPair = 0u>
 struct MixPolicy {
   static constexpr unsigned wide = kWide;
   static constexpr unsigned madd = kMadd;
+  static constexpr unsigned pair = kPair;
   static constexpr bool madd_inject = kMaddInject;
 };
 
@@ -73,34 +76,37 @@ __device__ __forceinline__ uint32_t add32(uint32_t a, uint32_t b, const PipeCons
   else return a + b;
 }
 
-// rotl(x1, R) ^ x0
-template <int R, bool kWideRot>
+// rotl(x1, R) ^ x0; kHow 0: funnel shift, 1: one wide multiply, 2: low and high multiplies
+template <int R, int kHow>
 __device__ __forceinline__ uint32_t rotxor(uint32_t x1, uint32_t x0, const PipeConsts& pc) {
-  if constexpr (kWideRot) {
+  if constexpr (kHow == 1) {
     const uint64_t t = (uint64_t)x1 * pc.pow2[R];
     return ((uint32_t)t | (uint32_t)(t >> 32)) ^ x0;
+  } else if constexpr (kHow == 2) {
+    return ((x1 * pc.pow2[R]) | __umulhi(x1, pc.pow2[R])) ^ x0;
   } else {
     return __funnelshift_l(x1, x1, R) ^ x0;
   }
 }
 
-template <class Mix, int J, int R, int N>
+template <class Mix, int Q, int R, int N>
 __device__ __forceinline__ void round_n(uint32_t (&x0)[N], uint32_t (&x1)[N], const PipeConsts& pc) {
+  constexpr int how = ((Mix::wide >> Q) & 1u) ? 1 : (((Mix::pair >> Q) & 1u) ? 2 : 0);
 #pragma unroll
   for (int j = 0; j < N; ++j) {
-    x0[j] = add32<((Mix::madd >> J) & 1u) != 0>(x0[j], x1[j], pc);
-    x1[j] = rotxor<R, ((Mix::wide >> J) & 1u) != 0>(x1[j], x0[j], pc);
+    x0[j] = add32<((Mix::madd >> Q) & 1u) != 0>(x0[j], x1[j], pc);
+    x1[j] = rotxor<R, how>(x1[j], x0[j], pc);
   }
 }
 
-// Four rounds of one step over N blocks, round-major so the N chains interleave.
-template <class Mix, int N, int R0, int R1, int R2, int R3>
+// Four rounds of step S over N blocks, round-major so the N chains interleave.
+template <class Mix, int N, int S, int R0, int R1, int R2, int R3>
 __device__ __forceinline__ void four_rounds(uint32_t (&x0)[N], uint32_t (&x1)[N],
                                             const PipeConsts& pc) {
-  round_n<Mix, 0, R0>(x0, x1, pc);
-  round_n<Mix, 1, R1>(x0, x1, pc);
-  round_n<Mix, 2, R2>(x0, x1, pc);
-  round_n<Mix, 3, R3>(x0, x1, pc);
+  round_n<Mix, 4 * S + 0, R0>(x0, x1, pc);
+  round_n<Mix, 4 * S + 1, R1>(x0, x1, pc);
+  round_n<Mix, 4 * S + 2, R2>(x0, x1, pc);
+  round_n<Mix, 4 * S + 3, R3>(x0, x1, pc);
 }
 
 template <class Mix, int N>
@@ -118,15 +124,15 @@ template <int N, class Mix = DefaultMix>
 __device__ __forceinline__ void threefry20(const KeySchedule& s, uint32_t (&x0)[N],
                                            uint32_t (&x1)[N], const PipeConsts& pc) {
   inject<Mix, N>(x0, x1, s.k0, s.k1, pc);
-  four_rounds<Mix, N, 13, 15, 26, 6>(x0, x1, pc);
+  four_rounds<Mix, N, 0, 13, 15, 26, 6>(x0, x1, pc);
   inject<Mix, N>(x0, x1, s.a[0], s.b[0], pc);
-  four_rounds<Mix, N, 17, 29, 16, 24>(x0, x1, pc);
+  four_rounds<Mix, N, 1, 17, 29, 16, 24>(x0, x1, pc);
   inject<Mix, N>(x0, x1, s.a[1], s.b[1], pc);
-  four_rounds<Mix, N, 13, 15, 26, 6>(x0, x1, pc);
+  four_rounds<Mix, N, 2, 13, 15, 26, 6>(x0, x1, pc);
   inject<Mix, N>(x0, x1, s.a[2], s.b[2], pc);
-  four_rounds<Mix, N, 17, 29, 16, 24>(x0, x1, pc);
+  four_rounds<Mix, N, 3, 17, 29, 16, 24>(x0, x1, pc);
   inject<Mix, N>(x0, x1, s.a[3], s.b[3], pc);
-  four_rounds<Mix, N, 13, 15, 26, 6>(x0, x1, pc);
+  four_rounds<Mix, N, 4, 13, 15, 26, 6>(x0, x1, pc);
   inject<Mix, N>(x0, x1, s.a[4], s.b[4], pc);
 }
 

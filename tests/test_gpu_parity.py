@@ -39,6 +39,24 @@ def take(t, idx):
     return to_np(flat[ti])
 
 
+def _as_float(a, dt):
+    if dt == "bfloat16":
+        return (a.astype(np.uint32) << 16).view(np.float32)
+    if dt == "float16":
+        return a.view(np.float16)
+    return a
+
+
+def same_bits(got, want, dt):
+    """Bitwise equality, NaN payloads aside (any NaN equals any NaN)."""
+    gv, wv = _as_float(got, dt), _as_float(want, dt)
+    gn, wn = np.isnan(gv), np.isnan(wv)
+    if not np.array_equal(gn, wn):
+        return False
+    ub = f"u{got.itemsize}"
+    return np.array_equal(got[~gn].view(ub), want[~wn].view(ub))
+
+
 @pytest.fixture(scope="module", autouse=True)
 def _gpu():
     if not torch.cuda.is_available():
@@ -185,7 +203,7 @@ def test_uniform_exact(oracle, part, dt):
             got = out.detach().cpu().view(torch.uint16).numpy() if dt in ("float16", "bfloat16") \
                 else to_np(out)
             want = oracle.uniform(key, dt, n, part, mn, mx)
-            assert np.array_equal(got.view(f"u{got.itemsize}"), want.view(f"u{want.itemsize}")), (mn, mx, n)
+            assert same_bits(got, want, dt), (mn, mx, n)
 
 
 def test_uniform_unfused_flag(oracle):
@@ -347,3 +365,34 @@ def test_config5_x64_normal_bernoulli(oracle):
     assert np.array_equal(gb, wb)
     frac = ber.float().mean().item()
     assert abs(frac - 0.3) < 1e-3
+
+
+# ---- bits into host memory (the host-buffer entry point) -----------------------------------------
+
+def test_random_bits_to_host(oracle):
+    from jaxr_b200.shard import random_bits_to_host
+    k = jr.random_key(123)
+    n = (1 << 26) + 12345  # several 64 MiB chunks and a ragged tail
+    h = torch.empty(n, dtype=torch.uint32, pin_memory=True)
+    for _ in range(2):  # two calls in a row reuse the staging buffers
+        out = random_bits_to_host(k, (n,), out=h)
+        assert out.device.type == "cpu"
+        idx = _sample_idx(n)
+        assert np.array_equal(out.numpy()[idx], oracle.bits_at(oracle.seed(123), 32, n, True, idx))
+    whole = jr.random_bits(k, (n,))
+    assert torch.equal(out.view(torch.int32), whole.cpu().view(torch.int32))
+
+
+@pytest.mark.parametrize("part", [True, False], ids=["partitionable", "original"])
+@pytest.mark.parametrize("bw", [8, 16, 32, 64])
+def test_bits_host_abi_all_widths(oracle, part, bw):
+    import ctypes
+    from jaxr_b200 import _native as nat
+    keys = np.array([[0, 7], [3, 4], [0xFFFFFFFF, 1]], dtype=np.uint32)
+    size, begin, count = 300001, 17, 299000
+    npdt = {8: np.uint8, 16: np.uint16, 32: np.uint32, 64: np.uint64}[bw]
+    out = np.zeros((3, count), dtype=npdt)
+    nat.call("jxr_random_bits_host", keys.ctypes.data_as(ctypes.c_void_p), 3, size, begin, count,
+             int(part), bw, out.ctypes.data_as(ctypes.c_void_p))
+    for r in range(3):
+        assert np.array_equal(out[r], oracle.random_bits(keys[r], bw, size, part, begin, count))
