@@ -170,6 +170,29 @@ int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size
 int jxr_probe_cipher(uint64_t iters, int ctas_per_sm, uint32_t* sink, uint64_t* blocks_out,
                      void* stream);
 
+/* random_bits into HOST memory without allocating anything.  Some callers cannot
+ * allocate device memory while they run: a host framework that has reserved (nearly)
+ * all of the GPU for its own memory pool, as XLA's PJRT client does when it runs an FFI
+ * handler, where a cudaMalloc fails or stalls the device behind the framework's back.
+ * This variant of jxr_random_bits_host uses no cudaMalloc, cudaFree or any other
+ * allocating call: its device scratch is one array of fixed size compiled into the
+ * library (4096 keys + a 16 MiB staging buffer, 16 MiB + 32 KiB in all), held on every
+ * GPU that loads the library until the process exits.  It has no counterpart in the
+ * reference.
+ *  - nkeys may be at most 4096; larger batches are rejected with
+ *    JXR_ERR_INVALID_ARGUMENT.  count is produced in 16 MiB chunks, any length.
+ *  - Work is ordered on `stream` (NULL = legacy default stream) and the call returns
+ *    when host_out holds the result.  The first call on a device looks up the array's
+ *    device address (cudaGetSymbolAddress); make that first call before any stream
+ *    capture on that device.
+ *  - Every call on a device shares the one array, which keeps the last call's contents
+ *    (nothing in it needs to start at zero: keys and staging are rewritten before they
+ *    are read).  Calls that overlap on the GPU -- e.g. from two host threads at once on
+ *    the same device -- race on it: serialise them. */
+int jxr_random_bits_host_static(const uint32_t* keys_host, int64_t nkeys, uint64_t size,
+                                uint64_t begin, uint64_t count, int layout, int bit_width,
+                                void* host_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -583,6 +583,36 @@ __global__ void __launch_bounds__(kThreads) k_probe_cipher(uint64_t iters, uint3
 
 using namespace jxr;
 
+// ---- fixed device scratch for jxr_random_bits_host_static -----------------------------------
+
+// Some callers cannot allocate device memory while they run, so jxr_random_bits_host_static
+// works entirely in this statically sized array: the first kStaticKeyBytes hold the keys,
+// the rest is the staging buffer that each chunk is generated into before it is copied to
+// the host.  Every GPU that loads the library holds the array until the process exits.
+constexpr int64_t kStaticMaxKeys = 4096;
+constexpr size_t kStaticKeyBytes = 8 * (size_t)kStaticMaxKeys;  // 32 KiB
+constexpr size_t kStaticStageBytes = 16ull << 20;                // 16 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticKeyBytes + kStaticStageBytes];
+
+// Device address of g_static_scratch per device, looked up once with that device current
+// (the name is only a host-side stand-in for the array; host code must not pass it).
+static void* g_static_scratch_addr[64] = {};
+static std::mutex g_static_scratch_mu;
+
+static int static_scratch(int dev, unsigned char** out) {
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(JXR_ERR_CUDA, "cudaGetSymbolAddress(g_static_scratch): %s", cudaGetErrorString(e));
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = (unsigned char*)g_static_scratch_addr[dev];
+  return JXR_OK;
+}
+
+
 extern "C" {
 
 int jxr_abi_version(void) { return JXR_ABI_VERSION; }
@@ -931,6 +961,46 @@ int jxr_probe_cipher(uint64_t iters, int ctas_per_sm, uint32_t* sink, uint64_t* 
   k_probe_cipher<<<grid, kThreads, 0, (cudaStream_t)stream>>>(iters, sink, kPipe);
   JXR_CUDA(cudaGetLastError());
   *blocks_out = (uint64_t)grid * kThreads * 8ull * iters;
+  return JXR_OK;
+}
+
+int jxr_random_bits_host_static(const uint32_t* keys_host, int64_t nkeys, uint64_t size,
+                                uint64_t begin, uint64_t count, int layout, int bit_width,
+                                void* host_out, void* stream) {
+  int rc = check_request(keys_host, nkeys, size, begin, count, layout, host_out);
+  if (rc) return rc;
+  if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "requires 8-, 16-, 32- or 64-bit field width, got %d", bit_width);
+  if (nkeys > kStaticMaxKeys)
+    return fail(JXR_ERR_INVALID_ARGUMENT,
+                "jxr_random_bits_host_static takes at most %lld keys per call (its fixed device "
+                "scratch holds %lld), got %lld; split the batch or use jxr_random_bits_host",
+                (long long)kStaticMaxKeys, (long long)kStaticMaxKeys, (long long)nkeys);
+  if (!count || !nkeys) return JXR_OK;
+  int dev = 0;
+  JXR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(JXR_ERR_NO_DEVICE, "device index %d out of range", dev);
+  unsigned char* scratch = nullptr;
+  if ((rc = static_scratch(dev, &scratch))) return rc;
+  uint32_t* dkeys = (uint32_t*)scratch;
+  void* stage = scratch + kStaticKeyBytes;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t esz = (size_t)bit_width / 8;
+  const uint64_t chunk = kStaticStageBytes / esz;
+  // Everything is ordered on the caller's stream: the staging buffer is regenerated only
+  // after the copy of the previous chunk out of it has run.
+  JXR_CUDA(cudaMemcpyAsync(dkeys, keys_host, 8 * (size_t)nkeys, cudaMemcpyHostToDevice, st));
+  for (int64_t r = 0; r < nkeys; ++r) {
+    for (uint64_t off = 0; off < count; off += chunk) {
+      const uint64_t n = std::min(chunk, count - off);
+      if ((rc = jxr_random_bits(dkeys + 2 * r, 1, size, begin + off, n, layout, bit_width, stage,
+                                stream)))
+        return rc;
+      char* dst = (char*)host_out + ((uint64_t)r * count + off) * esz;
+      JXR_CUDA(cudaMemcpyAsync(dst, stage, n * esz, cudaMemcpyDeviceToHost, st));
+    }
+  }
+  JXR_CUDA(cudaStreamSynchronize(st));
   return JXR_OK;
 }
 
