@@ -76,12 +76,6 @@ __host__ __device__ constexpr int groups_for() {
   return sizeof(Out) >= 4 ? 4 : (sizeof(Out) == 2 ? 2 : 1);
 }
 
-// groups per thread in the key-batched kernel, which holds one key schedule per group
-template <class Out>
-__host__ __device__ constexpr int groups_nkey() {
-  return sizeof(Out) >= 8 ? 4 : (sizeof(Out) == 4 ? 2 : 1);
-}
-
 __host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
 
 // ---- single key ---------------------------------------------------------------------------
@@ -157,55 +151,85 @@ __global__ void __launch_bounds__(kThreads)
 
 // ---- key batches (vmap): rows of `count` outputs, one key per row ---------------------------
 
-template <class Op, int kCtr, class Mix = ProductMix>
+// A warp owns tiles of WT = 32 * G * V consecutive outputs of one row, so the key schedule
+// and the counters are per-warp values (as the single-key kernel's are per-CTA values);
+// row and column advance by a fixed stride per iteration, with one division per thread at
+// the start instead of one per tile.
+template <class Op, int kCtr, class Mix = ProductMix, int G = groups_for<typename Op::Out>()>
 __global__ void __launch_bounds__(kThreads)
     k_blocks_nkey(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
-                  uint64_t count, uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, Op op,
+                  uint64_t count, uint64_t tiles_per_row, uint64_t ntiles, int vec_ok, Op op,
                   PipeConsts pc, typename Op::Out* __restrict__ out) {
   using Out = typename Op::Out;
   constexpr int V = 16 / sizeof(Out);
-  constexpr int G = groups_nkey<Out>();
-  const uint64_t stride = (uint64_t)gridDim.x * (kThreads * G);
-  for (uint64_t base = (uint64_t)blockIdx.x * (kThreads * G); base < nchunks; base += stride) {
-    uint64_t row[G], pos[G];
-    KeySchedule s[G];
-    uint32_t x0[G][V], x1[G][V];
+  constexpr int N = G * V;
+  constexpr uint32_t WT = 32u * G * V;
+  const uint32_t lane = threadIdx.x & 31u, loff = lane * V;
+  const uint64_t w0 = ((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const uint64_t nw = ((uint64_t)gridDim.x * kThreads) >> 5;
+  if (w0 >= ntiles) return;
+  uint64_t row = w0 / tiles_per_row, col = w0 - row * tiles_per_row;
+  const uint64_t drow = nw / tiles_per_row, dcol = nw - drow * tiles_per_row;
+  for (uint64_t w = w0; w < ntiles; w += nw) {
+    const KeySchedule s = make_schedule(__ldg(keys + 2 * row), __ldg(keys + 2 * row + 1));
+    const uint64_t p0 = col * WT;     // first output of the tile within its row
+    const uint64_t e0 = begin + p0;   // its element index in the request
+    uint32_t x0[N], x1[N];
+    if (kCtr == kCtrIndex) {
+      const uint32_t lo = (uint32_t)e0;
+      if (lo <= 0xFFFFFFFFu - WT) {
+        const uint32_t hi = (uint32_t)(e0 >> 32), base = lo + loff;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
-      const uint64_t cc = c < nchunks ? c : nchunks - 1;
-      row[g] = cc / chunks_per_row;
-      pos[g] = (cc - row[g] * chunks_per_row) * V;
-      s[g] = make_schedule(__ldg(keys + 2 * row[g]), __ldg(keys + 2 * row[g] + 1));
+        for (int g = 0; g < G; ++g)
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const uint64_t i = begin + pos[g] + v;  // element index within the request
-        if (kCtr == kCtrIndex) {
-          x0[g][v] = (uint32_t)(i >> 32);
-          x1[g][v] = (uint32_t)i;
-        } else {
-          x0[g][v] = (uint32_t)i;
-          x1[g][v] = (uint32_t)(size + i);
-        }
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) threefry20<V, Mix>(s[g], x0[g], x1[g], pc);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const uint64_t c = base + (uint64_t)g * kThreads + threadIdx.x;
-      if (c >= nchunks) continue;
-      Vec16<Out> r;
-#pragma unroll
-      for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g][v], x1[g][v]);
-      Out* dst = out + row[g] * count + pos[g];
-      if (vec_ok && pos[g] + V <= count) {
-        *reinterpret_cast<uint4*>(dst) = r.u;
+          for (int v = 0; v < V; ++v) {
+            x0[g * V + v] = hi;
+            x1[g * V + v] = base + (uint32_t)(g * 32 * V + v);
+          }
       } else {
 #pragma unroll
-        for (int v = 0; v < V; ++v)
-          if (pos[g] + v < count) dst[v] = r.v[v];
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            const uint64_t i = e0 + loff + (uint32_t)(g * 32 * V + v);
+            x0[g * V + v] = (uint32_t)(i >> 32);
+            x1[g * V + v] = (uint32_t)i;
+          }
       }
+    } else {
+      const uint32_t a = (uint32_t)e0 + loff, b = (uint32_t)(size + e0) + loff;
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          x0[g * V + v] = a + (uint32_t)(g * 32 * V + v);
+          x1[g * V + v] = b + (uint32_t)(g * 32 * V + v);
+        }
+    }
+    threefry20<N, Mix>(s, x0, x1, pc);
+    Out* orow = out + row * count;
+    if (vec_ok && p0 + WT <= count) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        Vec16<Out> r;
+#pragma unroll
+        for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g * V + v], x1[g * V + v]);
+        *reinterpret_cast<uint4*>(orow + p0 + loff + g * 32 * V) = r.u;
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const uint64_t p = p0 + loff + (uint64_t)g * 32 * V;
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (p + v < count) orow[p + v] = apply(op, x0[g * V + v], x1[g * V + v]);
+      }
+    }
+    col += dcol;
+    row += drow;
+    if (col >= tiles_per_row) {
+      col -= tiles_per_row;
+      ++row;
     }
   }
 }

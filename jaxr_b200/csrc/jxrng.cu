@@ -143,15 +143,15 @@ int launch_blocks(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t b
     if ((rc = resident_grid(k, ntiles, &grid))) return rc;
     k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, vec_ok, op, kPipe, (Out*)out);
   } else {
-    const uint64_t cpr = (count + V - 1) / V;
-    if (cpr > ~0ull / (uint64_t)nkeys) return fail(JXR_ERR_INVALID_ARGUMENT, "request too large");
-    const uint64_t nchunks = cpr * (uint64_t)nkeys;
+    constexpr uint64_t WT = 32ull * G * V;
+    const uint64_t tpr = (count + WT - 1) / WT;
+    if (tpr > ~0ull / (uint64_t)nkeys) return fail(JXR_ERR_INVALID_ARGUMENT, "request too large");
+    const uint64_t ntiles = tpr * (uint64_t)nkeys;
     const int vec_ok = ((uintptr_t)out % 16 == 0) && (count * sizeof(Out)) % 16 == 0;
-    constexpr int GN = groups_nkey<Out>();
-    const uint64_t ctas = (nchunks + kThreads * GN - 1) / (kThreads * GN);
+    const uint64_t ctas = (ntiles + kThreads / 32 - 1) / (kThreads / 32);
     auto k = k_blocks_nkey<Op, kCtr>;
     if ((rc = resident_grid(k, ctas, &grid))) return rc;
-    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, cpr, nchunks, vec_ok, op, kPipe,
+    k<<<grid, kThreads, 0, st>>>(keys, size, begin, count, tpr, ntiles, vec_ok, op, kPipe,
                                  (Out*)out);
   }
   JXR_CUDA(cudaGetLastError());
