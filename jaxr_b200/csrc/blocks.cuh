@@ -18,6 +18,7 @@
 #pragma once
 
 #include <cstdint>
+#include <type_traits>
 
 #include "samplers.cuh"
 #include "threefry.cuh"
@@ -76,11 +77,22 @@ __host__ __device__ constexpr int groups_for() {
   return sizeof(Out) >= 4 ? 4 : (sizeof(Out) == 2 ? 2 : 1);
 }
 
+// An op may set kGroups (e.g. transform-heavy samplers, which need registers for the
+// transform more than blocks in flight); otherwise groups_for<Out>.
+template <class Op, class = void>
+struct GroupsOf {
+  static constexpr int value = groups_for<typename Op::Out>();
+};
+template <class Op>
+struct GroupsOf<Op, std::void_t<decltype(Op::kGroups)>> {
+  static constexpr int value = Op::kGroups;
+};
+
 __host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
 
 // ---- single key ---------------------------------------------------------------------------
 
-template <class Op, int kCtr, class Mix = ProductMix, int G = groups_for<typename Op::Out>()>
+template <class Op, int kCtr, class Mix = ProductMix, int G = GroupsOf<Op>::value>
 __global__ void __launch_bounds__(kThreads)
     k_blocks_1key(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
                   uint64_t count, int vec_ok, Op op, PipeConsts pc,
@@ -155,7 +167,7 @@ __global__ void __launch_bounds__(kThreads)
 // and the counters are per-warp values (as the single-key kernel's are per-CTA values);
 // row and column advance by a fixed stride per iteration, with one division per thread at
 // the start instead of one per tile.
-template <class Op, int kCtr, class Mix = ProductMix, int G = groups_for<typename Op::Out>()>
+template <class Op, int kCtr, class Mix = ProductMix, int G = GroupsOf<Op>::value>
 __global__ void __launch_bounds__(kThreads)
     k_blocks_nkey(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
                   uint64_t count, uint64_t tiles_per_row, uint64_t ntiles, int vec_ok, Op op,

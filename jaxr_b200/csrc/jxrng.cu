@@ -133,7 +133,7 @@ int launch_blocks(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t b
                   uint64_t count, const Op& op, void* out, cudaStream_t st) {
   using Out = typename Op::Out;
   constexpr int V = 16 / sizeof(Out);
-  constexpr int G = groups_for<Out>();
+  constexpr int G = GroupsOf<Op>::value;
   if (count == 0 || nkeys == 0) return JXR_OK;
   int grid = 0, rc;
   if (nkeys == 1) {

@@ -13,8 +13,8 @@
 // reference's recorded samples show fused multiply-adds (the uniform's affine map,
 // test-random.R:43 and :160; the erf_inv Horner steps), __fmaf_rn/__fma_rn is used.
 // The float32 erf_inv takes log1p of the rounded float -(x*x) in double precision
-// and rounds it to float: the correctly rounded value, which reproduces every
-// float32 normal the reference recorded.
+// (log1p_neg) and rounds it to float, which reproduces every float32 normal the
+// reference recorded.
 #pragma once
 
 #include <cstdint>
@@ -29,11 +29,57 @@ __device__ __forceinline__ double xla_max(double a, double b) {
   return (a >= b || a != a) ? a : b;
 }
 
+// ---- log1p -----------------------------------------------------------------------------
+
+// log1p(y) for y <= 0 (and NaN), the argument erf_inv gives it (y = -x*x), branch-free.
+// Method of W. J. Cody and W. Waite, "Software Manual for the Elementary Functions"
+// (1980): t = 1 + y = 2^e m with m in [sqrt(1/2), sqrt(2)), log m = 2 atanh(s) =
+// 2 (s + s^3/3 + s^5/5 + ...) with s = (m - 1) / (m + 1), |s| < 0.1716, ten terms; the
+// rounding error of 1 + y is added back as (y - (t - 1)) / t.  Within 2 ulp of a
+// correctly rounded log1p.  The CPU oracle performs the same operations in the same
+// order, so both produce the same double.
+__device__ __forceinline__ double log1p_neg(double y) {
+  const double t = __dadd_rn(1.0, y);
+  const double corr =
+      __dmul_rn(__dsub_rn(y, __dsub_rn(t, 1.0)), (double)__frcp_rn(__double2float_rn(t)));
+  const unsigned long long b64 = (unsigned long long)__double_as_longlong(t);
+  const uint32_t hi = (uint32_t)(b64 >> 32), mh = hi & 0x000FFFFFu;
+  const bool big = mh >= 0x6A09Eu;  // mantissa >= sqrt(2): use m / 2
+  const int e = (int)((hi >> 20) & 0x7FFu) - 1023 + (big ? 1 : 0);
+  const double m = __longlong_as_double(
+      (long long)((((unsigned long long)(mh | ((big ? 1022u : 1023u) << 20))) << 32) |
+                  (b64 & 0xFFFFFFFFull)));
+  const double a = __dsub_rn(m, 1.0), b = __dadd_rn(m, 1.0);
+  double r = (double)__frcp_rn(__double2float_rn(b));  // 1 / b to float precision
+  r = __fma_rn(r, __fma_rn(-b, r, 1.0), r);            // and two Newton steps
+  const double s0 = __dmul_rn(a, r);
+  const double s = __fma_rn(r, __fma_rn(-b, s0, a), s0);
+  const double z = __dmul_rn(s, s);
+  double p = 0x1.8618618618618p-5;          // 1/21
+  p = __fma_rn(p, z, 0x1.af286bca1af28p-5);  // 1/19
+  p = __fma_rn(p, z, 0x1.e1e1e1e1e1e1ep-5);  // 1/17
+  p = __fma_rn(p, z, 0x1.1111111111111p-4);  // 1/15
+  p = __fma_rn(p, z, 0x1.3b13b13b13b14p-4);  // 1/13
+  p = __fma_rn(p, z, 0x1.745d1745d1746p-4);  // 1/11
+  p = __fma_rn(p, z, 0x1.c71c71c71c71cp-4);  // 1/9
+  p = __fma_rn(p, z, 0x1.2492492492492p-3);  // 1/7
+  p = __fma_rn(p, z, 0x1.999999999999ap-3);  // 1/5
+  p = __fma_rn(p, z, 0x1.5555555555555p-2);  // 1/3
+  const double s2 = __dadd_rn(s, s);
+  const double lm = __fma_rn(__dmul_rn(s2, z), p, s2);
+  const double LN2_HI = 0x1.62e42fefa3800p-1, LN2_LO = 0x1.ef35793c76730p-45;
+  const double de = (double)e;
+  double res = __fma_rn(de, LN2_HI, __fma_rn(de, LN2_LO, __dadd_rn(lm, corr)));
+  if (!(t > 0.0)) res = (t == 0.0) ? -__longlong_as_double(0x7FF0000000000000ll)
+                                   : __longlong_as_double(0x7FF8000000000000ll);
+  return res;
+}
+
 // ---- erf_inv --------------------------------------------------------------------------
 
 __device__ __forceinline__ float erfinv_f32(float x) {
   const float y = -__fmul_rn(x, x);
-  const float w0 = -__double2float_rn(log1p((double)y));
+  const float w0 = -__double2float_rn(log1p_neg((double)y));
   float p, w;
   if (w0 < 5.0f) {
     w = __fsub_rn(w0, 2.5f);
@@ -63,7 +109,7 @@ __device__ __forceinline__ float erfinv_f32(float x) {
 }
 
 __device__ __forceinline__ double erfinv_f64(double x) {
-  const double w0 = -log1p(-__dmul_rn(x, x));
+  const double w0 = -log1p_neg(-__dmul_rn(x, x));
   double p, w;
   if (w0 < 6.25) {
     w = __dsub_rn(w0, 3.125);
@@ -233,6 +279,7 @@ struct OpUniformH {
 // so u = 2 f + lo is exact and the fused and unfused forms agree.
 struct OpNormalF32 {
   static constexpr int kBits = 32;
+  static constexpr int kGroups = 1;  // 4 blocks per thread: the transform needs the registers
   using Bits = uint32_t;
   using Out = float;
   __device__ __forceinline__ Out operator()(Bits b) const {
@@ -244,6 +291,7 @@ struct OpNormalF32 {
 
 struct OpNormalF64 {
   static constexpr int kBits = 64;
+  static constexpr int kGroups = 2;
   using Bits = uint64_t;
   using Out = double;
   __device__ __forceinline__ Out operator()(Bits b) const {
@@ -257,6 +305,7 @@ struct OpNormalF64 {
 template <bool BF>
 struct OpNormalH {
   static constexpr int kBits = BF ? 8 : 16;
+  static constexpr int kGroups = 1;
   using Bits = typename UintOf<kBits>::T;
   using Out = uint16_t;
   __device__ __forceinline__ Out operator()(Bits b) const {

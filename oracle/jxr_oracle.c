@@ -266,6 +266,52 @@ static float f64_to_f32_odd(double x) {
  * for a single +, -, *). */
 static inline float rh(float f, int bf16) { return half_bits_to_f32(f32_to_half_bits(f, bf16), bf16); }
 
+/* ---- log1p ----------------------------------------------------------------------------- */
+
+static inline double bits_to_f64(uint64_t u) { double d; memcpy(&d, &u, 8); return d; }
+static inline uint64_t f64_to_bits(double d) { uint64_t u; memcpy(&u, &d, 8); return u; }
+
+/* log1p(y) for y <= 0 (and NaN), the argument erf_inv gives it (y = -x*x): the same
+ * operations as the kernels' log1p_neg, so both round identically.  Method of W. J. Cody
+ * and W. Waite, "Software Manual for the Elementary Functions" (1980): t = 1 + y =
+ * 2^e m with m in [sqrt(1/2), sqrt(2)), log m = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ...)
+ * with s = (m - 1) / (m + 1), |s| < 0.1716, ten terms; the rounding error of 1 + y is
+ * added back as (y - (t - 1)) / t.  Within 2 ulp of a correctly rounded log1p. */
+static double log1p_neg(double y) {
+  const double t = 1.0 + y;
+  const double corr = (y - (t - 1.0)) * (double)(1.0f / (float)t);
+  const uint64_t b64 = f64_to_bits(t);
+  const uint32_t hi = (uint32_t)(b64 >> 32), mh = hi & 0x000FFFFFu;
+  const int big = mh >= 0x6A09Eu; /* mantissa >= sqrt(2): use m / 2 */
+  const int e = (int)((hi >> 20) & 0x7FFu) - 1023 + big;
+  const double m =
+      bits_to_f64(((uint64_t)(mh | ((big ? 1022u : 1023u) << 20)) << 32) | (b64 & 0xFFFFFFFFull));
+  const double a = m - 1.0, b = m + 1.0;
+  double r = (double)(1.0f / (float)b); /* 1 / b to float precision, then two Newton steps */
+  r = fma(r, fma(-b, r, 1.0), r);
+  const double s0 = a * r;
+  const double s = fma(r, fma(-b, s0, a), s0);
+  const double z = s * s;
+  double p = 0x1.8618618618618p-5; /* 1/21 */
+  p = fma(p, z, 0x1.af286bca1af28p-5); /* 1/19 */
+  p = fma(p, z, 0x1.e1e1e1e1e1e1ep-5); /* 1/17 */
+  p = fma(p, z, 0x1.1111111111111p-4); /* 1/15 */
+  p = fma(p, z, 0x1.3b13b13b13b14p-4); /* 1/13 */
+  p = fma(p, z, 0x1.745d1745d1746p-4); /* 1/11 */
+  p = fma(p, z, 0x1.c71c71c71c71cp-4); /* 1/9 */
+  p = fma(p, z, 0x1.2492492492492p-3); /* 1/7 */
+  p = fma(p, z, 0x1.999999999999ap-3); /* 1/5 */
+  p = fma(p, z, 0x1.5555555555555p-2); /* 1/3 */
+  const double s2 = s + s;
+  const double lm = fma(s2 * z, p, s2);
+  const double LN2_HI = 0x1.62e42fefa3800p-1, LN2_LO = 0x1.ef35793c76730p-45;
+  double res = fma((double)e, LN2_HI, fma((double)e, LN2_LO, lm + corr));
+  if (!(t > 0.0)) res = (t == 0.0) ? -INFINITY : NAN;
+  return res;
+}
+
+double orc_log1p_neg(double y) { return log1p_neg(y); }
+
 /* ---- erf_inv --------------------------------------------------------------------------- */
 
 /* Giles (2011), single precision: two polynomials in w = -log(1 - x^2), split at w = 5. */
@@ -277,8 +323,8 @@ static const float GS_GE5[9] = {-0.000200214257f, 0.000100950558f, 0.00134934322
                                 0.00943887047f, 1.00167406f, 2.83297682f};
 
 float orc_erfinv_f32(float x, int fma) {
-  /* log1p of the rounded float -(x*x), correctly rounded to float (through double). */
-  const float w0 = -(float)log1p((double)(-(x * x)));
+  /* log1p of the rounded float -(x*x), evaluated in double and rounded once */
+  const float w0 = -(float)log1p_neg((double)(-(x * x)));
   const int lt = w0 < 5.0f;
   const float* c = lt ? GS_LT5 : GS_GE5;
   const float w = lt ? w0 - 2.5f : sqrtf(w0) - 3.0f;
@@ -315,7 +361,7 @@ static const double GD_GE16[17] = {
     1.0103004648645343977,      4.8499064014085844221};
 
 double orc_erfinv_f64(double x, int fma_) {
-  const double w0 = -log1p(-(x * x));
+  const double w0 = -log1p_neg(-(x * x));
   const double* c;
   int n;
   double w;

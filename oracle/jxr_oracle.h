@@ -58,10 +58,14 @@ int orc_random_bits(const uint32_t key[2], int bit_width, uint64_t size, int par
 /* erf_inv as lowered by the reference's default path: M. Giles, "Approximating
  * the erfinv function" (GPU Computing Gems Jade, 2011), with the logarithm
  * taken as -log1p(-x*x) and erf_inv(+-1) = +-inf (R/lax_special.R:1327-1331
- * emits chlo.erf_inv).  fma selects a fused Horner evaluation. */
+ * emits chlo.erf_inv).  fma selects a fused Horner evaluation.  The logarithm is
+ * log1p_neg below, evaluated in double (and, for float32, rounded once). */
 float orc_erfinv_f32(float x, int fma);
 double orc_erfinv_f64(double x, int fma);
 void orc_erfinv_arr(const void* x, int64_t n, int dtype, int fma, void* out);
+
+/* log1p(y) for y <= 0 as the kernels evaluate it (Cody and Waite reduction). */
+double orc_log1p_neg(double y);
 
 /* Samplers (R/random.R:288-304, :502-508, :656-666).  dtype is an ORC_ code;
  * 16-bit results are returned as their raw bits in a uint16_t array.

@@ -50,6 +50,8 @@ def lib():
         L.orc_erfinv_f64.argtypes = [dbl, i32]
         L.orc_erfinv_f64.restype = dbl
         L.orc_erfinv_arr.argtypes = [vp, i64, i32, i32, vp]
+        L.orc_log1p_neg.argtypes = [dbl]
+        L.orc_log1p_neg.restype = dbl
         L.orc_uniform.argtypes = [u32p, i32, u64, i32, dbl, dbl, i32, u64, u64, vp]
         L.orc_normal.argtypes = [u32p, i32, u64, i32, i32, u64, u64, vp]
         L.orc_bernoulli.argtypes = [u32p, i32, dbl, u64, i32, u64, u64, vp]
