@@ -369,6 +369,45 @@ def run_ours(args):
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
     }
 
+    # the whole request on rank 0 (timed separately from generation): rank r's kernel
+    # storing its slab straight into rank 0's HBM over NVLink, and, for comparison,
+    # generating slabs locally then assembling them with NCCL point-to-point
+    gather = None
+    if world > 1 and not args.no_gather:
+        from jaxr_b200.shard import close_peer_mappings, gather_to, random_bits_gathered
+
+        def timed(fn, reps=3):
+            fn()
+            best = None
+            for _ in range(reps):
+                barrier()
+                torch.cuda.synchronize()
+                g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                g0.record()
+                r = fn()
+                g1.record()
+                g1.synchronize()
+                del r
+                t = max_over_ranks(g0.elapsed_time(g1))
+                best = t if best is None else min(best, t)
+            return best
+
+        nccl_ms = timed(lambda: gather_to(random_bits_shard(key, (TOTAL,), rank, world, out=out), 0))
+        torch.cuda.empty_cache()
+        whole = torch.empty(TOTAL, dtype=torch.uint32, device=dev) if rank == 0 else None
+        direct_ms = timed(lambda: random_bits_gathered(key, (TOTAL,), root=0, out=whole))
+        close_peer_mappings()
+        del whole
+        torch.cuda.empty_cache()
+        into_root = TOTAL * 4 * (world - 1) / world
+        gather = {"root": 0, "bytes": TOTAL * 4, "unit": "ms",
+                  "direct_ms": direct_ms, "nccl_ms": nccl_ms,
+                  "direct_nvlink_GBps_into_root": into_root / (direct_ms * 1e-3) / 1e9,
+                  "note": "whole 2^34-word request assembled on rank 0, max over ranks: direct = "
+                          "every rank's kernel stores its slab into rank 0's buffer through a "
+                          "CUDA IPC peer mapping (random_bits_gathered); nccl = each rank "
+                          "generates its slab locally, then NCCL point-to-point to rank 0"}
+
     # end to end through the public API with a host buffer: key in, bits out to pinned
     # host memory, chunked generation overlapped with the copies
     e2e = None
@@ -405,6 +444,8 @@ def run_ours(args):
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": args.steps, "clocks": clocks,
         }
+        if gather is not None:
+            line["gather"] = gather
         print(json.dumps(line), flush=True)
     del out
     if world > 1:
@@ -428,6 +469,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="N > 1: skip timing the whole request assembled on rank 0")
     args = ap.parse_args()
     if args.warmup < 3:
         log("note: warmup raised to 3")

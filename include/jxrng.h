@@ -170,6 +170,18 @@ int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size
 int jxr_probe_cipher(uint64_t iters, int ctas_per_sm, uint32_t* sink, uint64_t* blocks_out,
                      void* stream);
 
+/* Device memory shared between the processes of one node, so that a bits kernel on one
+ * GPU can write its shard of a request straight into another GPU's buffer over NVLink
+ * (plain stores through a peer mapping), for callers who want a whole request on one
+ * device.  jxr_ipc_export: a 64-byte handle for the
+ * allocation holding dev_ptr and dev_ptr's offset into it.  jxr_ipc_open: map a handle
+ * exported by another process (peer access enabled lazily); add the offset to the
+ * returned base.  jxr_ipc_close: unmap.  No counterpart in the reference, which runs on
+ * one device (src/pjrt.cpp:751). */
+int jxr_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset);
+int jxr_ipc_open(const void* handle, void** base_out);
+int jxr_ipc_close(void* base);
+
 /* random_bits into HOST memory without allocating anything.  Some callers cannot
  * allocate device memory while they run: a host framework that has reserved (nearly)
  * all of the GPU for its own memory pool, as XLA's PJRT client does when it runs an FFI

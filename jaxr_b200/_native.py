@@ -53,6 +53,9 @@ SIGNATURES = {
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],
     "jxr_random_bits_host_static": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp, _vp],
+    "jxr_ipc_export": [_vp, _vp, ctypes.POINTER(ctypes.c_uint64)],
+    "jxr_ipc_open": [_vp, ctypes.POINTER(ctypes.c_void_p)],
+    "jxr_ipc_close": [_vp],
 }
 
 

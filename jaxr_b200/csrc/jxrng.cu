@@ -15,6 +15,7 @@
 // resident CTAs (a multiple of the SM count) strides over the work.
 #include "jxrng.h"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -1001,6 +1002,45 @@ int jxr_random_bits_host_static(const uint32_t* keys_host, int64_t nkeys, uint64
     }
   }
   JXR_CUDA(cudaStreamSynchronize(st));
+  return JXR_OK;
+}
+
+// ---- device memory shared between the processes of one node (CUDA IPC) -------------------
+
+int jxr_ipc_export(const void* dev_ptr, void* handle, uint64_t* offset) {
+  if (!dev_ptr || !handle || !offset) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  using AddrRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddrRangeFn addr_range = nullptr;
+  if (!addr_range) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    JXR_CUDA(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess)
+      return fail(JXR_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+    addr_range = (AddrRangeFn)fn;
+  }
+  CUdeviceptr base = 0;
+  size_t bytes = 0;
+  if (addr_range(&base, &bytes, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "pointer %p is not device memory", dev_ptr);
+  cudaIpcMemHandle_t h;
+  JXR_CUDA(cudaIpcGetMemHandle(&h, (void*)base));
+  std::memcpy(handle, &h, sizeof h);
+  *offset = (uint64_t)((CUdeviceptr)dev_ptr - base);
+  return JXR_OK;
+}
+
+int jxr_ipc_open(const void* handle, void** base_out) {
+  if (!handle || !base_out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof h);
+  JXR_CUDA(cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return JXR_OK;
+}
+
+int jxr_ipc_close(void* base) {
+  if (!base) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  JXR_CUDA(cudaIpcCloseMemHandle(base));
   return JXR_OK;
 }
 

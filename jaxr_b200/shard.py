@@ -3,11 +3,18 @@
 Every element of a threefry request depends only on (key, element index), so device
 r of G produces elements [r*size/G, (r+1)*size/G) of the C-order result with no
 communication (the partitionable layout; for the original layout the same element
-range is produced from the blocks that feed it).  `gather_to` assembles the whole
-array on one device when a caller asks for it, over NVLink through NCCL.
+range is produced from the blocks that feed it).
+
+When a caller wants the whole array on one device there are two ways:
+`random_bits_gathered` has every rank's kernel store its slab directly into the root
+GPU's buffer over NVLink (a CUDA IPC peer mapping, plain stores), so generation and
+transfer are one pass; `gather_to` copies slabs that already exist to the root with NCCL
+point-to-point.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -91,3 +98,67 @@ def gather_to(local, root, group=None):
     for w in dist.batch_isend_irecv([dist.P2POp(dist.isend, view, root, group=group)]):
         w.wait()
     return None
+
+
+# ---- whole request on one device, written over NVLink by every rank's kernel ----------------
+
+_peer_maps = {}  # IPC handle -> base address of the mapping in this process
+
+
+def _export(t):
+    handle = (ctypes.c_uint8 * 64)()
+    off = ctypes.c_uint64(0)
+    nat.call("jxr_ipc_export", t.data_ptr(), handle, ctypes.byref(off))
+    return bytes(handle), off.value
+
+
+def _open(handle):
+    base = _peer_maps.get(handle)
+    if base is None:
+        buf = (ctypes.c_uint8 * 64).from_buffer_copy(handle)
+        ptr = ctypes.c_void_p(0)
+        nat.call("jxr_ipc_open", buf, ctypes.byref(ptr))
+        base = _peer_maps[handle] = ptr.value
+    return base
+
+
+def close_peer_mappings():
+    """Unmap every peer buffer random_bits_gathered opened in this process."""
+    for base in _peer_maps.values():
+        nat.call("jxr_ipc_close", base)
+    _peer_maps.clear()
+
+
+def random_bits_gathered(key, shape, root=0, dtype=None, out=None, group=None):
+    """random_bits(key, shape, dtype) on rank `root`, generated by all ranks: rank r's
+    kernel computes elements shard_range(size, r, world) and stores them straight into the
+    root's buffer through a peer mapping over NVLink.  Collective (every rank calls it
+    with the same key and shape); returns the flattened result on the root and None
+    elsewhere.  `out`, on the root, is reused as the destination; the mapping of a buffer
+    stays open in the other processes until close_peer_mappings()."""
+    import torch.distributed as dist
+    k, _, nb = _check_key("bits", key)
+    if nb:
+        raise JaxValueError("random_bits_gathered takes a single key")
+    dt = default_uint() if dtype is None else canonicalize_dtype(dtype)
+    size = _size(canon_shape(shape))
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    kd = _flat_keys(k)
+    whole = None
+    if rank == root:
+        whole = out if out is not None else torch.empty(size, dtype=_TORCH[dt], device=kd.device)
+        if whole.numel() != size or whole.dtype != _TORCH[dt] or not whole.is_contiguous():
+            raise JaxValueError(f"out must be a contiguous {dt} tensor of {size} elements")
+        meta = [_export(whole)]
+    else:
+        meta = [None]
+    dist.broadcast_object_list(meta, src=root, group=group)
+    handle, off = meta[0]
+    base = whole.data_ptr() if rank == root else _open(handle) + off
+    lo, hi = shard_range(size, rank, world)
+    esz = _BITS[dt] // 8
+    nat.call("jxr_random_bits", _ptr(kd), 1, size, lo, hi - lo, _layout(), _BITS[dt],
+             base + lo * esz, _stream())
+    torch.cuda.current_stream().synchronize()
+    dist.barrier(group=group)
+    return whole

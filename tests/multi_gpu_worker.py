@@ -15,7 +15,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
 import jaxr_b200 as jr  # noqa: E402
-from jaxr_b200.shard import gather_to, random_bits_shard  # noqa: E402
+from jaxr_b200.shard import (close_peer_mappings, gather_to, random_bits_gathered,  # noqa: E402
+                             random_bits_shard)
 
 
 def main():
@@ -38,7 +39,13 @@ def main():
                 idx = np.unique(np.random.default_rng(0).integers(0, size, 2048))
                 got = whole.view(torch.int32)[torch.from_numpy(idx).to(dev)].cpu().numpy().view(np.uint32)
                 ok &= bool(np.array_equal(got, orc.bits_at(orc.seed(123), 32, size, part, idx)))
+            # every rank stores its slab straight into rank 0's buffer over NVLink
+            for _ in range(2):  # the second call reuses the peer mapping
+                g = random_bits_gathered(key, (size,), root=0)
+                if rank == 0:
+                    ok &= bool(torch.equal(g.view(torch.int32), mine.view(torch.int32)))
         torch.cuda.synchronize()
+    close_peer_mappings()
     flag = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
     if rank == 0:
