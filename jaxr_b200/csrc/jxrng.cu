@@ -116,14 +116,27 @@ struct HostCopyCtx {
 
 HostCopyCtx g_host_ctx[64];
 
+// Resident CTAs per SM of each kernel, queried once per kernel (all devices this library
+// runs on are sm_100, so the answer does not depend on the device).
+std::mutex g_occ_mu;
+std::vector<std::pair<const void*, int>> g_occ;
+
 template <class K>
 int resident_grid(K kernel, uint64_t work_ctas, int* grid) {
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
   int per_sm = 0;
-  JXR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0));
-  if (per_sm < 1) per_sm = 1;
+  {
+    std::lock_guard<std::mutex> lock(g_occ_mu);
+    for (const auto& e : g_occ)
+      if (e.first == (const void*)kernel) per_sm = e.second;
+    if (per_sm == 0) {
+      JXR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, 0));
+      if (per_sm < 1) per_sm = 1;
+      g_occ.emplace_back((const void*)kernel, per_sm);
+    }
+  }
   const uint64_t wave = (uint64_t)di.sms * (uint64_t)per_sm;
   *grid = (int)std::min<uint64_t>(std::max<uint64_t>(work_ctas, 1), wave);
   return JXR_OK;
@@ -272,6 +285,85 @@ int launch_words(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t be
   return JXR_OK;
 }
 
+// ---- original layout, requests of 2^32 - 1 words or more ----------------------------------
+
+// Above 2^32 - 1 words the original layout splits the key (R/prng.R:233-245): with
+// U = 2^32 - 1, nseg = nwords / U + 1 keys come from split_original(key, nseg), key s
+// hashes iota(U) (the last one iota(nwords mod U)), and the word streams are
+// concatenated.  Each thread derives the key of the segment it is in (two cipher blocks,
+// cached while the segment stays the same) and computes every word it needs directly:
+// one block per 32-bit word, so this path runs at half the rate of k_words, which serves
+// all smaller requests.
+struct SegState {
+  uint64_t seg = ~0ull;
+  uint64_t len = 0;
+  KeySchedule ks;
+};
+
+__device__ __forceinline__ uint32_t word_of_hash(const KeySchedule& ks, uint64_t n, uint64_t j) {
+  // word j of threefry_2x32(key, iota(n)) (R/prng.R:102-120)
+  const uint64_t half = (n + 1) / 2;
+  uint32_t a[1], b[1];
+  const bool first = j < half;
+  a[0] = (uint32_t)(first ? j : j - half);
+  b[0] = first ? (half + j < n ? (uint32_t)(half + j) : 0u) : (uint32_t)j;
+  threefry20<1>(ks, a, b);
+  return first ? a[0] : b[0];
+}
+
+__device__ __forceinline__ uint32_t segmented_word(const KeySchedule& parent, uint64_t nwords,
+                                                   uint64_t g, SegState& st) {
+  constexpr uint64_t U = 0xFFFFFFFFull;
+  const uint64_t nseg = nwords / U + 1;
+  const uint64_t seg = g / U;
+  if (seg != st.seg) {
+    st.ks = make_schedule(word_of_hash(parent, 2 * nseg, 2 * seg),
+                          word_of_hash(parent, 2 * nseg, 2 * seg + 1));
+    st.len = seg + 1 < nseg ? U : nwords - seg * U;
+    st.seg = seg;
+  }
+  return word_of_hash(st.ks, st.len, g - seg * U);
+}
+
+template <class Op>
+__global__ void __launch_bounds__(kThreads)
+    k_original_segmented(const uint32_t* __restrict__ key, uint64_t size, uint64_t begin,
+                         uint64_t count, Op op, typename Op::Out* __restrict__ out) {
+  constexpr int W = Op::kBits;
+  const KeySchedule parent = make_schedule(__ldg(key), __ldg(key + 1));
+  SegState hi_st, lo_st;
+  const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+  for (uint64_t p = (uint64_t)blockIdx.x * kThreads + threadIdx.x; p < count; p += stride) {
+    const uint64_t e = begin + p;
+    if constexpr (W == 64) {  // (bits[e] << 32) | bits[size + e] over 2 size words
+      const uint64_t hi = segmented_word(parent, 2 * size, e, hi_st);
+      const uint64_t lo = segmented_word(parent, 2 * size, size + e, lo_st);
+      out[p] = op((hi << 32) | lo);
+    } else if constexpr (W == 32) {
+      out[p] = op(segmented_word(parent, size, e, hi_st));
+    } else {  // little-endian W-bit pieces of ceil(W size / 32) words
+      constexpr int per = 32 / W;
+      const uint64_t nwords = (size + per - 1) / per;
+      const uint32_t w = segmented_word(parent, nwords, e / per, hi_st);
+      out[p] = op((typename Op::Bits)(w >> (W * (int)(e % per))));
+    }
+  }
+}
+
+template <class Op>
+int launch_original_segmented(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                              uint64_t count, const Op& op, void* out, cudaStream_t st) {
+  using Out = typename Op::Out;
+  if (count == 0 || nkeys == 0) return JXR_OK;
+  int grid = 0, rc;
+  auto k = k_original_segmented<Op>;
+  if ((rc = resident_grid(k, (count + kThreads - 1) / kThreads, &grid))) return rc;
+  for (int64_t r = 0; r < nkeys; ++r)
+    k<<<grid, kThreads, 0, st>>>(keys + 2 * r, size, begin, count, op, (Out*)out + (uint64_t)r * count);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
 // ---- dispatch by layout -------------------------------------------------------------------
 
 // Ops drawing W <= 32 bits: partitionable -> k_blocks, original -> k_words.
@@ -282,12 +374,13 @@ int launch_op(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin
   if (layout == JXR_LAYOUT_PARTITIONABLE)
     return launch_blocks<Op, kCtrIndex>(keys, nkeys, size, begin, count, op, out, st);
   if constexpr (Op::kBits == 64) {
-    if (size >= 0x7FFFFFFFull)
-      return fail(JXR_ERR_NOT_IMPLEMENTED,
-                  "original-layout 64-bit requests of 2^31-1 or more elements (key splitting, "
-                  "R/prng.R:236-245) are not supported");
+    if (size >= 0x7FFFFFFFull)  // 2 size >= 2^32 - 1 words: the key is split
+      return launch_original_segmented<Op>(keys, nkeys, size, begin, count, op, out, st);
     return launch_blocks<Op, kCtrPair>(keys, nkeys, size, begin, count, op, out, st);
   } else {
+    constexpr uint64_t per = 32 / Op::kBits;
+    if ((size + per - 1) / per >= 0xFFFFFFFFull)
+      return launch_original_segmented<Op>(keys, nkeys, size, begin, count, op, out, st);
     return launch_words<Op>(keys, nkeys, size, begin, count, op, out, st);
   }
 }
@@ -764,9 +857,7 @@ int jxr_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uin
   if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, normal_out))) return rc;
   if (count && nkeys && !bern_out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == JXR_F64) {
-    if (layout == JXR_LAYOUT_ORIGINAL && size >= 0x7FFFFFFFull)
-      return fail(JXR_ERR_NOT_IMPLEMENTED, "original-layout 64-bit requests of 2^31-1 or more elements are not supported");
+  if (dtype == JXR_F64 && !(layout == JXR_LAYOUT_ORIGINAL && size >= 0x7FFFFFFFull)) {
     return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout, OpNormalF64{},
                                    OpBernoulliF64{p}, normal_out, bern_out, st);
   }

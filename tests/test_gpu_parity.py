@@ -396,3 +396,49 @@ def test_bits_host_abi_all_widths(oracle, part, bw):
              int(part), bw, out.ctypes.data_as(ctypes.c_void_p))
     for r in range(3):
         assert np.array_equal(out[r], oracle.random_bits(keys[r], bw, size, part, begin, count))
+
+
+# ---- original layout above 2^32 - 1 words: the key is split (R/prng.R:233-245) ----------------
+
+U32M = (1 << 32) - 1
+SPLIT_CASES = {  # bit width -> (size, element ranges around the segment boundaries)
+    32: ((1 << 32) + 105, [(0, 40), (U32M - 20, 40), ((1 << 32) + 105 - 30, 30)]),
+    64: ((1 << 31) + 3, [(0, 40), ((1 << 31) - 12, 15), (1 << 30, 16)]),
+    16: ((1 << 33) + 107, [(0, 40), (2 * U32M - 20, 40), ((1 << 33) + 107 - 25, 25)]),
+    8: ((1 << 34) + 109, [(0, 64), (4 * U32M - 30, 60), ((1 << 34) + 109 - 33, 33)]),
+}
+
+
+@pytest.mark.parametrize("bw", [8, 16, 32, 64])
+def test_original_layout_key_splitting(oracle, bw):
+    from jaxr_b200 import _native as nat
+    size, ranges = SPLIT_CASES[bw]
+    key = np.array([0x13198A2E, 0x03707344], np.uint32)
+    kd = dev_key(np.stack([key, key ^ 0x5A5A5A5A]))
+    dt = {8: torch.uint8, 16: torch.uint16, 32: torch.uint32, 64: torch.uint64}[bw]
+    for begin, count in ranges:
+        out = torch.empty((2, count), dtype=dt, device="cuda")
+        nat.call("jxr_random_bits", kd.data_ptr(), 2, size, begin, count, 0, bw, out.data_ptr(),
+                 torch.cuda.current_stream().cuda_stream)
+        got = to_np(out)
+        for r, k in enumerate((key, key ^ 0x5A5A5A5A)):
+            want = oracle.bits_at(k, bw, size, False, range(begin, begin + count))
+            assert np.array_equal(got[r], want), (bw, begin, r)
+
+
+def test_original_layout_key_splitting_samplers(oracle):
+    from jaxr_b200 import _native as nat
+    key = np.array([0, 42], np.uint32)
+    kd = dev_key(key)
+    st = torch.cuda.current_stream().cuda_stream
+    size, begin, count = (1 << 32) + 105, U32M - 20, 40
+    out = torch.empty(count, dtype=torch.float32, device="cuda")
+    nat.call("jxr_uniform", kd.data_ptr(), 1, size, begin, count, 0, nat.F32, -2.0, 3.0, 0,
+             out.data_ptr(), st)
+    want = oracle.uniform_at(key, "float32", size, False, -2.0, 3.0, True, range(begin, begin + count))
+    assert np.array_equal(to_np(out), want.astype(np.float32))
+    size, begin, count = (1 << 31) + 3, (1 << 31) - 12, 15
+    out = torch.empty(count, dtype=torch.float64, device="cuda")
+    nat.call("jxr_normal", kd.data_ptr(), 1, size, begin, count, 0, nat.F64, out.data_ptr(), st)
+    want = oracle.normal_at(key, "float64", size, False, True, range(begin, begin + count))
+    assert np.all(np.abs(to_np(out) - want) <= 1e-12 * np.abs(want))
