@@ -186,6 +186,49 @@ WORKLOADS = {
 }
 
 
+def workload_cpu_baseline(c, min_seconds=2.0):
+    """The same workload's first outputs computed by the oracle port on all host threads,
+    repeated for about min_seconds: 32-bit output words per second."""
+    import ctypes
+
+    import numpy as np
+    from oracle import oracle as orc
+    lib = orc.lib()
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    if c == "c1":
+        key, n, words_per, fn = orc.seed(0), 1 << 20, 1, "bits"
+    elif c in ("c2", "c2o"):
+        key, n, words_per, fn = orc.seed(42), 1 << 22, 1, "normal32"
+    elif c == "c3":
+        key, n, words_per, fn = orc.split(orc.seed(7), 1, True)[0], 1 << 22, 1, "uniform32"
+    else:
+        key, n, words_per, fn = orc.fold_in(orc.seed(2024, True), 17), 1 << 21, 2, "normal64"
+    size = {"c1": 1 << 20, "c2": 1 << 26, "c2o": 1 << 26, "c3": 1024, "c5": 1 << 28}[c]
+    part = int(c != "c2o")
+    k = (ctypes.c_uint32 * 2)(int(key[0]), int(key[1]))
+    out = np.empty(n, dtype=np.float64 if fn == "normal64" else np.uint32)
+    optr = out.ctypes.data_as(ctypes.c_void_p)
+
+    def once():
+        if fn == "bits":
+            lib.orc_random_bits(k, 32, size, part, 0, n, optr)
+        elif fn == "normal32":
+            lib.orc_normal(k, orc.F32, size, part, 1, 0, n, optr)
+        elif fn == "uniform32":  # the same per-output work as 4096 rows of 1024, one key
+            lib.orc_uniform(k, orc.F32, n, 1, -2.0, 3.0, 1, 0, n, optr)
+        else:
+            lib.orc_normal(k, orc.F64, size, part, 1, 0, n, optr)
+    once()
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < min_seconds:
+        once()
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": reps * n * words_per / dt, "unit": "words/s", "cores": threads, "kind": "port",
+            "sample": f"first {n} outputs of the workload, {reps} times (C restatement, OpenMP)"}
+
+
 def run_workload(args):
     """One JSON line for a secondary workload: device time per call of the public API,
     32-bit words of output per second, and the cipher-block rate against the probe."""
@@ -257,6 +300,7 @@ def run_workload(args):
     except (OSError, ValueError, KeyError):
         pass
     bps = blocks / (ms * 1e-3)
+    cpu = None if args.no_cpu_baseline else workload_cpu_baseline(c)
     line = {
         "metric": "threefry 32-bit words/s (device-timed), secondary workload", "value": words / (ms * 1e-3),
         "unit": "words/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -272,7 +316,7 @@ def run_workload(args):
                      "hbm": {"achieved": out_bytes / (ms * 1e-3) / 1e9, "peak": hbm_peak,
                              "unit": "GB/s",
                              "frac": out_bytes / (ms * 1e-3) / 1e9 / hbm_peak if hbm_peak else None}},
-        "gpu_launches": args.steps, "clocks": clocks,
+        "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": cpu,
     }
     jr.enable_x64(old[0])
     jr.jax_config_update("jax_threefry_partitionable", old[1])
