@@ -147,6 +147,44 @@ int jxr_uniform_affine(const void* unit, const void* minval, const void* maxval,
 int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p, int64_t n,
                                int dtype, uint8_t* out, void* stream);
 
+/* The log-transform samplers (R/random.R:1422-1516) fused like jxr_uniform, kind:
+ * 0 exponential -log1p(-u); 1 gumbel (mode "low") -log(-log(u)), u from (tiny, 1);
+ * 2 logistic log(x) - log1p(-x), x from (tiny, 1); 3 laplace sign(u) log1p(-|u|),
+ * u from (-1 + 2^-(nmant+1), 1).  out: dtype[nkeys][count]. */
+int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+               uint64_t count, int layout, int kind, int dtype, void* out, void* stream);
+
+/* randint (R/random.R:306-359) from its two draws: hi and lo are nbits-bit (32 or 64)
+ * random_bits of the two halves of split(key); minval/maxval are the bounds already
+ * clipped and converted to the sampling dtype (signed if is_signed), sign- or
+ * zero-extended to int64; out_of_range flags where maxval exceeded that dtype's maximum.
+ * Each parameter array has stride 0 (one value for all) or 1.  Writes the low out_bits of
+ * minval + ((hi % span) * (2^nbits % span) + lo % span) % span. */
+int jxr_randint_combine(const void* hi, const void* lo, int64_t n, int nbits, int is_signed,
+                        const int64_t* minval, int64_t minval_stride, const int64_t* maxval,
+                        int64_t maxval_stride, const uint8_t* out_of_range, int64_t oor_stride,
+                        int out_bits, void* out, void* stream);
+
+/* gumbel modes "high" and "highest" (R/random.R:1465-1489) from the two rows of a (2, n)
+ * draw of one key: mode 0 ("high") takes uniforms of dtype, mode 1 ("highest", float32
+ * only) 32-bit random_bits.  out: dtype[n]. */
+int jxr_gumbel_rows(const void* row0, const void* row1, int64_t n, int mode, int dtype,
+                    void* out, void* stream);
+
+/* random_truncated_normal (R/random.R:586-603) with scalar bounds: uniform(erf(lower/sqrt2),
+ * erf(upper/sqrt2)), sqrt(2) erf_inv, clipped to the open interval; the two erf values are
+ * computed on the host once per call. */
+int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                         uint64_t count, int layout, int dtype, double lower, double upper,
+                         void* out, void* stream);
+
+/* random_truncated_normal with per-element bounds: unit is the uniform(0, 1) draw of the
+ * key (dtype[n]); lower and upper are dtype arrays with stride 0 (one value) or 1.  The erf
+ * of the bounds is evaluated on the device (CUDA's erf in double, rounded to dtype). */
+int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t lower_stride,
+                                   const void* upper, int64_t upper_stride, int64_t n, int dtype,
+                                   void* out, void* stream);
+
 /* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
  * element-wise for F32 or F64. */
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);

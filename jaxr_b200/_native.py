@@ -49,6 +49,12 @@ SIGNATURES = {
     "jxr_normal_from_bits": [_vp, _i64, _int, _vp, _vp],
     "jxr_uniform_affine": [_vp, _vp, _vp, _i64, _int, _u32, _vp, _vp],
     "jxr_bernoulli_from_uniform": [_vp, _vp, _vp, _i64, _int, _vp, _vp],
+    "jxr_sample": [_vp, _i64, _u64, _u64, _u64, _int, _int, _int, _vp, _vp],
+    "jxr_randint_combine": [_vp, _vp, _i64, _int, _int, _vp, _i64, _vp, _i64, _vp, _i64, _int,
+                            _vp, _vp],
+    "jxr_gumbel_rows": [_vp, _vp, _i64, _int, _int, _vp, _vp],
+    "jxr_truncated_normal": [_vp, _i64, _u64, _u64, _u64, _int, _int, _dbl, _dbl, _vp, _vp],
+    "jxr_truncated_normal_from_unit": [_vp, _vp, _i64, _vp, _i64, _i64, _int, _vp, _vp],
     "jxr_erf_inv": [_vp, _i64, _int, _vp, _vp],
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],

@@ -2,7 +2,8 @@
 
 Only the options this path reads are kept: jax_enable_x64 (default dtypes and seed
 width), jax_threefry_partitionable (counter layout), jax_default_prng_impl and
-jax_random_seed_offset; jax_legacy_prng_key governs raw uint32 keys.
+jax_random_seed_offset; jax_legacy_prng_key governs raw uint32 keys;
+jax_use_high_dynamic_range_gumbel picks random_gumbel's default mode.
 """
 
 from __future__ import annotations
@@ -19,6 +20,7 @@ _DEFAULTS = {
     "jax_default_prng_impl": "threefry2x32",
     "jax_random_seed_offset": 0,
     "jax_legacy_prng_key": "allow",
+    "jax_use_high_dynamic_range_gumbel": False,
 }
 
 _config = dict(_DEFAULTS)
@@ -49,7 +51,8 @@ def jax_config_update(name, value):
     if name not in _config:
         raise JaxValueError(f"Unrecognized config option: {name}")
     old = _config[name]
-    if name in ("jax_enable_x64", "jax_threefry_partitionable"):
+    if name in ("jax_enable_x64", "jax_threefry_partitionable",
+                "jax_use_high_dynamic_range_gumbel"):
         value = bool(value)
     if name == "jax_legacy_prng_key" and value not in ("allow", "warn", "error"):
         raise JaxValueError("jax_legacy_prng_key must be one of 'allow', 'warn', 'error'")

@@ -23,6 +23,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <limits>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -568,6 +569,113 @@ __global__ void k_bern_unit_h(const uint16_t* __restrict__ ulo, const uint16_t* 
   }
 }
 
+// the 16-bit float next to the 16-bit value x toward +inf (up) or -inf, as raw bits
+__device__ __forceinline__ uint16_t half_next(float x, bool up, bool bf) {
+  const uint16_t b = bf ? __bfloat16_as_ushort(__float2bfloat16_rn(x))
+                        : __half_as_ushort(__float2half_rn(x));
+  const uint16_t inf = bf ? 0x7F80u : 0x7C00u;
+  if (x != x || b == (up ? inf : (uint16_t)(0x8000u | inf))) return b;
+  if ((b & 0x7FFFu) == 0) return up ? 0x0001u : 0x8001u;  // +-0 -> smallest subnormal
+  const bool neg = b & 0x8000u;
+  return (uint16_t)((up != neg) ? b + 1 : b - 1);
+}
+
+// truncated normal with per-element bounds (R/random.R:586-603) from the unit draw
+// f = uniform(0, 1): a = erf(lower / sqrt2), b = erf(upper / sqrt2) (CUDA's erf in double,
+// rounded to the dtype), u = max(a, f (b - a) + a), sqrt2 erf_inv(u), clipped to
+// [nextafter(lower, inf), nextafter(upper, -inf)].  Bounds have stride 0 or 1.
+template <int D>
+__global__ void k_trunc_unit(const void* __restrict__ unit, const void* __restrict__ lower,
+                             int64_t ls, const void* __restrict__ upper, int64_t us, int64_t n,
+                             void* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if constexpr (D == JXR_F32) {
+      const float s2 = 1.41421354f;
+      const float lo = ((const float*)lower)[i * ls], hi = ((const float*)upper)[i * us];
+      const float a = __double2float_rn(erf((double)__fdiv_rn(lo, s2)));
+      const float b = __double2float_rn(erf((double)__fdiv_rn(hi, s2)));
+      const float u = xla_max(a, __fmaf_rn(((const float*)unit)[i], __fsub_rn(b, a), a));
+      const float x = __fmul_rn(s2, erfinv_f32(u));
+      const float cl = nextafterf(lo, __int_as_float(0x7F800000)),
+                  ch = nextafterf(hi, __int_as_float(0xFF800000));
+      ((float*)out)[i] = xla_min(ch, xla_max(cl, x));
+    } else if constexpr (D == JXR_F64) {
+      const double s2 = 1.4142135623730951;
+      const double lo = ((const double*)lower)[i * ls], hi = ((const double*)upper)[i * us];
+      const double a = erf(__ddiv_rn(lo, s2)), b = erf(__ddiv_rn(hi, s2));
+      const double u = xla_max(a, __fma_rn(((const double*)unit)[i], __dsub_rn(b, a), a));
+      const double x = __dmul_rn(s2, erfinv_f64(u));
+      const double inf = __longlong_as_double(0x7FF0000000000000ll);
+      ((double*)out)[i] = xla_min(nextafter(hi, -inf), xla_max(nextafter(lo, inf), x));
+    } else {
+      constexpr bool BF = D == JXR_BF16;
+      const float s2 = rh<BF>(1.41421354f);
+      const uint16_t lb = ((const uint16_t*)lower)[i * ls], ub = ((const uint16_t*)upper)[i * us];
+      const float lo = h2f<BF>(lb), hi = h2f<BF>(ub);
+      const float a = rh<BF>(__double2float_rn(erf((double)rh<BF>(__fdiv_rn(lo, s2)))));
+      const float b = rh<BF>(__double2float_rn(erf((double)rh<BF>(__fdiv_rn(hi, s2)))));
+      const float d = rh<BF>(__fsub_rn(b, a));
+      const float f = h2f<BF>(((const uint16_t*)unit)[i]);
+      const float u = xla_max(a, h2f<BF>(d2h<BF>(__fma_rn((double)f, (double)d, (double)a))));
+      const float x = rh<BF>(__fmul_rn(s2, rh<BF>(erfinv_f32(u))));
+      ((uint16_t*)out)[i] = f2h<BF>(xla_min(h2f<BF>(half_next(hi, false, BF)),
+                                            xla_max(h2f<BF>(half_next(lo, true, BF)), x)));
+    }
+  }
+}
+
+// gumbel modes "high"/"highest" from the two rows of a (2, n) draw
+template <int D, int kMode>
+__global__ void k_gumbel_rows(const void* __restrict__ row0, const void* __restrict__ row1,
+                              int64_t n, void* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if constexpr (kMode == 1) {  // highest, float32 bits
+      ((float*)out)[i] = gumbel_highest_f32(((const uint32_t*)row0)[i], ((const uint32_t*)row1)[i]);
+    } else if constexpr (D == JXR_F32) {
+      ((float*)out)[i] = gumbel_high_f32(((const float*)row0)[i], ((const float*)row1)[i]);
+    } else if constexpr (D == JXR_F64) {
+      ((double*)out)[i] = gumbel_high_f64(((const double*)row0)[i], ((const double*)row1)[i]);
+    } else {
+      constexpr bool BF = D == JXR_BF16;
+      const float r = gumbel_high_h<BF>(h2f<BF>(((const uint16_t*)row0)[i]),
+                                        h2f<BF>(((const uint16_t*)row1)[i]));
+      ((uint16_t*)out)[i] = f2h<BF>(r);
+    }
+  }
+}
+
+// randint: out = low out_bits of (minval + offset(hi, lo, span)) in the sampling dtype
+template <class U, bool kSigned>
+__global__ void k_randint_combine(const U* __restrict__ hi, const U* __restrict__ lo, int64_t n,
+                                  const int64_t* __restrict__ mn, int64_t mn_stride,
+                                  const int64_t* __restrict__ mx, int64_t mx_stride,
+                                  const uint8_t* __restrict__ oor, int64_t oor_stride,
+                                  int out_bits, void* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t a = mn[i * mn_stride], b = mx[i * mx_stride];
+    const bool empty = kSigned ? (b <= a) : ((uint64_t)b <= (uint64_t)a);
+    U span = (U)((U)b - (U)a);
+    if (empty) span = 1;
+    if (oor[i * oor_stride] && !empty) span = (U)(span + 1);
+    U off;
+    if (span == 0) {  // full range: x % 0 is x (XLA), the multiplier is 0
+      off = lo[i];
+    } else {
+      off = randint_offset<U>(hi[i], lo[i], span);
+    }
+    const uint64_t r = (uint64_t)(U)((U)a + off);
+    switch (out_bits) {
+      case 8: ((uint8_t*)out)[i] = (uint8_t)r; break;
+      case 16: ((uint16_t*)out)[i] = (uint16_t)r; break;
+      case 32: ((uint32_t*)out)[i] = (uint32_t)r; break;
+      default: ((uint64_t*)out)[i] = r; break;
+    }
+  }
+}
+
 int small_grid(int64_t n, int* grid) {
   DeviceInfo di;
   int rc = device_info(&di);
@@ -974,6 +1082,198 @@ int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p
       break;
     default:
       k_bern_unit_h<true><<<grid, 256, 0, st>>>((U16)u_lo, (U16)u_hi, (U16)p, n, 0x1p-7f, out);
+  }
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+               uint64_t count, int layout, int kind, int dtype, void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  if (kind < kExponential || kind > kLaplace)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "kind must be 0..3 (exponential, gumbel, logistic, laplace), got %d", kind);
+  cudaStream_t st = (cudaStream_t)stream;
+  // the kind's uniform draw: (0, 1), (tiny, 1) or (-1 + 2^-(nmant+1), 1)
+  auto lo_of = [&](double tiny, double epsneg) {
+    return kind == kExponential ? 0.0 : (kind == kLaplace ? -1.0 + epsneg : tiny);
+  };
+#define JXR_SAMPLE(KIND)                                                                       \
+  case KIND:                                                                                   \
+    switch (dtype) {                                                                           \
+      case JXR_F32: {                                                                          \
+        const float mn = (float)lo_of(0x1p-126, 0x1p-24), d = 1.0f - mn;                       \
+        return launch_op(keys, nkeys, size, begin, count, layout,                              \
+                         OpLogSampler<KIND, 0>{{mn, d}}, out, st);                             \
+      }                                                                                        \
+      case JXR_F64: {                                                                          \
+        const double mn = lo_of(0x1p-1022, 0x1p-53), d = 1.0 - mn;                             \
+        return launch_op(keys, nkeys, size, begin, count, layout,                              \
+                         OpLogSampler<KIND, 1>{{mn, d}}, out, st);                             \
+      }                                                                                        \
+      case JXR_F16: {                                                                          \
+        const float mn = to_half_value(lo_of(0x1p-14, 0x1p-11), false);                        \
+        const float d = to_half_value(1.0 - (double)mn, false);                                \
+        return launch_op(keys, nkeys, size, begin, count, layout,                              \
+                         OpLogSampler<KIND, 2>{{{mn, d}}}, out, st);                           \
+      }                                                                                        \
+      default: {                                                                               \
+        const float mn = to_half_value(lo_of(0x1p-126, 0x1p-8), true);                         \
+        const float d = to_half_value(1.0 - (double)mn, true);                                 \
+        return launch_op(keys, nkeys, size, begin, count, layout,                              \
+                         OpLogSampler<KIND, 3>{{{mn, d}}}, out, st);                           \
+      }                                                                                        \
+    }
+  switch (kind) {
+    JXR_SAMPLE(kExponential)
+    JXR_SAMPLE(kGumbel)
+    JXR_SAMPLE(kLogistic)
+    JXR_SAMPLE(kLaplace)
+  }
+#undef JXR_SAMPLE
+  return fail(JXR_ERR_INVALID_ARGUMENT, "unreachable");
+}
+
+int jxr_randint_combine(const void* hi, const void* lo, int64_t n, int nbits, int is_signed,
+                        const int64_t* minval, int64_t minval_stride, const int64_t* maxval,
+                        int64_t maxval_stride, const uint8_t* out_of_range, int64_t oor_stride,
+                        int out_bits, void* out, void* stream) {
+  if (nbits != 32 && nbits != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "randint samples in 32 or 64 bits, got %d", nbits);
+  if (out_bits != 8 && out_bits != 16 && out_bits != 32 && out_bits != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "out_bits must be 8, 16, 32 or 64, got %d", out_bits);
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!hi || !lo || !minval || !maxval || !out_of_range || !out)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((minval_stride | maxval_stride | oor_stride) & ~1ll)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "parameter strides must be 0 (broadcast) or 1");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (nbits == 32) {
+    if (is_signed)
+      k_randint_combine<uint32_t, true><<<grid, 256, 0, st>>>((const uint32_t*)hi, (const uint32_t*)lo, n, minval, minval_stride, maxval, maxval_stride, out_of_range, oor_stride, out_bits, out);
+    else
+      k_randint_combine<uint32_t, false><<<grid, 256, 0, st>>>((const uint32_t*)hi, (const uint32_t*)lo, n, minval, minval_stride, maxval, maxval_stride, out_of_range, oor_stride, out_bits, out);
+  } else {
+    if (is_signed)
+      k_randint_combine<uint64_t, true><<<grid, 256, 0, st>>>((const uint64_t*)hi, (const uint64_t*)lo, n, minval, minval_stride, maxval, maxval_stride, out_of_range, oor_stride, out_bits, out);
+    else
+      k_randint_combine<uint64_t, false><<<grid, 256, 0, st>>>((const uint64_t*)hi, (const uint64_t*)lo, n, minval, minval_stride, maxval, maxval_stride, out_of_range, oor_stride, out_bits, out);
+  }
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_gumbel_rows(const void* row0, const void* row1, int64_t n, int mode, int dtype,
+                    void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (mode != 0 && mode != 1)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "mode must be 0 (high) or 1 (highest), got %d", mode);
+  if (mode == 1 && dtype != JXR_F32)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "mode highest is float32 only");
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!row0 || !row1 || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (mode == 1) k_gumbel_rows<JXR_F32, 1><<<grid, 256, 0, st>>>(row0, row1, n, out);
+  else if (dtype == JXR_F32) k_gumbel_rows<JXR_F32, 0><<<grid, 256, 0, st>>>(row0, row1, n, out);
+  else if (dtype == JXR_F64) k_gumbel_rows<JXR_F64, 0><<<grid, 256, 0, st>>>(row0, row1, n, out);
+  else if (dtype == JXR_F16) k_gumbel_rows<JXR_F16, 0><<<grid, 256, 0, st>>>(row0, row1, n, out);
+  else k_gumbel_rows<JXR_BF16, 0><<<grid, 256, 0, st>>>(row0, row1, n, out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+namespace {
+// The 16-bit float next to the 16-bit value x toward +inf (up) or -inf, on the host.
+float half_step(float x, bool up, bool bf) {
+  uint16_t b;
+  if (bf) {
+    uint32_t w;
+    std::memcpy(&w, &x, 4);
+    b = (uint16_t)(w >> 16);
+  } else {
+    b = __half_as_ushort(__float2half_rn(x));
+  }
+  const uint16_t inf = bf ? 0x7F80u : 0x7C00u;
+  if (x != x || b == (up ? inf : (uint16_t)(0x8000u | inf))) return x;
+  if ((b & 0x7FFFu) == 0) b = up ? 0x0001u : 0x8001u;
+  else b = (uint16_t)((up != (bool)(b & 0x8000u)) ? b + 1 : b - 1);
+  if (bf) {
+    const uint32_t w = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &w, 4);
+    return f;
+  }
+  return __half2float(__ushort_as_half(b));
+}
+}  // namespace
+
+int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                         uint64_t count, int layout, int dtype, double lower, double upper,
+                         void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const double inf = std::numeric_limits<double>::infinity();
+  switch (dtype) {
+    case JXR_F32: {
+      const float s2 = 1.41421354f, lo = (float)lower, hi = (float)upper;
+      const float a = (float)std::erf((double)(lo / s2)), b = (float)std::erf((double)(hi / s2));
+      const float cl = std::nextafter(lo, (float)inf), ch = std::nextafter(hi, (float)-inf);
+      return launch_op(keys, nkeys, size, begin, count, layout,
+                       OpTruncNormal<0>{{a, b - a}, cl, ch}, out, st);
+    }
+    case JXR_F64: {
+      const double s2 = 1.4142135623730951;
+      const double a = std::erf(lower / s2), b = std::erf(upper / s2);
+      return launch_op(keys, nkeys, size, begin, count, layout,
+                       OpTruncNormal<1>{{a, b - a}, std::nextafter(lower, inf),
+                                        std::nextafter(upper, -inf)},
+                       out, st);
+    }
+    default: {
+      const bool bf = dtype == JXR_BF16;
+      const float s2 = to_half_value(1.4142135623730951, bf);
+      const float lo = to_half_value(lower, bf), hi = to_half_value(upper, bf);
+      // the division and erf are evaluated in float32 and rounded to 16 bits
+      const float ql = to_half_value((double)(lo / s2), bf), qh = to_half_value((double)(hi / s2), bf);
+      const float a = to_half_value((double)(float)std::erf((double)ql), bf);
+      const float b = to_half_value((double)(float)std::erf((double)qh), bf);
+      const float d = to_half_value((double)b - (double)a, bf);
+      const float cl = half_step(lo, true, bf), ch = half_step(hi, false, bf);
+      if (bf)
+        return launch_op(keys, nkeys, size, begin, count, layout,
+                         OpTruncNormal<3>{{{a, d}, cl, ch}}, out, st);
+      return launch_op(keys, nkeys, size, begin, count, layout,
+                       OpTruncNormal<2>{{{a, d}, cl, ch}}, out, st);
+    }
+  }
+}
+
+int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t lower_stride,
+                                   const void* upper, int64_t upper_stride, int64_t n, int dtype,
+                                   void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!unit || !lower || !upper || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((lower_stride | upper_stride) & ~1ll)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "bound strides must be 0 (broadcast) or 1");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (dtype) {
+    case JXR_F32: k_trunc_unit<JXR_F32><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
+    case JXR_F64: k_trunc_unit<JXR_F64><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
+    case JXR_F16: k_trunc_unit<JXR_F16><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
+    default: k_trunc_unit<JXR_BF16><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out);
   }
   JXR_CUDA(cudaGetLastError());
   return JXR_OK;

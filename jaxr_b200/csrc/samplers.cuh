@@ -28,20 +28,23 @@ __device__ __forceinline__ float xla_max(float a, float b) { return (a >= b || a
 __device__ __forceinline__ double xla_max(double a, double b) {
   return (a >= b || a != a) ? a : b;
 }
+// lax_min likewise.
+__device__ __forceinline__ float xla_min(float a, float b) { return (a <= b || a != a) ? a : b; }
+__device__ __forceinline__ double xla_min(double a, double b) {
+  return (a <= b || a != a) ? a : b;
+}
 
 // ---- log1p -----------------------------------------------------------------------------
 
-// log1p(y) for y <= 0 (and NaN), the argument erf_inv gives it (y = -x*x), branch-free.
-// Method of W. J. Cody and W. Waite, "Software Manual for the Elementary Functions"
-// (1980): t = 1 + y = 2^e m with m in [sqrt(1/2), sqrt(2)), log m = 2 atanh(s) =
-// 2 (s + s^3/3 + s^5/5 + ...) with s = (m - 1) / (m + 1), |s| < 0.1716, ten terms; the
-// rounding error of 1 + y is added back as (y - (t - 1)) / t.  Within 2 ulp of a
-// correctly rounded log1p.  The CPU oracle performs the same operations in the same
-// order, so both produce the same double.
-__device__ __forceinline__ double log1p_neg(double y) {
-  const double t = __dadd_rn(1.0, y);
-  const double corr =
-      __dmul_rn(__dsub_rn(y, __dsub_rn(t, 1.0)), (double)__frcp_rn(__double2float_rn(t)));
+// Logarithms in double precision, branch-free, after W. J. Cody and W. Waite, "Software
+// Manual for the Elementary Functions" (1980): t = 2^e m with m in [sqrt(1/2), sqrt(2)),
+// log m = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ...) with s = (m - 1) / (m + 1),
+// |s| < 0.1716, ten terms.  Within 2 ulp of correctly rounded results.  The CPU oracle
+// performs the same operations in the same order, so both produce the same doubles.
+// log of t > 0 after Cody and Waite, plus a small correction term added before the
+// exponent part; shared by log1p_neg and log_pos.  t = 0 gives -inf, t < 0 or NaN NaN,
+// t = inf inf; t is a normal number in every use here (>= the float32 tiny).
+__device__ __forceinline__ double log_core(double t, double corr) {
   const unsigned long long b64 = (unsigned long long)__double_as_longlong(t);
   const uint32_t hi = (uint32_t)(b64 >> 32), mh = hi & 0x000FFFFFu;
   const bool big = mh >= 0x6A09Eu;  // mantissa >= sqrt(2): use m / 2
@@ -70,10 +73,23 @@ __device__ __forceinline__ double log1p_neg(double y) {
   const double LN2_HI = 0x1.62e42fefa3800p-1, LN2_LO = 0x1.ef35793c76730p-45;
   const double de = (double)e;
   double res = __fma_rn(de, LN2_HI, __fma_rn(de, LN2_LO, __dadd_rn(lm, corr)));
-  if (!(t > 0.0)) res = (t == 0.0) ? -__longlong_as_double(0x7FF0000000000000ll)
-                                   : __longlong_as_double(0x7FF8000000000000ll);
+  const double inf = __longlong_as_double(0x7FF0000000000000ll);
+  if (!(t > 0.0)) res = (t == 0.0) ? -inf : __longlong_as_double(0x7FF8000000000000ll);
+  if (t == inf) res = inf;
   return res;
 }
+
+// log1p(y) for y <= 0 (and NaN), the argument erf_inv gives it (y = -x*x), branch-free:
+// t = 1 + y and the rounding error of that sum added back as (y - (t - 1)) / t.
+__device__ __forceinline__ double log1p_neg(double y) {
+  const double t = __dadd_rn(1.0, y);
+  const double corr =
+      __dmul_rn(__dsub_rn(y, __dsub_rn(t, 1.0)), (double)__frcp_rn(__double2float_rn(t)));
+  return log_core(t, corr);
+}
+
+// log(x) for x > 0.
+__device__ __forceinline__ double log_pos(double x) { return log_core(x, 0.0); }
 
 // ---- erf_inv --------------------------------------------------------------------------
 
@@ -340,5 +356,216 @@ struct OpBernoulliH {
   float p;  // value of a 16-bit float
   __device__ __forceinline__ Out operator()(Bits b) const { return unit_h<BF>(b) < p; }
 };
+
+// ---- log-transform samplers (R/random.R:1422-1516) -------------------------------------
+//
+//   exponential  -log1p(-u),              u = uniform(0, 1)
+//   gumbel       -log(-log(u)),           u = uniform(tiny, 1)          (mode "low")
+//   logistic     log(x) - log1p(-x),      x = uniform(tiny, 1)
+//   laplace      sign(u) log1p(-|u|),     u = uniform(-1 + 2^-(nmant+1), 1)
+// Each float op of the reference's chain is rounded to the dtype once: the logarithms
+// are evaluated in double (log_core) and rounded to float32 (then, for 16-bit dtypes,
+// to 16 bits, as XLA evaluates 16-bit transcendentals in float32).
+
+enum { kExponential = 0, kGumbel = 1, kLogistic = 2, kLaplace = 3 };
+
+template <int kKind, int D>
+struct OpLogSampler;
+
+template <int kKind>
+struct OpLogSampler<kKind, 0> {  // float32
+  static constexpr int kBits = 32;
+  static constexpr int kGroups = 1;
+  using Bits = uint32_t;
+  using Out = float;
+  OpUniformF32<true> uni;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float u = uni(b);
+    if constexpr (kKind == kExponential) {
+      return -__double2float_rn(log1p_neg(-(double)u));
+    } else if constexpr (kKind == kGumbel) {
+      const float a = __double2float_rn(log_pos((double)u));
+      return -__double2float_rn(log_pos(-(double)a));
+    } else if constexpr (kKind == kLogistic) {
+      const float a = __double2float_rn(log_pos((double)u));
+      const float c = __double2float_rn(log1p_neg(-(double)u));
+      return __fsub_rn(a, c);
+    } else {
+      const float l = __double2float_rn(log1p_neg(-(double)fabsf(u)));
+      return u < 0.0f ? -l : l;
+    }
+  }
+};
+
+template <int kKind>
+struct OpLogSampler<kKind, 1> {  // float64
+  static constexpr int kBits = 64;
+  static constexpr int kGroups = 2;
+  using Bits = uint64_t;
+  using Out = double;
+  OpUniformF64<true> uni;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const double u = uni(b);
+    if constexpr (kKind == kExponential) {
+      return -log1p_neg(-u);
+    } else if constexpr (kKind == kGumbel) {
+      return -log_pos(-log_pos(u));
+    } else if constexpr (kKind == kLogistic) {
+      return __dsub_rn(log_pos(u), log1p_neg(-u));
+    } else {
+      const double l = log1p_neg(-fabs(u));
+      return u < 0.0 ? -l : l;
+    }
+  }
+};
+
+template <int kKind, bool BF>
+struct OpLogSamplerH {  // float16 / bfloat16: float32 arithmetic rounded to 16 bits
+  static constexpr int kBits = BF ? 8 : 16;
+  static constexpr int kGroups = 1;
+  using Bits = typename UintOf<kBits>::T;
+  using Out = uint16_t;
+  OpUniformH<BF, true> uni;
+  __device__ __forceinline__ static float lg(double v) { return rh<BF>(__double2float_rn(v)); }
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float u = h2f<BF>(uni(b));
+    float r;
+    if constexpr (kKind == kExponential) {
+      r = -lg(log1p_neg(-(double)u));
+    } else if constexpr (kKind == kGumbel) {
+      r = -lg(log_pos(-(double)lg(log_pos((double)u))));
+    } else if constexpr (kKind == kLogistic) {
+      r = rh<BF>(__fsub_rn(lg(log_pos((double)u)), lg(log1p_neg(-(double)u))));
+    } else {
+      const float l = lg(log1p_neg(-(double)fabsf(u)));
+      r = u < 0.0f ? -l : l;
+    }
+    return f2h<BF>(r);
+  }
+};
+template <int kKind>
+struct OpLogSampler<kKind, 2> : OpLogSamplerH<kKind, false> {};
+template <int kKind>
+struct OpLogSampler<kKind, 3> : OpLogSamplerH<kKind, true> {};
+
+// ---- randint (R/random.R:306-359): two draws of the split key combined exactly ---------
+
+// hi, lo: nbits-bit draws; span, mult as the reference computes them per element.
+template <class U>
+__device__ __forceinline__ U randint_offset(U hi, U lo, U span) {
+  U m = (U)(((U)1 << (sizeof(U) * 4)) % span);
+  m = (U)(m * m) % span;
+  return (U)((U)((hi % span) * m) + (lo % span)) % span;
+}
+
+// ---- truncated normal (R/random.R:586-603) ----------------------------------------------
+//
+// u = uniform(a, b) with a = erf(lower / sqrt 2), b = erf(upper / sqrt 2), then
+// sqrt(2) erf_inv(u) clipped to [nextafter(lower, inf), nextafter(upper, -inf)].  a, b and
+// the clip bounds are parameters (computed once per call on the host).
+
+template <int D>
+struct OpTruncNormal;
+
+template <>
+struct OpTruncNormal<0> {  // float32
+  static constexpr int kBits = 32;
+  static constexpr int kGroups = 1;
+  using Bits = uint32_t;
+  using Out = float;
+  OpUniformF32<true> uni;
+  float lo, hi;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float x = __fmul_rn(1.41421354f, erfinv_f32(uni(b)));
+    return xla_min(hi, xla_max(lo, x));
+  }
+};
+
+template <>
+struct OpTruncNormal<1> {  // float64
+  static constexpr int kBits = 64;
+  static constexpr int kGroups = 2;
+  using Bits = uint64_t;
+  using Out = double;
+  OpUniformF64<true> uni;
+  double lo, hi;
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const double x = __dmul_rn(1.4142135623730951, erfinv_f64(uni(b)));
+    return xla_min(hi, xla_max(lo, x));
+  }
+};
+
+template <bool BF>
+struct OpTruncNormalH {
+  static constexpr int kBits = BF ? 8 : 16;
+  static constexpr int kGroups = 1;
+  using Bits = typename UintOf<kBits>::T;
+  using Out = uint16_t;
+  OpUniformH<BF, true> uni;
+  float lo, hi;  // values of 16-bit floats
+  __device__ __forceinline__ Out operator()(Bits b) const {
+    const float e = rh<BF>(erfinv_f32(h2f<BF>(uni(b))));
+    const float x = rh<BF>(__fmul_rn(rh<BF>(1.41421354f), e));
+    return f2h<BF>(xla_min(hi, xla_max(lo, x)));
+  }
+};
+template <>
+struct OpTruncNormal<2> : OpTruncNormalH<false> {};
+template <>
+struct OpTruncNormal<3> : OpTruncNormalH<true> {};
+
+// ---- gumbel modes "high" and "highest" (R/random.R:1465-1489) ----------------------------
+//
+// Both draw a (2, n) array and combine element i of row 0 with element i of row 1.
+// "high": high, low uniforms in [0, 1); x = high if high >= 0.5, else
+// high + 2^-nmant low + max(2^-(2 nmant + 1), tiny); result -log(-log1p(-x)).
+
+__device__ __forceinline__ float gumbel_high_f32(float high, float low) {
+  const float x = high >= 0.5f ? high : __fadd_rn(__fadd_rn(high, __fmul_rn(0x1p-23f, low)), 0x1p-47f);
+  const float a = __double2float_rn(log1p_neg(-(double)x));
+  return -__double2float_rn(log_pos(-(double)a));
+}
+__device__ __forceinline__ double gumbel_high_f64(double high, double low) {
+  const double x =
+      high >= 0.5 ? high : __dadd_rn(__dadd_rn(high, __dmul_rn(0x1p-52, low)), 0x1p-105);
+  return -log_pos(-log1p_neg(-x));
+}
+template <bool BF>
+__device__ __forceinline__ float gumbel_high_h(float high, float low) {
+  // f16: 2^-10 low + max(2^-21, 2^-14); bf16: 2^-7 low + max(2^-15, 2^-126)
+  const float x = high >= 0.5f ? high
+                               : rh<BF>(__fadd_rn(rh<BF>(__fadd_rn(high, rh<BF>(__fmul_rn(BF ? 0x1p-7f : 0x1p-10f, low)))),
+                                                  BF ? 0x1p-15f : 0x1p-14f));
+  const float a = rh<BF>(__double2float_rn(log1p_neg(-(double)x)));
+  return -rh<BF>(__double2float_rn(log_pos(-(double)a)));
+}
+
+// XLA shift semantics: amounts of 32 or more give 0.
+__device__ __forceinline__ uint32_t xshl(uint32_t x, uint32_t s) { return s >= 32u ? 0u : x << s; }
+__device__ __forceinline__ uint32_t xshr(uint32_t x, uint32_t s) { return s >= 32u ? 0u : x >> s; }
+
+// The 64-bit fixed-point fraction hi:lo as a float32 in (0, 1), keeping the leading 24
+// significant bits (R/random.R:1446-1462).
+__device__ __forceinline__ float safe_int_to_float(uint32_t hi, uint32_t lo) {
+  const uint32_t hiclz = (uint32_t)__clz(hi), loclz = (uint32_t)__clz(lo);
+  uint32_t mant = xshl(hi, hiclz) | (hiclz == 32u ? xshl(lo, loclz) : xshr(lo, 32u - hiclz));
+  mant = (mant >> 8) & 0x7FFFFFu;
+  const uint32_t ex = ((126u - (hiclz == 32u ? 32u + loclz : hiclz)) << 23) & 0x3FC00000u;
+  return __uint_as_float(ex | mant);
+}
+
+// "highest" (float32): b0, b1 are 32-bit draws of rows 0 and 1; values below 1/2 use
+// 1 - bits (the 64-bit negation) through log1p, the others log.
+__device__ __forceinline__ float gumbel_highest_f32(uint32_t b0, uint32_t b1) {
+  const bool flip = b0 < 0x80000000u;
+  const uint32_t n1 = ~b1, n0 = ~b0 + (n1 == 0xFFFFFFFFu ? 1u : 0u);
+  const float x = flip ? safe_int_to_float(b0, b1) : safe_int_to_float(n0, n1 + 1u);
+  if (flip) {
+    const float a = __double2float_rn(log1p_neg(-(double)x));
+    return -__double2float_rn(log_pos(-(double)a));
+  }
+  const float a = __double2float_rn(log_pos((double)x));
+  return -__double2float_rn(log_pos(-(double)a));
+}
 
 }  // namespace jxr

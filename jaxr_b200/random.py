@@ -850,6 +850,242 @@ def random_normal_bernoulli(key, p=0.5, shape=(), dtype=None):
             _rebatch(bout.view(torch.bool).reshape(bshape + shape), nb))
 
 
+# ---- log-transform samplers (R/random.R:1420-1516) ------------------------------------------
+
+_SAMPLE_KIND = {"exponential": 0, "gumbel": 1, "logistic": 2, "laplace": 3}
+
+
+def _k_sample(kd, size, dt, kind, layout):
+    _check_size(size, layout)
+    out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    nat.call("jxr_sample", _ptr(kd), kd.shape[0], size, 0, size, layout, _SAMPLE_KIND[kind],
+             _FLOAT_CODE[dt], _ptr(out), _stream())
+    return _as_float_view(out, dt)
+
+
+def _log_sampler(kind, key, shape, dtype):
+    k, _, nb = _check_key(kind, key)
+    dt = _float_dtype(kind, dtype)
+    shape = canon_shape(shape)
+    out = _k_sample(_flat_keys(k), _size(shape), dt, kind, _layout())
+    return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
+
+
+def random_exponential(key, shape=(), dtype=None):
+    """Exponential(1) samples -log1p(-u), u uniform in [0, 1) (R/random.R:1420-1432)."""
+    return _log_sampler("exponential", key, shape, dtype)
+
+
+def random_laplace(key, shape=(), dtype=None):
+    """Laplace(0, 1) samples sign(u) log1p(-|u|), u uniform in (-1, 1)
+    (R/random.R:1492-1503)."""
+    return _log_sampler("laplace", key, shape, dtype)
+
+
+def random_logistic(key, shape=(), dtype=None):
+    """Logistic samples log(x) - log1p(-x), x uniform in [tiny, 1) (R/random.R:1505-1516)."""
+    return _log_sampler("logistic", key, shape, dtype)
+
+
+def random_gumbel(key, shape=(), dtype=None, mode=None):
+    """Gumbel samples (R/random.R:1434-1489).  mode "low" (the default unless
+    jax_use_high_dynamic_range_gumbel is set) is -log(-log(u)), u uniform in [tiny, 1);
+    "high" and "highest" (float32; other dtypes take "high") combine two draws for more
+    dynamic range near u = 0."""
+    k, _, nb = _check_key("gumbel", key)
+    dt = _float_dtype("gumbel", dtype)
+    shape = canon_shape(shape)
+    if mode is None:
+        mode = "high" if cfg.jax_config("jax_use_high_dynamic_range_gumbel") else "low"
+    if mode not in ("highest", "high", "low"):
+        raise JaxValueError(f"Must provide valid mode for gumbel got: {mode}")
+    kd = _flat_keys(k)
+    size = _size(shape)
+    layout = _layout()
+    if mode == "low":
+        out = _k_sample(kd, size, dt, "gumbel", layout)
+        return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
+    if dt == "float32" and mode == "highest":
+        rows = _k_bits(kd, 2 * size, 32, layout).reshape(kd.shape[0], 2, size)
+        code = 1
+    else:
+        rows = _raw16(_k_uniform(kd, 2 * size, dt, 0.0, 1.0, layout), dt).reshape(
+            kd.shape[0], 2, size)
+        code = 0
+    out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    for r in range(kd.shape[0] if size else 0):
+        nat.call("jxr_gumbel_rows", _ptr(rows[r, 0]), _ptr(rows[r, 1]), size, code,
+                 _FLOAT_CODE[dt], _ptr(out[r]), _stream())
+    return _rebatch(_as_float_view(out, dt).reshape(k.shape[:nb] + shape), nb)
+
+
+# ---- truncated normal (R/random.R:576-603) ---------------------------------------------------
+
+def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
+    """Normal samples truncated to (lower, upper): sqrt(2) erf_inv(u) with u uniform in
+    [erf(lower / sqrt 2), erf(upper / sqrt 2)), clipped to the open interval
+    (R/random.R:576-603).  Scalar bounds run in one fused kernel; array bounds
+    (broadcast to `shape`) take the unit draw and a per-element transform."""
+    if shape is not None:
+        shape = canon_shape(shape)
+    k, _, nb = _check_key("truncated_normal", key)
+    dt = _float_dtype("truncated_normal", dtype)
+    lo_s, lo_t = _param(lower, dt)
+    hi_s, hi_t = _param(upper, dt)
+    if shape is None:
+        shape = tuple(torch.broadcast_shapes(
+            tuple(lo_t.shape) if lo_t is not None else (),
+            tuple(hi_t.shape) if hi_t is not None else ()))
+    kd = _flat_keys(k)
+    size = _size(shape)
+    layout = _layout()
+    bshape = k.shape[:nb]
+    if lo_t is None and hi_t is None:
+        _check_size(size, layout)
+        out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+        nat.call("jxr_truncated_normal", _ptr(kd), kd.shape[0], size, 0, size, layout,
+                 _FLOAT_CODE[dt], float(lo_s), float(hi_s), _ptr(out), _stream())
+        return _rebatch(_as_float_view(out, dt).reshape(bshape + shape), nb)
+    lo = _broadcast_param(lo_t if lo_t is not None else torch.tensor(lo_s), shape, dt,
+                          "truncated_normal")
+    hi = _broadcast_param(hi_t if hi_t is not None else torch.tensor(hi_s), shape, dt,
+                          "truncated_normal")
+    unit = _k_uniform(kd, size, dt, 0.0, 1.0, layout)
+    out = torch.empty_like(unit)
+    for r in range(kd.shape[0] if size else 0):
+        nat.call("jxr_truncated_normal_from_unit", _ptr(_raw16(unit[r], dt)),
+                 _ptr(_raw16(lo, dt)), 1, _ptr(_raw16(hi, dt)), 1, size, _FLOAT_CODE[dt],
+                 _ptr(_raw16(out[r], dt)), _stream())
+    return _rebatch(out.reshape(bshape + shape), nb)
+
+
+# ---- randint (R/random.R:306-359) -------------------------------------------------------------
+
+_INT_INFO = {"int8": (8, True), "int16": (16, True), "int32": (32, True), "int64": (64, True),
+             "uint8": (8, False), "uint16": (16, False), "uint32": (32, False),
+             "uint64": (64, False)}
+
+
+def _int_range(bits, signed):
+    return (-(1 << (bits - 1)), (1 << (bits - 1)) - 1) if signed else (0, (1 << bits) - 1)
+
+
+def _wrap_int(v, bits, signed):
+    v &= (1 << bits) - 1
+    return v - (1 << bits) if signed and v >> (bits - 1) else v
+
+
+def _int_bound(x, name):
+    """A randint bound as (numpy object array of exact Python ints, dtype name): whole
+    numbers become the default int dtype (R/random.R:126-130), integer arrays keep their
+    (canonical) dtype, other floats are converted to the default int by truncation
+    (R/random.R:333-334)."""
+    x, nb = _unbatch(x)
+    if nb:
+        raise JaxNotImplementedError("batched sampler parameters are not supported")
+    dint = default_int()
+    if isinstance(x, torch.Tensor):
+        a, adt = x.detach().cpu().numpy(), _NAME[x.dtype]
+    else:
+        a = np.asarray(x)
+        adt = None if a.dtype.kind in "fb" or not isinstance(x, np.ndarray) else a.dtype.name
+    if a.dtype.kind == "b":
+        a = a.astype(np.int64)
+    if adt is not None and adt in _INT_INFO:
+        dt = canonicalize_dtype(adt)
+        bits, signed = _INT_INFO[dt]
+        vals = np.vectorize(lambda v: _wrap_int(int(v), bits, signed), otypes=[object])(a) \
+            if a.size else a.astype(object)
+        return vals, dt
+    f = a.astype(np.float64)
+    bits, signed = _INT_INFO[dint]
+    lo, hi = _int_range(bits, signed)
+    if a.dtype.kind in "iu" or (f.size and np.all(np.isfinite(f)) and np.all(f == np.round(f))):
+        ints = [int(v) for v in (a.ravel() if a.dtype.kind in "iu" else f.ravel())]
+        for v in ints:
+            if not lo <= v <= hi:
+                raise JaxOverflowError(f"Python int {v} too large to convert to {dint}")
+        return np.array(ints, dtype=object).reshape(a.shape), dint
+
+    def trunc(v):  # float -> int conversion: toward zero, saturating, NaN -> 0
+        if v != v:
+            return 0
+        if v == float("inf"):
+            return hi
+        if v == float("-inf"):
+            return lo
+        return min(max(int(v), lo), hi)
+    return np.array([trunc(float(v)) for v in f.ravel()], dtype=object).reshape(f.shape), dint
+
+
+def random_randint(key, shape, minval, maxval, dtype=None):
+    """Integers uniform in [minval, maxval) (R/random.R:306-359): two draws of nbits-bit
+    random bits from the halves of split(key) combined modulo the span; dtypes narrower
+    than 32 bits sample in int32."""
+    k, _, nb = _check_key("randint", key)
+    dt = canonicalize_dtype(dtype if dtype is not None else "int")
+    shape = canon_shape(shape)
+    if dt not in _INT_INFO:
+        raise JaxTypeError(f"randint only accepts integer dtypes, got {dt}")
+    mn, mn_dt = _int_bound(minval, "minval")
+    mx, mx_dt = _int_bound(maxval, "maxval")
+    dbits, dsigned = _INT_INFO[dt]
+    if dbits < 32:  # sample in int32, bounds wrapped to int32 and clipped (:320-325)
+        lo_d, hi_d = _int_range(dbits, dsigned)
+        mn = np.vectorize(lambda v: min(max(_wrap_int(v, 32, True), lo_d), hi_d),
+                          otypes=[object])(mn) if mn.size else mn
+        mx = np.vectorize(lambda v: min(max(_wrap_int(v, 32, True), lo_d), hi_d + 1),
+                          otypes=[object])(mx) if mx.size else mx
+        sbits, ssigned = 32, True
+    else:
+        sbits, ssigned = dbits, dsigned
+    try:
+        b = tuple(np.broadcast_shapes(shape, mn.shape, mx.shape))
+    except ValueError:
+        b = None
+    if b != tuple(shape):
+        raise JaxValueError(
+            "randint parameter shapes must be broadcast-compatible with shape argument, and the "
+            "result of broadcasting the shapes must equal the shape argument, but got result "
+            f"{shape_str(b or np.broadcast_shapes(mn.shape, mx.shape))} for shape argument "
+            f"{shape_str(shape)}.")
+    smin, smax = _int_range(sbits, ssigned)
+    kd = _flat_keys(k)
+    size = _size(shape)
+    layout = _layout()
+    _check_size(size, layout)
+    dev = kd.device
+
+    def as_param(vals, f):
+        flat = [f(int(v)) for v in np.asarray(vals, dtype=object).ravel()]
+        if len(flat) != 1:
+            flat = [f(int(v)) for v in np.broadcast_to(np.asarray(vals, dtype=object),
+                                                       shape).ravel()]
+        t = torch.tensor([_wrap_int(v, 64, True) for v in flat], dtype=torch.int64)
+        return t.to(dev), (0 if len(flat) == 1 else 1)
+
+    clip = lambda v: min(max(v, smin), smax)  # noqa: E731 - convert_and_clip_integer
+    oor_t, oor_s = as_param(mx, lambda v: int(v > smax))
+    mn_t, mn_s = as_param(mn, clip)
+    mx_t, mx_s = as_param(mx, clip)
+    oor_t = oor_t.to(torch.uint8)
+    halves = _k_split(kd, (2,), layout)
+    hi = _k_bits(halves[:, 0].contiguous(), size, sbits, layout)
+    lo = _k_bits(halves[:, 1].contiguous(), size, sbits, layout)
+    out = torch.empty((kd.shape[0], size), dtype=_TORCH[dt], device=dev)
+    if size:
+        if mn_s == 0 and mx_s == 0:  # one call over every key's row
+            nat.call("jxr_randint_combine", _ptr(hi), _ptr(lo), kd.shape[0] * size, sbits,
+                     int(ssigned), _ptr(mn_t), 0, _ptr(mx_t), 0, _ptr(oor_t), 0, dbits,
+                     _ptr(out), _stream())
+        else:
+            for r in range(kd.shape[0]):
+                nat.call("jxr_randint_combine", _ptr(hi[r]), _ptr(lo[r]), size, sbits,
+                         int(ssigned), _ptr(mn_t), mn_s, _ptr(mx_t), mx_s, _ptr(oor_t),
+                         int(oor_t.numel() != 1), dbits, _ptr(out[r]), _stream())
+    return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
+
+
 # ---- erf_inv (R/lax.R:222) ---------------------------------------------------------------------
 
 def lax_erf_inv(x):

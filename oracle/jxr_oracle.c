@@ -271,15 +271,14 @@ static inline float rh(float f, int bf16) { return half_bits_to_f32(f32_to_half_
 static inline double bits_to_f64(uint64_t u) { double d; memcpy(&d, &u, 8); return d; }
 static inline uint64_t f64_to_bits(double d) { uint64_t u; memcpy(&u, &d, 8); return u; }
 
-/* log1p(y) for y <= 0 (and NaN), the argument erf_inv gives it (y = -x*x): the same
- * operations as the kernels' log1p_neg, so both round identically.  Method of W. J. Cody
- * and W. Waite, "Software Manual for the Elementary Functions" (1980): t = 1 + y =
- * 2^e m with m in [sqrt(1/2), sqrt(2)), log m = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ...)
- * with s = (m - 1) / (m + 1), |s| < 0.1716, ten terms; the rounding error of 1 + y is
- * added back as (y - (t - 1)) / t.  Within 2 ulp of a correctly rounded log1p. */
-static double log1p_neg(double y) {
-  const double t = 1.0 + y;
-  const double corr = (y - (t - 1.0)) * (double)(1.0f / (float)t);
+/* Logarithms in double precision after W. J. Cody and W. Waite, "Software Manual for the
+ * Elementary Functions" (1980), performing the same operations in the same order as the
+ * kernels (jaxr_b200/csrc/samplers.cuh), so both produce the same doubles: t = 2^e m with
+ * m in [sqrt(1/2), sqrt(2)), log m = 2 atanh(s) = 2 (s + s^3/3 + s^5/5 + ...) with
+ * s = (m - 1) / (m + 1), |s| < 0.1716, ten terms, plus a correction term corr added
+ * before the exponent part.  t = 0 gives -inf, t < 0 or NaN NaN, t = inf inf.  Within
+ * 2 ulp of correctly rounded results. */
+static double log_core(double t, double corr) {
   const uint64_t b64 = f64_to_bits(t);
   const uint32_t hi = (uint32_t)(b64 >> 32), mh = hi & 0x000FFFFFu;
   const int big = mh >= 0x6A09Eu; /* mantissa >= sqrt(2): use m / 2 */
@@ -307,10 +306,23 @@ static double log1p_neg(double y) {
   const double LN2_HI = 0x1.62e42fefa3800p-1, LN2_LO = 0x1.ef35793c76730p-45;
   double res = fma((double)e, LN2_HI, fma((double)e, LN2_LO, lm + corr));
   if (!(t > 0.0)) res = (t == 0.0) ? -INFINITY : NAN;
+  if (t == INFINITY) res = INFINITY;
   return res;
 }
 
+/* log1p(y) for y <= 0 (and NaN), the argument erf_inv gives it (y = -x*x): t = 1 + y and
+ * the rounding error of that sum added back as (y - (t - 1)) / t. */
+static double log1p_neg(double y) {
+  const double t = 1.0 + y;
+  const double corr = (y - (t - 1.0)) * (double)(1.0f / (float)t);
+  return log_core(t, corr);
+}
+
+/* log(x) for x > 0. */
+static double log_pos(double x) { return log_core(x, 0.0); }
+
 double orc_log1p_neg(double y) { return log1p_neg(y); }
+double orc_log_pos(double x) { return log_pos(x); }
 
 /* ---- erf_inv --------------------------------------------------------------------------- */
 
@@ -503,5 +515,224 @@ int orc_bernoulli(const uint32_t key[2], int p_dtype, double p, uint64_t size,
   for (int64_t t = 0; t < (int64_t)count; ++t)
     out[t] = orc_uniform_at(key, p_dtype, size, partitionable, 0.0, 1.0, 0,
                             begin + (uint64_t)t) < pc;
+  return 0;
+}
+
+/* ---- log-transform samplers (R/random.R:1422-1516) ------------------------------------- */
+
+/* u = uniform(lo, 1) in dtype (fused multiply-add, as the recorded samples have it), then
+ * exponential -log1p(-u) (:1431-1434), gumbel mode "low" -log(-log(u)) (:1488), logistic
+ * log(u) - log1p(-u) (:1512-1515), laplace sign(u) log1p(-|u|) (:1500-1504), with
+ * lo = 0, tiny, tiny, -1 + 2^-(nmant+1).  Each float operation is rounded to the dtype
+ * once; 16-bit dtypes evaluate each function in float32 and round the result to 16 bits,
+ * as XLA does. */
+double orc_sample_at(const uint32_t key[2], int kind, int dtype, uint64_t size,
+                     int partitionable, uint64_t i) {
+  switch (dtype) {
+    case ORC_F32: {
+      const double lo = kind == ORC_EXPONENTIAL ? 0.0
+                        : kind == ORC_LAPLACE   ? -1.0 + 0x1p-24
+                                                : 0x1p-126;
+      const float u = (float)orc_uniform_at(key, ORC_F32, size, partitionable, lo, 1.0, 1, i);
+      switch (kind) {
+        case ORC_EXPONENTIAL: return -(float)log1p_neg(-(double)u);
+        case ORC_GUMBEL: {
+          const float a = (float)log_pos((double)u);
+          return -(float)log_pos(-(double)a);
+        }
+        case ORC_LOGISTIC: {
+          const float a = (float)log_pos((double)u);
+          const float c = (float)log1p_neg(-(double)u);
+          return (float)(a - c);
+        }
+        default: {
+          const float l = (float)log1p_neg(-(double)fabsf(u));
+          return u < 0.0f ? -l : l;
+        }
+      }
+    }
+    case ORC_F64: {
+      const double lo = kind == ORC_EXPONENTIAL ? 0.0
+                        : kind == ORC_LAPLACE   ? -1.0 + 0x1p-53
+                                                : 0x1p-1022;
+      const double u = orc_uniform_at(key, ORC_F64, size, partitionable, lo, 1.0, 1, i);
+      switch (kind) {
+        case ORC_EXPONENTIAL: return -log1p_neg(-u);
+        case ORC_GUMBEL: return -log_pos(-log_pos(u));
+        case ORC_LOGISTIC: return log_pos(u) - log1p_neg(-u);
+        default: {
+          const double l = log1p_neg(-fabs(u));
+          return u < 0.0 ? -l : l;
+        }
+      }
+    }
+    case ORC_F16:
+    case ORC_BF16: {
+      const int bf = dtype == ORC_BF16;
+      const double tiny = bf ? 0x1p-126 : 0x1p-14;
+      const double lo = kind == ORC_EXPONENTIAL ? 0.0
+                        : kind == ORC_LAPLACE   ? -1.0 + (bf ? 0x1p-8 : 0x1p-11)
+                                                : tiny;
+      const float u = (float)orc_uniform_at(key, dtype, size, partitionable, lo, 1.0, 1, i);
+#define LG(v) rh((float)(v), bf)
+      switch (kind) {
+        case ORC_EXPONENTIAL: return -LG(log1p_neg(-(double)u));
+        case ORC_GUMBEL: return -LG(log_pos(-(double)LG(log_pos((double)u))));
+        case ORC_LOGISTIC: return rh(LG(log_pos((double)u)) - LG(log1p_neg(-(double)u)), bf);
+        default: {
+          const float l = LG(log1p_neg(-(double)fabsf(u)));
+          return u < 0.0f ? -l : l;
+        }
+      }
+#undef LG
+    }
+  }
+  return NAN;
+}
+
+int orc_sample(const uint32_t key[2], int kind, int dtype, uint64_t size, int partitionable,
+               uint64_t begin, uint64_t count, void* out) {
+  if (dtype < ORC_F32 || dtype > ORC_BF16) return 1;
+  if (kind < ORC_EXPONENTIAL || kind > ORC_LAPLACE) return 1;
+  if (begin > size || count > size - begin) return 2;
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t)
+    store_float(out, dtype, t,
+                orc_sample_at(key, kind, dtype, size, partitionable, begin + (uint64_t)t));
+  return 0;
+}
+
+/* ---- gumbel modes "high" and "highest" (R/random.R:1465-1489) ------------------------- */
+
+/* XLA shifts: amounts of 32 or more give 0. */
+static inline uint32_t xshl(uint32_t x, uint32_t s) { return s >= 32u ? 0u : x << s; }
+static inline uint32_t xshr(uint32_t x, uint32_t s) { return s >= 32u ? 0u : x >> s; }
+static inline uint32_t clz32(uint32_t x) { return x ? (uint32_t)__builtin_clz(x) : 32u; }
+
+/* R/random.R:1446-1462: u32 pair (hi, lo) to a float32 in (0, 1). */
+static float safe_int_to_float(uint32_t hi, uint32_t lo) {
+  const uint32_t hiclz = clz32(hi), loclz = clz32(lo);
+  uint32_t mant = xshl(hi, hiclz) | (hiclz == 32u ? xshl(lo, loclz) : xshr(lo, 32u - hiclz));
+  mant = xshr(mant, 32u - 23u - 1u) & ((1u << 23) - 1u);
+  uint32_t ex = xshl(126u - (hiclz == 32u ? 32u + loclz : hiclz), 23u);
+  ex &= (1u << 30) - (1u << 22);
+  return bits_f32(ex | mant);
+}
+
+/* Element i of random_gumbel(key, (size), dtype, mode): mode 0 "high", 1 "highest" (float32;
+ * other dtypes take "high").  Both draw a (2, size) array: row r of element i is linear
+ * index r * size + i. */
+double orc_gumbel_mode_at(const uint32_t key[2], int mode, int dtype, uint64_t size,
+                          int partitionable, uint64_t i) {
+  const uint64_t n2 = 2 * size;
+  if (mode == 1 && dtype == ORC_F32) {
+    const uint32_t b0 = (uint32_t)orc_bits_at(key, 32, n2, partitionable, i);
+    const uint32_t b1 = (uint32_t)orc_bits_at(key, 32, n2, partitionable, size + i);
+    uint32_t n0 = ~b0, n1 = ~b1;
+    n0 += (n1 == 0xFFFFFFFFu) ? 1u : 0u; /* carry of the 64-bit negation */
+    n1 += 1u;
+    const int flip = b0 < 0x80000000u;
+    const float x = flip ? safe_int_to_float(b0, b1) : safe_int_to_float(n0, n1);
+    if (flip) return -(float)log_pos(-(double)(float)log1p_neg(-(double)x));
+    return -(float)log_pos(-(double)(float)log_pos((double)x));
+  }
+  switch (dtype) {
+    case ORC_F32: {
+      const float h = (float)orc_uniform_at(key, ORC_F32, n2, partitionable, 0.0, 1.0, 1, i);
+      const float l = (float)orc_uniform_at(key, ORC_F32, n2, partitionable, 0.0, 1.0, 1, size + i);
+      const float x = h >= 0.5f ? h : (h + 0x1p-23f * l) + 0x1p-47f;
+      return -(float)log_pos(-(double)(float)log1p_neg(-(double)x));
+    }
+    case ORC_F64: {
+      const double h = orc_uniform_at(key, ORC_F64, n2, partitionable, 0.0, 1.0, 1, i);
+      const double l = orc_uniform_at(key, ORC_F64, n2, partitionable, 0.0, 1.0, 1, size + i);
+      const double x = h >= 0.5 ? h : (h + 0x1p-52 * l) + 0x1p-105;
+      return -log_pos(-log1p_neg(-x));
+    }
+    default: {
+      const int bf = dtype == ORC_BF16;
+      const float h = (float)orc_uniform_at(key, dtype, n2, partitionable, 0.0, 1.0, 1, i);
+      const float l = (float)orc_uniform_at(key, dtype, n2, partitionable, 0.0, 1.0, 1, size + i);
+      /* 2^-nmant low + max(2^-(2 nmant + 1), tiny), each operation rounded to 16 bits */
+      const float c = bf ? 0x1p-15f : 0x1p-14f;
+      const float x = h >= 0.5f ? h : rh(rh(h + rh((bf ? 0x1p-7f : 0x1p-10f) * l, bf), bf) + c, bf);
+      const float a = rh((float)log1p_neg(-(double)x), bf);
+      return -rh((float)log_pos(-(double)a), bf);
+    }
+  }
+}
+
+/* ---- truncated normal (R/random.R:586-603) -------------------------------------------- */
+
+/* the 16-bit float after the 16-bit value x toward +inf (up) or -inf */
+static float half_step(float x, int up, int bf) {
+  uint16_t b = f32_to_half_bits(x, bf);
+  const uint16_t inf = bf ? 0x7F80u : 0x7C00u;
+  if (isnan(x) || b == (up ? inf : (uint16_t)(0x8000u | inf))) return x;
+  if ((b & 0x7FFFu) == 0) b = up ? 0x0001u : 0x8001u; /* +-0: the smallest subnormal */
+  else if (up == !(b & 0x8000u)) b = (uint16_t)(b + 1); /* away from zero */
+  else b = (uint16_t)(b - 1);
+  return half_bits_to_f32(b, bf);
+}
+
+/* Element i of random_truncated_normal(key, lower, upper, (size), dtype), scalar bounds:
+ * a = erf(lower / sqrt2), b = erf(upper / sqrt2) in dtype (erf from libm, rounded),
+ * u = uniform(a, b) (fused multiply-add), sqrt2 * erf_inv(u) (fused Horner), clipped to
+ * [nextafter(lower, inf), nextafter(upper, -inf)]. */
+double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
+                               int partitionable, double lower, double upper, uint64_t i) {
+  switch (dtype) {
+    case ORC_F32: {
+      const float s2 = 1.41421356237309504880f, lo = (float)lower, hi = (float)upper;
+      const float a = (float)erf((double)(lo / s2)), b = (float)erf((double)(hi / s2));
+      const float u = (float)orc_uniform_at(key, ORC_F32, size, partitionable, a, b, 1, i);
+      const float x = s2 * orc_erfinv_f32(u, 1);
+      const float cl = nextafterf(lo, INFINITY), ch = nextafterf(hi, -INFINITY);
+      const float m = isnan(x) ? x : (cl >= x ? cl : x);
+      return isnan(m) ? m : (ch <= m ? ch : m);
+    }
+    case ORC_F64: {
+      const double s2 = 1.41421356237309504880;
+      const double a = erf(lower / s2), b = erf(upper / s2);
+      const double u = orc_uniform_at(key, ORC_F64, size, partitionable, a, b, 1, i);
+      const double x = s2 * orc_erfinv_f64(u, 1);
+      const double cl = nextafter(lower, INFINITY), ch = nextafter(upper, -INFINITY);
+      const double m = isnan(x) ? x : (cl >= x ? cl : x);
+      return isnan(m) ? m : (ch <= m ? ch : m);
+    }
+    default: {
+      const int bf = dtype == ORC_BF16;
+      const float s2 = rh(f64_to_f32_odd(1.41421356237309504880), bf);
+      const float lo = rh(f64_to_f32_odd(lower), bf), hi = rh(f64_to_f32_odd(upper), bf);
+      const float a = rh((float)erf((double)rh(lo / s2, bf)), bf);
+      const float b = rh((float)erf((double)rh(hi / s2, bf)), bf);
+      const float u = (float)orc_uniform_at(key, dtype, size, partitionable, a, b, 1, i);
+      const float e = rh(orc_erfinv_f32(u, 1), bf);
+      const float x = rh(s2 * e, bf);
+      const float cl = half_step(lo, 1, bf), ch = half_step(hi, 0, bf);
+      const float m = isnan(x) ? x : (cl >= x ? cl : x);
+      return isnan(m) ? m : (ch <= m ? ch : m);
+    }
+  }
+}
+
+int orc_gumbel_mode(const uint32_t key[2], int mode, int dtype, uint64_t size,
+                    int partitionable, void* out) {
+  if (dtype < ORC_F32 || dtype > ORC_BF16) return 1;
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)size; ++t)
+    store_float(out, dtype, t, orc_gumbel_mode_at(key, mode, dtype, size, partitionable, (uint64_t)t));
+  return 0;
+}
+
+int orc_truncated_normal(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
+                         double lower, double upper, uint64_t begin, uint64_t count, void* out) {
+  if (dtype < ORC_F32 || dtype > ORC_BF16) return 1;
+  if (begin > size || count > size - begin) return 2;
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t)
+    store_float(out, dtype, t,
+                orc_truncated_normal_at(key, dtype, size, partitionable, lower, upper,
+                                        begin + (uint64_t)t));
   return 0;
 }

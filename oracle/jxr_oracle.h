@@ -64,8 +64,10 @@ float orc_erfinv_f32(float x, int fma);
 double orc_erfinv_f64(double x, int fma);
 void orc_erfinv_arr(const void* x, int64_t n, int dtype, int fma, void* out);
 
-/* log1p(y) for y <= 0 as the kernels evaluate it (Cody and Waite reduction). */
+/* log1p(y) for y <= 0 and log(x) for x > 0 as the kernels evaluate them (Cody and Waite
+ * reduction). */
 double orc_log1p_neg(double y);
+double orc_log_pos(double x);
 
 /* Samplers (R/random.R:288-304, :502-508, :656-666).  dtype is an ORC_ code;
  * 16-bit results are returned as their raw bits in a uint16_t array.
@@ -87,6 +89,25 @@ double orc_uniform_at(const uint32_t key[2], int dtype, uint64_t size, int parti
                       double minval, double maxval, int mul_add_fma, uint64_t i);
 double orc_normal_at(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
                      int erfinv_fma, uint64_t i);
+
+/* Log-transform samplers (R/random.R:1422-1516): kind 0 exponential, 1 gumbel (mode
+ * "low"), 2 logistic, 3 laplace, in dtype (ORC_ code). */
+enum { ORC_EXPONENTIAL = 0, ORC_GUMBEL = 1, ORC_LOGISTIC = 2, ORC_LAPLACE = 3 };
+int orc_sample(const uint32_t key[2], int kind, int dtype, uint64_t size, int partitionable,
+               uint64_t begin, uint64_t count, void* out);
+double orc_sample_at(const uint32_t key[2], int kind, int dtype, uint64_t size,
+                     int partitionable, uint64_t i);
+
+/* random_gumbel modes "high" (0) and "highest" (1, float32) (R/random.R:1465-1489) and
+ * random_truncated_normal with scalar bounds (R/random.R:586-603). */
+int orc_gumbel_mode(const uint32_t key[2], int mode, int dtype, uint64_t size,
+                    int partitionable, void* out);
+double orc_gumbel_mode_at(const uint32_t key[2], int mode, int dtype, uint64_t size,
+                          int partitionable, uint64_t i);
+int orc_truncated_normal(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
+                         double lower, double upper, uint64_t begin, uint64_t count, void* out);
+double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
+                               int partitionable, double lower, double upper, uint64_t i);
 
 /* Number of OpenMP threads used by the array functions (0 = default). */
 void orc_set_threads(int n);

@@ -59,6 +59,13 @@ def lib():
         L.orc_uniform_at.restype = dbl
         L.orc_normal_at.argtypes = [u32p, i32, u64, i32, i32, u64]
         L.orc_normal_at.restype = dbl
+        L.orc_log_pos.argtypes = [dbl]
+        L.orc_log_pos.restype = dbl
+        L.orc_sample.argtypes = [u32p, i32, i32, u64, i32, u64, u64, vp]
+        L.orc_sample_at.argtypes = [u32p, i32, i32, u64, i32, u64]
+        L.orc_sample_at.restype = dbl
+        L.orc_gumbel_mode.argtypes = [u32p, i32, i32, u64, i32, vp]
+        L.orc_truncated_normal.argtypes = [u32p, i32, u64, i32, dbl, dbl, u64, u64, vp]
         L.orc_set_threads.argtypes = [i32]
         L.orc_get_threads.restype = i32
         _lib = L
@@ -180,6 +187,114 @@ def normal_at(key, dtype, size, partitionable, fma, idx):
     code = DTYPE_CODE[dtype]
     return np.array([L.orc_normal_at(k, code, int(size), int(bool(partitionable)), int(fma),
                                      int(i)) for i in idx])
+
+
+SAMPLE_KIND = {"exponential": 0, "gumbel": 1, "logistic": 2, "laplace": 3}
+
+
+def sample(key, kind, dtype, size, partitionable=True, begin=0, count=None):
+    """exponential / gumbel (mode "low") / logistic / laplace samples (R/random.R:1422-1516);
+    16-bit dtypes as raw uint16 bits."""
+    code = DTYPE_CODE[dtype]
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=NP_FLOAT[code])
+    rc = lib().orc_sample(_key(key), SAMPLE_KIND[kind], code, int(size),
+                          int(bool(partitionable)), int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_sample failed ({rc})")
+    return out
+
+
+def sample_at(key, kind, dtype, size, partitionable, idx):
+    L = lib()
+    k = _key(key)
+    return np.array([L.orc_sample_at(k, SAMPLE_KIND[kind], DTYPE_CODE[dtype], int(size),
+                                     int(bool(partitionable)), int(i)) for i in idx])
+
+
+def gumbel_mode(key, mode, dtype, size, partitionable=True):
+    """random_gumbel(key, (size), dtype, mode) for mode "high" or "highest"."""
+    code = DTYPE_CODE[dtype]
+    out = np.empty(int(size), dtype=NP_FLOAT[code])
+    rc = lib().orc_gumbel_mode(_key(key), {"high": 0, "highest": 1}[mode], code, int(size),
+                               int(bool(partitionable)), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_gumbel_mode failed ({rc})")
+    return out
+
+
+def truncated_normal(key, dtype, size, lower, upper, partitionable=True, begin=0, count=None):
+    code = DTYPE_CODE[dtype]
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=NP_FLOAT[code])
+    rc = lib().orc_truncated_normal(_key(key), code, int(size), int(bool(partitionable)),
+                                    float(lower), float(upper), int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_truncated_normal failed ({rc})")
+    return out
+
+
+INT_INFO = {"int8": (8, True), "int16": (16, True), "int32": (32, True), "int64": (64, True),
+            "uint8": (8, False), "uint16": (16, False), "uint32": (32, False),
+            "uint64": (64, False)}
+
+
+def _int_range(bits, signed):
+    return (-(1 << (bits - 1)), (1 << (bits - 1)) - 1) if signed else (0, (1 << bits) - 1)
+
+
+def _wrap(v, bits, signed):
+    v &= (1 << bits) - 1
+    return v - (1 << bits) if signed and v >> (bits - 1) else v
+
+
+def randint(key, shape, minval, maxval, dtype, partitionable=True):
+    """random_randint (R/random.R:308-359) for integer bounds, restated with exact Python
+    integers: minval/maxval are ints or integer arrays broadcastable to `shape`, already
+    in the bounds' dtype (values as given).  Returns a flat numpy array of `dtype`.
+
+    dtypes narrower than 32 bits sample in int32 with the bounds wrapped to int32 and
+    clipped to [min, max] and [min, max + 1] (:320-325); the sampling dtype's bounds are
+    clipped to its range, maxval beyond its maximum widens the span by one (:338-350); the
+    offset is ((hi % span) * (2^nbits % span) + lo % span) % span in nbits-bit unsigned
+    arithmetic with XLA's x % 0 = x (:351-358), hi and lo the nbits-bit draws of the two
+    halves of split(key)."""
+    dbits, dsigned = INT_INFO[dtype]
+    size = int(np.prod(shape, dtype=np.int64)) if len(shape) else 1
+    mn = [int(v) for v in np.broadcast_to(np.asarray(minval, dtype=object), shape).ravel()]
+    mx = [int(v) for v in np.broadcast_to(np.asarray(maxval, dtype=object), shape).ravel()]
+    if dbits < 32:
+        lo_d, hi_d = _int_range(dbits, dsigned)
+        mn = [min(max(_wrap(v, 32, True), lo_d), hi_d) for v in mn]
+        mx = [min(max(_wrap(v, 32, True), lo_d), hi_d + 1) for v in mx]
+        sbits, ssigned = 32, True
+    else:
+        sbits, ssigned = dbits, dsigned
+    smin, smax = _int_range(sbits, ssigned)
+    oor = [v > smax for v in mx]
+    mn = [min(max(v, smin), smax) for v in mn]
+    mx = [min(max(v, smin), smax) for v in mx]
+    M = 1 << sbits
+    ks = split(key, 2, partitionable)
+    hi = random_bits(ks[0], sbits, size, partitionable)
+    lo = random_bits(ks[1], sbits, size, partitionable)
+
+    def xrem(a, b):
+        return a if b == 0 else a % b
+
+    out = []
+    for i in range(size):
+        span = (mx[i] - mn[i]) % M
+        if mx[i] <= mn[i]:
+            span = 1
+        elif oor[i]:
+            span = (span + 1) % M
+        mult = xrem((1 << (sbits // 2)) % M, span)
+        mult = xrem(mult * mult % M, span)
+        off = xrem((xrem(int(hi[i]), span) * mult % M + xrem(int(lo[i]), span)) % M, span)
+        r = _wrap(mn[i] + off, sbits, ssigned)
+        out.append(_wrap(r, dbits, dsigned))
+    return np.array(out, dtype=np.dtype(dtype))
 
 
 def set_threads(n):

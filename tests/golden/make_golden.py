@@ -195,6 +195,20 @@ def case(name, source, op, args, dtype, shape, values, compare, **extra):
 
 # ---- the cases ---------------------------------------------------------------------------
 
+def _log_allowance(name):
+    """Ulp allowance of the log-transform samplers against the recorded values.  Their
+    logarithms are evaluated here to within an ulp of the correctly rounded result; the
+    reference's float32 values come from XLA's own float32 log/log1p, which is up to an ulp
+    from correctly rounded (its float64 values are correctly rounded; ours are within 3
+    ulp).  gumbel "high" takes log(-a) of a = log1p(-x) near -1, which multiplies a
+    one-ulp difference in a by 16 (test-random.R:10-27 allows 16 ulp for all samplers)."""
+    if name in ("exponential", "gumbel", "gumbel_highest", "laplace", "logistic"):
+        return {"max_ulp": 3}
+    if name == "gumbel_high":
+        return {"max_ulp": 16}
+    return {}
+
+
 def build(ref):
     tt = os.path.join(ref, "tests", "testthat")
     prng = os.path.join(tt, "test-prng.R")
@@ -284,14 +298,33 @@ def build(ref):
         "bernoulli": ("bernoulli", {"seed": 7, "shape": [8], "p": 0.3}),
         "bernoulli_high": ("bernoulli", {"seed": 7, "shape": [8], "p": 0.3, "mode": "high"}),
         "bernoulli_vec": ("bernoulli", {"seed": 7, "shape": [3], "p": [0.1, 0.5, 0.9]}),
+        # randint (test-random.R:133-139)
+        "randint_0_6": ("randint", {"seed": 0, "shape": [6], "minval": 0, "maxval": 10}),
+        "randint_42_neg": ("randint", {"seed": 42, "shape": [5], "minval": -5, "maxval": 5}),
+        "randint_u8": ("randint", {"seed": 0, "shape": [6], "minval": 0, "maxval": 256,
+                                   "dtype": "uint8"}),
+        "randint_i8": ("randint", {"seed": 42, "shape": [6], "minval": -128, "maxval": 127,
+                                   "dtype": "int8"}),
+        "randint_vec": ("randint", {"seed": 0, "shape": [2, 3], "minval": [0, 10, 100],
+                                    "maxval": [5, 20, 1000]}),
+        "randint_empty": ("randint", {"seed": 0, "shape": [4], "minval": 5, "maxval": 5}),
+        # log-transform samplers and truncated normal (test-random.R:213-226)
+        "exponential": ("exponential", {"seed": 7, "shape": [4]}),
+        "gumbel": ("gumbel", {"seed": 7, "shape": [4]}),
+        "gumbel_high": ("gumbel", {"seed": 7, "shape": [4], "mode": "high"}),
+        "gumbel_highest": ("gumbel", {"seed": 7, "shape": [4], "mode": "highest"}),
+        "laplace": ("laplace", {"seed": 7, "shape": [4]}),
+        "logistic": ("logistic", {"seed": 7, "shape": [4]}),
+        "truncnorm": ("truncated_normal", {"seed": 7, "shape": [4], "lower": -1, "upper": 2}),
     }
     for name, (op, args) in rr_calls.items():
         (shape, vals, dt), line = rr[name]
         shape = [shape] if isinstance(shape, int) else shape
-        cmp = "exact" if dt in ("bool", "uint32") else "ulp16"
+        cmp = "ulp16" if dt.startswith("float") else "exact"
         if name.startswith("unif_"):
             args["result_as"] = "float32"  # the test compares jnp_astype(..., "float32")
-        cases.append(case(name, src(rand, line), op, args, dt, shape, vals, cmp))
+        cases.append(case(name, src(rand, line), op, args, dt, shape, vals, cmp,
+                          **_log_allowance(name)))
 
     # x64 samplers (test-random.R:158-206).
     x64ref = named_list(rand, "ref", indent="  ")
@@ -301,12 +334,21 @@ def build(ref):
         "uniform_42_23_m": ("uniform", {"seed": 42, "shape": [2, 3], "minval": -2, "maxval": 3}),
         "normal_0_5": ("normal", {"seed": 0, "shape": [5]}),
         "np_uniform_0_5": ("uniform", {"seed": 0, "shape": [5], "partitionable": False}),
+        "randint_0_6": ("randint", {"seed": 0, "shape": [6], "minval": 0, "maxval": 10}),
+        "randint_42_neg": ("randint", {"seed": 42, "shape": [5], "minval": -5, "maxval": 5}),
+        "exponential": ("exponential", {"seed": 7, "shape": [4]}),
+        "gumbel": ("gumbel", {"seed": 7, "shape": [4]}),
+        "truncnorm": ("truncated_normal", {"seed": 7, "shape": [4], "lower": -1, "upper": 2}),
     }
     for name, (op, args) in x64_calls.items():
         (shape, vals, dt), line = x64ref[name]
         shape = [shape] if isinstance(shape, int) else shape
         args = dict(args, x64=True)
-        cases.append(case(f"x64_{name}", src(rand, line), op, args, dt, shape, vals, "ulp16"))
+        # the reference holds its float64 truncated normal to 1e-14 relative (test-random.R:193)
+        cmp = ("exact" if not dt.startswith("float") else
+               "rel:1e-14" if name == "truncnorm" else "ulp16")
+        cases.append(case(f"x64_{name}", src(rand, line), op, args, dt, shape, vals, cmp,
+                          **_log_allowance(name)))
     (shape, vals, dt), line = rr["uniform_0_5"]
     ln206 = next(k + 1 for k, l in enumerate(text) if 'random_uniform(k0, 5, "float32")' in l)
     cases.append(case("x64_uniform_0_5_f32", src(rand, ln206), "uniform",

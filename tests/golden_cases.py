@@ -42,6 +42,8 @@ def expected(case):
         a = np.array([_f(v) for v in vals], dtype=np.float64).astype(dt)
     elif dt == "bool":
         a = np.array(vals, dtype=bool)
+    elif dt.startswith("int"):
+        a = np.array([int(v) for v in vals], dtype=np.int64).astype(dt)
     else:
         a = np.array([int(v) for v in vals], dtype=np.uint64).astype(dt)
     return a.reshape(shape)
@@ -80,7 +82,7 @@ def check(case, got):
     if tuple(got.shape) != tuple(want.shape):
         return False, f"shape {got.shape} != {want.shape}"
     cmp = case["compare"]
-    if want.dtype.kind in "ub":
+    if want.dtype.kind in "uib":
         ok = np.array_equal(got.astype(want.dtype), want)
         return ok, "exact" if ok else f"got {got.ravel().tolist()} want {want.ravel().tolist()}"
     got = got.astype(want.dtype)
@@ -226,6 +228,22 @@ def evaluate(case, be):
                 bool).reshape(shape)
         u = np.asarray(be.uniform(k, dt, shape_size(shape), part, 0.0, 1.0)).reshape(shape)
         return u < np.asarray(p, dtype=npdt)
+    if op == "randint":
+        dt = a.get("dtype", "int64" if x64 else "int32")
+        shape = tuple(a["shape"])
+        return np.asarray(be.randint(key_of(a["seed"]), shape, a["minval"], a["maxval"], dt,
+                                     part)).reshape(shape)
+    if op in ("exponential", "gumbel", "laplace", "logistic", "truncated_normal"):
+        dt = float_dtype(a)
+        shape = tuple(a["shape"])
+        k = key_of(a["seed"])
+        n = shape_size(shape)
+        if op == "truncated_normal":
+            out = be.truncated_normal(k, dt, n, part, float(a["lower"]), float(a["upper"]))
+        else:
+            out = be.sample(k, op, dt, n, part, a.get("mode", "low"))
+        out = np.asarray(out).reshape(shape)
+        return bits_to_float32(out, dt) if dt in ("float16", "bfloat16") else out
     if op == "erf_inv":
         dt = a["dtype"]
         xs = np.array([_f(v) for v in a["x"]], dtype=np.float64).astype(dt)
@@ -281,3 +299,14 @@ class OracleBackend:
 
     def erfinv(self, xs, dt):
         return self.o.erfinv(xs, dt, fma=self.erfinv_fma)
+
+    def randint(self, key, shape, mn, mx, dt, part):
+        return self.o.randint(key, shape, mn, mx, dt, part)
+
+    def sample(self, key, kind, dt, n, part, mode="low"):
+        if kind == "gumbel" and mode != "low":
+            return self.o.gumbel_mode(key, mode, dt, n, part)
+        return self.o.sample(key, kind, dt, n, part)
+
+    def truncated_normal(self, key, dt, n, part, lower, upper):
+        return self.o.truncated_normal(key, dt, n, lower, upper, part)

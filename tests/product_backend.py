@@ -84,6 +84,28 @@ class ProductBackend:
             return to_np(jr.lax_erf_inv(torch.tensor(np.asarray(xs))))
 
 
+    def randint(self, key, shape, mn, mx, dt, part):
+        with flags(dt.endswith("64") or self.x64, part):
+            mn = torch.tensor(mn, dtype=torch.int32) if isinstance(mn, list) else mn
+            mx = torch.tensor(mx, dtype=torch.int32) if isinstance(mx, list) else mx
+            return to_np(jr.random_randint(torch.tensor(np.asarray(key, np.uint32)), shape, mn,
+                                           mx, dt))
+
+    def sample(self, key, kind, dt, n, part, mode="low"):
+        fn = {"exponential": jr.random_exponential, "gumbel": jr.random_gumbel,
+              "laplace": jr.random_laplace, "logistic": jr.random_logistic}[kind]
+        kw = {"mode": mode} if kind == "gumbel" else {}
+        with flags(dt == "float64" or self.x64, part):
+            out = fn(torch.tensor(np.asarray(key, np.uint32)), (n,), dt, **kw)
+        return _raw(out, dt)
+
+    def truncated_normal(self, key, dt, n, part, lower, upper):
+        with flags(dt == "float64" or self.x64, part):
+            out = jr.random_truncated_normal(torch.tensor(np.asarray(key, np.uint32)), lower,
+                                             upper, (n,), dt)
+        return _raw(out, dt)
+
+
 def _raw(out, dt):
     """16-bit floats as their raw bits (as the oracle returns them)."""
     if dt in ("float16", "bfloat16"):

@@ -76,7 +76,8 @@ def test_golden_through_public_api(case):
     assert ok, f"{case['name']} ({case['source']}): {detail}"
     want = expected(case)
     if want.dtype.kind == "f" and np.all(np.isfinite(want)):
-        assert max_ulp(np.asarray(got).astype(want.dtype), want) == 0, case["source"]
+        assert max_ulp(np.asarray(got).astype(want.dtype), want) <= case.get("max_ulp", 0), \
+            case["source"]
 
 
 def _golden(name):

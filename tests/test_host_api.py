@@ -148,3 +148,66 @@ def test_key_array_surface():
     assert jr.random_key_impl(k) == "threefry2x32"
     assert jr.random_key_data(k) is k.data
     assert jr.random_Key(k) is k
+
+
+def test_derived_sampler_argument_errors():
+    # test-random.R:387, :393; R/random.R:1438-1444, :46-53
+    k = raw(2)
+    with pytest.raises(jr.JaxTypeError, match="randint only accepts integer dtypes, got float32"):
+        jr.random_randint(k, 3, 0, 5, dtype="float32")
+    with pytest.raises(jr.JaxValueError, match="Must provide valid mode for gumbel got: medium"):
+        jr.random_gumbel(k, 2, mode="medium")
+    for fn, name in ((jr.random_exponential, "exponential"), (jr.random_laplace, "laplace"),
+                     (jr.random_logistic, "logistic"), (jr.random_gumbel, "gumbel")):
+        with pytest.raises(jr.JaxValueError,
+                           match=f"dtype argument to `{name}` must be a float dtype, got int32"):
+            fn(k, 3, dtype="int32")
+    with pytest.raises(jr.JaxValueError, match="dtype argument to `truncated_normal` must be a "
+                                               "float dtype, got int32"):
+        jr.random_truncated_normal(k, -1, 1, 3, dtype="int32")
+    with pytest.raises(jr.JaxValueError, match=r"randint parameter shapes must be "
+                                               r"broadcast-compatible with shape argument.*"
+                                               r"for shape argument \(2,\)"):
+        jr.random_randint(k, 2, np.array([0, 1, 2], dtype=np.int32), 5)
+    with pytest.raises(jr.JaxValueError, match="split accepts a single key|randint accepts a "
+                                               "single key"):
+        jr.random_randint(raw(2, 2), 3, 0, 5)
+    with pytest.raises(jr.JaxOverflowError, match="too large to convert to int32"):
+        jr.random_randint(k, 3, 0, 1 << 40)
+
+
+def test_randint_bounds_follow_reference(monkeypatch):
+    """The bounds that reach the combine kernel (R/random.R:313-350): dtypes narrower than
+    32 bits sample in int32 with maxval clipped to max + 1; a maxval above the sampling
+    dtype's maximum flags the span to grow by one; whole floats are ints, other floats
+    truncate."""
+    calls = []
+
+    def fake_call(name, *args):
+        calls.append((name, args))
+
+    monkeypatch.setattr(jrr, "_flat_keys", lambda k: k.data.reshape(-1, 2))
+    monkeypatch.setattr(jrr, "_k_split", lambda kd, shape, layout: torch.zeros(
+        (kd.shape[0], 2, 2), dtype=U32))
+    monkeypatch.setattr(jrr, "_k_bits", lambda kd, size, bw, layout: torch.zeros(
+        (kd.shape[0], size), dtype=jrr._TORCH[f"uint{bw}"]))
+    monkeypatch.setattr(jrr.nat, "call", fake_call)
+    monkeypatch.setattr(jrr, "_ptr", lambda t: t)
+    monkeypatch.setattr(jrr, "_stream", lambda: None)
+
+    def bounds(*args, **kw):
+        calls.clear()
+        jr.random_randint(raw(2), *args, **kw)
+        (name, a), = calls
+        assert name == "jxr_randint_combine"
+        return (a[3], a[4], a[5].tolist(), a[7].tolist(), a[9].tolist(), a[11])
+
+    # nbits, signed, minval, maxval, out_of_range, out_bits
+    assert bounds(6, 0, 256, "uint8") == (32, 1, [0], [256], [0], 8)
+    assert bounds(6, -1000, 1000, "int8") == (32, 1, [-128], [128], [0], 8)
+    assert bounds(6, 0, 10) == (32, 1, [0], [10], [0], 32)
+    assert bounds(6, 0.0, 7.9) == (32, 1, [0], [7], [0], 32)  # 7.9 truncates
+    with jr.with_jax_config("jax_enable_x64", True):
+        assert bounds(6, 0, 1 << 40, "int32") == (32, 1, [0], [2**31 - 1], [1], 32)
+        assert bounds(6, -5, 1 << 33, "uint32") == (32, 0, [0], [2**32 - 1], [1], 32)
+        assert bounds(6, 0, 10, "uint64") == (64, 0, [0], [10], [0], 64)

@@ -5,7 +5,9 @@ them from tests/testthat/test-prng.R, test-random.R, test-scipy-special.R and th
 fixtures stateful_rng.json, lax_x32.json, lax_x64.json).  Integer and key data
 must agree exactly.  Floats are held to the reference's own rule (16 ulp, or the
 relative tolerance of the fixture) and, tighter, to 0 ulp: the oracle reproduces
-every recorded float bit for bit.
+every recorded float bit for bit, except the log-transform samplers, whose recorded
+float32 values carry XLA's own float32 logarithm; those are held to the case's
+"max_ulp" (3, and 16 for gumbel mode "high"; see make_golden._log_allowance).
 """
 
 import numpy as np
@@ -23,14 +25,16 @@ def test_oracle_matches_reference_golden(case):
     assert ok, f"{case['name']} ({case['source']}): {detail}"
     want = expected(case)
     if want.dtype.kind == "f":
-        assert max_ulp(np.asarray(got).astype(want.dtype), want) == 0, case["source"]
+        assert max_ulp(np.asarray(got).astype(want.dtype), want) <= case.get("max_ulp", 0), \
+            case["source"]
 
 
 def test_golden_covers_the_path():
     ops = {c["op"] for c in CASES}
     assert {"threefry_2x32", "seed", "split", "fold_in", "bits", "uniform", "normal",
             "bernoulli", "vmap_split", "vmap_fold_in", "vmap_uniform", "vmap_normal",
-            "erf_inv"} <= ops
+            "erf_inv", "randint", "exponential", "gumbel", "laplace", "logistic",
+            "truncated_normal"} <= ops
     # both layouts and x64 are pinned
     assert any(c["args"].get("partitionable") is False for c in CASES)
     assert any(c["args"].get("x64") for c in CASES)
