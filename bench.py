@@ -183,7 +183,15 @@ WORKLOADS = {
     "c3": "vmap(function(k) random_uniform(k, 1024, minval=-2, maxval=3))(random_split(random_key(7L), 65536)) float32",
     "c5": "x64: random_normal(random_fold_in(random_key(2024L), 17L), (16384, 16384)) float64 and "
           "random_bernoulli(same key, 0.3, same shape), one fused pass",
+    "exp": "random_exponential(random_key(7L), (8192, 8192)) float32",
+    "gumbel": "random_gumbel(random_key(7L), (8192, 8192)) float32, mode low",
+    "logistic": "random_logistic(random_key(7L), (8192, 8192)) float32",
+    "truncnorm": "random_truncated_normal(random_key(7L), -1, 2, (8192, 8192)) float32",
+    "randint": "random_randint(random_key(7L), (8192, 8192), 0L, 1000L) int32 "
+               "(split, two 32-bit draws, combine)",
 }
+
+_SAMPLER_WORKLOADS = {"exp": "exponential", "gumbel": "gumbel", "logistic": "logistic"}
 
 
 def workload_cpu_baseline(c, min_seconds=2.0):
@@ -196,6 +204,8 @@ def workload_cpu_baseline(c, min_seconds=2.0):
     lib = orc.lib()
     threads = os.cpu_count() or 1
     orc.set_threads(threads)
+    if c in _SAMPLER_WORKLOADS or c in ("truncnorm", "randint"):
+        return sampler_cpu_baseline(c, min_seconds)
     if c == "c1":
         key, n, words_per, fn = orc.seed(0), 1 << 20, 1, "bits"
     elif c in ("c2", "c2o"):
@@ -227,6 +237,46 @@ def workload_cpu_baseline(c, min_seconds=2.0):
     dt = time.perf_counter() - t0
     return {"value": reps * n * words_per / dt, "unit": "words/s", "cores": threads, "kind": "port",
             "sample": f"first {n} outputs of the workload, {reps} times (C restatement, OpenMP)"}
+
+
+def sampler_cpu_baseline(c, min_seconds=2.0):
+    """The derived-sampler workloads' first 2^22 outputs by the oracle port on all host
+    threads (randint: the two bit draws in C, the modular combine in numpy)."""
+    import ctypes
+
+    import numpy as np
+    from oracle import oracle as orc
+    lib = orc.lib()
+    threads = os.cpu_count() or 1
+    orc.set_threads(threads)
+    n, size = 1 << 22, 1 << 26
+    key = orc.seed(7)
+    k = (ctypes.c_uint32 * 2)(int(key[0]), int(key[1]))
+    out = np.empty(n, dtype=np.float32)
+    optr = out.ctypes.data_as(ctypes.c_void_p)
+
+    def once():
+        if c in _SAMPLER_WORKLOADS:
+            lib.orc_sample(k, orc.SAMPLE_KIND[_SAMPLER_WORKLOADS[c]], orc.F32, size, 1, 0, n, optr)
+        elif c == "truncnorm":
+            lib.orc_truncated_normal(k, orc.F32, size, 1, -1.0, 2.0, 0, n, optr)
+        else:
+            ks = orc.split(key, 2, True)
+            hi = orc.random_bits(ks[0], 32, size, True, 0, n).astype(np.uint64)
+            lo = orc.random_bits(ks[1], 32, size, True, 0, n).astype(np.uint64)
+            span = np.uint64(1000)
+            mult = np.uint64((1 << 32) % 1000)
+            off = ((hi % span) * mult % (np.uint64(1) << np.uint64(32)) + lo % span) % span
+            out.view(np.int32)[:] = off.astype(np.int32)
+    once()
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < min_seconds:
+        once()
+        reps += 1
+    dt = time.perf_counter() - t0
+    return {"value": reps * n / dt, "unit": "words/s", "cores": threads, "kind": "port",
+            "sample": f"first {n} outputs of the workload, {reps} times (C restatement, OpenMP"
+                      + (", numpy combine)" if c == "randint" else ")")}
 
 
 def run_workload(args):
@@ -262,6 +312,19 @@ def run_workload(args):
         key = jr.random_fold_in(jr.random_key(2024), 17)
         step = lambda: jr.random_normal_bernoulli(key, 0.3, (16384, 16384))
         words, blocks, out_bytes, dt = 1 << 29, 1 << 28, 9 << 28, "f64"
+    elif c in _SAMPLER_WORKLOADS or c == "truncnorm":
+        key = jr.random_key(7)
+        if c == "truncnorm":
+            step = lambda: jr.random_truncated_normal(key, -1, 2, (8192, 8192))
+        else:
+            fn = getattr(jr, "random_" + _SAMPLER_WORKLOADS[c])
+            step = lambda: fn(key, (8192, 8192))
+        words, blocks, out_bytes, dt = 1 << 26, 1 << 26, 4 << 26, "f32"
+    elif c == "randint":
+        key = jr.random_key(7)
+        step = lambda: jr.random_randint(key, (8192, 8192), 0, 1000)
+        # two 2^26-word draws (written and read back by the combine) and the int32 result
+        words, blocks, out_bytes, dt = 1 << 26, 1 << 27, 3 * (4 << 26), "int32"
     else:
         raise SystemExit(f"unknown config {c}")
     small = out_bytes < (1 << 30)
@@ -506,7 +569,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c4",
                     help="c4 = the 2^34-word bits request (the benchmark); c1, c2, c2o, c3, c5 = "
-                         "the other workloads, one GPU, one JSON line each; 'all' = every one")
+                         "the other workloads, one GPU, one JSON line each; exp, gumbel, "
+                         "logistic, truncnorm, randint = the derived samplers; 'all' = every "
+                         "secondary workload; 'samplers' = the derived samplers")
     ap.add_argument("--words-log2", type=int, default=34,
                     help="request size 2^k words (34 = the benchmark; smaller only for profiling)")
     ap.add_argument("--e2e-words", type=int, default=1 << 30)
@@ -523,9 +588,11 @@ def main():
     TOTAL = 1 << args.words_log2
     if args.impl == "reference":
         return run_reference(args)
-    if args.config == "all":
+    if args.config in ("all", "samplers"):
         rc = 0
-        for c in ("c1", "c2", "c2o", "c3", "c5"):
+        names = (["c1", "c2", "c2o", "c3", "c5"] if args.config == "all" else []) + list(
+            WORKLOADS)[5:]
+        for c in names:
             args.config = c
             rc |= run_workload(args)
         return rc

@@ -185,6 +185,36 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
                                    const void* upper, int64_t upper_stride, int64_t n, int dtype,
                                    void* out, void* stream);
 
+/* The shuffle of random_permutation (rnd_shuffle, R/random.R:402-413) over an array of
+ * shape (outer, n, inner), shuffling each 1-D slice along the middle axis (outer = inner = 1
+ * for a vector).  Writes perm[f] = the flat index of the source element that lands at flat
+ * position f (total = outer * n * inner < 2^31).  Each of the ceil(3 log(total) /
+ * log(2^32 - 1)) rounds splits the key, draws 32-bit sort keys and sorts stably.  scratch
+ * (256-byte aligned) holds jxr_shuffle_scratch_bytes(total) bytes.  Synchronises `stream`
+ * to read back the sort's bounds-check flag. */
+size_t jxr_shuffle_scratch_bytes(int64_t total);
+int jxr_shuffle(const uint32_t* key, int64_t outer, int64_t n, int64_t inner, int layout,
+                uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream);
+
+/* jnp_take along the middle axis: out[o][i][:] = src[o][idx[i]][:], rows of row_bytes bytes,
+ * src of shape (outer, n_src, row), out (outer, n_idx, row).  An index >= n_src is skipped
+ * and, if err (device int) is given, sets *err = 4. */
+int jxr_take(const void* src, int64_t outer, int64_t n_src, const uint32_t* idx, int64_t n_idx,
+             int64_t row_bytes, void* out, int* err, void* stream);
+
+/* random_choice with p (R/random.R:440-459).  With replacement: from unit = uniform(0, 1)
+ * draws (dtype float32/float64, n of them) and the cumulative sums cuml (m >= 1, dtype),
+ * out[i] = searchsorted_left(cuml, cuml[m-1] * (1 - unit[i])) as int32 or int64
+ * (out_bits).  Without replacement: x = gumbel draws, jxr_add_log adds log(p) in place,
+ * and jxr_argsort_float (stable; descending for top_k, ties to the lower index) orders
+ * them; -0 sorts as +0.  scratch: 256-byte aligned, jxr_argsort_scratch_bytes(n) bytes. */
+int jxr_choice_p_from_unit(const void* unit, int64_t n, int dtype, const void* cuml, int64_t m,
+                           int out_bits, void* out, void* stream);
+int jxr_add_log(void* x, const void* p, int64_t n, int dtype, void* stream);
+size_t jxr_argsort_scratch_bytes(int64_t n);
+int jxr_argsort_float(const void* x, int64_t n, int dtype, int descending, uint32_t* idx,
+                      void* scratch, size_t scratch_bytes, void* stream);
+
 /* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
  * element-wise for F32 or F64. */
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);

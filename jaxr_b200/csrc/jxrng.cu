@@ -30,6 +30,7 @@
 
 #include "blocks.cuh"
 #include "samplers.cuh"
+#include "sort.cuh"
 #include "threefry.cuh"
 
 namespace jxr {
@@ -578,6 +579,37 @@ __device__ __forceinline__ uint16_t half_next(float x, bool up, bool bf) {
   if ((b & 0x7FFFu) == 0) return up ? 0x0001u : 0x8001u;  // +-0 -> smallest subnormal
   const bool neg = b & 0x8000u;
   return (uint16_t)((up != neg) ? b + 1 : b - 1);
+}
+
+// random_choice with p and replace (R/random.R:446-450): r = total * (1 - u) in the dtype,
+// index = number of cumulative sums strictly below r (searchsorted, side left)
+template <class T>
+__global__ void k_choice_p(const T* __restrict__ unit, int64_t n, const T* __restrict__ cuml,
+                           int64_t m, int out_bits, void* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    T r;
+    if constexpr (sizeof(T) == 4) r = __fmul_rn(cuml[m - 1], __fsub_rn(1.0f, unit[i]));
+    else r = __dmul_rn(cuml[m - 1], __dsub_rn(1.0, unit[i]));
+    int64_t lo = 0, hi = m;  // first index with cuml[idx] >= r
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if (cuml[mid] < r) lo = mid + 1;
+      else hi = mid;
+    }
+    if (out_bits == 64) ((int64_t*)out)[i] = lo;
+    else ((int32_t*)out)[i] = (int32_t)lo;
+  }
+}
+
+// x[i] += log(p[i]) in the dtype (the log evaluated in double and rounded once)
+template <class T>
+__global__ void k_add_log(T* __restrict__ x, const T* __restrict__ p, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if constexpr (sizeof(T) == 4) x[i] = __fadd_rn(x[i], __double2float_rn(log_pos((double)p[i])));
+    else x[i] = __dadd_rn(x[i], log_pos(p[i]));
+  }
 }
 
 // truncated normal with per-element bounds (R/random.R:586-603) from the unit draw
@@ -1276,6 +1308,235 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
     default: k_trunc_unit<JXR_BF16><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out);
   }
   JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+// ---- permutation: stable radix sort of (random key, position) pairs ----------------------
+
+namespace {
+int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+struct SortScratch {
+  uint32_t *ka, *kb, *va, *vb, *counts, *totals, *keys6;
+  int* err;
+};
+
+// Bytes of scratch for a shuffle of `total` elements; with base != nullptr also the
+// pointers into it.
+size_t shuffle_scratch(int64_t total, char* base, SortScratch* s) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~(size_t)255;
+    return o;
+  };
+  const size_t nb = (size_t)total * 4;
+  const size_t o_ka = take(nb), o_kb = take(nb), o_va = take(nb), o_vb = take(nb);
+  const size_t o_counts = take((size_t)256 * (size_t)sort_tiles(total) * 4);
+  const size_t o_tot = take(256 * 4), o_keys = take(6 * 4), o_err = take(16);
+  if (base) {
+    s->ka = (uint32_t*)(base + o_ka);
+    s->kb = (uint32_t*)(base + o_kb);
+    s->va = (uint32_t*)(base + o_va);
+    s->vb = (uint32_t*)(base + o_vb);
+    s->counts = (uint32_t*)(base + o_counts);
+    s->totals = (uint32_t*)(base + o_tot);
+    s->keys6 = (uint32_t*)(base + o_keys);
+    s->err = (int*)(base + o_err);
+  }
+  return off;
+}
+
+// Sorts (k, v) by the low `bits` bits of k (a multiple of 8), stably; k2 / v2 are scratch
+// of the same size.  On return k / v point at the sorted pairs, k2 / v2 at free buffers.
+int sort_pairs(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n, int bits,
+               const SortScratch& s, cudaStream_t st) {
+  const int64_t nt = sort_tiles(n);
+  JXR_CUDA(cudaFuncSetAttribute(k_sort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kSortScatterSmem));
+  for (int shift = 0; shift < bits; shift += 8) {
+    k_sort_hist<<<(unsigned)nt, kSortThreads, 0, st>>>(k, n, shift, nt, s.counts);
+    k_sort_scan_rows<<<256, 1024, 0, st>>>(s.counts, nt, s.totals);
+    k_sort_scatter<<<(unsigned)nt, kSortThreads, kSortScatterSmem, st>>>(
+        k, v, n, shift, nt, s.counts, s.totals, k2, v2, s.err);
+    JXR_CUDA(cudaGetLastError());
+    std::swap(k, k2);
+    std::swap(v, v2);
+  }
+  return JXR_OK;
+}
+}  // namespace
+
+size_t jxr_shuffle_scratch_bytes(int64_t total) {
+  if (total < 0) return 0;
+  return shuffle_scratch(total, nullptr, nullptr);
+}
+
+int jxr_shuffle(const uint32_t* key, int64_t outer, int64_t n, int64_t inner, int layout,
+                uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream) {
+  if (outer < 0 || n < 0 || inner < 0)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "outer, n and inner must be >= 0");
+  if (layout != JXR_LAYOUT_ORIGINAL && layout != JXR_LAYOUT_PARTITIONABLE)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "layout must be 0 or 1, got %d", layout);
+  if ((n && outer > INT64_MAX / n) || (n && outer && inner > INT64_MAX / (outer * n)))
+    return fail(JXR_ERR_INVALID_ARGUMENT, "outer * n * inner overflows");
+  const int64_t total = outer * n * inner;
+  if (total > (int64_t)0x7FFFFFFF)
+    return fail(JXR_ERR_INVALID_ARGUMENT,
+                "shuffle of %lld elements: at most 2^31 - 1 (32-bit positions)", (long long)total);
+  if (!total) return JXR_OK;
+  if (!key || !perm || !scratch) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((uintptr_t)scratch % 256)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "scratch must be 256-byte aligned");
+  const size_t need = shuffle_scratch(total, nullptr, nullptr);
+  if (scratch_bytes < need)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "scratch of %zu bytes, need %zu", scratch_bytes, need);
+  SortScratch s;
+  shuffle_scratch(total, (char*)scratch, &s);
+  cudaStream_t st = (cudaStream_t)stream;
+  int grid, rc;
+  if ((rc = small_grid(total, &grid))) return rc;
+  // rounds = ceil(3 log(max(1, size)) / log(2^32 - 1)) (R/random.R:404-406)
+  const int rounds =
+      (int)std::ceil(3.0 * std::log(std::max(1.0, (double)total)) / std::log(4294967295.0));
+  int segbits = 0;
+  for (int64_t nseg = outer * inner; nseg > 1 && ((int64_t)1 << segbits) < nseg;) ++segbits;
+  JXR_CUDA(cudaMemsetAsync(s.err, 0, sizeof(int), st));
+  JXR_CUDA(cudaMemcpyAsync(s.keys6, key, 8, cudaMemcpyDeviceToDevice, st));
+  k_iota_u32<<<grid, 256, 0, st>>>(perm, total);
+  for (int r = 0; r < rounds; ++r) {
+    // ks = split(key); key = ks[0]; sort keys = random_bits(ks[1], 32, shape)
+    if ((rc = jxr_split(s.keys6, 1, 2, layout, s.keys6 + 2, stream))) return rc;
+    JXR_CUDA(cudaMemcpyAsync(s.keys6, s.keys6 + 2, 8, cudaMemcpyDeviceToDevice, st));
+    if ((rc = jxr_random_bits(s.keys6 + 4, 1, (uint64_t)total, 0, (uint64_t)total, layout, 32,
+                              s.ka, stream)))
+      return rc;
+    uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
+    k_iota_u32<<<grid, 256, 0, st>>>(v, total);
+    if ((rc = sort_pairs(k, v, k2, v2, total, 32, s, st))) return rc;
+    if (segbits) {  // then by segment (the slice along the middle axis), stably
+      k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
+      if ((rc = sort_pairs(k, v, k2, v2, total, (segbits + 7) / 8 * 8, s, st))) return rc;
+    }
+    k_shuffle_place<<<grid, 256, 0, st>>>(v, perm, total, n, inner, k2, s.err);
+    JXR_CUDA(cudaMemcpyAsync(perm, k2, (size_t)total * 4, cudaMemcpyDeviceToDevice, st));
+  }
+  JXR_CUDA(cudaGetLastError());
+  int err = 0;
+  JXR_CUDA(cudaMemcpyAsync(&err, s.err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  JXR_CUDA(cudaStreamSynchronize(st));
+  if (err) return fail(JXR_ERR_CUDA, "shuffle: a bounds check in the sort failed (code %d)", err);
+  return JXR_OK;
+}
+
+int jxr_take(const void* src, int64_t outer, int64_t n_src, const uint32_t* idx, int64_t n_idx,
+             int64_t row_bytes, void* out, int* err, void* stream) {
+  if (outer < 0 || n_src < 0 || n_idx < 0 || row_bytes < 0)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
+  const int64_t total_bytes = outer * n_idx * row_bytes;
+  if (!total_bytes) return JXR_OK;
+  if (!src || !idx || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  const uintptr_t al = (uintptr_t)src | (uintptr_t)out | (uintptr_t)row_bytes;
+  cudaStream_t st = (cudaStream_t)stream;
+  int grid, rc;
+#define JXR_TAKE(T)                                                                           \
+  {                                                                                           \
+    const int64_t row = row_bytes / (int64_t)sizeof(T);                                       \
+    if ((rc = small_grid(outer * n_idx * row, &grid))) return rc;                             \
+    k_take_rows<T><<<grid, 256, 0, st>>>((const T*)src, outer, n_src, idx, n_idx, row,         \
+                                         (T*)out, err);                                       \
+  }
+  if (al % 16 == 0) JXR_TAKE(uint4)
+  else if (al % 8 == 0) JXR_TAKE(uint2)
+  else if (al % 4 == 0) JXR_TAKE(uint32_t)
+  else if (al % 2 == 0) JXR_TAKE(uint16_t)
+  else JXR_TAKE(uint8_t)
+#undef JXR_TAKE
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_choice_p_from_unit(const void* unit, int64_t n, int dtype, const void* cuml, int64_t m,
+                           int out_bits, void* out, void* stream) {
+  if (dtype != JXR_F32 && dtype != JXR_F64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "dtype must be float32 or float64, got %d", dtype);
+  if (out_bits != 32 && out_bits != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "out_bits must be 32 or 64, got %d", out_bits);
+  if (n < 0 || m < 1) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0 and m >= 1");
+  if (!n) return JXR_OK;
+  if (!unit || !cuml || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == JXR_F32)
+    k_choice_p<float><<<grid, 256, 0, st>>>((const float*)unit, n, (const float*)cuml, m, out_bits, out);
+  else
+    k_choice_p<double><<<grid, 256, 0, st>>>((const double*)unit, n, (const double*)cuml, m, out_bits, out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_add_log(void* x, const void* p, int64_t n, int dtype, void* stream) {
+  if (dtype != JXR_F32 && dtype != JXR_F64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "dtype must be float32 or float64, got %d", dtype);
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!x || !p) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == JXR_F32) k_add_log<float><<<grid, 256, 0, st>>>((float*)x, (const float*)p, n);
+  else k_add_log<double><<<grid, 256, 0, st>>>((double*)x, (const double*)p, n);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+size_t jxr_argsort_scratch_bytes(int64_t n) { return jxr_shuffle_scratch_bytes(n); }
+
+int jxr_argsort_float(const void* x, int64_t n, int dtype, int descending, uint32_t* idx,
+                      void* scratch, size_t scratch_bytes, void* stream) {
+  if (dtype != JXR_F32 && dtype != JXR_F64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "dtype must be float32 or float64, got %d", dtype);
+  if (n < 0 || n > (int64_t)0x7FFFFFFF)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "n must be in [0, 2^31 - 1]");
+  if (!n) return JXR_OK;
+  if (!x || !idx || !scratch) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((uintptr_t)scratch % 256)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "scratch must be 256-byte aligned");
+  const size_t need = shuffle_scratch(n, nullptr, nullptr);
+  if (scratch_bytes < need)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "scratch of %zu bytes, need %zu", scratch_bytes, need);
+  SortScratch s;
+  shuffle_scratch(n, (char*)scratch, &s);
+  cudaStream_t st = (cudaStream_t)stream;
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  JXR_CUDA(cudaMemsetAsync(s.err, 0, sizeof(int), st));
+  // keys: ka = high (or only) word, kb = low word of float64
+  if (dtype == JXR_F32) k_float_sort_keys<false><<<grid, 256, 0, st>>>(x, n, descending != 0, s.ka, s.kb);
+  else k_float_sort_keys<true><<<grid, 256, 0, st>>>(x, n, descending != 0, s.ka, s.kb);
+  uint32_t *k, *v = s.va, *k2, *v2 = s.vb;
+  k_iota_u32<<<grid, 256, 0, st>>>(v, n);
+  if (dtype == JXR_F64) {
+    // LSD: by the low word, then the high words (gathered into the new order) stably
+    k = s.kb;
+    k2 = idx;  // free until the end: holds one ping-pong buffer of keys
+    if ((rc = sort_pairs(k, v, k2, v2, n, 32, s, st))) return rc;
+    uint32_t* hi_sorted = (k == s.kb) ? idx : s.kb;
+    k_gather_u32<<<grid, 256, 0, st>>>(s.ka, v, n, hi_sorted);
+    k = hi_sorted;
+    k2 = s.ka;
+  } else {
+    k = s.ka;
+    k2 = s.kb;
+  }
+  if ((rc = sort_pairs(k, v, k2, v2, n, 32, s, st))) return rc;
+  JXR_CUDA(cudaMemcpyAsync(idx, v, (size_t)n * 4, cudaMemcpyDeviceToDevice, st));
+  JXR_CUDA(cudaGetLastError());
+  int err = 0;
+  JXR_CUDA(cudaMemcpyAsync(&err, s.err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  JXR_CUDA(cudaStreamSynchronize(st));
+  if (err) return fail(JXR_ERR_CUDA, "argsort: a bounds check in the sort failed (code %d)", err);
   return JXR_OK;
 }
 

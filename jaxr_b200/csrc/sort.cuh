@@ -1,0 +1,270 @@
+// Stable LSD radix sort of (uint32 key, uint32 value) pairs and the shuffle built on it
+// (random_permutation, R/random.R:378-413).
+//
+// rnd_shuffle sorts the array by fresh 32-bit random keys, num_rounds times, with a
+// stable key-value sort (lax_sort_key_val).  Here every round sorts (key, position)
+// pairs: 8 bits per pass, each pass a histogram kernel, a scan of the per-tile counts and
+// a scatter.  The scatter ranks a tile's elements stably (warp match_any per chunk of 256
+// elements, chunks in index order), places them by digit in shared memory and writes each
+// digit's run to its global offset, so the global stores are contiguous runs.
+#pragma once
+
+#include <cstdint>
+
+namespace jxr {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortItems = 32;
+constexpr int kSortTile = kSortThreads * kSortItems;  // 8192 elements per tile
+// dynamic shared memory of the scatter: keys and values of a tile, per-warp digit counts,
+// four 256-entry tables
+constexpr int kSortScatterSmem = 2 * kSortTile * 4 + 8 * 256 * 4 + 4 * 256 * 4;
+
+// counts[d * ntiles + t] = number of keys of tile t whose digit at `shift` is d
+__global__ void __launch_bounds__(kSortThreads)
+k_sort_hist(const uint32_t* __restrict__ keys, int64_t n, int shift, int64_t ntiles,
+            uint32_t* __restrict__ counts) {
+  __shared__ uint32_t h[256];
+  h[threadIdx.x] = 0;
+  __syncthreads();
+  const int64_t base = (int64_t)blockIdx.x * kSortTile;
+#pragma unroll 4
+  for (int j = 0; j < kSortItems; ++j) {
+    const int64_t e = base + (int64_t)j * kSortThreads + threadIdx.x;
+    if (e < n) atomicAdd(&h[(keys[e] >> shift) & 255u], 1u);
+  }
+  __syncthreads();
+  counts[(int64_t)threadIdx.x * ntiles + blockIdx.x] = h[threadIdx.x];
+}
+
+// Exclusive scan of each digit's row of tile counts, in place; totals[d] = the row's sum.
+// One block of 1024 threads per digit.
+__global__ void __launch_bounds__(1024)
+k_sort_scan_rows(uint32_t* __restrict__ counts, int64_t ntiles, uint32_t* __restrict__ totals) {
+  __shared__ uint32_t sh[1024];
+  uint32_t* row = counts + (int64_t)blockIdx.x * ntiles;
+  const int64_t per = (ntiles + 1023) / 1024;
+  const int64_t b0 = (int64_t)threadIdx.x * per;
+  const int64_t b1 = b0 + per < ntiles ? b0 + per : ntiles;
+  uint32_t s = 0;
+  for (int64_t i = b0; i < b1; ++i) s += row[i];
+  sh[threadIdx.x] = s;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const uint32_t v = threadIdx.x >= (unsigned)off ? sh[threadIdx.x - off] : 0u;
+    __syncthreads();
+    sh[threadIdx.x] += v;
+    __syncthreads();
+  }
+  uint32_t run = sh[threadIdx.x] - s;
+  for (int64_t i = b0; i < b1; ++i) {
+    const uint32_t c = row[i];
+    row[i] = run;
+    run += c;
+  }
+  if (threadIdx.x == 1023) totals[blockIdx.x] = sh[1023];
+}
+
+// exclusive scan of v over the 256 threads of the block (all threads call it)
+__device__ __forceinline__ uint32_t block256_exclusive(uint32_t v, uint32_t* tmp) {
+  tmp[threadIdx.x] = v;
+  __syncthreads();
+  for (int off = 1; off < 256; off <<= 1) {
+    const uint32_t a = threadIdx.x >= (unsigned)off ? tmp[threadIdx.x - off] : 0u;
+    __syncthreads();
+    tmp[threadIdx.x] += a;
+    __syncthreads();
+  }
+  const uint32_t r = tmp[threadIdx.x] - v;
+  __syncthreads();
+  return r;
+}
+
+// One pass: pairs of tile t go, stably by digit, to their global positions.  Positions
+// outside [0, n) or a local rank outside the tile (which correct scans never give) are
+// skipped and set *err.
+__global__ void __launch_bounds__(kSortThreads)
+k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
+               int shift, int64_t ntiles, const uint32_t* __restrict__ counts,
+               const uint32_t* __restrict__ totals, uint32_t* __restrict__ keys_out,
+               uint32_t* __restrict__ vals_out, int* __restrict__ err) {
+  extern __shared__ uint32_t smem[];
+  uint32_t* s_keys = smem;                    // [kSortTile]
+  uint32_t* s_vals = s_keys + kSortTile;      // [kSortTile]
+  uint32_t* s_wc = s_vals + kSortTile;        // [8][256]
+  uint32_t* s_lbase = s_wc + 8 * 256;         // [256] tile-local start of each digit
+  uint32_t* s_gbase = s_lbase + 256;          // [256] global start of this tile's digit run
+  uint32_t* s_run = s_gbase + 256;            // [256]
+  uint32_t* s_tmp = s_run + 256;              // [256]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t base = (int64_t)blockIdx.x * kSortTile;
+  const int64_t rem = n - base;
+  const int cnt = rem < kSortTile ? (int)rem : kSortTile;
+
+  // tile histogram -> local and global digit starts
+  s_wc[tid] = 0;
+  __syncthreads();
+  for (int j = 0; j < kSortItems; ++j) {
+    const int i = j * kSortThreads + tid;
+    if (i < cnt) atomicAdd(&s_wc[(keys[base + i] >> shift) & 255u], 1u);
+  }
+  __syncthreads();
+  const uint32_t mine = s_wc[tid];
+  __syncthreads();
+  const uint32_t lb = block256_exclusive(mine, s_tmp);
+  const uint32_t gb = block256_exclusive(totals[tid], s_tmp);
+  s_lbase[tid] = lb;
+  s_run[tid] = lb;
+  s_gbase[tid] = gb + counts[(int64_t)tid * ntiles + blockIdx.x];
+  __syncthreads();
+
+  // stable local ranks, chunk by chunk (chunk j holds elements j*256 .. j*256+255 in order)
+  const unsigned lt = (1u << lane) - 1u;
+  for (int j = 0; j < kSortItems; ++j) {
+    const int i = j * kSortThreads + tid;
+    const bool valid = i < cnt;
+    const uint32_t key = valid ? keys[base + i] : 0u;
+    const uint32_t d = valid ? ((key >> shift) & 255u) : 256u;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s_wc[w * 256 + tid] = 0;
+    __syncthreads();
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, d);
+    const int rank = __popc(peers & lt);
+    if (valid && lane == __ffs(peers) - 1) s_wc[warp * 256 + d] = (uint32_t)__popc(peers);
+    __syncthreads();
+    {
+      uint32_t run = s_run[tid];
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        const uint32_t c = s_wc[w * 256 + tid];
+        s_wc[w * 256 + tid] = run;
+        run += c;
+      }
+      s_run[tid] = run;
+    }
+    __syncthreads();
+    if (valid) {
+      const uint32_t lp = s_wc[warp * 256 + d] + (uint32_t)rank;
+      if (lp < (uint32_t)kSortTile) {
+        s_keys[lp] = key;
+        s_vals[lp] = vals[base + i];
+      } else {
+        atomicExch(err, 1);
+      }
+    }
+    __syncthreads();
+  }
+
+  // write each digit's run to its global position
+  for (int i = tid; i < cnt; i += kSortThreads) {
+    const uint32_t key = s_keys[i];
+    const uint32_t d = (key >> shift) & 255u;
+    const int64_t g = (int64_t)s_gbase[d] + (int64_t)i - (int64_t)s_lbase[d];
+    if (g >= 0 && g < n) {
+      keys_out[g] = key;
+      vals_out[g] = s_vals[i];
+    } else {
+      atomicExch(err, 2);
+    }
+  }
+}
+
+__global__ void k_iota_u32(uint32_t* __restrict__ out, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = (uint32_t)i;
+}
+
+// segment id of the element at flat position f of an (outer, n, inner) array, the
+// segment being the 1-D slice along the middle axis: seg = o * inner + r
+__global__ void k_segment_keys(const uint32_t* __restrict__ pos, int64_t total, int64_t n,
+                               int64_t inner, uint32_t* __restrict__ seg) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t f = pos[i];
+    const int64_t o = f / (n * inner), r = f % inner;
+    seg[i] = (uint32_t)(o * inner + r);
+  }
+}
+
+// After a round's sort (segment-major, by key within a segment): the element at sorted
+// position p = seg * n + j moves to (o, j, r) of the array; its source is the element
+// that was at flat position pos[p], whose original index is perm[pos[p]].
+__global__ void k_shuffle_place(const uint32_t* __restrict__ pos, const uint32_t* __restrict__ perm,
+                                int64_t total, int64_t n, int64_t inner,
+                                uint32_t* __restrict__ perm_out, int* __restrict__ err) {
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < total;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t seg = p / n, j = p % n;
+    const int64_t o = seg / inner, r = seg % inner;
+    const int64_t dst = (o * n + j) * inner + r;
+    const uint32_t src = pos[p];
+    if (dst < total && (int64_t)src < total) perm_out[dst] = perm[src];
+    else atomicExch(err, 3);
+  }
+}
+
+// out[o][i][:] = src[o][idx[i]][:] for rows of `row` units of W bytes; idx values must be
+// < n_src (rows of src along the middle axis); others are skipped and set *err
+template <class W>
+__global__ void k_take_rows(const W* __restrict__ src, int64_t outer, int64_t n_src,
+                            const uint32_t* __restrict__ idx, int64_t n_idx, int64_t row,
+                            W* __restrict__ out, int* __restrict__ err) {
+  const int64_t total = outer * n_idx * row;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t u = t % row, oi = t / row;
+    const int64_t i = oi % n_idx, o = oi / n_idx;
+    const uint32_t s = idx[i];
+    if ((int64_t)s < n_src) out[t] = src[(o * n_src + s) * row + u];
+    else atomicExch(err, 4);
+  }
+}
+
+// out[f] = src[idx[f]] for elements of W bytes
+template <class W>
+__global__ void k_take_flat(const W* __restrict__ src, int64_t total,
+                            const uint32_t* __restrict__ idx, W* __restrict__ out,
+                            int* __restrict__ err) {
+  for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < total;
+       f += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t s = idx[f];
+    if ((int64_t)s < total) out[f] = src[s];
+    else atomicExch(err, 4);
+  }
+}
+
+// Sortable unsigned keys of floats (ascending order of value; -0 ordered as +0);
+// descending flips them.  float64 keys are split into high and low words.
+__device__ __forceinline__ uint32_t float_order_key(uint32_t b) {
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+template <bool kF64>
+__global__ void k_float_sort_keys(const void* __restrict__ x, int64_t n, bool descending,
+                                  uint32_t* __restrict__ hi, uint32_t* __restrict__ lo) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if constexpr (kF64) {
+      const double v = ((const double*)x)[i];
+      unsigned long long b = (unsigned long long)__double_as_longlong(v == 0.0 ? 0.0 : v);
+      b = (b & 0x8000000000000000ull) ? ~b : (b | 0x8000000000000000ull);
+      if (descending) b = ~b;
+      hi[i] = (uint32_t)(b >> 32);
+      lo[i] = (uint32_t)b;
+    } else {
+      const float v = ((const float*)x)[i];
+      uint32_t k = float_order_key(__float_as_uint(v == 0.0f ? 0.0f : v));
+      hi[i] = descending ? ~k : k;
+    }
+  }
+}
+
+// out[i] = src[idx[i]] for 32-bit words
+__global__ void k_gather_u32(const uint32_t* __restrict__ src, const uint32_t* __restrict__ idx,
+                             int64_t n, uint32_t* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = src[idx[i]];
+}
+
+}  // namespace jxr

@@ -1086,6 +1086,194 @@ def random_randint(key, shape, minval, maxval, dtype=None):
     return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
 
 
+# ---- permutation and choice (R/random.R:361-464) ---------------------------------------------
+
+def _norm_axis(axis, rank):
+    a = int(axis)
+    out = a + rank if a < 0 else a
+    if (out < 0 or out >= max(rank, 1)) and not (rank == 0 and out == 0):
+        raise JaxValueError(f"axis {a} is out of bounds for array of rank {rank}")
+    return out
+
+
+def _as_device_array(x):
+    """An array argument as a contiguous device tensor of its canonical dtype (R numbers:
+    default float; whole R integers: int32; logicals: bool)."""
+    if isinstance(x, torch.Tensor):
+        t = x
+    else:
+        a = np.asarray(x)
+        if a.dtype.kind == "f":
+            a = a.astype(default_float())
+        elif a.dtype.kind in "iu":
+            a = a.astype(canonicalize_dtype(a.dtype.name) if isinstance(x, np.ndarray)
+                         else "int32")
+        t = torch.from_numpy(np.ascontiguousarray(a))
+    name = canonicalize_dtype(t.dtype)
+    return t.to(device=_device(), dtype=_TORCH[name]).contiguous()
+
+
+def _k_shuffle(kd_row, outer, n, inner, layout):
+    """Flat source index of every position after rnd_shuffle (uint32 tensor)."""
+    total = outer * n * inner
+    perm = torch.empty(total, dtype=torch.uint32, device=kd_row.device)
+    if total:
+        nbytes = nat.lib().jxr_shuffle_scratch_bytes(total)
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=kd_row.device)
+        nat.call("jxr_shuffle", _ptr(kd_row), outer, n, inner, layout, _ptr(perm), _ptr(scratch),
+                 nbytes, _stream())
+    return perm
+
+
+def _take(x, idx, axis):
+    """jnp_take(x, idx, axis) for a device tensor x and uint32 (or non-negative int)
+    indices of any shape: result shape x.shape[:axis] + idx.shape + x.shape[axis+1:]."""
+    outer = _size(tuple(x.shape[:axis]))
+    n_src = x.shape[axis]
+    inner = _size(tuple(x.shape[axis + 1:]))
+    flat = idx.reshape(-1).contiguous()
+    if flat.dtype != torch.uint32:
+        flat = flat.to(torch.int64).to(torch.int32).view(torch.uint32)
+    out = torch.empty(tuple(x.shape[:axis]) + tuple(idx.shape) + tuple(x.shape[axis + 1:]),
+                      dtype=x.dtype, device=x.device)
+    nat.call("jxr_take", _ptr(x), outer, n_src, _ptr(flat), flat.numel(),
+             inner * x.element_size(), _ptr(out), None, _stream())
+    return out
+
+
+def random_permutation(key, x, axis=0, independent=False):
+    """A shuffled copy of x along `axis`, or of arange(x) for an integer x (int32)
+    (R/random.R:378-400).  Every round of rnd_shuffle (R/random.R:402-413) draws 32-bit sort
+    keys with the threefry kernels and sorts (key, position) pairs with a stable radix sort
+    on the device."""
+    k, _, nb = _check_key("permutation", key)
+    xv, xnb = _unbatch(x)
+    if xnb:
+        raise JaxNotImplementedError("batched permutation arguments are not supported")
+    ndim = xv.ndim if isinstance(xv, (torch.Tensor, np.ndarray)) else np.ndim(xv)
+    axis = _norm_axis(axis, max(ndim, 1))
+    kd = _flat_keys(k)
+    layout = _layout()
+    bshape = k.shape[:nb]
+    if ndim == 0:
+        if isinstance(xv, (torch.Tensor, np.ndarray)):
+            t = torch.as_tensor(xv)
+            if t.dtype.is_floating_point or t.dtype.is_complex or t.dtype == torch.bool:
+                raise JaxTypeError("x must be an integer or at least 1-dimensional")
+            n = int(t.item())
+        elif isinstance(xv, bool) or not isinstance(xv, numbers.Real) or xv != int(xv):
+            raise JaxTypeError("x must be an integer or at least 1-dimensional")
+        else:
+            n = int(xv)
+        n = max(n, 0)
+        outs = [_k_shuffle(kd[r], 1, n, 1, layout).view(torch.int32) for r in range(kd.shape[0])]
+        out = torch.stack(outs) if outs else torch.empty((0, n), dtype=torch.int32)
+        return _rebatch(out.reshape(bshape + (n,)), nb)
+    xt = _as_device_array(xv)
+    shape = tuple(xt.shape)
+    outer, n, inner = _size(shape[:axis]), shape[axis], _size(shape[axis + 1:])
+    outs = []
+    for r in range(kd.shape[0]):
+        if independent or xt.ndim == 1:
+            perm = _k_shuffle(kd[r], outer, n, inner, layout)
+            outs.append(_take(xt.reshape(-1), perm, 0).reshape(shape))
+        else:
+            ind = _k_shuffle(kd[r], 1, n, 1, layout)
+            outs.append(_take(xt, ind, axis))
+    out = torch.stack(outs) if outs else torch.empty((0,) + shape, dtype=xt.dtype)
+    return _rebatch(out.reshape(bshape + shape), nb)
+
+
+def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
+    """Samples of a (an integer n: arange(n)) along `axis` (R/random.R:417-464): with
+    replacement through randint; without, the first draws of a permutation; with p,
+    searchsorted of the cumulative sums (replace) or the top draws of gumbel + log(p)."""
+    k, _, nb = _check_key("choice", key)
+    if nb:
+        raise JaxNotImplementedError("random_choice takes a single key")
+    shape = canon_shape(shape)
+    av, anb = _unbatch(a)
+    if anb:
+        raise JaxNotImplementedError("batched choice arguments are not supported")
+    if isinstance(av, (torch.Tensor, np.ndarray)) and np.ndim(av) > 0:
+        arr = _as_device_array(av)
+        axis = _norm_axis(axis, arr.ndim)
+        n_inputs = arr.shape[axis]
+        adtype = arr.dtype
+    elif isinstance(av, (list, tuple)) and len(av) != 1:
+        arr = _as_device_array(av)
+        axis = _norm_axis(axis, arr.ndim)
+        n_inputs = arr.shape[axis]
+        adtype = arr.dtype
+    else:
+        arr = None
+        v = av[0] if isinstance(av, (list, tuple)) else av
+        v = v.item() if isinstance(v, (torch.Tensor, np.ndarray)) else v
+        n_inputs = int(v)
+        adtype = _TORCH[default_int()] if float(v) == int(v) else _TORCH[default_float()]
+    n_draws = _size(shape)
+    if n_draws == 0:
+        return torch.zeros(shape, dtype=adtype, device=_device())
+    if n_inputs <= 0:
+        raise JaxValueError("a must be greater than 0 unless no samples are taken")
+    if not replace and n_draws > n_inputs:
+        raise JaxValueError(f"Cannot take a larger sample (size {n_draws}) than population "
+                            f"(size {n_inputs}) when 'replace=False'")
+    if p is None:
+        if replace:
+            ind = random_randint(key, shape, 0, n_inputs)
+            result = ind if arr is None else _take(arr, ind, axis)
+        else:
+            kd = _flat_keys(k)
+            if arr is None:
+                perm = _k_shuffle(kd[0], 1, n_inputs, 1, _layout()).view(torch.int32)
+                result = perm[:n_draws].reshape(shape)
+            else:
+                ind = _k_shuffle(kd[0], 1, n_inputs, 1, _layout())[:n_draws]
+                result = _take(arr, ind.reshape(shape), axis)
+        return result
+    # promote_dtypes_inexact: float arrays keep their dtype, everything else is the
+    # default float
+    if isinstance(p, torch.Tensor):
+        pt = p
+        pdt = _NAME[p.dtype] if p.dtype.is_floating_point else default_float()
+    else:
+        pa = np.asarray(p)
+        pdt = (canonicalize_dtype(pa.dtype.name) if isinstance(p, np.ndarray) and pa.dtype.kind == "f"
+               else default_float())
+        pt = torch.from_numpy(np.ascontiguousarray(pa, dtype=np.float64))
+    pdt = canonicalize_dtype(pdt)
+    if pdt not in ("float32", "float64"):
+        raise JaxNotImplementedError(f"random_choice with p of dtype {pdt}")
+    if tuple(pt.shape) != (n_inputs,):
+        raise JaxValueError(f"p must be None or a 1D vector with the same size as a.shape[axis]. "
+                            f"p has shape {shape_str(tuple(pt.shape))} and a.shape[axis] is "
+                            f"{n_inputs}.")
+    dint = default_int()
+    kd = _flat_keys(k)
+    layout = _layout()
+    if replace:
+        # cumulative sums in the dtype, left to right (jnp_cumsum)
+        cuml_h = np.cumsum(pt.detach().cpu().numpy().astype(pdt), dtype=pdt)
+        cuml = torch.from_numpy(cuml_h).to(kd.device)
+        unit = _k_uniform(kd, n_draws, pdt, 0.0, 1.0, layout)
+        ind = torch.empty(n_draws, dtype=_TORCH[dint], device=kd.device)
+        nat.call("jxr_choice_p_from_unit", _ptr(unit), n_draws, _FLOAT_CODE[pdt], _ptr(cuml),
+                 n_inputs, _BITS[dint], _ptr(ind), _stream())
+    else:
+        g = random_gumbel(key, (n_inputs,), pdt, mode=mode).reshape(-1).contiguous()
+        pd = pt.to(device=kd.device, dtype=_TORCH[pdt]).contiguous()
+        nat.call("jxr_add_log", _ptr(g), _ptr(pd), n_inputs, _FLOAT_CODE[pdt], _stream())
+        order = torch.empty(n_inputs, dtype=torch.uint32, device=kd.device)
+        nbytes = nat.lib().jxr_argsort_scratch_bytes(n_inputs)
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=kd.device)
+        nat.call("jxr_argsort_float", _ptr(g), n_inputs, _FLOAT_CODE[pdt], 1, _ptr(order),
+                 _ptr(scratch), nbytes, _stream())
+        ind = order[:n_draws].view(torch.int32).to(_TORCH[dint])
+    ind = ind.reshape(shape)
+    return ind if arr is None else _take(arr, ind, axis)
+
+
 # ---- erf_inv (R/lax.R:222) ---------------------------------------------------------------------
 
 def lax_erf_inv(x):

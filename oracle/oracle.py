@@ -297,6 +297,69 @@ def randint(key, shape, minval, maxval, dtype, partitionable=True):
     return np.array(out, dtype=np.dtype(dtype))
 
 
+def shuffle(key, outer, n, inner, partitionable=True):
+    """rnd_shuffle (R/random.R:402-413) over an (outer, n, inner) array, shuffling each 1-D
+    slice along the middle axis: returns cur with cur[f] = the flat source index of the
+    element at flat position f.  Each of ceil(3 log(max(1, size)) / log(2^32 - 1)) rounds
+    splits the key (ks[0] carries on), draws 32-bit keys from ks[1] over the whole array and
+    sorts every slice stably by them (lax_sort_key_val is stable)."""
+    import math
+    total = outer * n * inner
+    rounds = int(math.ceil(3 * math.log(max(1, total)) / math.log(2 ** 32 - 1)))
+    cur = np.arange(total, dtype=np.int64)
+    for _ in range(rounds):
+        ks = split(key, 2, partitionable)
+        key = ks[0]
+        sk = random_bits(ks[1], 32, total, partitionable).reshape(outer, n, inner)
+        order = np.argsort(sk, axis=1, kind="stable")
+        cur = np.take_along_axis(cur.reshape(outer, n, inner), order, axis=1).ravel()
+    return cur
+
+
+def permutation(key, x, axis=0, independent=False, partitionable=True):
+    """random_permutation (R/random.R:378-400): an integer x permutes arange(x) (int32); an
+    array is shuffled along `axis`, slices independently or (the default) all by one
+    shuffled index vector."""
+    if np.ndim(x) == 0:
+        n = int(x)
+        return np.arange(max(n, 0), dtype=np.int32)[shuffle(key, 1, max(n, 0), 1, partitionable)]
+    x = np.asarray(x)
+    axis = axis + x.ndim if axis < 0 else axis
+    outer = int(np.prod(x.shape[:axis], dtype=np.int64))
+    n = x.shape[axis]
+    inner = int(np.prod(x.shape[axis + 1:], dtype=np.int64))
+    if independent or x.ndim == 1:
+        return x.ravel()[shuffle(key, outer, n, inner, partitionable)].reshape(x.shape)
+    ind = shuffle(key, 1, n, 1, partitionable)
+    return np.take(x, ind, axis=axis)
+
+
+def choice(key, a, shape=(), replace=True, p=None, axis=0, partitionable=True, x64=False):
+    """random_choice (R/random.R:417-464) for p = None, and for p with replace = True
+    (cumulative sum, r = total * (1 - u), searchsorted left)."""
+    shape = tuple(shape)
+    scalar = np.ndim(a) == 0
+    arr = None if scalar else np.asarray(a)
+    n_inputs = int(a) if scalar else arr.shape[axis]
+    n_draws = int(np.prod(shape, dtype=np.int64)) if shape else 1
+    dint = "int64" if x64 else "int32"
+    if p is None:
+        if replace:
+            ind = randint(key, shape, 0, n_inputs, dint, partitionable).reshape(shape)
+            return ind if scalar else np.take(arr, ind, axis=axis)
+        perm = permutation(key, n_inputs if scalar else arr, axis, False, partitionable)
+        ind_axis = 0 if scalar else axis
+        return np.take(perm, np.arange(n_draws), axis=ind_axis).reshape(
+            shape if scalar else arr.shape[:axis] + shape + arr.shape[axis + 1:])
+    fdt = "float64" if x64 else "float32"
+    pa = np.asarray(p, dtype=fdt)
+    cuml = np.cumsum(pa, dtype=fdt)
+    u = uniform(key, fdt, n_draws, partitionable).astype(fdt)
+    r = (cuml[-1] * (np.asarray(1, dtype=fdt) - u).astype(fdt)).astype(fdt)
+    ind = np.searchsorted(cuml, r, side="left").astype(dint).reshape(shape)
+    return ind if scalar else np.take(arr, ind, axis=axis)
+
+
 def set_threads(n):
     lib().orc_set_threads(int(n))
 

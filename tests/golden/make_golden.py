@@ -316,6 +316,12 @@ def build(ref):
         "laplace": ("laplace", {"seed": 7, "shape": [4]}),
         "logistic": ("logistic", {"seed": 7, "shape": [4]}),
         "truncnorm": ("truncated_normal", {"seed": 7, "shape": [4], "lower": -1, "upper": 2}),
+        # permutation and choice (test-random.R:338-344, :251)
+        "permutation": ("permutation", {"seed": 7, "x": 10}),
+        "perm_arr": ("permutation", {"seed": 7, "x": "arange12_f32_4x3"}),
+        "choice": ("choice", {"seed": 7, "a": 10, "shape": [4]}),
+        "choice_norep": ("choice", {"seed": 7, "a": 10, "shape": [4], "replace": False}),
+        "choice_p": ("choice", {"seed": 7, "a": 5, "shape": [6], "p": [0.1, 0.2, 0.3, 0.2, 0.2]}),
     }
     for name, (op, args) in rr_calls.items():
         (shape, vals, dt), line = rr[name]
@@ -325,6 +331,13 @@ def build(ref):
             args["result_as"] = "float32"  # the test compares jnp_astype(..., "float32")
         cases.append(case(name, src(rand, line), op, args, dt, shape, vals, cmp,
                           **_log_allowance(name)))
+
+    # choice from an array (test-random.R:342, values inline in the call)
+    ln = next(k + 1 for k, l in enumerate(open(rand).read().split("\n"))
+              if "random_choice(kd, jnp_arange(5L) * 10L, c(2, 2))" in l)
+    cases.append(case("choice_arr", src(rand, ln), "choice",
+                      {"seed": 7, "a": [0, 10, 20, 30, 40], "shape": [2, 2]}, "int32", [2, 2],
+                      [40, 20, 0, 20], "exact"))
 
     # x64 samplers (test-random.R:158-206).
     x64ref = named_list(rand, "ref", indent="  ")

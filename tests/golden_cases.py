@@ -244,6 +244,17 @@ def evaluate(case, be):
             out = be.sample(k, op, dt, n, part, a.get("mode", "low"))
         out = np.asarray(out).reshape(shape)
         return bits_to_float32(out, dt) if dt in ("float16", "bfloat16") else out
+    if op == "permutation":
+        x = a["x"]
+        if x == "arange12_f32_4x3":
+            x = np.arange(12, dtype=np.float32).reshape(4, 3)
+        return np.asarray(be.permutation(key_of(a["seed"]), x, part))
+    if op == "choice":
+        a_ = a["a"]
+        if isinstance(a_, list):
+            a_ = np.asarray(a_, dtype=np.int32)
+        return np.asarray(be.choice(key_of(a["seed"]), a_, tuple(a["shape"]),
+                                    a.get("replace", True), a.get("p"), part, x64))
     if op == "erf_inv":
         dt = a["dtype"]
         xs = np.array([_f(v) for v in a["x"]], dtype=np.float64).astype(dt)
@@ -310,3 +321,9 @@ class OracleBackend:
 
     def truncated_normal(self, key, dt, n, part, lower, upper):
         return self.o.truncated_normal(key, dt, n, lower, upper, part)
+
+    def permutation(self, key, x, part):
+        return self.o.permutation(key, x, 0, False, part)
+
+    def choice(self, key, a, shape, replace, p, part, x64):
+        return self.o.choice(key, a, shape, replace, p, 0, part, x64)

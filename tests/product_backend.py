@@ -106,6 +106,17 @@ class ProductBackend:
         return _raw(out, dt)
 
 
+    def permutation(self, key, x, part):
+        with flags(self.x64, part):
+            return to_np(jr.random_permutation(torch.tensor(np.asarray(key, np.uint32)), x))
+
+    def choice(self, key, a, shape, replace, p, part, x64):
+        with flags(x64, part):
+            a = torch.from_numpy(a) if isinstance(a, np.ndarray) else a
+            return to_np(jr.random_choice(torch.tensor(np.asarray(key, np.uint32)), a, shape,
+                                          replace, p))
+
+
 def _raw(out, dt):
     """16-bit floats as their raw bits (as the oracle returns them)."""
     if dt in ("float16", "bfloat16"):

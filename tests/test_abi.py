@@ -13,7 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 def declared():
     text = open(os.path.join(ROOT, "include", "jxrng.h")).read()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(jxr_\w+)\(", text, re.M)))
+    return sorted(set(re.findall(r"^(?:int|size_t|const char\*)\s+(jxr_\w+)\(", text, re.M)))
 
 
 def test_library_exports_every_declared_symbol():

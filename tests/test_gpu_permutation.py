@@ -1,0 +1,163 @@
+"""Parity of random_permutation / random_choice (R/random.R:361-464) with the CPU oracle,
+on the GPU: the device radix sort must reproduce the stable sort of every shuffle round
+exactly, for one, two and three rounds (n up to 2^22), independent slices along any axis,
+both counter layouts, and key batches."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import jaxr_b200 as jr
+from oracle import oracle as orc
+from product_backend import flags, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from jaxr_b200 import build
+    build.build()
+
+
+def dev_key(k):
+    return torch.tensor(np.asarray(k, dtype=np.uint32)).cuda()
+
+
+def rounds(n):
+    return int(math.ceil(3 * math.log(max(1, n)) / math.log(2 ** 32 - 1)))
+
+
+@pytest.mark.parametrize("part", [True, False])
+def test_permutation_of_n_exact(part):
+    key = orc.seed(2718)
+    for n in (0, 1, 2, 3, 10, 255, 256, 257, 1625, 1626, 8191, 8192, 8193, 100003):
+        with flags(False, part):
+            got = to_np(jr.random_permutation(dev_key(key), n))
+        want = orc.permutation(key, n, partitionable=part)
+        assert got.dtype == np.int32
+        assert np.array_equal(got, want), (n, rounds(n))
+
+
+def test_permutation_three_rounds():
+    """n = 2^22: three shuffle rounds (ceil(3 * 22 ln 2 / ln(2^32 - 1)) = 3), 512 tiles per
+    sort pass; compared in full with the oracle, and checked to be a permutation."""
+    key = orc.seed(5)
+    n = 1 << 22
+    assert rounds(n) == 3
+    got = to_np(jr.random_permutation(dev_key(key), n))
+    want = orc.permutation(key, n)
+    assert np.array_equal(got, want)
+    assert np.array_equal(np.sort(got), np.arange(n, dtype=np.int32))
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.float64, torch.int8, torch.int16,
+                                torch.bfloat16, torch.uint8, torch.int64])
+def test_permutation_of_arrays(dt):
+    key = orc.seed(9)
+    x = torch.arange(60).reshape(5, 4, 3).to(dt)
+    xn = x.float().numpy() if dt == torch.bfloat16 else x.numpy()
+    with flags(dt in (torch.float64, torch.int64)):
+        for axis in (0, 1, 2, -1):
+            got = jr.random_permutation(dev_key(key), x, axis=axis)
+            want = orc.permutation(key, xn, axis=axis)
+            assert np.array_equal(to_np(got), want), (dt, axis)
+            got = jr.random_permutation(dev_key(key), x, axis=axis, independent=True)
+            want = orc.permutation(key, xn, axis=axis, independent=True)
+            assert np.array_equal(to_np(got), want), (dt, axis, "independent")
+
+
+def test_permutation_independent_many_segments():
+    """(700, 3000) independent along axis 1: 2.1M elements, 700 segments -> two shuffle
+    rounds, each a 32-bit sort then a 16-bit segment sort."""
+    key = orc.seed(77)
+    x = torch.arange(700 * 3000, dtype=torch.int32).reshape(700, 3000)
+    got = to_np(jr.random_permutation(dev_key(key), x, axis=1, independent=True))
+    want = orc.permutation(key, x.numpy(), axis=1, independent=True)
+    assert np.array_equal(got, want)
+    got = to_np(jr.random_permutation(dev_key(key), x, axis=0, independent=True))
+    want = orc.permutation(key, x.numpy(), axis=0, independent=True)
+    assert np.array_equal(got, want)
+
+
+def test_permutation_key_batches():
+    keys = np.stack([orc.seed(s) for s in range(3)])
+    out = jr.vmap(lambda k: jr.random_permutation(k, 50))(dev_key(keys))
+    for r in range(3):
+        assert np.array_equal(to_np(out[r]), orc.permutation(keys[r], 50))
+
+
+def test_permutation_errors():
+    k = dev_key(orc.seed(0))
+    with pytest.raises(jr.JaxTypeError, match="x must be an integer or at least 1-dimensional"):
+        jr.random_permutation(k, 2.5)
+    with pytest.raises(jr.JaxValueError, match="axis 2 is out of bounds for array of rank 1"):
+        jr.random_permutation(k, torch.arange(4), axis=2)
+
+
+def test_choice_variants():
+    key = orc.seed(11)
+    a = np.arange(40, dtype=np.int32).reshape(8, 5)
+    at = torch.from_numpy(a)
+    for shape in ((3,), (2, 2), ()):
+        for replace in (True, False):
+            got = to_np(jr.random_choice(dev_key(key), 30, shape, replace))
+            want = orc.choice(key, 30, shape, replace)
+            assert np.array_equal(got.ravel(), np.asarray(want).ravel()), (shape, replace)
+            got = to_np(jr.random_choice(dev_key(key), at, shape, replace))
+            want = orc.choice(key, a, shape, replace)
+            assert np.array_equal(got.ravel(), np.asarray(want).ravel()), (shape, replace)
+    p = [0.05, 0.3, 0.15, 0.0, 0.5]
+    for x64 in (False, True):
+        with flags(x64):
+            got = to_np(jr.random_choice(dev_key(key), 5, (1000,), True, p))
+        assert np.array_equal(got, orc.choice(key, 5, (1000,), True, p, x64=x64))
+        assert not np.any(got == 3)
+    assert to_np(jr.random_choice(dev_key(key), 10, (0,))).shape == (0,)
+    with pytest.raises(jr.JaxValueError, match=r"Cannot take a larger sample \(size 5\)"):
+        jr.random_choice(dev_key(key), 3, 5, replace=False)
+    with pytest.raises(jr.JaxValueError, match="a must be greater than 0"):
+        jr.random_choice(dev_key(key), 0, 2)
+    with pytest.raises(jr.JaxValueError, match="p must be None or a 1D vector"):
+        jr.random_choice(dev_key(key), 5, 2, p=[0.5, 0.5])
+
+
+def test_choice_p_without_replacement():
+    """gumbel + log(p), top_k: the device argsort against numpy's stable argsort of the
+    same gumbel + log(p) values; zero-probability entries are never drawn."""
+    key = orc.seed(3)
+    p = np.array([0.1, 0.0, 0.3, 0.2, 0.15, 0.25], dtype=np.float32)
+    got = to_np(jr.random_choice(dev_key(key), 6, (5,), False, p))
+    g = orc.sample(key, "gumbel", "float32", 6)
+    lp = np.array([np.float32(orc.lib().orc_log_pos(float(v))) if v > 0 else -np.inf for v in p],
+                  dtype=np.float32)
+    want = np.argsort(-(g + lp).astype(np.float32), kind="stable")[:5]
+    assert np.array_equal(got, want)
+    assert 1 not in got
+
+
+@pytest.mark.parametrize("dt", ["float32", "float64"])
+def test_argsort_float_stable(dt):
+    """Descending and ascending stable argsort of floats with ties, both zeros and infinities,
+    against numpy (2^20 + 3 values: 129 tiles, the last one partial)."""
+    from jaxr_b200 import _native as nat
+    rng = np.random.default_rng(1)
+    n = (1 << 20) + 3
+    x = rng.integers(-50, 50, n).astype(dt) / 4
+    x[:5] = [0.0, -0.0, np.inf, -np.inf, 0.0]
+    xt = torch.from_numpy(x).cuda()
+    code = 0 if dt == "float32" else 1
+    for desc in (0, 1):
+        idx = torch.empty(n, dtype=torch.uint32, device="cuda")
+        nb = nat.lib().jxr_argsort_scratch_bytes(n)
+        scratch = torch.empty(nb, dtype=torch.uint8, device="cuda")
+        nat.call("jxr_argsort_float", xt.data_ptr(), n, code, desc, idx.data_ptr(),
+                 scratch.data_ptr(), nb, torch.cuda.current_stream().cuda_stream)
+        got = to_np(idx).astype(np.int64)
+        key = np.where(x == 0, 0.0, x)
+        want = np.argsort(-key if desc else key, kind="stable")
+        assert np.array_equal(got, want), (dt, desc)

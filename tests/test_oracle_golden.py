@@ -34,7 +34,7 @@ def test_golden_covers_the_path():
     assert {"threefry_2x32", "seed", "split", "fold_in", "bits", "uniform", "normal",
             "bernoulli", "vmap_split", "vmap_fold_in", "vmap_uniform", "vmap_normal",
             "erf_inv", "randint", "exponential", "gumbel", "laplace", "logistic",
-            "truncated_normal"} <= ops
+            "truncated_normal", "permutation", "choice"} <= ops
     # both layouts and x64 are pinned
     assert any(c["args"].get("partitionable") is False for c in CASES)
     assert any(c["args"].get("x64") for c in CASES)
