@@ -189,7 +189,18 @@ WORKLOADS = {
     "truncnorm": "random_truncated_normal(random_key(7L), -1, 2, (8192, 8192)) float32",
     "randint": "random_randint(random_key(7L), (8192, 8192), 0L, 1000L) int32 "
                "(split, two 32-bit draws, combine)",
+    "perm": "random_permutation(random_key(7L), 2^26) int32: 3 shuffle rounds, each 2^26 "
+            "32-bit sort keys and a 4-pass stable radix sort of (key, position) pairs",
 }
+
+# Kernels of this library one call launches (1 unless listed): randint = split, two bit
+# draws, combine; perm = iota, then per round split, bits and 4 x (histogram, scan,
+# scatter).
+LAUNCHES_PER_CALL = {"randint": 4, "perm": 1 + 3 * 14}
+
+# Algorithmic HBM bytes per element of one shuffle round: the 32-bit sort keys written
+# once, then per 8-bit pass one read and one write of the (key, position) pair.
+PERM_BYTES_PER_ROUND = 4 + 4 * 16
 
 _SAMPLER_WORKLOADS = {"exp": "exponential", "gumbel": "gumbel", "logistic": "logistic"}
 
@@ -206,6 +217,18 @@ def workload_cpu_baseline(c, min_seconds=2.0):
     orc.set_threads(threads)
     if c in _SAMPLER_WORKLOADS or c in ("truncnorm", "randint"):
         return sampler_cpu_baseline(c, min_seconds)
+    if c == "perm":  # the restatement (C bits, numpy stable argsort) on 2^22 elements
+        n = 1 << 22
+        orc.set_threads(threads)
+        orc.permutation(orc.seed(7), n)
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min_seconds:
+            orc.permutation(orc.seed(7), n)
+            reps += 1
+        dt = time.perf_counter() - t0
+        return {"value": reps * n / dt, "unit": "words/s", "cores": threads, "kind": "port",
+                "sample": f"random_permutation of 2^22 (3 rounds, as 2^26), {reps} times "
+                          "(C bits on all threads, numpy stable argsort on one)"}
     if c == "c1":
         key, n, words_per, fn = orc.seed(0), 1 << 20, 1, "bits"
     elif c in ("c2", "c2o"):
@@ -325,6 +348,11 @@ def run_workload(args):
         step = lambda: jr.random_randint(key, (8192, 8192), 0, 1000)
         # two 2^26-word draws (written and read back by the combine) and the int32 result
         words, blocks, out_bytes, dt = 1 << 26, 1 << 27, 3 * (4 << 26), "int32"
+    elif c == "perm":
+        key = jr.random_key(7)
+        step = lambda: jr.random_permutation(key, 1 << 26)
+        # 3 rounds: 2^26 cipher blocks and PERM_BYTES_PER_ROUND bytes per element each
+        words, blocks, out_bytes, dt = 1 << 26, 3 << 26, 3 * PERM_BYTES_PER_ROUND << 26, "int32"
     else:
         raise SystemExit(f"unknown config {c}")
     small = out_bytes < (1 << 30)
@@ -363,6 +391,16 @@ def run_workload(args):
     except (OSError, ValueError, KeyError):
         pass
     bps = blocks / (ms * 1e-3)
+    gbs = out_bytes / (ms * 1e-3) / 1e9
+    hbm = {"achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+           "frac": gbs / hbm_peak if hbm_peak else None}
+    if c == "perm":  # a sort: memory-bound, the cipher is 3 blocks per element
+        roofline = dict(hbm, bound="hbm", bytes_per_element=3 * PERM_BYTES_PER_ROUND,
+                        int_frac=bps / peak_blocks)
+    else:
+        roofline = {"bound": "int", "unit": "Tops/s", "achieved": bps * OPS_PER_BLOCK / 1e12,
+                    "peak": peak_blocks * OPS_PER_BLOCK / 1e12, "frac": bps / peak_blocks,
+                    "ops_per_block": OPS_PER_BLOCK, "hbm": hbm}
     cpu = None if args.no_cpu_baseline else workload_cpu_baseline(c)
     line = {
         "metric": "threefry 32-bit words/s (device-timed), secondary workload", "value": words / (ms * 1e-3),
@@ -373,13 +411,9 @@ def run_workload(args):
                    "cipher_blocks": blocks,
                    "l2": "flushed (256 MiB write) before every timed call" if small else
                          "outputs larger than L2"},
-        "roofline": {"bound": "int", "unit": "Tops/s", "achieved": bps * OPS_PER_BLOCK / 1e12,
-                     "peak": peak_blocks * OPS_PER_BLOCK / 1e12, "frac": bps / peak_blocks,
-                     "ops_per_block": OPS_PER_BLOCK,
-                     "hbm": {"achieved": out_bytes / (ms * 1e-3) / 1e9, "peak": hbm_peak,
-                             "unit": "GB/s",
-                             "frac": out_bytes / (ms * 1e-3) / 1e9 / hbm_peak if hbm_peak else None}},
-        "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": cpu,
+        "roofline": roofline,
+        "gpu_launches": args.steps * LAUNCHES_PER_CALL.get(c, 1), "clocks": clocks,
+        "cpu_baseline": cpu,
     }
     jr.enable_x64(old[0])
     jr.jax_config_update("jax_threefry_partitionable", old[1])
@@ -570,8 +604,9 @@ def main():
     ap.add_argument("--config", default="c4",
                     help="c4 = the 2^34-word bits request (the benchmark); c1, c2, c2o, c3, c5 = "
                          "the other workloads, one GPU, one JSON line each; exp, gumbel, "
-                         "logistic, truncnorm, randint = the derived samplers; 'all' = every "
-                         "secondary workload; 'samplers' = the derived samplers")
+                         "logistic, truncnorm, randint, perm = the derived samplers and the "
+                         "permutation; 'all' = every secondary workload; 'samplers' = the "
+                         "derived samplers and the permutation")
     ap.add_argument("--words-log2", type=int, default=34,
                     help="request size 2^k words (34 = the benchmark; smaller only for profiling)")
     ap.add_argument("--e2e-words", type=int, default=1 << 30)

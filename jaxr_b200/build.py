@@ -15,7 +15,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libjxrng.so")
 SOURCES = [os.path.join(CSRC, "jxrng.cu")]
-HEADERS = [os.path.join(CSRC, f) for f in ("threefry.cuh", "samplers.cuh", "blocks.cuh")] + [
+# every header the library includes: a change to any of them rebuilds it
+HEADERS = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")) + [
     os.path.join(ROOT, "include", "jxrng.h")]
 
 NVCC_FLAGS = [

@@ -1403,24 +1403,25 @@ int jxr_shuffle(const uint32_t* key, int64_t outer, int64_t n, int64_t inner, in
   for (int64_t nseg = outer * inner; nseg > 1 && ((int64_t)1 << segbits) < nseg;) ++segbits;
   JXR_CUDA(cudaMemsetAsync(s.err, 0, sizeof(int), st));
   JXR_CUDA(cudaMemcpyAsync(s.keys6, key, 8, cudaMemcpyDeviceToDevice, st));
-  k_iota_u32<<<grid, 256, 0, st>>>(perm, total);
+  // values are original flat indices: v[f] = index of the element now at position f
+  uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
+  k_iota_u32<<<grid, 256, 0, st>>>(v, total);
   for (int r = 0; r < rounds; ++r) {
     // ks = split(key); key = ks[0]; sort keys = random_bits(ks[1], 32, shape)
     if ((rc = jxr_split(s.keys6, 1, 2, layout, s.keys6 + 2, stream))) return rc;
     JXR_CUDA(cudaMemcpyAsync(s.keys6, s.keys6 + 2, 8, cudaMemcpyDeviceToDevice, st));
     if ((rc = jxr_random_bits(s.keys6 + 4, 1, (uint64_t)total, 0, (uint64_t)total, layout, 32,
-                              s.ka, stream)))
+                              k, stream)))
       return rc;
-    uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
-    k_iota_u32<<<grid, 256, 0, st>>>(v, total);
     if ((rc = sort_pairs(k, v, k2, v2, total, 32, s, st))) return rc;
     if (segbits) {  // then by segment (the slice along the middle axis), stably
       k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
       if ((rc = sort_pairs(k, v, k2, v2, total, (segbits + 7) / 8 * 8, s, st))) return rc;
+      k_shuffle_place<<<grid, 256, 0, st>>>(v, total, n, inner, v2, s.err);
+      std::swap(v, v2);
     }
-    k_shuffle_place<<<grid, 256, 0, st>>>(v, perm, total, n, inner, k2, s.err);
-    JXR_CUDA(cudaMemcpyAsync(perm, k2, (size_t)total * 4, cudaMemcpyDeviceToDevice, st));
   }
+  JXR_CUDA(cudaMemcpyAsync(perm, v, (size_t)total * 4, cudaMemcpyDeviceToDevice, st));
   JXR_CUDA(cudaGetLastError());
   int err = 0;
   JXR_CUDA(cudaMemcpyAsync(&err, s.err, sizeof(int), cudaMemcpyDeviceToHost, st));

@@ -4,8 +4,8 @@
 // rnd_shuffle sorts the array by fresh 32-bit random keys, num_rounds times, with a
 // stable key-value sort (lax_sort_key_val).  Here every round sorts (key, position)
 // pairs: 8 bits per pass, each pass a histogram kernel, a scan of the per-tile counts and
-// a scatter.  The scatter ranks a tile's elements stably (warp match_any per chunk of 256
-// elements, chunks in index order), places them by digit in shared memory and writes each
+// a scatter.  The scatter ranks a tile's elements stably (warp match_any per chunk of 32,
+// running counts per virtual warp), places them by digit in shared memory and writes each
 // digit's run to its global offset, so the global stores are contiguous runs.
 #pragma once
 
@@ -16,9 +16,9 @@ namespace jxr {
 constexpr int kSortThreads = 256;
 constexpr int kSortItems = 32;
 constexpr int kSortTile = kSortThreads * kSortItems;  // 8192 elements per tile
-// dynamic shared memory of the scatter: keys and values of a tile, per-warp digit counts,
-// four 256-entry tables
-constexpr int kSortScatterSmem = 2 * kSortTile * 4 + 8 * 256 * 4 + 4 * 256 * 4;
+// dynamic shared memory of the scatter: keys and values of a tile, digit counts of 16
+// virtual warps, three 256-entry tables
+constexpr int kSortScatterSmem = 2 * kSortTile * 4 + 16 * 256 * 4 + 3 * 256 * 4;
 
 // counts[d * ntiles + t] = number of keys of tile t whose digit at `shift` is d
 __global__ void __launch_bounds__(kSortThreads)
@@ -26,13 +26,17 @@ k_sort_hist(const uint32_t* __restrict__ keys, int64_t n, int shift, int64_t nti
             uint32_t* __restrict__ counts) {
   __shared__ uint32_t h[256];
   h[threadIdx.x] = 0;
-  __syncthreads();
   const int64_t base = (int64_t)blockIdx.x * kSortTile;
-#pragma unroll 4
+  uint32_t d[kSortItems];  // all loads in flight before the first atomic
+#pragma unroll
   for (int j = 0; j < kSortItems; ++j) {
     const int64_t e = base + (int64_t)j * kSortThreads + threadIdx.x;
-    if (e < n) atomicAdd(&h[(keys[e] >> shift) & 255u], 1u);
+    d[j] = e < n ? (keys[e] >> shift) & 255u : 256u;
   }
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kSortItems; ++j)
+    if (d[j] < 256u) atomicAdd(&h[d[j]], 1u);
   __syncthreads();
   counts[(int64_t)threadIdx.x * ntiles + blockIdx.x] = h[threadIdx.x];
 }
@@ -80,80 +84,99 @@ __device__ __forceinline__ uint32_t block256_exclusive(uint32_t v, uint32_t* tmp
   return r;
 }
 
-// One pass: pairs of tile t go, stably by digit, to their global positions.  Positions
-// outside [0, n) or a local rank outside the tile (which correct scans never give) are
-// skipped and set *err.
-__global__ void __launch_bounds__(kSortThreads)
+// One pass: pairs of tile t go, stably by digit, to their global positions.  The tile is
+// ranked by 16 "virtual warps" of 512 elements (warp w takes [w * 1024, (w + 1) * 1024) as
+// two halves, ranked interleaved for ILP), each in chunks of 32: match_any gives the lanes
+// of equal digit, and the group's leader adds the group's size to the virtual warp's
+// running count of that digit in shared memory with an atomic that returns the count
+// before it (the group's start).  One scan over (digit, virtual warp) then gives every
+// element its place in the tile; the tile is staged in shared memory by digit and each
+// digit's run written to its global offset, so the global stores are contiguous runs.
+// Positions outside [0, n) or a local rank outside the tile (which correct scans never
+// give) are skipped and set *err.
+__global__ void __launch_bounds__(kSortThreads, 2)
 k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
                int shift, int64_t ntiles, const uint32_t* __restrict__ counts,
                const uint32_t* __restrict__ totals, uint32_t* __restrict__ keys_out,
                uint32_t* __restrict__ vals_out, int* __restrict__ err) {
+  constexpr int kWarps = kSortThreads / 32, kPerWarp = kSortTile / kWarps;  // 1024
+  constexpr int kHalf = kPerWarp / 2, kChunks = kHalf / 32;                  // 512, 16
+  constexpr int kVW = 2 * kWarps;                                            // 16
   extern __shared__ uint32_t smem[];
   uint32_t* s_keys = smem;                    // [kSortTile]
   uint32_t* s_vals = s_keys + kSortTile;      // [kSortTile]
-  uint32_t* s_wc = s_vals + kSortTile;        // [8][256]
-  uint32_t* s_lbase = s_wc + 8 * 256;         // [256] tile-local start of each digit
+  uint32_t* s_wc = s_vals + kSortTile;        // [kVW][256] counts, then start positions
+  uint32_t* s_lbase = s_wc + kVW * 256;       // [256] tile-local start of each digit
   uint32_t* s_gbase = s_lbase + 256;          // [256] global start of this tile's digit run
-  uint32_t* s_run = s_gbase + 256;            // [256]
-  uint32_t* s_tmp = s_run + 256;              // [256]
+  uint32_t* s_tmp = s_gbase + 256;            // [256]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t base = (int64_t)blockIdx.x * kSortTile;
   const int64_t rem = n - base;
   const int cnt = rem < kSortTile ? (int)rem : kSortTile;
+  uint32_t* wc0 = s_wc + (2 * warp) * 256;
+  uint32_t* wc1 = wc0 + 256;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) wc0[lane * 16 + q] = 0;  // both halves' counters
+  __syncwarp();
 
-  // tile histogram -> local and global digit starts
-  s_wc[tid] = 0;
-  __syncthreads();
-  for (int j = 0; j < kSortItems; ++j) {
-    const int i = j * kSortThreads + tid;
-    if (i < cnt) atomicAdd(&s_wc[(keys[base + i] >> shift) & 255u], 1u);
+  const unsigned lt = (1u << lane) - 1u;
+  const int i0 = warp * kPerWarp + lane;  // element of chunk c: i0 + c * 32 (+ kHalf)
+  uint32_t kreg[2 * kChunks], vreg[2 * kChunks], pk[2 * kChunks];
+#pragma unroll
+  for (int c = 0; c < 2 * kChunks; ++c) {
+    const int i = i0 + c * 32;
+    kreg[c] = i < cnt ? keys[base + i] : 0u;
+    vreg[c] = i < cnt ? vals[base + i] : 0u;
+  }
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    const bool va = i0 + c * 32 < cnt, vb = i0 + (c + kChunks) * 32 < cnt;
+    const uint32_t da = va ? ((kreg[c] >> shift) & 255u) : 256u;
+    const uint32_t db = vb ? ((kreg[c + kChunks] >> shift) & 255u) : 256u;
+    const unsigned pa = __match_any_sync(0xFFFFFFFFu, da);
+    const unsigned pb = __match_any_sync(0xFFFFFFFFu, db);
+    const int la = __ffs(pa) - 1, lb_ = __ffs(pb) - 1;
+    uint32_t oa = 0, ob = 0;
+    if (va && lane == la) oa = atomicAdd(&wc0[da], (uint32_t)__popc(pa));
+    if (vb && lane == lb_) ob = atomicAdd(&wc1[db], (uint32_t)__popc(pb));
+    oa = __shfl_sync(0xFFFFFFFFu, oa, la);
+    ob = __shfl_sync(0xFFFFFFFFu, ob, lb_);
+    pk[c] = va ? (da << 16) | (oa + (uint32_t)__popc(pa & lt)) : 0xFFFFFFFFu;
+    pk[c + kChunks] = vb ? (db << 16) | (ob + (uint32_t)__popc(pb & lt)) : 0xFFFFFFFFu;
   }
   __syncthreads();
-  const uint32_t mine = s_wc[tid];
-  __syncthreads();
-  const uint32_t lb = block256_exclusive(mine, s_tmp);
+
+  // thread d: starts of digit d for each virtual warp within the tile, the tile's digit
+  // starts, and the global start of the tile's run of digit d
+  uint32_t run = 0;
+#pragma unroll
+  for (int w = 0; w < kVW; ++w) {
+    const uint32_t c = s_wc[w * 256 + tid];
+    s_wc[w * 256 + tid] = run;
+    run += c;
+  }
+  const uint32_t lbase = block256_exclusive(run, s_tmp);
   const uint32_t gb = block256_exclusive(totals[tid], s_tmp);
-  s_lbase[tid] = lb;
-  s_run[tid] = lb;
+#pragma unroll
+  for (int w = 0; w < kVW; ++w) s_wc[w * 256 + tid] += lbase;
+  s_lbase[tid] = lbase;
   s_gbase[tid] = gb + counts[(int64_t)tid * ntiles + blockIdx.x];
   __syncthreads();
 
-  // stable local ranks, chunk by chunk (chunk j holds elements j*256 .. j*256+255 in order)
-  const unsigned lt = (1u << lane) - 1u;
-  for (int j = 0; j < kSortItems; ++j) {
-    const int i = j * kSortThreads + tid;
-    const bool valid = i < cnt;
-    const uint32_t key = valid ? keys[base + i] : 0u;
-    const uint32_t d = valid ? ((key >> shift) & 255u) : 256u;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s_wc[w * 256 + tid] = 0;
-    __syncthreads();
-    const unsigned peers = __match_any_sync(0xFFFFFFFFu, d);
-    const int rank = __popc(peers & lt);
-    if (valid && lane == __ffs(peers) - 1) s_wc[warp * 256 + d] = (uint32_t)__popc(peers);
-    __syncthreads();
-    {
-      uint32_t run = s_run[tid];
-#pragma unroll
-      for (int w = 0; w < 8; ++w) {
-        const uint32_t c = s_wc[w * 256 + tid];
-        s_wc[w * 256 + tid] = run;
-        run += c;
-      }
-      s_run[tid] = run;
-    }
-    __syncthreads();
-    if (valid) {
-      const uint32_t lp = s_wc[warp * 256 + d] + (uint32_t)rank;
+  for (int c = 0; c < 2 * kChunks; ++c) {
+    if (pk[c] != 0xFFFFFFFFu) {
+      const uint32_t* wc = c < kChunks ? wc0 : wc1;
+      const uint32_t lp = wc[pk[c] >> 16] + (pk[c] & 0xFFFFu);
       if (lp < (uint32_t)kSortTile) {
-        s_keys[lp] = key;
-        s_vals[lp] = vals[base + i];
+        s_keys[lp] = kreg[c];
+        s_vals[lp] = vreg[c];
       } else {
         atomicExch(err, 1);
       }
     }
-    __syncthreads();
   }
+  __syncthreads();
 
   // write each digit's run to its global position
   for (int i = tid; i < cnt; i += kSortThreads) {
@@ -175,31 +198,31 @@ __global__ void k_iota_u32(uint32_t* __restrict__ out, int64_t n) {
     out[i] = (uint32_t)i;
 }
 
-// segment id of the element at flat position f of an (outer, n, inner) array, the
-// segment being the 1-D slice along the middle axis: seg = o * inner + r
-__global__ void k_segment_keys(const uint32_t* __restrict__ pos, int64_t total, int64_t n,
+// segment id of an element of an (outer, n, inner) array from its flat index f, the
+// segment being the 1-D slice along the middle axis: seg = o * inner + r.  An element
+// never leaves its slice, so its original index gives the segment of its current position.
+__global__ void k_segment_keys(const uint32_t* __restrict__ idx, int64_t total, int64_t n,
                                int64_t inner, uint32_t* __restrict__ seg) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t f = pos[i];
+    const int64_t f = idx[i];
     const int64_t o = f / (n * inner), r = f % inner;
     seg[i] = (uint32_t)(o * inner + r);
   }
 }
 
-// After a round's sort (segment-major, by key within a segment): the element at sorted
-// position p = seg * n + j moves to (o, j, r) of the array; its source is the element
-// that was at flat position pos[p], whose original index is perm[pos[p]].
-__global__ void k_shuffle_place(const uint32_t* __restrict__ pos, const uint32_t* __restrict__ perm,
-                                int64_t total, int64_t n, int64_t inner,
-                                uint32_t* __restrict__ perm_out, int* __restrict__ err) {
+// After a segmented round's sort (segment-major, by key within a segment) the element at
+// sorted position p = seg * n + j moves to (o, j, r): perm_out[(o n + j) inner + r] =
+// sorted[p], sorted holding original indices.
+__global__ void k_shuffle_place(const uint32_t* __restrict__ sorted, int64_t total, int64_t n,
+                                int64_t inner, uint32_t* __restrict__ perm_out,
+                                int* __restrict__ err) {
   for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < total;
        p += (int64_t)gridDim.x * blockDim.x) {
     const int64_t seg = p / n, j = p % n;
     const int64_t o = seg / inner, r = seg % inner;
     const int64_t dst = (o * n + j) * inner + r;
-    const uint32_t src = pos[p];
-    if (dst < total && (int64_t)src < total) perm_out[dst] = perm[src];
+    if (dst < total) perm_out[dst] = sorted[p];
     else atomicExch(err, 3);
   }
 }
