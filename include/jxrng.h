@@ -33,8 +33,8 @@
  *  - rnd_normal_real / lax_erf_inv              R/random.R:501-508, R/lax.R:222
  *  - rnd_bernoulli (mode "low")                 R/random.R:655-666
  * The reference reaches these through .Call(jaxr_compile/jaxr_execute)
- * (src/pjrt.cpp:255, :725) on the XLA CPU plugin; INTEGRATION.md shows the
- * .Call shim that binds this ABI instead.
+ * (src/pjrt.cpp:255, :725) on the XLA CPU plugin; a .Call shim over this ABI
+ * replaces them.
  */
 #ifndef JXRNG_H
 #define JXRNG_H
@@ -58,6 +58,9 @@ enum {
 
 /* layouts: the value of jax_threefry_partitionable */
 enum { JXR_LAYOUT_ORIGINAL = 0, JXR_LAYOUT_PARTITIONABLE = 1 };
+
+/* key implementations (R/prng.R:430-440) */
+enum { JXR_IMPL_THREEFRY = 0, JXR_IMPL_RBG = 1, JXR_IMPL_UNSAFE_RBG = 2 };
 
 /* floating dtypes (16-bit results are stored as their raw bits) */
 enum { JXR_F32 = 0, JXR_F64 = 1, JXR_F16 = 2, JXR_BF16 = 3 };
@@ -153,6 +156,10 @@ int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p
  * u from (-1 + 2^-(nmant+1), 1).  out: dtype[nkeys][count]. */
 int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
                uint64_t count, int layout, int kind, int dtype, void* out, void* stream);
+/* The same transforms of n random_bits values (the dtype's draw width: 32/64/16/8 bits for
+ * float32/float64/float16/bfloat16), e.g. the bits of an rbg key. */
+int jxr_sample_from_bits(const void* bits, int64_t n, int kind, int dtype, void* out,
+                         void* stream);
 
 /* randint (R/random.R:306-359) from its two draws: hi and lo are nbits-bit (32 or 64)
  * random_bits of the two halves of split(key); minval/maxval are the bounds already
@@ -177,6 +184,8 @@ int jxr_gumbel_rows(const void* row0, const void* row1, int64_t n, int mode, int
 int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
                          uint64_t count, int layout, int dtype, double lower, double upper,
                          void* out, void* stream);
+int jxr_truncated_normal_from_bits(const void* bits, int64_t n, int dtype, double lower,
+                                   double upper, void* out, void* stream);
 
 /* random_truncated_normal with per-element bounds: unit is the uniform(0, 1) draw of the
  * key (dtype[n]); lower and upper are dtype arrays with stride 0 (one value) or 1.  The erf
@@ -191,10 +200,11 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
  * position f (total = outer * n * inner < 2^31).  Each of the ceil(3 log(total) /
  * log(2^32 - 1)) rounds splits the key, draws 32-bit sort keys and sorts stably.  scratch
  * (256-byte aligned) holds jxr_shuffle_scratch_bytes(total) bytes.  Synchronises `stream`
- * to read back the sort's bounds-check flag. */
+ * to read back the sort's bounds-check flag.  impl: the key's implementation (JXR_IMPL_*;
+ * key is u32[2] for threefry2x32, u32[4] for rbg and unsafe_rbg). */
 size_t jxr_shuffle_scratch_bytes(int64_t total);
-int jxr_shuffle(const uint32_t* key, int64_t outer, int64_t n, int64_t inner, int layout,
-                uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream);
+int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t inner,
+                int layout, uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream);
 
 /* jnp_take along the middle axis: out[o][i][:] = src[o][idx[i]][:], rows of row_bytes bytes,
  * src of shape (outer, n_src, row), out (outer, n_idx, row).  An index >= n_src is skipped
@@ -214,6 +224,23 @@ int jxr_add_log(void* x, const void* p, int64_t n, int dtype, void* stream);
 size_t jxr_argsort_scratch_bytes(int64_t n);
 int jxr_argsort_float(const void* x, int64_t n, int dtype, int descending, uint32_t* idx,
                       void* scratch, size_t scratch_bytes, void* stream);
+
+/* The rbg and unsafe_rbg implementations (R/prng.R:382-426): XLA's RngBitGenerator,
+ * Philox4x32-10 with key (k0, k1) and 128-bit counter k0 | k1 << 32 | k2 << 64 | k3 << 96
+ * advanced by one per block of four 32-bit outputs (key: a device u32[4]).
+ * jxr_rbg_bits: elements [begin, begin + count) of a size-element request of bit_width-bit
+ * values (8/16 take the low bits of one 32-bit output per element, 64 two outputs, low
+ * first); new_key (device u32[4], may be NULL) receives the state after the whole request.
+ * jxr_rbg_blocks: blocks first + i * stride, i < n, 4 words each (unsafe_rbg split).
+ * jxr_rbg_unsafe_fold_in: keys[i] ^ row 9 of the (10, 4) request of rbg_seed(data[i]);
+ * keys u32[nkeys][4], data u32[ndata], broadcasting; lanes_from_first != 0 draws output i
+ * from row 9 + 10 i of data[0]'s request (rng_bit_generator under vmap). */
+int jxr_rbg_bits(const uint32_t* key, uint64_t size, uint64_t begin, uint64_t count, int bit_width,
+                 void* out, uint32_t* new_key, void* stream);
+int jxr_rbg_blocks(const uint32_t* key, uint64_t first, uint64_t stride, int64_t n, uint32_t* out,
+                   void* stream);
+int jxr_rbg_unsafe_fold_in(const uint32_t* keys, int64_t nkeys, const uint32_t* data, int64_t ndata,
+                           int lanes_from_first, uint32_t* out, void* stream);
 
 /* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
  * element-wise for F32 or F64. */

@@ -56,12 +56,17 @@ SIGNATURES = {
     "jxr_truncated_normal": [_vp, _i64, _u64, _u64, _u64, _int, _int, _dbl, _dbl, _vp, _vp],
     "jxr_truncated_normal_from_unit": [_vp, _vp, _i64, _vp, _i64, _i64, _int, _vp, _vp],
     "jxr_shuffle_scratch_bytes": [_i64],
-    "jxr_shuffle": [_vp, _i64, _i64, _i64, _int, _vp, _vp, ctypes.c_size_t, _vp],
+    "jxr_shuffle": [_vp, _int, _i64, _i64, _i64, _int, _vp, _vp, ctypes.c_size_t, _vp],
     "jxr_take": [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp],
     "jxr_choice_p_from_unit": [_vp, _i64, _int, _vp, _i64, _int, _vp, _vp],
     "jxr_add_log": [_vp, _vp, _i64, _int, _vp],
     "jxr_argsort_scratch_bytes": [_i64],
     "jxr_argsort_float": [_vp, _i64, _int, _int, _vp, _vp, ctypes.c_size_t, _vp],
+    "jxr_rbg_bits": [_vp, _u64, _u64, _u64, _int, _vp, _vp, _vp],
+    "jxr_rbg_blocks": [_vp, _u64, _u64, _i64, _vp, _vp],
+    "jxr_rbg_unsafe_fold_in": [_vp, _i64, _vp, _i64, _int, _vp, _vp],
+    "jxr_sample_from_bits": [_vp, _i64, _int, _int, _vp, _vp],
+    "jxr_truncated_normal_from_bits": [_vp, _i64, _int, _dbl, _dbl, _vp, _vp],
     "jxr_erf_inv": [_vp, _i64, _int, _vp, _vp],
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],

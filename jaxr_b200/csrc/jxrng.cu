@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "blocks.cuh"
+#include "philox.cuh"
 #include "samplers.cuh"
 #include "sort.cuh"
 #include "threefry.cuh"
@@ -678,6 +679,112 @@ __global__ void k_gumbel_rows(const void* __restrict__ row0, const void* __restr
   }
 }
 
+// rbg bits: elements [begin, begin + count) of a request of bit_width-bit values from the
+// Philox stream of key q.  Each thread takes G consecutive blocks (one 16-byte store's
+// worth when the output allows it); per block: 4 elements (8/16/32-bit) or 2 (64-bit).
+template <int kBits>
+__global__ void __launch_bounds__(256)
+k_rbg_bits(const uint32_t* __restrict__ key, uint64_t begin, uint64_t count, void* __restrict__ out) {
+  constexpr int kPer = kBits == 64 ? 2 : 4;           // elements per block
+  constexpr int kG = kBits == 8 ? 4 : kBits == 16 ? 2 : 1;  // blocks per 16-byte store
+  constexpr int kEsz = kBits / 8;
+  uint32_t q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = key[i];
+  const uint64_t end = begin + count;
+  const uint64_t b_first = begin / kPer, b_last = (end + kPer - 1) / kPer;  // [b_first, b_last)
+  const uint64_t groups = (b_last - b_first + kG - 1) / kG;
+  for (uint64_t g = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; g < groups;
+       g += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t b0 = b_first + g * kG;
+    uint32_t w[4 * kG];
+#pragma unroll
+    for (int j = 0; j < kG; ++j) {
+      const PhiloxOut o = rbg_block(q, b0 + j);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) w[4 * j + t] = o.w[t];
+    }
+    const uint64_t e0 = b0 * kPer;  // first element of the group
+    char* dst = (char*)out + (int64_t)(e0 - begin) * kEsz;
+    const bool full = e0 >= begin && e0 + kPer * kG <= end && ((uintptr_t)dst & 15u) == 0;
+    if (full) {
+      uint4 v;
+      if constexpr (kBits == 8) {
+        uint32_t p[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          p[j] = (w[4 * j] & 0xFFu) | (w[4 * j + 1] & 0xFFu) << 8 | (w[4 * j + 2] & 0xFFu) << 16 |
+                 (w[4 * j + 3] & 0xFFu) << 24;
+        v = make_uint4(p[0], p[1], p[2], p[3]);
+      } else if constexpr (kBits == 16) {
+        v = make_uint4((w[0] & 0xFFFFu) | w[1] << 16, (w[2] & 0xFFFFu) | w[3] << 16,
+                       (w[4] & 0xFFFFu) | w[5] << 16, (w[6] & 0xFFFFu) | w[7] << 16);
+      } else {
+        v = make_uint4(w[0], w[1], w[2], w[3]);  // 32-bit: 4 outputs; 64-bit: (w0|w1<<32, w2|w3<<32)
+      }
+      *(uint4*)dst = v;
+    } else {
+#pragma unroll
+      for (int t = 0; t < kPer * kG; ++t) {
+        const uint64_t e = e0 + t;
+        if (e < begin || e >= end) continue;
+        const int64_t i = (int64_t)(e - begin);
+        if constexpr (kBits == 8) ((uint8_t*)out)[i] = (uint8_t)w[t];
+        else if constexpr (kBits == 16) ((uint16_t*)out)[i] = (uint16_t)w[t];
+        else if constexpr (kBits == 32) ((uint32_t*)out)[i] = w[t];
+        else ((uint64_t*)out)[i] = (uint64_t)w[2 * t] | (uint64_t)w[2 * t + 1] << 32;
+      }
+    }
+  }
+}
+
+// blocks first + i * stride (i < n) of the stream of key q, 4 words each (unsafe_rbg split:
+// rows 0, 10, 20, ... of a (10 num, 4) request)
+__global__ void k_rbg_blocks(const uint32_t* __restrict__ key, uint64_t first, uint64_t stride,
+                             int64_t n, uint32_t* __restrict__ out) {
+  uint32_t q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = key[i];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const PhiloxOut o = rbg_block(q, first + (uint64_t)i * stride);
+    *(uint4*)(out + 4 * i) = make_uint4(o.w[0], o.w[1], o.w[2], o.w[3]);
+  }
+}
+
+// unsafe_rbg fold_in (R/prng.R:423-426): key ^ row 9 of a (10, 4) request from the key
+// rbg_seed(data) = (0, d, 0, d); the keys and data broadcast against each other.  With
+// lane_blocks > 0 every output i instead draws row 9 + 10 i of data[0]'s stream (the
+// batching rule of rng_bit_generator: all lanes from the first key).
+__global__ void k_rbg_unsafe_fold_in(const uint32_t* __restrict__ keys, int64_t nkeys,
+                                     const uint32_t* __restrict__ data, int64_t ndata,
+                                     int64_t n, int lanes_from_first, uint32_t* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t* k = keys + 4 * (nkeys == 1 ? 0 : i);
+    const uint32_t d = data[lanes_from_first || ndata == 1 ? 0 : i];
+    const uint32_t q[4] = {0u, d, 0u, d};
+    const PhiloxOut o = rbg_block(q, lanes_from_first ? 9u + 10u * (uint64_t)i : 9u);
+    *(uint4*)(out + 4 * i) =
+        make_uint4(k[0] ^ o.w[0], k[1] ^ o.w[1], k[2] ^ o.w[2], k[3] ^ o.w[3]);
+  }
+}
+
+// new state of rng_bit_generator: the 128-bit counter advanced by the blocks used
+__global__ void k_rbg_advance(const uint32_t* __restrict__ key, uint64_t nblocks,
+                              uint32_t* __restrict__ out) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint64_t lo = ((uint64_t)key[1] << 32 | key[0]);
+    const uint64_t hi = ((uint64_t)key[3] << 32 | key[2]);
+    const uint64_t l2 = lo + nblocks;
+    const uint64_t h2 = hi + (l2 < lo ? 1u : 0u);
+    out[0] = (uint32_t)l2;
+    out[1] = (uint32_t)(l2 >> 32);
+    out[2] = (uint32_t)h2;
+    out[3] = (uint32_t)(h2 >> 32);
+  }
+}
+
 // randint: out = low out_bits of (minval + offset(hi, lo, span)) in the sampling dtype
 template <class U, bool kSigned>
 __global__ void k_randint_combine(const U* __restrict__ hi, const U* __restrict__ lo, int64_t n,
@@ -1119,51 +1226,76 @@ int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p
   return JXR_OK;
 }
 
+}  // extern "C"
+
+namespace {
+// Calls f(op) with the fused op of a log-transform sampler of `kind` and `dtype`: the
+// kind's uniform draw is (0, 1), (tiny, 1) or (-1 + 2^-(nmant+1), 1).
+template <int K, class F>
+int visit_sample_kind(int dtype, F&& f) {
+  auto lo_of = [](double tiny, double epsneg) {
+    return K == kExponential ? 0.0 : (K == kLaplace ? -1.0 + epsneg : tiny);
+  };
+  switch (dtype) {
+    case JXR_F32: {
+      const float mn = (float)lo_of(0x1p-126, 0x1p-24), d = 1.0f - mn;
+      return f(OpLogSampler<K, 0>{{mn, d}});
+    }
+    case JXR_F64: {
+      const double mn = lo_of(0x1p-1022, 0x1p-53), d = 1.0 - mn;
+      return f(OpLogSampler<K, 1>{{mn, d}});
+    }
+    case JXR_F16: {
+      const float mn = to_half_value(lo_of(0x1p-14, 0x1p-11), false);
+      const float d = to_half_value(1.0 - (double)mn, false);
+      return f(OpLogSampler<K, 2>{{{mn, d}}});
+    }
+    default: {
+      const float mn = to_half_value(lo_of(0x1p-126, 0x1p-8), true);
+      const float d = to_half_value(1.0 - (double)mn, true);
+      return f(OpLogSampler<K, 3>{{{mn, d}}});
+    }
+  }
+}
+
+template <class F>
+int visit_sample_op(int kind, int dtype, F&& f) {
+  switch (kind) {
+    case kExponential: return visit_sample_kind<kExponential>(dtype, f);
+    case kGumbel: return visit_sample_kind<kGumbel>(dtype, f);
+    case kLogistic: return visit_sample_kind<kLogistic>(dtype, f);
+    case kLaplace: return visit_sample_kind<kLaplace>(dtype, f);
+  }
+  return fail(JXR_ERR_INVALID_ARGUMENT,
+              "kind must be 0..3 (exponential, gumbel, logistic, laplace), got %d", kind);
+}
+}  // namespace
+
+extern "C" {
+
 int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
                uint64_t count, int layout, int kind, int dtype, void* out, void* stream) {
   int rc = check_dtype(dtype);
   if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
-  if (kind < kExponential || kind > kLaplace)
-    return fail(JXR_ERR_INVALID_ARGUMENT, "kind must be 0..3 (exponential, gumbel, logistic, laplace), got %d", kind);
   cudaStream_t st = (cudaStream_t)stream;
-  // the kind's uniform draw: (0, 1), (tiny, 1) or (-1 + 2^-(nmant+1), 1)
-  auto lo_of = [&](double tiny, double epsneg) {
-    return kind == kExponential ? 0.0 : (kind == kLaplace ? -1.0 + epsneg : tiny);
-  };
-#define JXR_SAMPLE(KIND)                                                                       \
-  case KIND:                                                                                   \
-    switch (dtype) {                                                                           \
-      case JXR_F32: {                                                                          \
-        const float mn = (float)lo_of(0x1p-126, 0x1p-24), d = 1.0f - mn;                       \
-        return launch_op(keys, nkeys, size, begin, count, layout,                              \
-                         OpLogSampler<KIND, 0>{{mn, d}}, out, st);                             \
-      }                                                                                        \
-      case JXR_F64: {                                                                          \
-        const double mn = lo_of(0x1p-1022, 0x1p-53), d = 1.0 - mn;                             \
-        return launch_op(keys, nkeys, size, begin, count, layout,                              \
-                         OpLogSampler<KIND, 1>{{mn, d}}, out, st);                             \
-      }                                                                                        \
-      case JXR_F16: {                                                                          \
-        const float mn = to_half_value(lo_of(0x1p-14, 0x1p-11), false);                        \
-        const float d = to_half_value(1.0 - (double)mn, false);                                \
-        return launch_op(keys, nkeys, size, begin, count, layout,                              \
-                         OpLogSampler<KIND, 2>{{{mn, d}}}, out, st);                           \
-      }                                                                                        \
-      default: {                                                                               \
-        const float mn = to_half_value(lo_of(0x1p-126, 0x1p-8), true);                         \
-        const float d = to_half_value(1.0 - (double)mn, true);                                 \
-        return launch_op(keys, nkeys, size, begin, count, layout,                              \
-                         OpLogSampler<KIND, 3>{{{mn, d}}}, out, st);                           \
-      }                                                                                        \
-    }
-  switch (kind) {
-    JXR_SAMPLE(kExponential)
-    JXR_SAMPLE(kGumbel)
-    JXR_SAMPLE(kLogistic)
-    JXR_SAMPLE(kLaplace)
-  }
-#undef JXR_SAMPLE
-  return fail(JXR_ERR_INVALID_ARGUMENT, "unreachable");
+  return visit_sample_op(kind, dtype, [&](const auto& op) {
+    return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
+  });
+}
+
+int jxr_sample_from_bits(const void* bits, int64_t n, int kind, int dtype, void* out,
+                         void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return visit_sample_op(kind, dtype, [](const auto&) { return (int)JXR_OK; });
+  if (!bits || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  return visit_sample_op(kind, dtype, [&](const auto& op) {
+    return launch_from_bits(bits, n, op, out, st, grid);
+  });
 }
 
 int jxr_randint_combine(const void* hi, const void* lo, int64_t n, int nbits, int is_signed,
@@ -1246,28 +1378,25 @@ float half_step(float x, bool up, bool bf) {
 }
 }  // namespace
 
-int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
-                         uint64_t count, int layout, int dtype, double lower, double upper,
-                         void* out, void* stream) {
-  int rc = check_dtype(dtype);
-  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
-  cudaStream_t st = (cudaStream_t)stream;
+}  // extern "C"
+
+namespace {
+// Calls f(op) with the fused truncated-normal op of dtype for scalar bounds: a, b =
+// erf(lower / sqrt2), erf(upper / sqrt2) and the clip bounds, computed here once.
+template <class F>
+int visit_trunc_op(int dtype, double lower, double upper, F&& f) {
   const double inf = std::numeric_limits<double>::infinity();
   switch (dtype) {
     case JXR_F32: {
       const float s2 = 1.41421354f, lo = (float)lower, hi = (float)upper;
       const float a = (float)std::erf((double)(lo / s2)), b = (float)std::erf((double)(hi / s2));
       const float cl = std::nextafter(lo, (float)inf), ch = std::nextafter(hi, (float)-inf);
-      return launch_op(keys, nkeys, size, begin, count, layout,
-                       OpTruncNormal<0>{{a, b - a}, cl, ch}, out, st);
+      return f(OpTruncNormal<0>{{a, b - a}, cl, ch});
     }
     case JXR_F64: {
       const double s2 = 1.4142135623730951;
       const double a = std::erf(lower / s2), b = std::erf(upper / s2);
-      return launch_op(keys, nkeys, size, begin, count, layout,
-                       OpTruncNormal<1>{{a, b - a}, std::nextafter(lower, inf),
-                                        std::nextafter(upper, -inf)},
-                       out, st);
+      return f(OpTruncNormal<1>{{a, b - a}, std::nextafter(lower, inf), std::nextafter(upper, -inf)});
     }
     default: {
       const bool bf = dtype == JXR_BF16;
@@ -1279,13 +1408,39 @@ int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uin
       const float b = to_half_value((double)(float)std::erf((double)qh), bf);
       const float d = to_half_value((double)b - (double)a, bf);
       const float cl = half_step(lo, true, bf), ch = half_step(hi, false, bf);
-      if (bf)
-        return launch_op(keys, nkeys, size, begin, count, layout,
-                         OpTruncNormal<3>{{{a, d}, cl, ch}}, out, st);
-      return launch_op(keys, nkeys, size, begin, count, layout,
-                       OpTruncNormal<2>{{{a, d}, cl, ch}}, out, st);
+      if (bf) return f(OpTruncNormal<3>{{{a, d}, cl, ch}});
+      return f(OpTruncNormal<2>{{{a, d}, cl, ch}});
     }
   }
+}
+}  // namespace
+
+extern "C" {
+
+int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                         uint64_t count, int layout, int dtype, double lower, double upper,
+                         void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  return visit_trunc_op(dtype, lower, upper, [&](const auto& op) {
+    return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
+  });
+}
+
+int jxr_truncated_normal_from_bits(const void* bits, int64_t n, int dtype, double lower,
+                                   double upper, void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc) return rc;
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!bits || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  return visit_trunc_op(dtype, lower, upper, [&](const auto& op) {
+    return launch_from_bits(bits, n, op, out, st, grid);
+  });
 }
 
 int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t lower_stride,
@@ -1317,7 +1472,7 @@ namespace {
 int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
 
 struct SortScratch {
-  uint32_t *ka, *kb, *va, *vb, *counts, *totals, *keys6;
+  uint32_t *ka, *kb, *va, *vb, *counts, *totals, *keys12;  // keys12: 20 words of key scratch
   int* err;
 };
 
@@ -1333,7 +1488,7 @@ size_t shuffle_scratch(int64_t total, char* base, SortScratch* s) {
   const size_t nb = (size_t)total * 4;
   const size_t o_ka = take(nb), o_kb = take(nb), o_va = take(nb), o_vb = take(nb);
   const size_t o_counts = take((size_t)256 * (size_t)sort_tiles(total) * 4);
-  const size_t o_tot = take(256 * 4), o_keys = take(6 * 4), o_err = take(16);
+  const size_t o_tot = take(256 * 4), o_keys = take(20 * 4), o_err = take(16);
   if (base) {
     s->ka = (uint32_t*)(base + o_ka);
     s->kb = (uint32_t*)(base + o_kb);
@@ -1341,7 +1496,7 @@ size_t shuffle_scratch(int64_t total, char* base, SortScratch* s) {
     s->vb = (uint32_t*)(base + o_vb);
     s->counts = (uint32_t*)(base + o_counts);
     s->totals = (uint32_t*)(base + o_tot);
-    s->keys6 = (uint32_t*)(base + o_keys);
+    s->keys12 = (uint32_t*)(base + o_keys);
     s->err = (int*)(base + o_err);
   }
   return off;
@@ -1372,8 +1527,11 @@ size_t jxr_shuffle_scratch_bytes(int64_t total) {
   return shuffle_scratch(total, nullptr, nullptr);
 }
 
-int jxr_shuffle(const uint32_t* key, int64_t outer, int64_t n, int64_t inner, int layout,
-                uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream) {
+int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t inner,
+                int layout, uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream) {
+  if (impl < JXR_IMPL_THREEFRY || impl > JXR_IMPL_UNSAFE_RBG)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "impl must be 0 (threefry2x32), 1 (rbg) or 2 "
+                "(unsafe_rbg), got %d", impl);
   if (outer < 0 || n < 0 || inner < 0)
     return fail(JXR_ERR_INVALID_ARGUMENT, "outer, n and inner must be >= 0");
   if (layout != JXR_LAYOUT_ORIGINAL && layout != JXR_LAYOUT_PARTITIONABLE)
@@ -1402,17 +1560,37 @@ int jxr_shuffle(const uint32_t* key, int64_t outer, int64_t n, int64_t inner, in
   int segbits = 0;
   for (int64_t nseg = outer * inner; nseg > 1 && ((int64_t)1 << segbits) < nseg;) ++segbits;
   JXR_CUDA(cudaMemsetAsync(s.err, 0, sizeof(int), st));
-  JXR_CUDA(cudaMemcpyAsync(s.keys6, key, 8, cudaMemcpyDeviceToDevice, st));
+  // keys12: the running key (words 0..3), ks[0] (4..7), ks[1] (8..11); threefry keys use
+  // the first two words of each
+  const size_t kw = impl == JXR_IMPL_THREEFRY ? 8 : 16;
+  JXR_CUDA(cudaMemcpyAsync(s.keys12, key, kw, cudaMemcpyDeviceToDevice, st));
   // values are original flat indices: v[f] = index of the element now at position f
   uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
   k_iota_u32<<<grid, 256, 0, st>>>(v, total);
   for (int r = 0; r < rounds; ++r) {
     // ks = split(key); key = ks[0]; sort keys = random_bits(ks[1], 32, shape)
-    if ((rc = jxr_split(s.keys6, 1, 2, layout, s.keys6 + 2, stream))) return rc;
-    JXR_CUDA(cudaMemcpyAsync(s.keys6, s.keys6 + 2, 8, cudaMemcpyDeviceToDevice, st));
-    if ((rc = jxr_random_bits(s.keys6 + 4, 1, (uint64_t)total, 0, (uint64_t)total, layout, 32,
-                              k, stream)))
-      return rc;
+    uint32_t* ks0 = s.keys12 + 4;
+    uint32_t* ks1 = s.keys12 + 8;
+    if (impl == JXR_IMPL_THREEFRY) {
+      if ((rc = jxr_split(s.keys12, 1, 2, layout, ks0, stream))) return rc;  // ks0, then ks1
+      ks1 = ks0 + 2;
+    } else if (impl == JXR_IMPL_RBG) {
+      // each half split as a threefry key: (h0 ks0, h0 ks1, h1 ks0, h1 ks1) in tmp
+      uint32_t* tmp = s.keys12 + 12;
+      if ((rc = jxr_split(s.keys12, 2, 2, layout, tmp, stream))) return rc;
+      JXR_CUDA(cudaMemcpyAsync(ks0, tmp, 8, cudaMemcpyDeviceToDevice, st));
+      JXR_CUDA(cudaMemcpyAsync(ks0 + 2, tmp + 4, 8, cudaMemcpyDeviceToDevice, st));
+      JXR_CUDA(cudaMemcpyAsync(ks1, tmp + 2, 8, cudaMemcpyDeviceToDevice, st));
+      JXR_CUDA(cudaMemcpyAsync(ks1 + 2, tmp + 6, 8, cudaMemcpyDeviceToDevice, st));
+    } else {  // unsafe_rbg: rows 0 and 10 of the key's (20, 4) request
+      if ((rc = jxr_rbg_blocks(s.keys12, 0, 10, 2, ks0, stream))) return rc;
+    }
+    JXR_CUDA(cudaMemcpyAsync(s.keys12, ks0, kw, cudaMemcpyDeviceToDevice, st));
+    if (impl == JXR_IMPL_THREEFRY)
+      rc = jxr_random_bits(ks1, 1, (uint64_t)total, 0, (uint64_t)total, layout, 32, k, stream);
+    else
+      rc = jxr_rbg_bits(ks1, (uint64_t)total, 0, (uint64_t)total, 32, k, nullptr, stream);
+    if (rc) return rc;
     if ((rc = sort_pairs(k, v, k2, v2, total, 32, s, st))) return rc;
     if (segbits) {  // then by segment (the slice along the middle axis), stably
       k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
@@ -1538,6 +1716,66 @@ int jxr_argsort_float(const void* x, int64_t n, int dtype, int descending, uint3
   JXR_CUDA(cudaMemcpyAsync(&err, s.err, sizeof(int), cudaMemcpyDeviceToHost, st));
   JXR_CUDA(cudaStreamSynchronize(st));
   if (err) return fail(JXR_ERR_CUDA, "argsort: a bounds check in the sort failed (code %d)", err);
+  return JXR_OK;
+}
+
+int jxr_rbg_bits(const uint32_t* key, uint64_t size, uint64_t begin, uint64_t count, int bit_width,
+                 void* out, uint32_t* new_key, void* stream) {
+  if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "bit_width must be 8, 16, 32 or 64, got %d", bit_width);
+  if (begin > size || count > size - begin)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "range [%llu, +%llu) outside a request of %llu",
+                (unsigned long long)begin, (unsigned long long)count, (unsigned long long)size);
+  if (!key) return fail(JXR_ERR_INVALID_ARGUMENT, "null key");
+  if (count && !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null output");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (new_key) {  // the state after the request: counter + ceil(size / outputs per block)
+    const uint64_t per = bit_width == 64 ? 2 : 4;
+    k_rbg_advance<<<1, 32, 0, st>>>(key, (size + per - 1) / per, new_key);
+  }
+  if (count) {
+    const uint64_t per = bit_width == 64 ? 2 : 4, g = bit_width == 8 ? 4 : bit_width == 16 ? 2 : 1;
+    const uint64_t blocks = (begin + count + per - 1) / per - begin / per;
+    const uint64_t ctas = ((blocks + g - 1) / g + 255) / 256;  // one group of blocks per thread
+    int grid, rc;
+    if ((rc = resident_grid(k_rbg_bits<32>, ctas, &grid))) return rc;
+    switch (bit_width) {
+      case 8: k_rbg_bits<8><<<grid, 256, 0, st>>>(key, begin, count, out); break;
+      case 16: k_rbg_bits<16><<<grid, 256, 0, st>>>(key, begin, count, out); break;
+      case 32: k_rbg_bits<32><<<grid, 256, 0, st>>>(key, begin, count, out); break;
+      default: k_rbg_bits<64><<<grid, 256, 0, st>>>(key, begin, count, out);
+    }
+  }
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_rbg_blocks(const uint32_t* key, uint64_t first, uint64_t stride, int64_t n, uint32_t* out,
+                   void* stream) {
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!key || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((uintptr_t)out % 16) return fail(JXR_ERR_INVALID_ARGUMENT, "out must be 16-byte aligned");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  k_rbg_blocks<<<grid, 256, 0, (cudaStream_t)stream>>>(key, first, stride, n, out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_rbg_unsafe_fold_in(const uint32_t* keys, int64_t nkeys, const uint32_t* data, int64_t ndata,
+                           int lanes_from_first, uint32_t* out, void* stream) {
+  if (nkeys < 1 || ndata < 1 || (nkeys != ndata && nkeys != 1 && ndata != 1))
+    return fail(JXR_ERR_INVALID_ARGUMENT, "nkeys (%lld) and ndata (%lld) do not broadcast",
+                (long long)nkeys, (long long)ndata);
+  if (!keys || !data || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((uintptr_t)out % 16) return fail(JXR_ERR_INVALID_ARGUMENT, "out must be 16-byte aligned");
+  const int64_t n = std::max(nkeys, ndata);
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  k_rbg_unsafe_fold_in<<<grid, 256, 0, (cudaStream_t)stream>>>(keys, nkeys, data, ndata, n,
+                                                               lanes_from_first, out);
+  JXR_CUDA(cudaGetLastError());
   return JXR_OK;
 }
 

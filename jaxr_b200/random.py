@@ -255,10 +255,13 @@ def _vmap_out(out, level, size):
 # ---- key arrays (R/prng.R:455-584) ----------------------------------------------------------
 
 _IMPLS = {"threefry2x32": "fry", "rbg": "rbg", "unsafe_rbg": "urbg"}
+_KEY_WORDS = {"threefry2x32": 2, "rbg": 4, "unsafe_rbg": 4}  # key_shape (R/prng.R:430-440)
+_IMPL_CODE = {"threefry2x32": 0, "rbg": 1, "unsafe_rbg": 2}
 
 
 class PRNGKeyArray:
-    """A typed key array (jax_key_threefry2x32): uint32 key data of shape (*shape, 2)."""
+    """A typed key array: uint32 key data of shape (*shape, 2) for threefry2x32 and
+    (*shape, 4) for rbg and unsafe_rbg."""
 
     __slots__ = ("data", "impl")
 
@@ -303,7 +306,7 @@ class PRNGKeyArray:
 
 
 def _resolve_impl(spec):
-    """R/prng.R:444-453; only threefry2x32 has kernels here."""
+    """R/prng.R:444-453."""
     if spec is None:
         spec = cfg.jax_config("jax_default_prng_impl")
     if not isinstance(spec, str):
@@ -317,16 +320,12 @@ def _resolve_impl(spec):
         names = ", ".join(f'"{n}"' for n in _IMPLS)
         raise JaxValueError(f'unrecognized PRNG implementation "{spec}". Did you mean one of: '
                             f"{names}?")
-    if name != "threefry2x32":
-        raise JaxNotImplementedError(
-            f'PRNG implementation "{name}" (XLA RngBitGenerator) is not provided: these kernels '
-            "implement threefry2x32")
     return name
 
 
-def _as_uint32_data(x):
+def _as_uint32_data(x, impl="threefry2x32"):
     """Raw key data to a uint32 device tensor, checked as _check_prng_key_data
-    (R/prng.R:478-492)."""
+    (R/prng.R:478-492) for implementation `impl`."""
     if isinstance(x, torch.Tensor):
         t = x
         dt = _NAME[t.dtype]
@@ -347,9 +346,10 @@ def _as_uint32_data(x):
     if len(shape) < 1:
         raise JaxTypeError("JAX encountered invalid PRNG key data: expected key_data.ndim >= 1; "
                            f"got ndim={len(shape)}")
-    if shape[-1] != 2:
+    kw = _KEY_WORDS[impl]
+    if shape[-1] != kw:
         raise JaxTypeError("JAX encountered invalid PRNG key data: expected key_data.shape to end "
-                           f"with (2,); got shape={shape_str(shape)} for impl=threefry2x32")
+                           f"with ({kw},); got shape={shape_str(shape)} for impl={impl}")
     if dt != "uint32":
         raise JaxTypeError("JAX encountered invalid PRNG key data: expected key_data.dtype = "
                            f"uint32; got dtype={dt}")
@@ -376,7 +376,8 @@ def _check_key(name, key, allow_batched=False):
         k, wrapped = key, False
     elif isinstance(key, (torch.Tensor, np.ndarray, list, tuple, numbers.Number)) and not isinstance(key, str):
         _legacy_check()
-        k, wrapped = PRNGKeyArray(_as_uint32_data(key)), True
+        impl = _resolve_impl(None)  # raw keys use the default implementation
+        k, wrapped = PRNGKeyArray(_as_uint32_data(key, impl), impl), True
     else:
         raise JaxTypeError(f"unexpected PRNG key type {type(key).__name__}")
     per_shape = k.shape[nb:]
@@ -449,7 +450,10 @@ def _key_ctor(ctor, seed, impl_spec):
                            f"{shape_str(sshape[nb:])} != (). Use jax.vmap for batching")
     if not isinstance(s, (torch.Tensor, np.ndarray, numbers.Number)):
         raise JaxTypeError(f"PRNG key seed must be an integer; got {s!r}")
-    return _rebatch(PRNGKeyArray(_keys_from_seeds(s), impl), nb)
+    data = _keys_from_seeds(s)
+    if _KEY_WORDS[impl] == 4:  # rbg seed: the threefry seed twice (R/prng.R:385-388)
+        data = torch.cat([data, data], dim=-1)
+    return _rebatch(PRNGKeyArray(data, impl), nb)
 
 
 def random_key(seed, impl=None, dtype=None):
@@ -497,7 +501,7 @@ def random_wrap_key_data(key_bits_array, impl=None, dtype=None):
         impl = dtype
     name = _resolve_impl(impl)
     kb, nb = _unbatch(key_bits_array)
-    return _rebatch(PRNGKeyArray(_as_uint32_data(kb), name), nb)
+    return _rebatch(PRNGKeyArray(_as_uint32_data(kb, name), name), nb)
 
 
 def random_clone(key):
@@ -513,22 +517,58 @@ def random_Key(x):
 # ---- kernels on flat key batches -------------------------------------------------------------
 
 def _flat_keys(k):
-    """Key data as a contiguous (nkeys, 2) uint32 tensor on the current device."""
-    return k.data.to(_device()).reshape(-1, 2).contiguous()
+    """Key data as a contiguous (nkeys, 2) (threefry2x32) or (nkeys, 4) (rbg, unsafe_rbg)
+    uint32 tensor on the current device."""
+    return k.data.to(_device()).reshape(-1, _KEY_WORDS[k.impl]).contiguous()
 
 
-def _k_split(kd, shape, layout):
+def _is_rbg(kd):
+    return kd.shape[-1] == 4
+
+
+def _k_split(kd, shape, layout, impl="threefry2x32"):
+    """split of every key of kd into _size(shape) keys: (nkeys, num, key words)."""
     n = kd.shape[0]
     num = _size(shape)
-    out = torch.empty((n, num, 2), dtype=torch.uint32, device=kd.device)
-    nat.call("jxr_split", _ptr(kd), n, num, layout, _ptr(out), _stream())
+    if impl == "threefry2x32":
+        out = torch.empty((n, num, 2), dtype=torch.uint32, device=kd.device)
+        nat.call("jxr_split", _ptr(kd), n, num, layout, _ptr(out), _stream())
+        return out
+    out = torch.empty((n, num, 4), dtype=torch.uint32, device=kd.device)
+    if not n * num:
+        return out
+    if impl == "rbg":
+        # each half split as a threefry key (R/prng.R:391-397); key j = (half 0's key j,
+        # half 1's key j): the (2, num) halves of each key transposed to (num, 2)
+        tmp = torch.empty((2 * n, num, 2), dtype=torch.uint32, device=kd.device)
+        nat.call("jxr_split", _ptr(kd), 2 * n, num, layout, _ptr(tmp), _stream())
+        m = np.arange(2 * num, dtype=np.int64)
+        idx = torch.from_numpy(((m % 2) * num + m // 2).astype(np.uint32)).to(kd.device)
+        nat.call("jxr_take", _ptr(tmp), n, 2 * num, _ptr(idx), 2 * num, 8, _ptr(out), None,
+                 _stream())
+        return out
+    # unsafe_rbg (R/prng.R:415-420): rows 0, 10, 20, ... of rng_bit_generator(key, (10 num, 4));
+    # batched keys all draw from the first key (the primitive's batching rule)
+    nat.call("jxr_rbg_blocks", _ptr(kd[0]), 0, 10, n * num, _ptr(out), _stream())
     return out
 
 
-def _k_fold_in(kd, data):
+def _k_fold_in(kd, data, impl="threefry2x32"):
     n = max(kd.shape[0], data.shape[0])
-    out = torch.empty((n, 2), dtype=torch.uint32, device=kd.device)
-    nat.call("jxr_fold_in", _ptr(kd), kd.shape[0], _ptr(data), data.shape[0], _ptr(out), _stream())
+    if impl == "threefry2x32":
+        out = torch.empty((n, 2), dtype=torch.uint32, device=kd.device)
+        nat.call("jxr_fold_in", _ptr(kd), kd.shape[0], _ptr(data), data.shape[0], _ptr(out),
+                 _stream())
+        return out
+    out = torch.empty((n, 4), dtype=torch.uint32, device=kd.device)
+    if impl == "rbg":  # each half folded as a threefry key (R/prng.R:400-403)
+        keys = kd.expand(n, 4).contiguous().reshape(2 * n, 2)
+        d2 = data.expand(n).contiguous().repeat_interleave(2)
+        nat.call("jxr_fold_in", _ptr(keys), 2 * n, _ptr(d2), 2 * n, _ptr(out), _stream())
+        return out
+    # unsafe_rbg (R/prng.R:423-426)
+    nat.call("jxr_rbg_unsafe_fold_in", _ptr(kd), kd.shape[0], _ptr(data), data.shape[0],
+             int(data.shape[0] > 1), _ptr(out), _stream())
     return out
 
 
@@ -538,11 +578,23 @@ def _check_size(size, layout):
 
 
 def _k_bits(kd, size, bit_width, layout):
+    """(nkeys, size) random bits.  rbg / unsafe_rbg keys draw from XLA's RngBitGenerator;
+    batched keys of those all draw from the first key, (nkeys, size) of its stream (the
+    primitive's batching rule, R/prng.R:309-320)."""
     _check_size(size, layout)
     out = torch.empty((kd.shape[0], size), dtype=_TORCH[f"uint{bit_width}"], device=kd.device)
+    if _is_rbg(kd):
+        total = kd.shape[0] * size
+        nat.call("jxr_rbg_bits", _ptr(kd[0]), total, 0, total, bit_width, _ptr(out), None,
+                 _stream())
+        return out
     nat.call("jxr_random_bits", _ptr(kd), kd.shape[0], size, 0, size, layout, bit_width,
              _ptr(out), _stream())
     return out
+
+
+# bits per draw of the float samplers (R/random.R:288-299: bfloat16 uses 8 random bits)
+_DRAW_BITS = {"float32": 32, "float64": 64, "float16": 16, "bfloat16": 8}
 
 
 def _float_storage(dt):
@@ -556,6 +608,11 @@ def _as_float_view(t, dt):
 def _k_uniform(kd, size, dt, mn, mx, layout, flags=0):
     _check_size(size, layout)
     out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    if _is_rbg(kd):
+        bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
+        nat.call("jxr_uniform_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt], float(mn),
+                 float(mx), flags, _ptr(out), _stream())
+        return _as_float_view(out, dt)
     nat.call("jxr_uniform", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
              float(mn), float(mx), flags, _ptr(out), _stream())
     return _as_float_view(out, dt)
@@ -564,6 +621,11 @@ def _k_uniform(kd, size, dt, mn, mx, layout, flags=0):
 def _k_normal(kd, size, dt, layout):
     _check_size(size, layout)
     out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    if _is_rbg(kd):
+        bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
+        nat.call("jxr_normal_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt], _ptr(out),
+                 _stream())
+        return _as_float_view(out, dt)
     nat.call("jxr_normal", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
              _ptr(out), _stream())
     return _as_float_view(out, dt)
@@ -572,6 +634,13 @@ def _k_normal(kd, size, dt, layout):
 def _k_bernoulli(kd, size, dt, p, layout):
     _check_size(size, layout)
     out = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
+    if _is_rbg(kd):
+        u = _k_uniform(kd, size, dt, 0.0, 1.0, layout)
+        pt = _broadcast_param(torch.tensor(float(p), dtype=torch.float64), (size,), dt, "bernoulli")
+        for r in range(kd.shape[0] if size else 0):
+            nat.call("jxr_bernoulli_from_uniform", _ptr(_raw16(u[r].contiguous(), dt)), None,
+                     _ptr(_raw16(pt, dt)), size, _FLOAT_CODE[dt], _ptr(out[r]), _stream())
+        return out.view(torch.bool)
     nat.call("jxr_bernoulli", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
              float(p), _ptr(out), _stream())
     return out.view(torch.bool)
@@ -629,7 +698,8 @@ def random_split(key, num=2):
     k, wrapped, nb = _check_key("split", key)
     shape = canon_shape(num)
     bshape = k.shape[:nb]
-    out = _k_split(_flat_keys(k), shape, _layout()).reshape(bshape + shape + (2,))
+    out = _k_split(_flat_keys(k), shape, _layout(), k.impl).reshape(
+        bshape + shape + (_KEY_WORDS[k.impl],))
     return _rebatch(_return_keys(wrapped, PRNGKeyArray(out, k.impl)), nb)
 
 
@@ -671,7 +741,7 @@ def random_fold_in(key, data):
     if knb and dnb and kbshape != dbshape:
         raise JaxValueError("fold_in: key and data batch shapes differ")
     bshape = kbshape if knb >= dnb else dbshape
-    out = _k_fold_in(kd, dvals).reshape(bshape + (2,))
+    out = _k_fold_in(kd, dvals, k.impl).reshape(bshape + (_KEY_WORDS[k.impl],))
     return _rebatch(_return_keys(wrapped, PRNGKeyArray(out, k.impl)), nb)
 
 
@@ -772,7 +842,7 @@ def _complex_normal(k, bshape, shape, dt):
     (R/random.R:489-499)."""
     real = "float32" if dt == "complex64" else "float64"
     kd = _flat_keys(k)
-    halves = _k_split(kd, (2,), _layout())  # (n, 2, 2)
+    halves = _k_split(kd, (2,), _layout(), k.impl)  # (n, 2, key words)
     size = _size(shape)
     re = _k_normal(halves[:, 0].contiguous(), size, real, _layout())
     im = _k_normal(halves[:, 1].contiguous(), size, real, _layout())
@@ -841,6 +911,9 @@ def random_normal_bernoulli(key, p=0.5, shape=(), dtype=None):
     kd = _flat_keys(k)
     layout = _layout()
     _check_size(size, layout)
+    if _is_rbg(kd):  # two passes over the same bits
+        return random_normal(key, shape, dt), random_bernoulli(
+            key, torch.tensor(float(p), dtype=_TORCH[dt]), shape)
     nout = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
     bout = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
     nat.call("jxr_normal_bernoulli", _ptr(kd), kd.shape[0], size, 0, size, layout,
@@ -858,6 +931,11 @@ _SAMPLE_KIND = {"exponential": 0, "gumbel": 1, "logistic": 2, "laplace": 3}
 def _k_sample(kd, size, dt, kind, layout):
     _check_size(size, layout)
     out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    if _is_rbg(kd):
+        bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
+        nat.call("jxr_sample_from_bits", _ptr(bits), bits.numel(), _SAMPLE_KIND[kind],
+                 _FLOAT_CODE[dt], _ptr(out), _stream())
+        return _as_float_view(out, dt)
     nat.call("jxr_sample", _ptr(kd), kd.shape[0], size, 0, size, layout, _SAMPLE_KIND[kind],
              _FLOAT_CODE[dt], _ptr(out), _stream())
     return _as_float_view(out, dt)
@@ -943,8 +1021,13 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
     if lo_t is None and hi_t is None:
         _check_size(size, layout)
         out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
-        nat.call("jxr_truncated_normal", _ptr(kd), kd.shape[0], size, 0, size, layout,
-                 _FLOAT_CODE[dt], float(lo_s), float(hi_s), _ptr(out), _stream())
+        if _is_rbg(kd):
+            bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
+            nat.call("jxr_truncated_normal_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt],
+                     float(lo_s), float(hi_s), _ptr(out), _stream())
+        else:
+            nat.call("jxr_truncated_normal", _ptr(kd), kd.shape[0], size, 0, size, layout,
+                     _FLOAT_CODE[dt], float(lo_s), float(hi_s), _ptr(out), _stream())
         return _rebatch(_as_float_view(out, dt).reshape(bshape + shape), nb)
     lo = _broadcast_param(lo_t if lo_t is not None else torch.tensor(lo_s), shape, dt,
                           "truncated_normal")
@@ -1069,7 +1152,7 @@ def random_randint(key, shape, minval, maxval, dtype=None):
     mn_t, mn_s = as_param(mn, clip)
     mx_t, mx_s = as_param(mx, clip)
     oor_t = oor_t.to(torch.uint8)
-    halves = _k_split(kd, (2,), layout)
+    halves = _k_split(kd, (2,), layout, k.impl)
     hi = _k_bits(halves[:, 0].contiguous(), size, sbits, layout)
     lo = _k_bits(halves[:, 1].contiguous(), size, sbits, layout)
     out = torch.empty((kd.shape[0], size), dtype=_TORCH[dt], device=dev)
@@ -1113,15 +1196,15 @@ def _as_device_array(x):
     return t.to(device=_device(), dtype=_TORCH[name]).contiguous()
 
 
-def _k_shuffle(kd_row, outer, n, inner, layout):
+def _k_shuffle(kd_row, impl, outer, n, inner, layout):
     """Flat source index of every position after rnd_shuffle (uint32 tensor)."""
     total = outer * n * inner
     perm = torch.empty(total, dtype=torch.uint32, device=kd_row.device)
     if total:
         nbytes = nat.lib().jxr_shuffle_scratch_bytes(total)
         scratch = torch.empty(nbytes, dtype=torch.uint8, device=kd_row.device)
-        nat.call("jxr_shuffle", _ptr(kd_row), outer, n, inner, layout, _ptr(perm), _ptr(scratch),
-                 nbytes, _stream())
+        nat.call("jxr_shuffle", _ptr(kd_row), _IMPL_CODE[impl], outer, n, inner, layout,
+                 _ptr(perm), _ptr(scratch), nbytes, _stream())
     return perm
 
 
@@ -1155,6 +1238,8 @@ def random_permutation(key, x, axis=0, independent=False):
     kd = _flat_keys(k)
     layout = _layout()
     bshape = k.shape[:nb]
+    if nb and k.impl != "threefry2x32":
+        raise JaxNotImplementedError("random_permutation under vmap with rbg keys")
     if ndim == 0:
         if isinstance(xv, (torch.Tensor, np.ndarray)):
             t = torch.as_tensor(xv)
@@ -1166,7 +1251,8 @@ def random_permutation(key, x, axis=0, independent=False):
         else:
             n = int(xv)
         n = max(n, 0)
-        outs = [_k_shuffle(kd[r], 1, n, 1, layout).view(torch.int32) for r in range(kd.shape[0])]
+        outs = [_k_shuffle(kd[r], k.impl, 1, n, 1, layout).view(torch.int32)
+                for r in range(kd.shape[0])]
         out = torch.stack(outs) if outs else torch.empty((0, n), dtype=torch.int32)
         return _rebatch(out.reshape(bshape + (n,)), nb)
     xt = _as_device_array(xv)
@@ -1175,10 +1261,10 @@ def random_permutation(key, x, axis=0, independent=False):
     outs = []
     for r in range(kd.shape[0]):
         if independent or xt.ndim == 1:
-            perm = _k_shuffle(kd[r], outer, n, inner, layout)
+            perm = _k_shuffle(kd[r], k.impl, outer, n, inner, layout)
             outs.append(_take(xt.reshape(-1), perm, 0).reshape(shape))
         else:
-            ind = _k_shuffle(kd[r], 1, n, 1, layout)
+            ind = _k_shuffle(kd[r], k.impl, 1, n, 1, layout)
             outs.append(_take(xt, ind, axis))
     out = torch.stack(outs) if outs else torch.empty((0,) + shape, dtype=xt.dtype)
     return _rebatch(out.reshape(bshape + shape), nb)
@@ -1226,10 +1312,10 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
         else:
             kd = _flat_keys(k)
             if arr is None:
-                perm = _k_shuffle(kd[0], 1, n_inputs, 1, _layout()).view(torch.int32)
+                perm = _k_shuffle(kd[0], k.impl, 1, n_inputs, 1, _layout()).view(torch.int32)
                 result = perm[:n_draws].reshape(shape)
             else:
-                ind = _k_shuffle(kd[0], 1, n_inputs, 1, _layout())[:n_draws]
+                ind = _k_shuffle(kd[0], k.impl, 1, n_inputs, 1, _layout())[:n_draws]
                 result = _take(arr, ind.reshape(shape), axis)
         return result
     # promote_dtypes_inexact: float arrays keep their dtype, everything else is the
@@ -1272,6 +1358,38 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
         ind = order[:n_draws].view(torch.int32).to(_TORCH[dint])
     ind = ind.reshape(shape)
     return ind if arr is None else _take(arr, ind, axis)
+
+
+# ---- rng_bit_generator (R/prng.R:264-345) ---------------------------------------------------
+
+lax_RandomAlgorithm = {"RNG_DEFAULT": 0, "RNG_THREE_FRY": 1, "RNG_PHILOX": 2}
+
+
+def lax_rng_bit_generator(key, shape, dtype="uint32", algorithm=0):
+    """(new_key, bits): random bits from XLA's RngBitGenerator for a uint32[4] (or
+    uint64[2]) key (R/prng.R:322-345).  The default algorithm is Philox4x32-10, as XLA's CPU
+    backend runs it; new_key is the state after the request (the 128-bit counter advanced
+    by the blocks used)."""
+    shape = tuple(int(v) for v in np.atleast_1d(np.asarray(shape, dtype=np.int64)))
+    dt = canonicalize_dtype(dtype)
+    if dt not in ("uint8", "uint16", "uint32", "uint64"):
+        raise JaxTypeError(f"rng_bit_generator: unsupported dtype {dt}")
+    kt = key if isinstance(key, torch.Tensor) else torch.as_tensor(np.asarray(key))
+    kname = _NAME[kt.dtype]
+    if not ((kname == "uint32" and tuple(kt.shape) == (4,)) or
+            (kname == "uint64" and tuple(kt.shape) == (2,))):
+        raise JaxValueError("rng_bit_generator: key must be uint32[4] or uint64[2], got "
+                            f"{kname}{list(kt.shape)}")
+    if int(algorithm) == lax_RandomAlgorithm["RNG_THREE_FRY"]:
+        raise JaxNotImplementedError("rng_bit_generator with RNG_THREE_FRY: only the default "
+                                     "(Philox) algorithm is provided")
+    k4 = kt.to(_device()).contiguous().view(torch.uint32).reshape(4)
+    size = _size(shape)
+    out = torch.empty(size, dtype=_TORCH[dt], device=k4.device)
+    new = torch.empty(4, dtype=torch.uint32, device=k4.device)
+    nat.call("jxr_rbg_bits", _ptr(k4), size, 0, size, _BITS[dt], _ptr(out), _ptr(new), _stream())
+    new_key = new if kname == "uint32" else new.view(torch.uint64)
+    return new_key, out.reshape(shape)
 
 
 # ---- erf_inv (R/lax.R:222) ---------------------------------------------------------------------

@@ -20,9 +20,19 @@ import torch
 
 from . import _native as nat
 from . import config as cfg
-from .random import (_TORCH, _BITS, _check_key, _flat_keys, _layout, _ptr, _size, _stream,
-                     canon_shape, canonicalize_dtype, default_uint)
+from .random import (_TORCH, _BITS, _KEY_WORDS, _check_key, _flat_keys, _layout, _ptr, _size,
+                     _stream, canon_shape, canonicalize_dtype, default_uint)
 from .errors import JaxValueError
+
+
+def _bits_range(k, kd, size, lo, n, bit_width, out_ptr):
+    """Elements [lo, lo + n) of random_bits(k, (size,)) written at out_ptr: threefry keys
+    through the cipher kernels, rbg / unsafe_rbg keys through the Philox stream."""
+    if _KEY_WORDS[k.impl] == 4:
+        nat.call("jxr_rbg_bits", _ptr(kd), size, lo, n, bit_width, out_ptr, None, _stream())
+    else:
+        nat.call("jxr_random_bits", _ptr(kd), 1, size, lo, n, _layout(), bit_width, out_ptr,
+                 _stream())
 
 
 def shard_range(size, rank, world):
@@ -46,8 +56,7 @@ def random_bits_shard(key, shape, rank, world, dtype=None, out=None):
         out = torch.empty(n, dtype=_TORCH[dt], device=k.data.device)
     elif out.numel() != n or out.dtype != _TORCH[dt] or not out.is_contiguous():
         raise JaxValueError(f"out must be a contiguous {dt} tensor of {n} elements")
-    nat.call("jxr_random_bits", _ptr(_flat_keys(k)), 1, size, lo, n, _layout(), _BITS[dt],
-             _ptr(out), _stream())
+    _bits_range(k, _flat_keys(k), size, lo, n, _BITS[dt], _ptr(out))
     return out
 
 
@@ -61,6 +70,8 @@ def random_bits_to_host(key, shape, dtype=None, out=None):
     dt = default_uint() if dtype is None else canonicalize_dtype(dtype)
     shape = canon_shape(shape)
     size = _size(shape)
+    if k.impl != "threefry2x32":
+        raise JaxValueError("random_bits_to_host takes a threefry2x32 key")
     if out is None:
         out = torch.empty(size, dtype=_TORCH[dt], pin_memory=True)
     keys_host = k.data.reshape(-1, 2).cpu().contiguous()
@@ -157,8 +168,7 @@ def random_bits_gathered(key, shape, root=0, dtype=None, out=None, group=None):
     base = whole.data_ptr() if rank == root else _open(handle) + off
     lo, hi = shard_range(size, rank, world)
     esz = _BITS[dt] // 8
-    nat.call("jxr_random_bits", _ptr(kd), 1, size, lo, hi - lo, _layout(), _BITS[dt],
-             base + lo * esz, _stream())
+    _bits_range(k, kd, size, lo, hi - lo, _BITS[dt], base + lo * esz)
     torch.cuda.current_stream().synchronize()
     dist.barrier(group=group)
     return whole

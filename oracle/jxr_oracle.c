@@ -736,3 +736,77 @@ int orc_truncated_normal(const uint32_t key[2], int dtype, uint64_t size, int pa
                                         begin + (uint64_t)t));
   return 0;
 }
+
+/* ---- rbg / unsafe_rbg: XLA's RngBitGenerator (R/prng.R:264-426) ----------------------- */
+
+/* Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC'11): out = the block of counter c under
+ * key k. */
+void orc_philox4x32(const uint32_t c[4], const uint32_t k[2], uint32_t out[4]) {
+  uint32_t c0 = c[0], c1 = c[1], c2 = c[2], c3 = c[3], k0 = k[0], k1 = k[1];
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c0, p1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1;
+    c0 = n0;
+    c1 = (uint32_t)p1;
+    c2 = n2;
+    c3 = (uint32_t)p0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  out[0] = c0;
+  out[1] = c1;
+  out[2] = c2;
+  out[3] = c3;
+}
+
+/* Block b of the stream of the u32[4] key q: Philox key (q0, q1), counter = q as a 128-bit
+ * number (q0 lowest) + b.  This is how the recorded rbg values of the reference
+ * (tests/testthat/test-prng.R:48-54) come out of XLA's RngBitGenerator. */
+static void rbg_block(const uint32_t q[4], uint64_t b, uint32_t out[4]) {
+  const uint64_t lo = (uint64_t)q[1] << 32 | q[0], hi = (uint64_t)q[3] << 32 | q[2];
+  const uint64_t l2 = lo + b, h2 = hi + (l2 < lo);
+  const uint32_t c[4] = {(uint32_t)l2, (uint32_t)(l2 >> 32), (uint32_t)h2, (uint32_t)(h2 >> 32)};
+  const uint32_t k[2] = {q[0], q[1]};
+  orc_philox4x32(c, k, out);
+}
+
+/* Elements [begin, begin + count) of lax_rng_bit_generator(key, (size), uint<bits>): element
+ * e of a 32-bit request is word e % 4 of block e / 4; 8/16-bit elements are the low bits of
+ * the 32-bit element; 64-bit element e is words 2(e % 2), 2(e % 2) + 1 (low first) of block
+ * e / 2. */
+int orc_rbg_bits(const uint32_t q[4], int bit_width, uint64_t size, uint64_t begin,
+                 uint64_t count, void* out) {
+  if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64) return 1;
+  if (begin > size || count > size - begin) return 2;
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < (int64_t)count; ++t) {
+    const uint64_t e = begin + (uint64_t)t;
+    uint32_t w[4];
+    if (bit_width == 64) {
+      rbg_block(q, e / 2, w);
+      ((uint64_t*)out)[t] = (uint64_t)w[2 * (e % 2)] | (uint64_t)w[2 * (e % 2) + 1] << 32;
+    } else {
+      rbg_block(q, e / 4, w);
+      const uint32_t v = w[e % 4];
+      if (bit_width == 8) ((uint8_t*)out)[t] = (uint8_t)v;
+      else if (bit_width == 16) ((uint16_t*)out)[t] = (uint16_t)v;
+      else ((uint32_t*)out)[t] = v;
+    }
+  }
+  return 0;
+}
+
+/* unsafe_rbg split (R/prng.R:415-420): key i = row 10 i of the (10 num, 4) request. */
+void orc_rbg_unsafe_split(const uint32_t q[4], int64_t num, uint32_t* out) {
+  for (int64_t i = 0; i < num; ++i) rbg_block(q, 10 * (uint64_t)i, out + 4 * i);
+}
+
+/* unsafe_rbg fold_in (R/prng.R:423-426): key ^ row 9 of the (10, 4) request of the key
+ * rbg_seed(data) = threefry_seed(data) twice = (0, data, 0, data). */
+void orc_rbg_unsafe_fold_in(const uint32_t q[4], uint32_t data, uint32_t out[4]) {
+  const uint32_t s[4] = {0u, data, 0u, data};
+  uint32_t w[4];
+  rbg_block(s, 9, w);
+  for (int i = 0; i < 4; ++i) out[i] = q[i] ^ w[i];
+}

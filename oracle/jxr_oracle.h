@@ -109,6 +109,14 @@ int orc_truncated_normal(const uint32_t key[2], int dtype, uint64_t size, int pa
 double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
                                int partitionable, double lower, double upper, uint64_t i);
 
+/* rbg / unsafe_rbg (R/prng.R:264-426): XLA's RngBitGenerator as Philox4x32-10 with key
+ * (q0, q1) and the key q as 128-bit counter, advanced per block of four 32-bit outputs. */
+void orc_philox4x32(const uint32_t c[4], const uint32_t k[2], uint32_t out[4]);
+int orc_rbg_bits(const uint32_t q[4], int bit_width, uint64_t size, uint64_t begin,
+                 uint64_t count, void* out);
+void orc_rbg_unsafe_split(const uint32_t q[4], int64_t num, uint32_t* out);
+void orc_rbg_unsafe_fold_in(const uint32_t q[4], uint32_t data, uint32_t out[4]);
+
 /* Number of OpenMP threads used by the array functions (0 = default). */
 void orc_set_threads(int n);
 int orc_get_threads(void);

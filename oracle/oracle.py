@@ -66,6 +66,10 @@ def lib():
         L.orc_sample_at.restype = dbl
         L.orc_gumbel_mode.argtypes = [u32p, i32, i32, u64, i32, vp]
         L.orc_truncated_normal.argtypes = [u32p, i32, u64, i32, dbl, dbl, u64, u64, vp]
+        L.orc_philox4x32.argtypes = [u32p, u32p, u32p]
+        L.orc_rbg_bits.argtypes = [u32p, i32, u64, u64, u64, vp]
+        L.orc_rbg_unsafe_split.argtypes = [u32p, i64, u32p]
+        L.orc_rbg_unsafe_fold_in.argtypes = [u32p, ctypes.c_uint32, u32p]
         L.orc_set_threads.argtypes = [i32]
         L.orc_get_threads.restype = i32
         _lib = L
@@ -358,6 +362,55 @@ def choice(key, a, shape=(), replace=True, p=None, axis=0, partitionable=True, x
     r = (cuml[-1] * (np.asarray(1, dtype=fdt) - u).astype(fdt)).astype(fdt)
     ind = np.searchsorted(cuml, r, side="left").astype(dint).reshape(shape)
     return ind if scalar else np.take(arr, ind, axis=axis)
+
+
+def _key4(q):
+    return (ctypes.c_uint32 * 4)(*[int(v) & 0xFFFFFFFF for v in q])
+
+
+def philox4x32(counter, key):
+    out = (ctypes.c_uint32 * 4)()
+    lib().orc_philox4x32((ctypes.c_uint32 * 4)(*counter), (ctypes.c_uint32 * 2)(*key), out)
+    return [int(v) for v in out]
+
+
+def rbg_seed(seed, x64=False):
+    """rbg / unsafe_rbg seed (R/prng.R:385-388): the threefry seed twice."""
+    return np.concatenate([seed_key := globals()["seed"](seed, x64), seed_key])
+
+
+def rbg_bits(q, bit_width, size, begin=0, count=None):
+    """lax_rng_bit_generator(q, (size), uint<bit_width>)[[2]] elements [begin, +count)."""
+    count = size - begin if count is None else count
+    out = np.empty(int(count), dtype=NP_BITS[bit_width])
+    rc = lib().orc_rbg_bits(_key4(q), bit_width, int(size), int(begin), int(count), _ptr(out))
+    if rc:
+        raise ValueError(f"orc_rbg_bits failed ({rc})")
+    return out
+
+
+def rbg_split(q, num, partitionable=True):
+    """rbg split (R/prng.R:391-397): each half of the key split as a threefry key; key j is
+    (half 0's key j, half 1's key j)."""
+    h0 = split(q[:2], num, partitionable)
+    h1 = split(q[2:], num, partitionable)
+    return np.concatenate([h0, h1], axis=1)
+
+
+def rbg_fold_in(q, data):
+    return np.concatenate([fold_in(q[:2], data), fold_in(q[2:], data)])
+
+
+def rbg_unsafe_split(q, num):
+    out = np.empty((int(num), 4), dtype=np.uint32)
+    lib().orc_rbg_unsafe_split(_key4(q), int(num), out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    return out
+
+
+def rbg_unsafe_fold_in(q, data):
+    out = (ctypes.c_uint32 * 4)()
+    lib().orc_rbg_unsafe_fold_in(_key4(q), int(data) & 0xFFFFFFFF, out)
+    return np.array(list(out), dtype=np.uint32)
 
 
 def set_threads(n):

@@ -259,6 +259,15 @@ def build(ref):
         "vmap_fold_in": ("vmap_fold_in", {"seed": 0, "data": [0, 1, 2]}),
         # vmap(function(s) random_key_data(random_key(s)))(jnp_arange(3L))
         "vmap_key": ("vmap_seed", {"seeds": [0, 1, 2]}),
+        # rbg / unsafe_rbg (test-prng.R:216-236, :249)
+        "rbg_bits": ("rbg_bits", {"seed": 0, "impl": "rbg", "shape": [4], "bits": 32}),
+        "rbg_bits_u8": ("rbg_bits", {"seed": 3, "impl": "rbg", "shape": [5], "bits": 8}),
+        "rbg_split": ("rbg_split", {"seed": 0, "impl": "rbg", "num": 3}),
+        "rbg_fold_in": ("rbg_fold_in", {"seed": 0, "impl": "rbg", "data": 5}),
+        "unsafe_rbg_split": ("rbg_split", {"seed": 0, "impl": "unsafe_rbg", "num": 3}),
+        "unsafe_rbg_fold_in": ("rbg_fold_in", {"seed": 0, "impl": "unsafe_rbg", "data": 5}),
+        # vmap(function(k) random_bits(k, 3))(random_split(random_key(0, impl = "rbg"), 2))
+        "rbg_vmap_bits": ("rbg_vmap_bits", {"seed": 0, "impl": "rbg", "nkeys": 2, "shape": [3]}),
     }
     for name, (op, args) in rp_calls.items():
         (shape, vals, dt), line = rp[name]
@@ -322,6 +331,8 @@ def build(ref):
         "choice": ("choice", {"seed": 7, "a": 10, "shape": [4]}),
         "choice_norep": ("choice", {"seed": 7, "a": 10, "shape": [4], "replace": False}),
         "choice_p": ("choice", {"seed": 7, "a": 5, "shape": [6], "p": [0.1, 0.2, 0.3, 0.2, 0.2]}),
+        # random_uniform(random_key(0, impl = "rbg"), 4) (test-random.R:140)
+        "rbg_uniform": ("uniform", {"seed": 0, "impl": "rbg", "shape": [4]}),
     }
     for name, (op, args) in rr_calls.items():
         (shape, vals, dt), line = rr[name]

@@ -151,10 +151,23 @@ def evaluate(case, be):
     part = bool(a.get("partitionable", True))
 
     def key_of(seed):
+        if a.get("impl", "threefry2x32") != "threefry2x32":
+            return be.rbg_seed(seed, x64, a["impl"])
         k = be.seed(seed, x64)
         if "fold" in a:
             k = be.fold_in(k, a["fold"])
         return k
+
+    if op == "rbg_bits":
+        n = shape_size(a["shape"])
+        return np.asarray(be.rbg_bits(key_of(a["seed"]), a["bits"], n)).reshape(tuple(a["shape"]))
+    if op == "rbg_split":
+        return np.asarray(be.rbg_split(key_of(a["seed"]), a["num"], a["impl"], part))
+    if op == "rbg_fold_in":
+        return np.asarray(be.rbg_fold_in(key_of(a["seed"]), a["data"], a["impl"]))
+    if op == "rbg_vmap_bits":
+        keys = be.rbg_split(key_of(a["seed"]), a["nkeys"], a["impl"], part)
+        return np.asarray(be.rbg_vmap_bits(keys, tuple(a["shape"])))
 
     if op == "threefry_2x32":
         return be.threefry_2x32(a["key"], a["count"])
@@ -287,6 +300,10 @@ class OracleBackend:
         return self.o.random_bits(key, bw, n, part)
 
     def uniform(self, key, dt, n, part, mn, mx):
+        if len(key) == 4:  # an rbg key: the same transform of the Philox bits
+            assert dt == "float32" and (mn, mx) == (0.0, 1.0)
+            b = self.o.rbg_bits(key, 32, n)
+            return ((b >> np.uint32(9)) | np.uint32(0x3F800000)).view(np.float32) - np.float32(1)
         return self.o.uniform(key, dt, n, part, mn, mx, fma=self.mul_add_fma)
 
     def uniform_array_bounds(self, key, dt, shape, part, mn, mx):
@@ -313,6 +330,27 @@ class OracleBackend:
 
     def randint(self, key, shape, mn, mx, dt, part):
         return self.o.randint(key, shape, mn, mx, dt, part)
+
+    def rbg_seed(self, s, x64, impl):
+        return self.o.rbg_seed(s, x64)
+
+    def rbg_bits(self, key, bw, n):
+        return self.o.rbg_bits(key, bw, n)
+
+    def rbg_split(self, key, num, impl, part):
+        if impl == "rbg":
+            return self.o.rbg_split(key, num, part)
+        return self.o.rbg_unsafe_split(key, num)
+
+    def rbg_fold_in(self, key, data, impl):
+        if impl == "rbg":
+            return self.o.rbg_fold_in(key, data)
+        return self.o.rbg_unsafe_fold_in(key, data)
+
+    def rbg_vmap_bits(self, keys, shape):
+        # the batching rule of rng_bit_generator: every lane draws from the first key
+        n = shape_size(shape)
+        return self.o.rbg_bits(keys[0], 32, len(keys) * n).reshape((len(keys),) + shape)
 
     def sample(self, key, kind, dt, n, part, mode="low"):
         if kind == "gumbel" and mode != "low":

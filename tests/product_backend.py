@@ -46,6 +46,27 @@ class ProductBackend:
         with flags(x64, self.part):
             return to_np(jr.random_PRNGKey(s))
 
+    def rbg_seed(self, s, x64, impl):
+        with flags(x64, self.part):
+            return jr.random_key(s, impl=impl)
+
+    def rbg_bits(self, key, bw, n):
+        with self._ctx():
+            return to_np(jr.random_bits(key, (n,), f"uint{bw}"))
+
+    def rbg_split(self, key, num, impl, part):
+        with self._ctx(part):
+            return to_np(jr.random_key_data(jr.random_split(key, num)))
+
+    def rbg_fold_in(self, key, data, impl):
+        with self._ctx():
+            return to_np(jr.random_key_data(jr.random_fold_in(key, data)))
+
+    def rbg_vmap_bits(self, keys, shape):
+        with self._ctx():
+            typed = jr.random_wrap_key_data(torch.tensor(np.asarray(keys, np.uint32)), impl="rbg")
+            return to_np(jr.vmap(lambda k: jr.random_bits(k, shape))(typed))
+
     def fold_in(self, key, data):
         with self._ctx():
             return to_np(jr.random_fold_in(torch.tensor(np.asarray(key, np.uint32)), int(data)))
@@ -59,6 +80,9 @@ class ProductBackend:
             return to_np(jr.random_bits(torch.tensor(np.asarray(key, np.uint32)), (n,), f"uint{bw}"))
 
     def uniform(self, key, dt, n, part, mn, mx):
+        if isinstance(key, jr.PRNGKeyArray):
+            with flags(dt == "float64" or self.x64, part):
+                return _raw(jr.random_uniform(key, (n,), dt, mn, mx), dt)
         with flags(dt == "float64" or self.x64, part):
             out = jr.random_uniform(torch.tensor(np.asarray(key, np.uint32)), (n,), dt, mn, mx)
         return _raw(out, dt)

@@ -187,7 +187,7 @@ def test_randint_bounds_follow_reference(monkeypatch):
         calls.append((name, args))
 
     monkeypatch.setattr(jrr, "_flat_keys", lambda k: k.data.reshape(-1, 2))
-    monkeypatch.setattr(jrr, "_k_split", lambda kd, shape, layout: torch.zeros(
+    monkeypatch.setattr(jrr, "_k_split", lambda kd, shape, layout, impl=None: torch.zeros(
         (kd.shape[0], 2, 2), dtype=U32))
     monkeypatch.setattr(jrr, "_k_bits", lambda kd, size, bw, layout: torch.zeros(
         (kd.shape[0], size), dtype=jrr._TORCH[f"uint{bw}"]))

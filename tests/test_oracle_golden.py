@@ -34,7 +34,8 @@ def test_golden_covers_the_path():
     assert {"threefry_2x32", "seed", "split", "fold_in", "bits", "uniform", "normal",
             "bernoulli", "vmap_split", "vmap_fold_in", "vmap_uniform", "vmap_normal",
             "erf_inv", "randint", "exponential", "gumbel", "laplace", "logistic",
-            "truncated_normal", "permutation", "choice"} <= ops
+            "truncated_normal", "permutation", "choice", "rbg_bits", "rbg_split",
+            "rbg_fold_in", "rbg_vmap_bits"} <= ops
     # both layouts and x64 are pinned
     assert any(c["args"].get("partitionable") is False for c in CASES)
     assert any(c["args"].get("x64") for c in CASES)
@@ -87,3 +88,31 @@ def test_original_layout_segments(oracle):
     last = oracle.random_bits(sub[1], 32, 6, False)
     got = oracle.bits_at(key, 32, size, False, [(1 << 32) - 1 + i for i in range(6)])
     assert np.array_equal(got, last)
+
+
+def test_philox_known_answers(oracle):
+    # Random123's published known-answer vectors for philox4x32-10 (the first is also the
+    # reference's rbg_bits, test-prng.R:50)
+    assert oracle.philox4x32([0, 0, 0, 0], [0, 0]) == [0x6627E8D5, 0xE169C58D, 0xBC57AC4C,
+                                                       0x9B00DBD8]
+    m = 0xFFFFFFFF
+    assert oracle.philox4x32([m, m, m, m], [m, m]) == [0x408F276D, 0x41C83B0E, 0xA20BC7C6,
+                                                       0x6D5451FD]
+    assert oracle.philox4x32([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344],
+                             [0xA4093822, 0x299F31D0]) == [0xD16CFE09, 0x94FDCCEB, 0x5001E420,
+                                                           0x24126EA1]
+
+
+def test_rbg_stream_layout(oracle):
+    """32-bit element e is word e % 4 of block e / 4; the 128-bit counter carries across
+    words; 8/16-bit elements are the low bits of the 32-bit ones."""
+    q = [0xFFFFFFFF, 0xFFFFFFFF, 0xFFFFFFFF, 7]
+    w = oracle.rbg_bits(q, 32, 12)
+    for b in range(3):
+        c = ((0xFFFFFFFF | 0xFFFFFFFF << 32 | 0xFFFFFFFF << 64 | 7 << 96) + b) % (1 << 128)
+        want = oracle.philox4x32([(c >> (32 * i)) & 0xFFFFFFFF for i in range(4)], q[:2])
+        assert list(w[4 * b:4 * b + 4]) == want
+    assert np.array_equal(oracle.rbg_bits(q, 8, 12), (w & 0xFF).astype(np.uint8))
+    assert np.array_equal(oracle.rbg_bits(q, 16, 12), (w & 0xFFFF).astype(np.uint16))
+    w64 = oracle.rbg_bits(q, 64, 6)
+    assert np.array_equal(w64, w.astype(np.uint64)[0::2] | w.astype(np.uint64)[1::2] << 32)
