@@ -191,6 +191,8 @@ WORKLOADS = {
                "(split, two 32-bit draws, combine)",
     "perm": "random_permutation(random_key(7L), 2^26) int32: 3 shuffle rounds, each 2^26 "
             "32-bit sort keys and a 4-pass stable radix sort of (key, position) pairs",
+    "rbg": "random_bits(random_key(0L, impl = \"rbg\"), 2^30) uint32: XLA RngBitGenerator "
+           "(Philox4x32-10), 4 words per block",
 }
 
 # Kernels of this library one call launches (1 unless listed): randint = split, two bit
@@ -217,6 +219,18 @@ def workload_cpu_baseline(c, min_seconds=2.0):
     orc.set_threads(threads)
     if c in _SAMPLER_WORKLOADS or c in ("truncnorm", "randint"):
         return sampler_cpu_baseline(c, min_seconds)
+    if c == "rbg":  # the C restatement of the Philox stream, 2^24 words
+        n = 1 << 24
+        out = np.empty(n, dtype=np.uint32)
+        q = orc._key4([0, 0, 0, 0])
+        lib.orc_rbg_bits(q, 32, 1 << 30, 0, n, out.ctypes.data_as(ctypes.c_void_p))
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < min_seconds:
+            lib.orc_rbg_bits(q, 32, 1 << 30, 0, n, out.ctypes.data_as(ctypes.c_void_p))
+            reps += 1
+        dt = time.perf_counter() - t0
+        return {"value": reps * n / dt, "unit": "words/s", "cores": threads, "kind": "port",
+                "sample": f"first 2^24 words, {reps} times (C restatement, OpenMP)"}
     if c == "perm":  # the restatement (C bits, numpy stable argsort) on 2^22 elements
         n = 1 << 22
         orc.set_threads(threads)
@@ -348,6 +362,11 @@ def run_workload(args):
         step = lambda: jr.random_randint(key, (8192, 8192), 0, 1000)
         # two 2^26-word draws (written and read back by the combine) and the int32 result
         words, blocks, out_bytes, dt = 1 << 26, 1 << 27, 3 * (4 << 26), "int32"
+    elif c == "rbg":
+        key = jr.random_key(0, impl="rbg")
+        step = lambda: jr.random_bits(key, (1 << 30,))
+        # a store-bound stream: 2^28 Philox blocks, 4 GiB written
+        words, blocks, out_bytes, dt = 1 << 30, 1 << 28, 4 << 30, "u32"
     elif c == "perm":
         key = jr.random_key(7)
         step = lambda: jr.random_permutation(key, 1 << 26)
@@ -397,6 +416,8 @@ def run_workload(args):
     if c == "perm":  # a sort: memory-bound, the cipher is 3 blocks per element
         roofline = dict(hbm, bound="hbm", bytes_per_element=3 * PERM_BYTES_PER_ROUND,
                         int_frac=bps / peak_blocks)
+    elif c == "rbg":  # Philox: ~40 multiplies per 4 words, below the store bandwidth
+        roofline = dict(hbm, bound="hbm", bytes_per_element=4)
     else:
         roofline = {"bound": "int", "unit": "Tops/s", "achieved": bps * OPS_PER_BLOCK / 1e12,
                     "peak": peak_blocks * OPS_PER_BLOCK / 1e12, "frac": bps / peak_blocks,
@@ -604,9 +625,9 @@ def main():
     ap.add_argument("--config", default="c4",
                     help="c4 = the 2^34-word bits request (the benchmark); c1, c2, c2o, c3, c5 = "
                          "the other workloads, one GPU, one JSON line each; exp, gumbel, "
-                         "logistic, truncnorm, randint, perm = the derived samplers and the "
-                         "permutation; 'all' = every secondary workload; 'samplers' = the "
-                         "derived samplers and the permutation")
+                         "logistic, truncnorm, randint, perm, rbg = the derived samplers, the "
+                         "permutation and rbg bits; 'all' = every secondary workload; "
+                         "'samplers' = those last seven")
     ap.add_argument("--words-log2", type=int, default=34,
                     help="request size 2^k words (34 = the benchmark; smaller only for profiling)")
     ap.add_argument("--e2e-words", type=int, default=1 << 30)
