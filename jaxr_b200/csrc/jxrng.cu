@@ -25,6 +25,7 @@
 #include <cstring>
 #include <limits>
 #include <mutex>
+#include <type_traits>
 #include <string>
 #include <vector>
 
@@ -386,6 +387,44 @@ int launch_op(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin
       return launch_original_segmented<Op>(keys, nkeys, size, begin, count, op, out, st);
     return launch_words<Op>(keys, nkeys, size, begin, count, op, out, st);
   }
+}
+
+// ---- float32 sampler tables ----------------------------------------------------------
+
+template <class Op>
+__global__ void k_build_table(Op op, float* __restrict__ table) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < (1u << 23);
+       i += gridDim.x * blockDim.x)
+    table[i] = op(i << 9);
+}
+
+// Requests of at least this many float32 samples use (and, the first time, build) the
+// sampler's table.
+constexpr uint64_t kTableMin = 1ull << 22;
+constexpr int kTables = 8;  // 0: normal, 1 + kind: the log-transform samplers
+std::mutex g_tab_mu;
+float* g_tables[64][kTables];
+
+// The table of `op` on the current device (built on stream st and waited for once), or
+// nullptr when the device memory for it cannot be had (the caller evaluates the op).
+template <class Op>
+const float* f32_table(int id, const Op& op, cudaStream_t st) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_tab_mu);
+  if (g_tables[dev][id]) return g_tables[dev][id];
+  float* t = nullptr;
+  if (cudaMalloc(&t, sizeof(float) << 23) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  k_build_table<Op><<<1024, 256, 0, st>>>(op, t);
+  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaFree(t);
+    return nullptr;
+  }
+  g_tables[dev][id] = t;
+  return t;
 }
 
 int check_request(const void* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
@@ -1077,7 +1116,12 @@ int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
   if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   switch (dtype) {
-    case JXR_F32: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32{}, out, st);
+    case JXR_F32: {
+      if (count * (uint64_t)nkeys >= kTableMin)
+        if (const float* t = f32_table(0, OpNormalF32{}, st))
+          return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{t}, out, st);
+      return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32{}, out, st);
+    }
     case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF64{}, out, st);
     case JXR_F16: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<false>{}, out, st);
     default: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<true>{}, out, st);
@@ -1278,7 +1322,14 @@ int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
   int rc = check_dtype(dtype);
   if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
+  const bool big = count * (uint64_t)nkeys >= kTableMin;
   return visit_sample_op(kind, dtype, [&](const auto& op) {
+    using O = std::decay_t<decltype(op)>;
+    if constexpr (std::is_same_v<typename O::Out, float>) {
+      if (big)
+        if (const float* t = f32_table(1 + kind, op, st))
+          return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{t}, out, st);
+    }
     return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
   });
 }

@@ -305,6 +305,17 @@ struct OpNormalF32 {
   }
 };
 
+// A float32 sampler whose output depends only on bits >> 9 (the 23 mantissa bits of its
+// unit float), read back from the table of its 2^23 results (32 MiB, built on the device by
+// the sampler's own op, so identical to evaluating it): the cipher plus one L2 load.
+struct OpTableF32 {
+  static constexpr int kBits = 32;
+  using Bits = uint32_t;
+  using Out = float;
+  const float* __restrict__ table;
+  __device__ __forceinline__ Out operator()(Bits b) const { return __ldg(table + (b >> 9)); }
+};
+
 struct OpNormalF64 {
   static constexpr int kBits = 64;
   static constexpr int kGroups = 2;
