@@ -161,6 +161,15 @@ int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
 int jxr_sample_from_bits(const void* bits, int64_t n, int kind, int dtype, void* out,
                          void* stream);
 
+/* randint (R/random.R:306-359) with scalar bounds in one pass, partitionable layout:
+ * keys_hi / keys_lo are the two halves of split(key) for each of nkeys keys (u32[nkeys][2]
+ * each); minval / maxval are the bounds clipped to the sampling dtype (nbits = 32 or 64,
+ * signed if is_signed), sign- or zero-extended; out_of_range says maxval exceeded the
+ * dtype's maximum.  Writes the low out_bits of each sample, out: [nkeys][count]. */
+int jxr_randint(const uint32_t* keys_hi, const uint32_t* keys_lo, int64_t nkeys, uint64_t size,
+                uint64_t begin, uint64_t count, int nbits, int is_signed, int64_t minval,
+                int64_t maxval, int out_of_range, int out_bits, void* out, void* stream);
+
 /* randint (R/random.R:306-359) from its two draws: hi and lo are nbits-bit (32 or 64)
  * random_bits of the two halves of split(key); minval/maxval are the bounds already
  * clipped and converted to the sampling dtype (signed if is_signed), sign- or

@@ -50,6 +50,8 @@ SIGNATURES = {
     "jxr_uniform_affine": [_vp, _vp, _vp, _i64, _int, _u32, _vp, _vp],
     "jxr_bernoulli_from_uniform": [_vp, _vp, _vp, _i64, _int, _vp, _vp],
     "jxr_sample": [_vp, _i64, _u64, _u64, _u64, _int, _int, _int, _vp, _vp],
+    "jxr_randint": [_vp, _vp, _i64, _u64, _u64, _u64, _int, _int, _i64, _i64, _int, _int, _vp,
+                    _vp],
     "jxr_randint_combine": [_vp, _vp, _i64, _int, _int, _vp, _i64, _vp, _i64, _vp, _i64, _int,
                             _vp, _vp],
     "jxr_gumbel_rows": [_vp, _vp, _i64, _int, _int, _vp, _vp],

@@ -824,6 +824,50 @@ __global__ void k_rbg_advance(const uint32_t* __restrict__ key, uint64_t nblocks
   }
 }
 
+// randint with scalar bounds in one pass (partitionable layout): element c of key row r
+// draws hi and lo from the two halves (kh, kl) of split(key) at counter c and writes the
+// low out_bits of a + offset (randint_offset with the span's multiplier precomputed).
+// Each thread takes 4 consecutive elements of one row.
+template <class U, class OutT>
+__global__ void __launch_bounds__(256)
+k_randint_fused(const uint32_t* __restrict__ kh, const uint32_t* __restrict__ kl, int64_t nkeys,
+                uint64_t begin, uint64_t count, U a, U span, U mult, PipeConsts pc,
+                OutT* __restrict__ out) {
+  constexpr int V = 4;
+  const uint64_t per_row = (count + V - 1) / V;
+  const uint64_t units = per_row * (uint64_t)nkeys;
+  for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units;
+       u += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = u / per_row, j0 = (u % per_row) * V;
+    const KeySchedule sh = make_schedule(kh[2 * r], kh[2 * r + 1]);
+    const KeySchedule sl = make_schedule(kl[2 * r], kl[2 * r + 1]);
+    uint32_t h0[V], h1[V], l0[V], l1[V];
+#pragma unroll
+    for (int t = 0; t < V; ++t) {
+      const uint64_t c = begin + j0 + t;
+      h0[t] = l0[t] = (uint32_t)(c >> 32);
+      h1[t] = l1[t] = (uint32_t)c;
+    }
+    threefry20<V, ProductMix>(sh, h0, h1, pc);
+    threefry20<V, ProductMix>(sl, l0, l1, pc);
+    OutT* dst = out + r * count + j0;
+#pragma unroll
+    for (int t = 0; t < V; ++t) {
+      if (j0 + t >= count) break;
+      U hi, lo;
+      if constexpr (sizeof(U) == 4) {
+        hi = h0[t] ^ h1[t];
+        lo = l0[t] ^ l1[t];
+      } else {
+        hi = (uint64_t)h0[t] << 32 | h1[t];
+        lo = (uint64_t)l0[t] << 32 | l1[t];
+      }
+      const U off = span == 0 ? lo : (U)((U)((hi % span) * mult) + lo % span) % span;
+      dst[t] = (OutT)(U)(a + off);
+    }
+  }
+}
+
 // randint: out = low out_bits of (minval + offset(hi, lo, span)) in the sampling dtype
 template <class U, bool kSigned>
 __global__ void k_randint_combine(const U* __restrict__ hi, const U* __restrict__ lo, int64_t n,
@@ -1347,6 +1391,61 @@ int jxr_sample_from_bits(const void* bits, int64_t n, int kind, int dtype, void*
   return visit_sample_op(kind, dtype, [&](const auto& op) {
     return launch_from_bits(bits, n, op, out, st, grid);
   });
+}
+
+int jxr_randint(const uint32_t* keys_hi, const uint32_t* keys_lo, int64_t nkeys, uint64_t size,
+                uint64_t begin, uint64_t count, int nbits, int is_signed, int64_t minval,
+                int64_t maxval, int out_of_range, int out_bits, void* out, void* stream) {
+  if (nbits != 32 && nbits != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "randint samples in 32 or 64 bits, got %d", nbits);
+  if (out_bits != 8 && out_bits != 16 && out_bits != 32 && out_bits != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "out_bits must be 8, 16, 32 or 64, got %d", out_bits);
+  if (out_bits > nbits)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "out_bits (%d) wider than the sampling width (%d)",
+                out_bits, nbits);
+  int rc = check_request(keys_hi, nkeys, size, begin, count, JXR_LAYOUT_PARTITIONABLE, out);
+  if (rc) return rc;
+  if (!count || !nkeys) return JXR_OK;
+  if (!keys_lo) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  // the span rules of R/random.R:343-350, in the sampling width
+  const bool empty = is_signed ? (maxval <= minval) : ((uint64_t)maxval <= (uint64_t)minval);
+  uint64_t span = (uint64_t)maxval - (uint64_t)minval;
+  if (nbits == 32) span &= 0xFFFFFFFFull;
+  if (empty) span = 1;
+  else if (out_of_range) span = nbits == 32 ? ((span + 1) & 0xFFFFFFFFull) : span + 1;
+  // multiplier = ((2^(nbits/2) % span)^2 mod 2^nbits) % span, as the reference's unsigned
+  // lax_mul wraps
+  uint64_t mult = 0;
+  if (span) {
+    if (nbits == 32) {
+      const uint32_t m = (uint32_t)((1ull << 16) % span);
+      mult = (uint32_t)(m * m) % span;
+    } else {
+      const uint64_t m = (1ull << 32) % span;
+      mult = (m * m) % span;
+    }
+  }
+  const uint64_t units = (count + 3) / 4 * (uint64_t)nkeys;
+  int grid;
+  if ((rc = resident_grid(k_randint_fused<uint32_t, uint32_t>, (units + 255) / 256, &grid)))
+    return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+#define JXR_RI(U, O)                                                                          \
+  k_randint_fused<U, O><<<grid, 256, 0, st>>>(keys_hi, keys_lo, nkeys, begin, count,          \
+                                              (U)(uint64_t)minval, (U)span, (U)mult, kPipe,  \
+                                              (O*)out)
+  if (nbits == 32) {
+    switch (out_bits) {
+      case 8: JXR_RI(uint32_t, uint8_t); break;
+      case 16: JXR_RI(uint32_t, uint16_t); break;
+      default: JXR_RI(uint32_t, uint32_t);
+    }
+  } else {
+    JXR_RI(uint64_t, uint64_t);
+  }
+#undef JXR_RI
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
 }
 
 int jxr_randint_combine(const void* hi, const void* lo, int64_t n, int nbits, int is_signed,

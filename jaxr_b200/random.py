@@ -1148,14 +1148,22 @@ def random_randint(key, shape, minval, maxval, dtype=None):
         return t.to(dev), (0 if len(flat) == 1 else 1)
 
     clip = lambda v: min(max(v, smin), smax)  # noqa: E731 - convert_and_clip_integer
+    halves = _k_split(kd, (2,), layout, k.impl)
+    out = torch.empty((kd.shape[0], size), dtype=_TORCH[dt], device=dev)
+    if (mn.size == 1 and mx.size == 1 and k.impl == "threefry2x32"
+            and layout == nat.LAYOUT_PARTITIONABLE):
+        # scalar bounds: both draws and the combine in one kernel
+        mn1, mx1 = int(np.asarray(mn).ravel()[0]), int(np.asarray(mx).ravel()[0])
+        nat.call("jxr_randint", _ptr(halves[:, 0].contiguous()), _ptr(halves[:, 1].contiguous()),
+                 kd.shape[0], size, 0, size, sbits, int(ssigned), _wrap_int(clip(mn1), 64, True),
+                 _wrap_int(clip(mx1), 64, True), int(mx1 > smax), dbits, _ptr(out), _stream())
+        return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
     oor_t, oor_s = as_param(mx, lambda v: int(v > smax))
     mn_t, mn_s = as_param(mn, clip)
     mx_t, mx_s = as_param(mx, clip)
     oor_t = oor_t.to(torch.uint8)
-    halves = _k_split(kd, (2,), layout, k.impl)
     hi = _k_bits(halves[:, 0].contiguous(), size, sbits, layout)
     lo = _k_bits(halves[:, 1].contiguous(), size, sbits, layout)
-    out = torch.empty((kd.shape[0], size), dtype=_TORCH[dt], device=dev)
     if size:
         if mn_s == 0 and mx_s == 0:  # one call over every key's row
             nat.call("jxr_randint_combine", _ptr(hi), _ptr(lo), kd.shape[0] * size, sbits,

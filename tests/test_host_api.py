@@ -199,6 +199,8 @@ def test_randint_bounds_follow_reference(monkeypatch):
         calls.clear()
         jr.random_randint(raw(2), *args, **kw)
         (name, a), = calls
+        if name == "jxr_randint":  # scalar bounds, one fused kernel
+            return (a[6], a[7], [a[8]], [a[9]], [a[10]], a[11])
         assert name == "jxr_randint_combine"
         return (a[3], a[4], a[5].tolist(), a[7].tolist(), a[9].tolist(), a[11])
 
@@ -207,6 +209,8 @@ def test_randint_bounds_follow_reference(monkeypatch):
     assert bounds(6, -1000, 1000, "int8") == (32, 1, [-128], [128], [0], 8)
     assert bounds(6, 0, 10) == (32, 1, [0], [10], [0], 32)
     assert bounds(6, 0.0, 7.9) == (32, 1, [0], [7], [0], 32)  # 7.9 truncates
+    with jr.with_jax_config("jax_threefry_partitionable", False):  # the three-kernel path
+        assert bounds(6, -1000, 1000, "int8") == (32, 1, [-128], [128], [0], 8)
     with jr.with_jax_config("jax_enable_x64", True):
         assert bounds(6, 0, 1 << 40, "int32") == (32, 1, [0], [2**31 - 1], [1], 32)
         assert bounds(6, -5, 1 << 33, "uint32") == (32, 0, [0], [2**32 - 1], [1], 32)
