@@ -4,7 +4,7 @@
 // rnd_shuffle sorts the array by fresh 32-bit random keys, num_rounds times, with a
 // stable key-value sort (lax_sort_key_val).  Here every round sorts (key, position)
 // pairs: 8 bits per pass, each pass a histogram kernel, a scan of the per-tile counts and
-// a scatter.  The scatter ranks a tile's elements stably (warp match_any per chunk of 32,
+// a scatter.  The scatter ranks a tile's elements stably (warp ballots per chunk of 32,
 // running counts per virtual warp), places them by digit in shared memory and writes each
 // digit's run to its global offset, so the global stores are contiguous runs.
 #pragma once
@@ -84,10 +84,23 @@ __device__ __forceinline__ uint32_t block256_exclusive(uint32_t v, uint32_t* tmp
   return r;
 }
 
+// Lanes of the warp holding the same 9-bit value (a digit, or 256 for no element): one
+// ballot per bit, the complement where this lane's bit is 0.
+__device__ __forceinline__ unsigned peers_of(uint32_t d) {
+  unsigned m = 0xFFFFFFFFu;
+#pragma unroll
+  for (int bit = 0; bit < 9; ++bit) {
+    const bool set = (d >> bit) & 1u;
+    const unsigned b = __ballot_sync(0xFFFFFFFFu, set);
+    m &= set ? b : ~b;
+  }
+  return m;
+}
+
 // One pass: pairs of tile t go, stably by digit, to their global positions.  The tile is
 // ranked by 16 "virtual warps" of 512 elements (warp w takes [w * 1024, (w + 1) * 1024) as
-// two halves, ranked interleaved for ILP), each in chunks of 32: match_any gives the lanes
-// of equal digit, and the group's leader adds the group's size to the virtual warp's
+// two halves, ranked interleaved for ILP), each in chunks of 32: nine ballots give the
+// lanes of equal digit, and the group's leader adds the group's size to the virtual warp's
 // running count of that digit in shared memory with an atomic that returns the count
 // before it (the group's start).  One scan over (digit, virtual warp) then gives every
 // element its place in the tile; the tile is staged in shared memory by digit and each
@@ -133,8 +146,7 @@ k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ v
     const bool va = i0 + c * 32 < cnt, vb = i0 + (c + kChunks) * 32 < cnt;
     const uint32_t da = va ? ((kreg[c] >> shift) & 255u) : 256u;
     const uint32_t db = vb ? ((kreg[c + kChunks] >> shift) & 255u) : 256u;
-    const unsigned pa = __match_any_sync(0xFFFFFFFFu, da);
-    const unsigned pb = __match_any_sync(0xFFFFFFFFu, db);
+    const unsigned pa = peers_of(da), pb = peers_of(db);
     const int la = __ffs(pa) - 1, lb_ = __ffs(pb) - 1;
     uint32_t oa = 0, ob = 0;
     if (va && lane == la) oa = atomicAdd(&wc0[da], (uint32_t)__popc(pa));

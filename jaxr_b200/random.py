@@ -1154,7 +1154,8 @@ def random_randint(key, shape, minval, maxval, dtype=None):
             and layout == nat.LAYOUT_PARTITIONABLE):
         # scalar bounds: both draws and the combine in one kernel
         mn1, mx1 = int(np.asarray(mn).ravel()[0]), int(np.asarray(mx).ravel()[0])
-        nat.call("jxr_randint", _ptr(halves[:, 0].contiguous()), _ptr(halves[:, 1].contiguous()),
+        kh, kl = halves[:, 0].contiguous(), halves[:, 1].contiguous()  # alive until launched
+        nat.call("jxr_randint", _ptr(kh), _ptr(kl),
                  kd.shape[0], size, 0, size, sbits, int(ssigned), _wrap_int(clip(mn1), 64, True),
                  _wrap_int(clip(mx1), 64, True), int(mx1 > smax), dbits, _ptr(out), _stream())
         return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
