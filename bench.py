@@ -148,7 +148,7 @@ def run_reference(args):
                                    "OpenMP over all host threads"},
         "e2e": {"value": value, "unit": "words/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -438,7 +438,7 @@ def run_workload(args):
     }
     jr.enable_x64(old[0])
     jr.jax_config_update("jax_threefry_partitionable", old[1])
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -608,7 +608,7 @@ def run_ours(args):
         }
         if gather is not None:
             line["gather"] = gather
-        print(json.dumps(line), flush=True)
+        emit(line)
     del out
     if world > 1:
         dist.barrier()
@@ -616,7 +616,29 @@ def run_ours(args):
     return 0
 
 
+_JSON_OUT = None
+
+
+def keep_stdout_for_json():
+    """Route file descriptor 1 to stderr for the rest of the process (library banners,
+    e.g. NCCL's version line, land there) and keep the original stdout for the JSON
+    result lines alone."""
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        fd = os.dup(1)
+        os.dup2(2, 1)
+        _JSON_OUT = os.fdopen(fd, "w")
+
+
+def emit(line):
+    keep_stdout_for_json()
+    _JSON_OUT.write(json.dumps(line) + "\n")
+    _JSON_OUT.flush()
+
+
 def main():
+    keep_stdout_for_json()
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
