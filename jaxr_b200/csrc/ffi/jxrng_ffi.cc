@@ -1,0 +1,193 @@
+// XLA typed-FFI handlers over libjxrng: the kernels made callable from jit-compiled jaxR
+// programs through ffi_register_target / ffi_call (R/ffi.R:58-81, :241-319), written
+// against XLA's FFI C API (xla/ffi/api/c_api.h).
+//
+//   jxr_ffi_random_bits      platform "cuda"  key u32[..., 2] and the result on the device,
+//                                             launched on XLA's stream
+//   jxr_ffi_random_bits_cpu  platform "cpu"   key and result in host memory (the CPU PJRT
+//                                             plugin jaxR runs on); the GPU computes the bits
+//                                             through jxr_random_bits_host_static, which
+//                                             allocates nothing
+//   jxr_ffi_uniform          platform "cuda"  float result, attributes minval, maxval
+//   jxr_ffi_normal           platform "cuda"  float result
+//
+// One argument, the key buffer (threefry2x32 data, u32[*batch, 2]: one key per batch row,
+// as ffi_call's vmap methods deliver them); one result, whose dtype gives the bit width
+// or the float type and whose element count divided by the number of keys gives each
+// key's request.  Attribute "partitionable" (a bool scalar; the value of
+// jax_threefry_partitionable, default true) selects the counter layout.  Errors come back
+// as XLA FFI errors carrying the library's message.
+
+#include <cstring>
+
+#include "jxrng.h"
+#include "xla/ffi/api/c_api.h"
+
+namespace {
+
+XLA_FFI_Error* error(const XLA_FFI_Api* api, XLA_FFI_Error_Code code, const char* msg) {
+  XLA_FFI_Error_Create_Args a;
+  std::memset(&a, 0, sizeof(a));
+  a.struct_size = XLA_FFI_Error_Create_Args_STRUCT_SIZE;
+  a.message = msg;
+  a.errc = code;
+  return api->XLA_FFI_Error_Create(&a);
+}
+
+// XLA first calls a handler with a metadata extension to learn its API version and traits.
+bool answer_metadata(XLA_FFI_CallFrame* cf) {
+  XLA_FFI_Extension_Base* ext = cf->extension_start;
+  if (!ext || ext->type != XLA_FFI_Extension_Metadata) return false;
+  XLA_FFI_Metadata* m = reinterpret_cast<XLA_FFI_Metadata_Extension*>(ext)->metadata;
+  m->api_version.major_version = XLA_FFI_API_MAJOR;
+  m->api_version.minor_version = XLA_FFI_API_MINOR;
+  m->traits = 0;
+  return true;
+}
+
+struct Frame {
+  const XLA_FFI_Buffer* key = nullptr;
+  const XLA_FFI_Buffer* out = nullptr;
+  int64_t nkeys = 0, out_elems = 0;
+  int layout = JXR_LAYOUT_PARTITIONABLE;
+  double minval = 0.0, maxval = 1.0;
+};
+
+int64_t elements(const XLA_FFI_Buffer* b) {
+  int64_t n = 1;
+  for (int64_t i = 0; i < b->rank; ++i) n *= b->dims[i];
+  return n;
+}
+
+bool name_is(const XLA_FFI_ByteSpan* s, const char* name) {
+  return s->len == std::strlen(name) && std::memcmp(s->ptr, name, s->len) == 0;
+}
+
+double scalar_value(const XLA_FFI_Scalar* sc) {
+  switch (sc->dtype) {
+    case XLA_FFI_DataType_PRED: return *static_cast<const uint8_t*>(sc->value) ? 1.0 : 0.0;
+    case XLA_FFI_DataType_S32: return *static_cast<const int32_t*>(sc->value);
+    case XLA_FFI_DataType_S64: return (double)*static_cast<const int64_t*>(sc->value);
+    case XLA_FFI_DataType_F32: return *static_cast<const float*>(sc->value);
+    case XLA_FFI_DataType_F64: return *static_cast<const double*>(sc->value);
+    default: return 0.0;
+  }
+}
+
+// Checks and decodes the frame: one u32[..., 2] key buffer, one result buffer, scalar
+// attributes.  Returns nullptr on success.
+XLA_FFI_Error* decode(XLA_FFI_CallFrame* cf, Frame* f) {
+  const XLA_FFI_Api* api = cf->api;
+  if (cf->args.size != 1 || cf->args.types[0] != XLA_FFI_ArgType_BUFFER)
+    return error(api, XLA_FFI_Error_Code_INVALID_ARGUMENT, "jxrng: expected one key buffer argument");
+  if (cf->rets.size != 1 || cf->rets.types[0] != XLA_FFI_RetType_BUFFER)
+    return error(api, XLA_FFI_Error_Code_INVALID_ARGUMENT, "jxrng: expected one result buffer");
+  f->key = static_cast<const XLA_FFI_Buffer*>(cf->args.args[0]);
+  f->out = static_cast<const XLA_FFI_Buffer*>(cf->rets.rets[0]);
+  if (f->key->dtype != XLA_FFI_DataType_U32 || f->key->rank < 1 ||
+      f->key->dims[f->key->rank - 1] != 2)
+    return error(api, XLA_FFI_Error_Code_INVALID_ARGUMENT,
+                 "jxrng: the key must be threefry2x32 key data, uint32[..., 2]");
+  f->nkeys = elements(f->key) / 2;
+  f->out_elems = elements(f->out);
+  if (f->nkeys < 1 || f->out_elems % f->nkeys)
+    return error(api, XLA_FFI_Error_Code_INVALID_ARGUMENT,
+                 "jxrng: the result's element count is not a multiple of the number of keys");
+  for (int64_t i = 0; i < cf->attrs.size; ++i) {
+    if (cf->attrs.types[i] != XLA_FFI_AttrType_SCALAR) continue;
+    const auto* sc = static_cast<const XLA_FFI_Scalar*>(cf->attrs.attrs[i]);
+    const XLA_FFI_ByteSpan* name = cf->attrs.names[i];
+    if (name_is(name, "partitionable"))
+      f->layout = scalar_value(sc) != 0.0 ? JXR_LAYOUT_PARTITIONABLE : JXR_LAYOUT_ORIGINAL;
+    else if (name_is(name, "minval")) f->minval = scalar_value(sc);
+    else if (name_is(name, "maxval")) f->maxval = scalar_value(sc);
+  }
+  return nullptr;
+}
+
+int bits_of(XLA_FFI_DataType t) {
+  switch (t) {
+    case XLA_FFI_DataType_U8: return 8;
+    case XLA_FFI_DataType_U16: return 16;
+    case XLA_FFI_DataType_U32: return 32;
+    case XLA_FFI_DataType_U64: return 64;
+    default: return 0;
+  }
+}
+
+int float_code(XLA_FFI_DataType t) {
+  switch (t) {
+    case XLA_FFI_DataType_F32: return JXR_F32;
+    case XLA_FFI_DataType_F64: return JXR_F64;
+    case XLA_FFI_DataType_F16: return JXR_F16;
+    case XLA_FFI_DataType_BF16: return JXR_BF16;
+    default: return -1;
+  }
+}
+
+XLA_FFI_Error* stream_of(XLA_FFI_CallFrame* cf, void** stream) {
+  XLA_FFI_Stream_Get_Args a;
+  std::memset(&a, 0, sizeof(a));
+  a.struct_size = XLA_FFI_Stream_Get_Args_STRUCT_SIZE;
+  a.ctx = cf->ctx;
+  XLA_FFI_Error* e = cf->api->XLA_FFI_Stream_Get(&a);
+  *stream = a.stream;
+  return e;
+}
+
+XLA_FFI_Error* status(const XLA_FFI_Api* api, int rc) {
+  if (rc == JXR_OK) return nullptr;
+  const XLA_FFI_Error_Code code = rc == JXR_ERR_INVALID_ARGUMENT ? XLA_FFI_Error_Code_INVALID_ARGUMENT
+                                  : rc == JXR_ERR_NOT_IMPLEMENTED ? XLA_FFI_Error_Code_UNIMPLEMENTED
+                                                                  : XLA_FFI_Error_Code_INTERNAL;
+  return error(api, code, jxr_last_error());
+}
+
+enum Kind { kBits, kBitsHost, kUniform, kNormal };
+
+XLA_FFI_Error* handle(XLA_FFI_CallFrame* cf, Kind kind) {
+  if (answer_metadata(cf)) return nullptr;
+  if (cf->stage != XLA_FFI_ExecutionStage_EXECUTE) return nullptr;
+  Frame f;
+  if (XLA_FFI_Error* e = decode(cf, &f)) return e;
+  const uint64_t size = (uint64_t)(f.out_elems / f.nkeys);
+  const uint32_t* keys = static_cast<const uint32_t*>(f.key->data);
+  void* out = f.out->data;
+  if (kind == kBitsHost) {
+    const int bits = bits_of(f.out->dtype);
+    if (!bits)
+      return error(cf->api, XLA_FFI_Error_Code_INVALID_ARGUMENT,
+                   "jxrng: random bits need an unsigned 8/16/32/64-bit result");
+    return status(cf->api, jxr_random_bits_host_static(keys, f.nkeys, size, 0, size, f.layout,
+                                                       bits, out, nullptr));
+  }
+  void* stream = nullptr;
+  if (XLA_FFI_Error* e = stream_of(cf, &stream)) return e;
+  if (kind == kBits) {
+    const int bits = bits_of(f.out->dtype);
+    if (!bits)
+      return error(cf->api, XLA_FFI_Error_Code_INVALID_ARGUMENT,
+                   "jxrng: random bits need an unsigned 8/16/32/64-bit result");
+    return status(cf->api, jxr_random_bits(keys, f.nkeys, size, 0, size, f.layout, bits, out,
+                                           stream));
+  }
+  const int dt = float_code(f.out->dtype);
+  if (dt < 0)
+    return error(cf->api, XLA_FFI_Error_Code_INVALID_ARGUMENT,
+                 "jxrng: the samplers need a float32/float64/float16/bfloat16 result");
+  if (kind == kUniform)
+    return status(cf->api, jxr_uniform(keys, f.nkeys, size, 0, size, f.layout, dt, f.minval,
+                                       f.maxval, 0, out, stream));
+  return status(cf->api, jxr_normal(keys, f.nkeys, size, 0, size, f.layout, dt, out, stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+XLA_FFI_Error* jxr_ffi_random_bits(XLA_FFI_CallFrame* cf) { return handle(cf, kBits); }
+XLA_FFI_Error* jxr_ffi_random_bits_cpu(XLA_FFI_CallFrame* cf) { return handle(cf, kBitsHost); }
+XLA_FFI_Error* jxr_ffi_uniform(XLA_FFI_CallFrame* cf) { return handle(cf, kUniform); }
+XLA_FFI_Error* jxr_ffi_normal(XLA_FFI_CallFrame* cf) { return handle(cf, kNormal); }
+
+}  // extern "C"
