@@ -442,6 +442,32 @@ def run_workload(args):
     return 0
 
 
+def bind_to_gpu_cpus(torch, dev_index):
+    """Restrict this process to the CPUs NVML reports as local to the GPU (NUMA), so that
+    pinned host buffers are allocated next to it; returns the previous CPU set, or None
+    when NVML cannot say.  Only this process's affinity changes."""
+    try:
+        import pynvml
+        p = torch.cuda.get_device_properties(dev_index)
+        bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            words = ((os.cpu_count() or 64) + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * w + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1}
+        old = os.sched_getaffinity(0)
+        cpus &= old
+        if cpus and cpus != old:
+            os.sched_setaffinity(0, cpus)
+            return old
+    except Exception as e:  # noqa: BLE001 - affinity is an optimisation only
+        log(f"note: no NUMA binding ({type(e).__name__}: {e})")
+    return None
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -458,6 +484,7 @@ def run_ours(args):
         log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    all_cpus = bind_to_gpu_cpus(torch, local)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
@@ -592,6 +619,8 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if all_cpus:  # the CPU baseline gets every host core back
+            os.sched_setaffinity(0, all_cpus)
         v, threads, sample = cpu_words_per_s()
         cpu = {"value": v, "unit": "words/s", "cores": threads, "kind": "port",
                "sample": sample + " (C restatement of the reference, OpenMP)"}
