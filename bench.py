@@ -174,7 +174,7 @@ def probe_peak(torch, nat, dev, iters=2000):
     return best
 
 
-# ---- the other BASELINE workloads (N = 1; not the driver's line) ---------------------------------
+# ---- the other named workloads C1-C3, C5 and the derived samplers (N = 1, one line each) ----
 
 WORKLOADS = {
     "c1": "random_bits(random_key(0L), shape=(2^20,)) uint32, partitionable, x32",

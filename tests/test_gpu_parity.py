@@ -3,7 +3,7 @@
 Integer bits and keys must match exactly; uniforms and bernoulli draws exactly
 (bitwise); normals within 2 ulp (float32) / 1e-12 relative (float64), and every
 normal the reference recorded at 0 ulp.  Sizes run from the empty request to the
-BASELINE workloads; large requests are checked at sampled positions, which the
+named workloads (C1-C5); large requests are checked at sampled positions, which the
 oracle computes element by element from their counters.
 """
 
@@ -288,7 +288,7 @@ def test_normal_bernoulli_fused_equals_separate():
                 assert np.array_equal(to_np(ber), to_np(jr.random_bernoulli(k, 0.3, (129, 33))))
 
 
-# ---- the BASELINE workloads, checked at sampled positions ---------------------------------------
+# ---- the named workloads C1-C5, checked at sampled positions ----------------------------------
 
 def _sample_idx(size, n=4096, seed=0):
     rng = np.random.default_rng(seed)
