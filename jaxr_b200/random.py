@@ -1284,8 +1284,11 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
     replacement through randint; without, the first draws of a permutation; with p,
     searchsorted of the cumulative sums (replace) or the top draws of gumbel + log(p)."""
     k, _, nb = _check_key("choice", key)
-    if nb:
-        raise JaxNotImplementedError("random_choice takes a single key")
+    if nb:  # vmap over keys: each key's choice, stacked along the batch axes
+        rows = [random_choice(PRNGKeyArray(d, k.impl), a, shape, replace, p, axis, mode)
+                for d in k.data.reshape((-1, _KEY_WORDS[k.impl]))]
+        out = torch.stack(rows) if rows else torch.empty((0,))
+        return _rebatch(out.reshape(k.shape[:nb] + tuple(out.shape[1:])), nb)
     shape = canon_shape(shape)
     av, anb = _unbatch(a)
     if anb:

@@ -161,3 +161,11 @@ def test_argsort_float_stable(dt):
         key = np.where(x == 0, 0.0, x)
         want = np.argsort(-key if desc else key, kind="stable")
         assert np.array_equal(got, want), (dt, desc)
+
+
+def test_choice_key_batches():
+    keys = np.stack([orc.seed(s) for s in range(3)])
+    out = jr.vmap(lambda k: jr.random_choice(k, 20, (4,), False))(dev_key(keys))
+    assert tuple(out.shape) == (3, 4)
+    for r in range(3):
+        assert np.array_equal(to_np(out[r]), orc.choice(keys[r], 20, (4,), False))
