@@ -1662,7 +1662,7 @@ int sort_pairs(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t
   for (int shift = 0; shift < bits; shift += 8) {
     k_sort_hist<<<(unsigned)nt, kSortThreads, 0, st>>>(k, n, shift, nt, s.counts);
     k_sort_scan_rows<<<256, 1024, 0, st>>>(s.counts, nt, s.totals);
-    k_sort_scatter<<<(unsigned)nt, kSortThreads, kSortScatterSmem, st>>>(
+    k_sort_scatter<<<(unsigned)nt, kScatterThreads, kSortScatterSmem, st>>>(
         k, v, n, shift, nt, s.counts, s.totals, k2, v2, s.err);
     JXR_CUDA(cudaGetLastError());
     std::swap(k, k2);

@@ -13,12 +13,14 @@
 
 namespace jxr {
 
-constexpr int kSortThreads = 256;
+constexpr int kSortThreads = 256;  // histogram CTAs
 constexpr int kSortItems = 32;
 constexpr int kSortTile = kSortThreads * kSortItems;  // 8192 elements per tile
-// dynamic shared memory of the scatter: keys and values of a tile, digit counts of 16
+constexpr int kScatterThreads = 512;                  // scatter CTAs: 16 warps per tile
+constexpr int kScatterVW = 2 * kScatterThreads / 32;  // virtual warps (two per warp)
+// dynamic shared memory of the scatter: keys and values of a tile, digit counts of the
 // virtual warps, three 256-entry tables
-constexpr int kSortScatterSmem = 2 * kSortTile * 4 + 16 * 256 * 4 + 3 * 256 * 4;
+constexpr int kSortScatterSmem = 2 * kSortTile * 4 + kScatterVW * 256 * 4 + 3 * 256 * 4;
 
 // counts[d * ntiles + t] = number of keys of tile t whose digit at `shift` is d
 __global__ void __launch_bounds__(kSortThreads)
@@ -27,16 +29,30 @@ k_sort_hist(const uint32_t* __restrict__ keys, int64_t n, int shift, int64_t nti
   __shared__ uint32_t h[256];
   h[threadIdx.x] = 0;
   const int64_t base = (int64_t)blockIdx.x * kSortTile;
-  uint32_t d[kSortItems];  // all loads in flight before the first atomic
+  const int64_t rem = n - base;
+  const int cnt = rem < kSortTile ? (int)rem : kSortTile;
+  // 16-byte loads when the buffer allows (tiles start 32 KiB apart, so the tile has the
+  // buffer's alignment); scalar loads for the rest
+  const int nvec = ((uintptr_t)keys & 15u) == 0 ? cnt / 4 : 0;
+  const uint4* k4 = reinterpret_cast<const uint4*>(keys + base);
+  uint4 q[kSortItems / 4];
 #pragma unroll
-  for (int j = 0; j < kSortItems; ++j) {
-    const int64_t e = base + (int64_t)j * kSortThreads + threadIdx.x;
-    d[j] = e < n ? (keys[e] >> shift) & 255u : 256u;
+  for (int j = 0; j < kSortItems / 4; ++j) {
+    const int v = j * kSortThreads + threadIdx.x;
+    q[j] = v < nvec ? k4[v] : make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
 #pragma unroll
-  for (int j = 0; j < kSortItems; ++j)
-    if (d[j] < 256u) atomicAdd(&h[d[j]], 1u);
+  for (int j = 0; j < kSortItems / 4; ++j) {
+    if (j * kSortThreads + (int)threadIdx.x < nvec) {
+      atomicAdd(&h[(q[j].x >> shift) & 255u], 1u);
+      atomicAdd(&h[(q[j].y >> shift) & 255u], 1u);
+      atomicAdd(&h[(q[j].z >> shift) & 255u], 1u);
+      atomicAdd(&h[(q[j].w >> shift) & 255u], 1u);
+    }
+  }
+  for (int i = nvec * 4 + threadIdx.x; i < cnt; i += kSortThreads)
+    atomicAdd(&h[(keys[base + i] >> shift) & 255u], 1u);
   __syncthreads();
   counts[(int64_t)threadIdx.x * ntiles + blockIdx.x] = h[threadIdx.x];
 }
@@ -69,17 +85,19 @@ k_sort_scan_rows(uint32_t* __restrict__ counts, int64_t ntiles, uint32_t* __rest
   if (threadIdx.x == 1023) totals[blockIdx.x] = sh[1023];
 }
 
-// exclusive scan of v over the 256 threads of the block (all threads call it)
+// exclusive scan over the 256 values v of threads 0..255 (every thread of the block calls
+// it; threads 256 and up pass 0 and get 0)
 __device__ __forceinline__ uint32_t block256_exclusive(uint32_t v, uint32_t* tmp) {
-  tmp[threadIdx.x] = v;
+  const bool on = threadIdx.x < 256u;
+  if (on) tmp[threadIdx.x] = v;
   __syncthreads();
   for (int off = 1; off < 256; off <<= 1) {
-    const uint32_t a = threadIdx.x >= (unsigned)off ? tmp[threadIdx.x - off] : 0u;
+    const uint32_t a = on && threadIdx.x >= (unsigned)off ? tmp[threadIdx.x - off] : 0u;
     __syncthreads();
-    tmp[threadIdx.x] += a;
+    if (on) tmp[threadIdx.x] += a;
     __syncthreads();
   }
-  const uint32_t r = tmp[threadIdx.x] - v;
+  const uint32_t r = on ? tmp[threadIdx.x] - v : 0u;
   __syncthreads();
   return r;
 }
@@ -98,8 +116,8 @@ __device__ __forceinline__ unsigned peers_of(uint32_t d) {
 }
 
 // One pass: pairs of tile t go, stably by digit, to their global positions.  The tile is
-// ranked by 16 "virtual warps" of 512 elements (warp w takes [w * 1024, (w + 1) * 1024) as
-// two halves, ranked interleaved for ILP), each in chunks of 32: nine ballots give the
+// ranked by 32 "virtual warps" of 256 elements (warp w of 16 takes [w * 512, (w + 1) * 512)
+// as two halves, ranked interleaved for ILP), each in chunks of 32: nine ballots give the
 // lanes of equal digit, and the group's leader adds the group's size to the virtual warp's
 // running count of that digit in shared memory with an atomic that returns the count
 // before it (the group's start).  One scan over (digit, virtual warp) then gives every
@@ -107,21 +125,20 @@ __device__ __forceinline__ unsigned peers_of(uint32_t d) {
 // digit's run written to its global offset, so the global stores are contiguous runs.
 // Positions outside [0, n) or a local rank outside the tile (which correct scans never
 // give) are skipped and set *err.
-__global__ void __launch_bounds__(kSortThreads, 2)
+__global__ void __launch_bounds__(kScatterThreads, 2)
 k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
                int shift, int64_t ntiles, const uint32_t* __restrict__ counts,
                const uint32_t* __restrict__ totals, uint32_t* __restrict__ keys_out,
                uint32_t* __restrict__ vals_out, int* __restrict__ err) {
-  constexpr int kWarps = kSortThreads / 32, kPerWarp = kSortTile / kWarps;  // 1024
-  constexpr int kHalf = kPerWarp / 2, kChunks = kHalf / 32;                  // 512, 16
-  constexpr int kVW = 2 * kWarps;                                            // 16
+  constexpr int kWarps = kScatterThreads / 32, kPerWarp = kSortTile / kWarps;  // 16, 512
+  constexpr int kHalf = kPerWarp / 2, kChunks = kHalf / 32;                     // 256, 8
   extern __shared__ uint32_t smem[];
-  uint32_t* s_keys = smem;                    // [kSortTile]
-  uint32_t* s_vals = s_keys + kSortTile;      // [kSortTile]
-  uint32_t* s_wc = s_vals + kSortTile;        // [kVW][256] counts, then start positions
-  uint32_t* s_lbase = s_wc + kVW * 256;       // [256] tile-local start of each digit
-  uint32_t* s_gbase = s_lbase + 256;          // [256] global start of this tile's digit run
-  uint32_t* s_tmp = s_gbase + 256;            // [256]
+  uint32_t* s_keys = smem;                        // [kSortTile]
+  uint32_t* s_vals = s_keys + kSortTile;          // [kSortTile]
+  uint32_t* s_wc = s_vals + kSortTile;            // [kScatterVW][256] counts, then starts
+  uint32_t* s_lbase = s_wc + kScatterVW * 256;    // [256] tile-local start of each digit
+  uint32_t* s_gbase = s_lbase + 256;              // [256] global start of this tile's digit run
+  uint32_t* s_tmp = s_gbase + 256;                // [256]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t base = (int64_t)blockIdx.x * kSortTile;
   const int64_t rem = n - base;
@@ -158,21 +175,25 @@ k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ v
   }
   __syncthreads();
 
-  // thread d: starts of digit d for each virtual warp within the tile, the tile's digit
-  // starts, and the global start of the tile's run of digit d
+  // thread d < 256: starts of digit d for each virtual warp within the tile, the tile's
+  // digit starts, and the global start of the tile's run of digit d
   uint32_t run = 0;
-#pragma unroll
-  for (int w = 0; w < kVW; ++w) {
-    const uint32_t c = s_wc[w * 256 + tid];
-    s_wc[w * 256 + tid] = run;
-    run += c;
+  if (tid < 256) {
+#pragma unroll 8
+    for (int w = 0; w < kScatterVW; ++w) {
+      const uint32_t c = s_wc[w * 256 + tid];
+      s_wc[w * 256 + tid] = run;
+      run += c;
+    }
   }
   const uint32_t lbase = block256_exclusive(run, s_tmp);
-  const uint32_t gb = block256_exclusive(totals[tid], s_tmp);
-#pragma unroll
-  for (int w = 0; w < kVW; ++w) s_wc[w * 256 + tid] += lbase;
-  s_lbase[tid] = lbase;
-  s_gbase[tid] = gb + counts[(int64_t)tid * ntiles + blockIdx.x];
+  const uint32_t gb = block256_exclusive(tid < 256 ? totals[tid] : 0u, s_tmp);
+  if (tid < 256) {
+#pragma unroll 8
+    for (int w = 0; w < kScatterVW; ++w) s_wc[w * 256 + tid] += lbase;
+    s_lbase[tid] = lbase;
+    s_gbase[tid] = gb + counts[(int64_t)tid * ntiles + blockIdx.x];
+  }
   __syncthreads();
 
 #pragma unroll
@@ -191,7 +212,7 @@ k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ v
   __syncthreads();
 
   // write each digit's run to its global position
-  for (int i = tid; i < cnt; i += kSortThreads) {
+  for (int i = tid; i < cnt; i += kScatterThreads) {
     const uint32_t key = s_keys[i];
     const uint32_t d = (key >> shift) & 255u;
     const int64_t g = (int64_t)s_gbase[d] + (int64_t)i - (int64_t)s_lbase[d];
