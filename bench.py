@@ -188,17 +188,17 @@ WORKLOADS = {
     "logistic": "random_logistic(random_key(7L), (8192, 8192)) float32",
     "truncnorm": "random_truncated_normal(random_key(7L), -1, 2, (8192, 8192)) float32",
     "randint": "random_randint(random_key(7L), (8192, 8192), 0L, 1000L) int32 "
-               "(split, two 32-bit draws, combine)",
+               "(split, then both 32-bit draws and the combine in one kernel)",
     "perm": "random_permutation(random_key(7L), 2^26) int32: 3 shuffle rounds, each 2^26 "
             "32-bit sort keys and a 4-pass stable radix sort of (key, position) pairs",
     "rbg": "random_bits(random_key(0L, impl = \"rbg\"), 2^30) uint32: XLA RngBitGenerator "
            "(Philox4x32-10), 4 words per block",
 }
 
-# Kernels of this library one call launches (1 unless listed): randint = split, two bit
-# draws, combine; perm = iota, then per round split, bits and 4 x (histogram, scan,
-# scatter).
-LAUNCHES_PER_CALL = {"randint": 4, "perm": 1 + 3 * 14}
+# Kernels of this library one call launches (1 unless listed): randint = split and the
+# fused draws + combine; perm = iota, then per round split, bits and 4 x (histogram,
+# scan, scatter).
+LAUNCHES_PER_CALL = {"randint": 2, "perm": 1 + 3 * 14}
 
 # Algorithmic HBM bytes per element of one shuffle round: the 32-bit sort keys written
 # once, then per 8-bit pass one read and one write of the (key, position) pair.
@@ -360,8 +360,8 @@ def run_workload(args):
     elif c == "randint":
         key = jr.random_key(7)
         step = lambda: jr.random_randint(key, (8192, 8192), 0, 1000)
-        # two 2^26-word draws (written and read back by the combine) and the int32 result
-        words, blocks, out_bytes, dt = 1 << 26, 1 << 27, 3 * (4 << 26), "int32"
+        # two cipher blocks per output (one per split key half), the int32 result written
+        words, blocks, out_bytes, dt = 1 << 26, 1 << 27, 4 << 26, "int32"
     elif c == "rbg":
         key = jr.random_key(0, impl="rbg")
         step = lambda: jr.random_bits(key, (1 << 30,))
