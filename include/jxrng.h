@@ -251,6 +251,17 @@ int jxr_rbg_blocks(const uint32_t* key, uint64_t first, uint64_t stride, int64_t
 int jxr_rbg_unsafe_fold_in(const uint32_t* keys, int64_t nkeys, const uint32_t* data, int64_t ndata,
                            int lanes_from_first, uint32_t* out, void* stream);
 
+/* random_bits over several GPUs from one process (the R session): device i of ndev
+ * computes elements [size * i / ndev, size * (i + 1) / ndev) of the request of one
+ * threefry key (keys[i]: that key's u32[2] on device i), on streams[i] (or the default
+ * stream).  With gather_to < 0 device i writes its slab to outs[i] (its own memory); with
+ * gather_to = g, every device's kernel stores its slab straight into gather_out (size
+ * elements on device g) through peer access over NVLink.  Asynchronous: synchronise the
+ * streams to wait.  The current device is left as it was. */
+int jxr_random_bits_multi(const int* devices, int ndev, const uint32_t* const* keys, uint64_t size,
+                          int layout, int bit_width, void* const* outs, int gather_to,
+                          void* gather_out, void* const* streams);
+
 /* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
  * element-wise for F32 or F64. */
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);

@@ -1929,6 +1929,54 @@ int jxr_rbg_unsafe_fold_in(const uint32_t* keys, int64_t nkeys, const uint32_t* 
   return JXR_OK;
 }
 
+int jxr_random_bits_multi(const int* devices, int ndev, const uint32_t* const* keys, uint64_t size,
+                          int layout, int bit_width, void* const* outs, int gather_to,
+                          void* gather_out, void* const* streams) {
+  if (ndev < 1 || !devices || !keys)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "need ndev >= 1 devices and their keys");
+  if (gather_to >= ndev) return fail(JXR_ERR_INVALID_ARGUMENT, "gather_to must be < ndev");
+  if (gather_to >= 0 ? !gather_out && size : !outs)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "null output");
+  if (bit_width != 8 && bit_width != 16 && bit_width != 32 && bit_width != 64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "bit_width must be 8, 16, 32 or 64, got %d", bit_width);
+  int prev = 0;
+  JXR_CUDA(cudaGetDevice(&prev));
+  int rc = JXR_OK;
+  for (int i = 0; i < ndev && rc == JXR_OK; ++i) {
+    const uint64_t lo = size * (uint64_t)i / (uint64_t)ndev;
+    const uint64_t hi = size * (uint64_t)(i + 1) / (uint64_t)ndev;
+    if (cudaSetDevice(devices[i]) != cudaSuccess) {
+      rc = fail(JXR_ERR_CUDA, "cannot select device %d", devices[i]);
+      break;
+    }
+    void* dst;
+    if (gather_to >= 0) {
+      const int root = devices[gather_to];
+      if (root != devices[i]) {  // this device stores straight into the root's buffer
+        int can = 0;
+        cudaDeviceCanAccessPeer(&can, devices[i], root);
+        if (!can) {
+          rc = fail(JXR_ERR_CUDA, "device %d cannot access device %d's memory", devices[i], root);
+          break;
+        }
+        const cudaError_t e = cudaDeviceEnablePeerAccess(root, 0);
+        if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+          rc = fail(JXR_ERR_CUDA, "peer access %d -> %d: %s", devices[i], root, cudaGetErrorString(e));
+          break;
+        }
+        cudaGetLastError();  // clear "already enabled"
+      }
+      dst = (char*)gather_out + lo * (uint64_t)(bit_width / 8);
+    } else {
+      dst = outs[i];
+    }
+    rc = jxr_random_bits(keys[i], 1, size, lo, hi - lo, layout, bit_width, dst,
+                         streams ? streams[i] : nullptr);
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream) {
   if (dtype != JXR_F32 && dtype != JXR_F64)
     return fail(JXR_ERR_INVALID_ARGUMENT, "erf_inv supports dtype 0 (f32) or 1 (f64), got %d", dtype);

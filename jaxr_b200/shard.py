@@ -172,3 +172,42 @@ def random_bits_gathered(key, shape, root=0, dtype=None, out=None, group=None):
     torch.cuda.current_stream().synchronize()
     dist.barrier(group=group)
     return whole
+
+
+# ---- several GPUs from one process -----------------------------------------------------------
+
+def random_bits_multi(key, shape, devices=None, dtype=None, gather_to=None):
+    """random_bits(key, shape, dtype) computed by several GPUs of this process (all visible
+    ones by default): device i produces elements shard_range(size, i, len(devices)).
+    Returns the list of slabs (a 1-D tensor on each device), or, with gather_to = i, the
+    whole flattened request on devices[i], every device's kernel storing its slab there
+    through peer access.  Threefry keys only."""
+    import torch
+    k, _, nb = _check_key("bits", key)
+    if nb or k.impl != "threefry2x32":
+        raise JaxValueError("random_bits_multi takes a single threefry2x32 key")
+    dt = default_uint() if dtype is None else canonicalize_dtype(dtype)
+    size = _size(canon_shape(shape))
+    devices = list(range(torch.cuda.device_count())) if devices is None else list(devices)
+    n = len(devices)
+    keys = [k.data.reshape(2).to(torch.device("cuda", d)).contiguous() for d in devices]
+    streams = [torch.cuda.current_stream(d).cuda_stream for d in devices]
+    dev_arr = (ctypes.c_int * n)(*devices)
+    key_arr = (ctypes.c_void_p * n)(*[t.data_ptr() for t in keys])
+    st_arr = (ctypes.c_void_p * n)(*streams)
+    if gather_to is None:
+        slabs = [torch.empty(shard_range(size, i, n)[1] - shard_range(size, i, n)[0],
+                             dtype=_TORCH[dt], device=torch.device("cuda", d))
+                 for i, d in enumerate(devices)]
+        out_arr = (ctypes.c_void_p * n)(*[t.data_ptr() for t in slabs])
+        nat.call("jxr_random_bits_multi", dev_arr, n, key_arr, size, _layout(), _BITS[dt],
+                 out_arr, -1, None, st_arr)
+        for d in devices:
+            torch.cuda.current_stream(d).synchronize()
+        return slabs
+    whole = torch.empty(size, dtype=_TORCH[dt], device=torch.device("cuda", devices[gather_to]))
+    nat.call("jxr_random_bits_multi", dev_arr, n, key_arr, size, _layout(), _BITS[dt], None,
+             int(gather_to), whole.data_ptr(), st_arr)
+    for d in devices:
+        torch.cuda.current_stream(d).synchronize()
+    return whole
