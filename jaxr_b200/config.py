@@ -3,7 +3,9 @@
 Only the options this path reads are kept: jax_enable_x64 (default dtypes and seed
 width), jax_threefry_partitionable (counter layout), jax_default_prng_impl and
 jax_random_seed_offset; jax_legacy_prng_key governs raw uint32 keys;
-jax_use_high_dynamic_range_gumbel picks random_gumbel's default mode.
+jax_use_high_dynamic_range_gumbel picks random_gumbel's default mode;
+jax_accurate_erf_inv (JAX's alternative erf_inv, R/lax_special.R:1324-1331) is recognised
+and refused by the functions that would use it.
 """
 
 from __future__ import annotations
@@ -21,6 +23,7 @@ _DEFAULTS = {
     "jax_random_seed_offset": 0,
     "jax_legacy_prng_key": "allow",
     "jax_use_high_dynamic_range_gumbel": False,
+    "jax_accurate_erf_inv": False,
 }
 
 _config = dict(_DEFAULTS)
@@ -52,7 +55,7 @@ def jax_config_update(name, value):
         raise JaxValueError(f"Unrecognized config option: {name}")
     old = _config[name]
     if name in ("jax_enable_x64", "jax_threefry_partitionable",
-                "jax_use_high_dynamic_range_gumbel"):
+                "jax_use_high_dynamic_range_gumbel", "jax_accurate_erf_inv"):
         value = bool(value)
     if name == "jax_legacy_prng_key" and value not in ("allow", "warn", "error"):
         raise JaxValueError("jax_legacy_prng_key must be one of 'allow', 'warn', 'error'")

@@ -215,3 +215,13 @@ def test_randint_bounds_follow_reference(monkeypatch):
         assert bounds(6, 0, 1 << 40, "int32") == (32, 1, [0], [2**31 - 1], [1], 32)
         assert bounds(6, -5, 1 << 33, "uint32") == (32, 0, [0], [2**32 - 1], [1], 32)
         assert bounds(6, 0, 10, "uint64") == (64, 0, [0], [10], [0], 64)
+
+
+def test_accurate_erf_inv_option_is_refused():
+    k = raw(2)
+    with jr.with_jax_config("jax_accurate_erf_inv", True):
+        for call in (lambda: jr.random_normal(k, 3), lambda: jr.lax_erf_inv(np.zeros(3)),
+                     lambda: jr.random_truncated_normal(k, -1, 1, 3)):
+            with pytest.raises(jr.JaxNotImplementedError, match="jax_accurate_erf_inv"):
+                call()
+    assert jr.jax_config("jax_accurate_erf_inv") is False
