@@ -443,3 +443,32 @@ def test_original_layout_key_splitting_samplers(oracle):
     nat.call("jxr_normal", kd.data_ptr(), 1, size, begin, count, 0, nat.F64, out.data_ptr(), st)
     want = oracle.normal_at(key, "float64", size, False, True, range(begin, begin + count))
     assert np.all(np.abs(to_np(out) - want) <= 1e-12 * np.abs(want))
+
+
+def test_bits_fuzz_ranges_and_batches(oracle):
+    """300 seeded random requests through jxr_random_bits: 1-5 keys, sizes up to 2^20 (and
+    a few past 2^32 words, checked by range), random [begin, begin + count), both layouts,
+    all widths; every element against the oracle."""
+    from jaxr_b200 import _native as nat
+    rng = np.random.default_rng(2026)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(300):
+        nkeys = int(rng.integers(1, 6))
+        big = rng.random() < 0.05
+        size = int(rng.integers(1 << 32, (1 << 33))) if big else int(rng.integers(0, 1 << 20))
+        begin = int(rng.integers(0, size + 1))
+        count = int(rng.integers(0, min(size - begin, 5000 if big else 1 << 18) + 1))
+        part = bool(rng.integers(0, 2)) if not big else True
+        bw = int(rng.choice([8, 16, 32, 64]))
+        keys = rng.integers(0, 1 << 32, (nkeys, 2), dtype=np.uint64).astype(np.uint32)
+        kd = torch.from_numpy(keys).cuda()
+        out = torch.empty((nkeys, max(count, 1)), dtype={8: torch.uint8, 16: torch.int16,
+                                                          32: torch.int32, 64: torch.int64}[bw],
+                          device="cuda")
+        nat.call("jxr_random_bits", kd.data_ptr(), nkeys, size, begin, count,
+                 1 if part else 0, bw, out.data_ptr(), stream)
+        got = out.cpu().numpy()[:, :count].view({8: np.uint8, 16: np.uint16, 32: np.uint32,
+                                                 64: np.uint64}[bw])
+        for r in range(nkeys):
+            want = oracle.random_bits(keys[r], bw, size, part, begin, count)
+            assert np.array_equal(got[r], want), (nkeys, size, begin, count, part, bw, r)
