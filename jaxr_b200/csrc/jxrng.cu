@@ -406,13 +406,21 @@ std::mutex g_tab_mu;
 float* g_tables[64][kTables];
 
 // The table of `op` on the current device (built on stream st and waited for once), or
-// nullptr when the device memory for it cannot be had (the caller evaluates the op).
+// nullptr when it cannot be built now (no device memory, or st is being captured into a
+// CUDA graph); the caller then evaluates the op.
 template <class Op>
 const float* f32_table(int id, const Op& op, cudaStream_t st) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(g_tab_mu);
   if (g_tables[dev][id]) return g_tables[dev][id];
+  // building allocates and waits for the stream, which a CUDA graph capture forbids: the
+  // caller then evaluates the op directly
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
   float* t = nullptr;
   if (cudaMalloc(&t, sizeof(float) << 23) != cudaSuccess) {
     cudaGetLastError();

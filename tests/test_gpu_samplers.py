@@ -250,3 +250,39 @@ def test_randint_large_uniformity():
     counts = torch.bincount(out.long(), minlength=10).cpu().numpy()
     assert counts.sum() == 1 << 24
     assert np.all(np.abs(counts - (1 << 24) / 10) < 0.005 * (1 << 24) / 10)
+
+
+_GRAPH_CHILD = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import jaxr_b200 as jr
+from jaxr_b200 import _native as nat
+n = 1 << 22
+key = jr.random_key_data(jr.random_key(4242)).cuda()
+out = torch.empty(n, dtype=torch.float32, device="cuda")
+g = torch.cuda.CUDAGraph()
+s = torch.cuda.Stream()
+s.wait_stream(torch.cuda.current_stream())
+with torch.cuda.stream(s):
+    with torch.cuda.graph(g, stream=s):
+        nat.call("jxr_sample", key.data_ptr(), 1, n, 0, n, 1, 0, 0, out.data_ptr(), s.cuda_stream)
+g.replay()
+torch.cuda.synchronize()
+want = jr.random_exponential(key, (n,))
+assert torch.equal(out.view(torch.int32), want.view(torch.int32))
+del g
+print("graph ok")
+"""
+
+
+def test_samplers_inside_a_cuda_graph():
+    """A fresh process captures a float32 exponential of 2^22 outputs into a CUDA graph
+    before the sampler's table exists: evaluated directly during capture (building the
+    table would wait on the stream), identical to the table path afterwards."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _GRAPH_CHILD, root], capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0 and "graph ok" in r.stdout, r.stderr[-2000:]
