@@ -917,6 +917,8 @@ int small_grid(int64_t n, int* grid) {
 
 // ---- fused normal + bernoulli (same key and shape: one cipher pass, two outputs) ---------
 
+constexpr int kNBBytes = 32;  // normal bytes per thread and iteration of k_normal_bernoulli
+
 template <class OpN, class OpB, int kCtr, bool kOneKey>
 __global__ void __launch_bounds__(kThreads)
     k_normal_bernoulli(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
@@ -924,7 +926,7 @@ __global__ void __launch_bounds__(kThreads)
                        OpB opb, PipeConsts pc, typename OpN::Out* __restrict__ nout,
                        uint8_t* __restrict__ bout) {
   using Out = typename OpN::Out;
-  constexpr int V = 16 / sizeof(Out);
+  constexpr int V = kNBBytes / sizeof(Out);  // outputs per iteration: two 16-byte stores
   const uint64_t stride = (uint64_t)gridDim.x * kThreads;
   for (uint64_t c = (uint64_t)blockIdx.x * kThreads + threadIdx.x; c < nchunks; c += stride) {
     const uint64_t row = kOneKey ? 0 : c / chunks_per_row;
@@ -938,24 +940,25 @@ __global__ void __launch_bounds__(kThreads)
       x1[v] = kCtr == kCtrIndex ? (uint32_t)i : (uint32_t)(size + i);
     }
     threefry20<V, ProductMix>(s, x0, x1, pc);
-    Vec16<Out> r;
+    Vec16<Out> r[2];
     uint8_t bb[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       const auto bits = Draw<OpN::kBits>::get(x0[v], x1[v]);
-      r.v[v] = opn(bits);
+      r[v / (V / 2)].v[v % (V / 2)] = opn(bits);
       bb[v] = opb(bits);
     }
     Out* dst = nout + row * count + pos;
     uint8_t* bdst = bout + row * count + pos;
     if (vec_ok && pos + V <= count) {
-      *reinterpret_cast<uint4*>(dst) = r.u;
+      reinterpret_cast<uint4*>(dst)[0] = r[0].u;
+      reinterpret_cast<uint4*>(dst)[1] = r[1].u;
 #pragma unroll
       for (int v = 0; v < V; ++v) bdst[v] = bb[v];
     } else {
 #pragma unroll
       for (int v = 0; v < V; ++v)
-        if (pos + v < count) { dst[v] = r.v[v]; bdst[v] = bb[v]; }
+        if (pos + v < count) { dst[v] = r[v / (V / 2)].v[v % (V / 2)]; bdst[v] = bb[v]; }
     }
   }
 }
@@ -965,7 +968,7 @@ int launch_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, 
                             uint64_t count, int layout, const OpN& opn, const OpB& opb, void* nout,
                             uint8_t* bout, cudaStream_t st) {
   using Out = typename OpN::Out;
-  constexpr int V = 16 / sizeof(Out);
+  constexpr int V = kNBBytes / sizeof(Out);
   if (count == 0 || nkeys == 0) return JXR_OK;
   const uint64_t cpr = (count + V - 1) / V;
   const uint64_t nchunks = cpr * (uint64_t)nkeys;
