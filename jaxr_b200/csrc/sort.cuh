@@ -4,9 +4,10 @@
 // rnd_shuffle sorts the array by fresh 32-bit random keys, num_rounds times, with a
 // stable key-value sort (lax_sort_key_val).  Here every round sorts (key, position)
 // pairs: 8 bits per pass, each pass a histogram kernel, a scan of the per-tile counts and
-// a scatter.  The scatter ranks a tile's elements stably (warp ballots per chunk of 32,
-// running counts per virtual warp), places them by digit in shared memory and writes each
-// digit's run to its global offset, so the global stores are contiguous runs.
+// a scatter.  The scatter ranks a tile's elements stably (per warp and chunk of 32, the
+// lanes of equal digit from bits ORed into shared memory, running counts per warp),
+// places them by digit in shared memory and writes each digit's run to its global
+// offset, so the global stores are contiguous runs.
 #pragma once
 
 #include <cstdint>
@@ -17,10 +18,10 @@ constexpr int kSortThreads = 256;  // histogram CTAs
 constexpr int kSortItems = 32;
 constexpr int kSortTile = kSortThreads * kSortItems;  // 8192 elements per tile
 constexpr int kScatterThreads = 512;                  // scatter CTAs: 16 warps per tile
-constexpr int kScatterVW = 2 * kScatterThreads / 32;  // virtual warps (two per warp)
-// dynamic shared memory of the scatter: keys and values of a tile, digit counts of the
-// virtual warps, three 256-entry tables
-constexpr int kSortScatterSmem = 2 * kSortTile * 4 + kScatterVW * 256 * 4 + 3 * 256 * 4;
+constexpr int kScatterWarps = kScatterThreads / 32;
+// dynamic shared memory of the scatter: keys and values of a tile, per warp the running
+// digit counts and the lane masks of one chunk, three 256-entry tables
+constexpr int kSortScatterSmem = 2 * kSortTile * 4 + 2 * kScatterWarps * 256 * 4 + 3 * 256 * 4;
 
 // counts[d * ntiles + t] = number of keys of tile t whose digit at `shift` is d
 __global__ void __launch_bounds__(kSortThreads)
@@ -102,85 +103,79 @@ __device__ __forceinline__ uint32_t block256_exclusive(uint32_t v, uint32_t* tmp
   return r;
 }
 
-// Lanes of the warp holding the same 9-bit value (a digit, or 256 for no element): one
-// ballot per bit, the complement where this lane's bit is 0.
-__device__ __forceinline__ unsigned peers_of(uint32_t d) {
-  unsigned m = 0xFFFFFFFFu;
-#pragma unroll
-  for (int bit = 0; bit < 9; ++bit) {
-    const bool set = (d >> bit) & 1u;
-    const unsigned b = __ballot_sync(0xFFFFFFFFu, set);
-    m &= set ? b : ~b;
-  }
-  return m;
-}
-
-// One pass: pairs of tile t go, stably by digit, to their global positions.  The tile is
-// ranked by 32 "virtual warps" of 256 elements (warp w of 16 takes [w * 512, (w + 1) * 512)
-// as two halves, ranked interleaved for ILP), each in chunks of 32: nine ballots give the
-// lanes of equal digit, and the group's leader adds the group's size to the virtual warp's
-// running count of that digit in shared memory with an atomic that returns the count
-// before it (the group's start).  One scan over (digit, virtual warp) then gives every
-// element its place in the tile; the tile is staged in shared memory by digit and each
-// digit's run written to its global offset, so the global stores are contiguous runs.
-// Positions outside [0, n) or a local rank outside the tile (which correct scans never
-// give) are skipped and set *err.
+// One pass: pairs of tile t go, stably by digit, to their global positions.  Warp w of 16
+// ranks the tile's elements [w * 512, (w + 1) * 512) in chunks of 32: the lanes of equal
+// digit are found by ORing each lane's bit into the warp's slot for its digit in shared
+// memory, and the group's leader adds the group's size to the warp's running count of that
+// digit with an atomic that returns the count before it (the group's start).  One scan over
+// (digit, warp) then gives every element its place in the tile; the tile is staged in
+// shared memory by digit and each digit's run written to its global offset, so the global
+// stores are contiguous runs.  Positions outside [0, n) or a local rank outside the tile
+// (which correct scans never give) are skipped and set *err.
 __global__ void __launch_bounds__(kScatterThreads, 2)
 k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
                int shift, int64_t ntiles, const uint32_t* __restrict__ counts,
                const uint32_t* __restrict__ totals, uint32_t* __restrict__ keys_out,
                uint32_t* __restrict__ vals_out, int* __restrict__ err) {
-  constexpr int kWarps = kScatterThreads / 32, kPerWarp = kSortTile / kWarps;  // 16, 512
-  constexpr int kHalf = kPerWarp / 2, kChunks = kHalf / 32;                     // 256, 8
+  constexpr int kPerWarp = kSortTile / kScatterWarps, kChunks = kPerWarp / 32;  // 512, 16
   extern __shared__ uint32_t smem[];
-  uint32_t* s_keys = smem;                        // [kSortTile]
-  uint32_t* s_vals = s_keys + kSortTile;          // [kSortTile]
-  uint32_t* s_wc = s_vals + kSortTile;            // [kScatterVW][256] counts, then starts
-  uint32_t* s_lbase = s_wc + kScatterVW * 256;    // [256] tile-local start of each digit
-  uint32_t* s_gbase = s_lbase + 256;              // [256] global start of this tile's digit run
-  uint32_t* s_tmp = s_gbase + 256;                // [256]
+  uint32_t* s_keys = smem;                          // [kSortTile]
+  uint32_t* s_vals = s_keys + kSortTile;            // [kSortTile]
+  uint32_t* s_wc = s_vals + kSortTile;              // [warps][256] counts, then starts
+  uint32_t* s_mask = s_wc + kScatterWarps * 256;    // [warps][256] lanes of a digit
+  uint32_t* s_lbase = s_mask + kScatterWarps * 256; // [256] tile-local start of each digit
+  uint32_t* s_gbase = s_lbase + 256;                // [256] global start of this tile's run
+  uint32_t* s_tmp = s_gbase + 256;                  // [256]
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t base = (int64_t)blockIdx.x * kSortTile;
   const int64_t rem = n - base;
   const int cnt = rem < kSortTile ? (int)rem : kSortTile;
-  uint32_t* wc0 = s_wc + (2 * warp) * 256;
-  uint32_t* wc1 = wc0 + 256;
+  uint32_t* wc = s_wc + warp * 256;
+  uint32_t* wm = s_mask + warp * 256;
 #pragma unroll
-  for (int q = 0; q < 16; ++q) wc0[lane * 16 + q] = 0;  // both halves' counters
+  for (int q = 0; q < 8; ++q) {
+    wc[lane * 8 + q] = 0;
+    wm[lane * 8 + q] = 0;
+  }
   __syncwarp();
 
-  const unsigned lt = (1u << lane) - 1u;
-  const int i0 = warp * kPerWarp + lane;  // element of chunk c: i0 + c * 32 (+ kHalf)
-  uint32_t kreg[2 * kChunks], vreg[2 * kChunks], pk[2 * kChunks];
+  const unsigned lt = (1u << lane) - 1u, me = 1u << lane;
+  const int i0 = warp * kPerWarp + lane;  // element of chunk c: i0 + c * 32
+  uint32_t kreg[kChunks], vreg[kChunks], pk[kChunks];
 #pragma unroll
-  for (int c = 0; c < 2 * kChunks; ++c) {
+  for (int c = 0; c < kChunks; ++c) {
     const int i = i0 + c * 32;
     kreg[c] = i < cnt ? keys[base + i] : 0u;
     vreg[c] = i < cnt ? vals[base + i] : 0u;
   }
+  // per chunk: lanes of equal digit from the OR of their bits in the warp's mask slot; the
+  // group's leader takes the group's start from the running count and clears the slot
 #pragma unroll
   for (int c = 0; c < kChunks; ++c) {
-    const bool va = i0 + c * 32 < cnt, vb = i0 + (c + kChunks) * 32 < cnt;
-    const uint32_t da = va ? ((kreg[c] >> shift) & 255u) : 256u;
-    const uint32_t db = vb ? ((kreg[c + kChunks] >> shift) & 255u) : 256u;
-    const unsigned pa = peers_of(da), pb = peers_of(db);
-    const int la = __ffs(pa) - 1, lb_ = __ffs(pb) - 1;
-    uint32_t oa = 0, ob = 0;
-    if (va && lane == la) oa = atomicAdd(&wc0[da], (uint32_t)__popc(pa));
-    if (vb && lane == lb_) ob = atomicAdd(&wc1[db], (uint32_t)__popc(pb));
-    oa = __shfl_sync(0xFFFFFFFFu, oa, la);
-    ob = __shfl_sync(0xFFFFFFFFu, ob, lb_);
-    pk[c] = va ? (da << 16) | (oa + (uint32_t)__popc(pa & lt)) : 0xFFFFFFFFu;
-    pk[c + kChunks] = vb ? (db << 16) | (ob + (uint32_t)__popc(pb & lt)) : 0xFFFFFFFFu;
+    const bool valid = i0 + c * 32 < cnt;
+    const uint32_t d = (kreg[c] >> shift) & 255u;
+    if (valid) atomicOr(&wm[d], me);
+    __syncwarp();
+    const unsigned peers = valid ? wm[d] : 0u;
+    __syncwarp();
+    const int leader = valid ? __ffs(peers) - 1 : lane;
+    uint32_t start = 0;
+    if (valid && lane == leader) {
+      start = atomicAdd(&wc[d], (uint32_t)__popc(peers));
+      wm[d] = 0;
+    }
+    start = __shfl_sync(0xFFFFFFFFu, start, leader);
+    __syncwarp();
+    pk[c] = valid ? (d << 16) | (start + (uint32_t)__popc(peers & lt)) : 0xFFFFFFFFu;
   }
   __syncthreads();
 
-  // thread d < 256: starts of digit d for each virtual warp within the tile, the tile's
-  // digit starts, and the global start of the tile's run of digit d
+  // thread d < 256: starts of digit d for each warp within the tile, the tile's digit
+  // starts, and the global start of the tile's run of digit d
   uint32_t run = 0;
   if (tid < 256) {
-#pragma unroll 8
-    for (int w = 0; w < kScatterVW; ++w) {
+#pragma unroll
+    for (int w = 0; w < kScatterWarps; ++w) {
       const uint32_t c = s_wc[w * 256 + tid];
       s_wc[w * 256 + tid] = run;
       run += c;
@@ -189,17 +184,16 @@ k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ v
   const uint32_t lbase = block256_exclusive(run, s_tmp);
   const uint32_t gb = block256_exclusive(tid < 256 ? totals[tid] : 0u, s_tmp);
   if (tid < 256) {
-#pragma unroll 8
-    for (int w = 0; w < kScatterVW; ++w) s_wc[w * 256 + tid] += lbase;
+#pragma unroll
+    for (int w = 0; w < kScatterWarps; ++w) s_wc[w * 256 + tid] += lbase;
     s_lbase[tid] = lbase;
     s_gbase[tid] = gb + counts[(int64_t)tid * ntiles + blockIdx.x];
   }
   __syncthreads();
 
 #pragma unroll
-  for (int c = 0; c < 2 * kChunks; ++c) {
+  for (int c = 0; c < kChunks; ++c) {
     if (pk[c] != 0xFFFFFFFFu) {
-      const uint32_t* wc = c < kChunks ? wc0 : wc1;
       const uint32_t lp = wc[pk[c] >> 16] + (pk[c] & 0xFFFFu);
       if (lp < (uint32_t)kSortTile) {
         s_keys[lp] = kreg[c];
