@@ -557,6 +557,17 @@ def run_ours(args):
                 "frac": (my_blocks * 4 / 1e9 / hbm_peak) if hbm_peak else None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
     }
+    # the nominal ceiling too: every SM lane issuing one 32-bit integer op per cycle at the
+    # SM clock sampled during the timed region, 100 ops per block
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    nominal = sms * 128 * mhz * 1e6 / 1e12
+    roofline["nominal"] = {"peak": nominal, "unit": "Tops/s",
+                           "frac": my_blocks * OPS_PER_BLOCK / 1e12 / nominal,
+                           "source": f"{sms} SMs x 128 lanes x {mhz:.0f} MHz (one integer op "
+                                     "per lane per cycle); the cipher issues ~77 instructions "
+                                     "per block, part of them on the FMA pipe, so this can "
+                                     "exceed 1"}
 
     # the whole request on rank 0 (timed separately from generation): rank r's kernel
     # storing its slab straight into rank 0's HBM over NVLink, and, for comparison,
