@@ -262,6 +262,15 @@ int jxr_random_bits_multi(const int* devices, int ndev, const uint32_t* const* k
                           int layout, int bit_width, void* const* outs, int gather_to,
                           void* gather_out, void* const* streams);
 
+/* Complex normals (R/random.R:489-499): out (complex64 / complex128, interleaved) =
+ * (re[i] + i im[i]) / divisor, each part divided in the real dtype (float32/float64). */
+int jxr_complex_from_parts(const void* re, const void* im, int64_t n, int dtype, double divisor,
+                           void* out, void* stream);
+
+/* Cumulative sum of m float32/float64 values, added left to right in the dtype (the
+ * probabilities of random_choice, R/random.R:446). */
+int jxr_cumsum(const void* x, int64_t m, int dtype, void* out, void* stream);
+
 /* lax_erf_inv (R/lax.R:222, lowered as chlo.erf_inv at R/lax_special.R:1327-1331),
  * element-wise for F32 or F64. */
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream);

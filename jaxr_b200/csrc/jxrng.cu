@@ -629,6 +629,37 @@ __device__ __forceinline__ uint16_t half_next(float x, bool up, bool bf) {
   return (uint16_t)((up != neg) ? b + 1 : b - 1);
 }
 
+// complex normals (R/random.R:489-499): (re + i im) / sqrt(2) from the two real normals,
+// each part divided in the real dtype, interleaved as complex64 / complex128
+template <class T>
+__global__ void k_complex_div(const T* __restrict__ re, const T* __restrict__ im, int64_t n,
+                              T divisor, T* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if constexpr (sizeof(T) == 4) {
+      out[2 * i] = __fdiv_rn(re[i], divisor);
+      out[2 * i + 1] = __fdiv_rn(im[i], divisor);
+    } else {
+      out[2 * i] = __ddiv_rn(re[i], divisor);
+      out[2 * i + 1] = __ddiv_rn(im[i], divisor);
+    }
+  }
+}
+
+// cumulative sum, left to right in the dtype (one thread: the order of the additions
+// defines the rounding)
+template <class T>
+__global__ void k_cumsum_seq(const T* __restrict__ x, int64_t m, T* __restrict__ out) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    T acc = 0;
+    for (int64_t i = 0; i < m; ++i) {
+      if constexpr (sizeof(T) == 4) acc = __fadd_rn(acc, x[i]);
+      else acc = __dadd_rn(acc, x[i]);
+      out[i] = acc;
+    }
+  }
+}
+
 // random_choice with p and replace (R/random.R:446-450): r = total * (1 - u) in the dtype,
 // index = number of cumulative sums strictly below r (searchsorted, side left)
 template <class T>
@@ -1986,6 +2017,37 @@ int jxr_random_bits_multi(const int* devices, int ndev, const uint32_t* const* k
   }
   cudaSetDevice(prev);
   return rc;
+}
+
+int jxr_complex_from_parts(const void* re, const void* im, int64_t n, int dtype, double divisor,
+                           void* out, void* stream) {
+  if (dtype != JXR_F32 && dtype != JXR_F64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "dtype must be float32 or float64, got %d", dtype);
+  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!n) return JXR_OK;
+  if (!re || !im || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  int grid, rc;
+  if ((rc = small_grid(n, &grid))) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == JXR_F32)
+    k_complex_div<float><<<grid, 256, 0, st>>>((const float*)re, (const float*)im, n, (float)divisor, (float*)out);
+  else
+    k_complex_div<double><<<grid, 256, 0, st>>>((const double*)re, (const double*)im, n, divisor, (double*)out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_cumsum(const void* x, int64_t m, int dtype, void* out, void* stream) {
+  if (dtype != JXR_F32 && dtype != JXR_F64)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "dtype must be float32 or float64, got %d", dtype);
+  if (m < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "m must be >= 0");
+  if (!m) return JXR_OK;
+  if (!x || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == JXR_F32) k_cumsum_seq<float><<<1, 32, 0, st>>>((const float*)x, m, (float*)out);
+  else k_cumsum_seq<double><<<1, 32, 0, st>>>((const double*)x, m, (double*)out);
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
 }
 
 int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream) {

@@ -856,8 +856,9 @@ def _complex_normal(k, bshape, shape, dt):
     re = _k_normal(halves[:, 0].contiguous(), size, real, _layout())
     im = _k_normal(halves[:, 1].contiguous(), size, real, _layout())
     # complex / complex(sqrt 2, 0): each part divided by sqrt(2) in the real dtype
-    s = torch.tensor(math.sqrt(2), dtype=_TORCH[real], device=re.device)
-    z = torch.complex(re / s, im / s)
+    z = torch.empty(re.shape, dtype=_TORCH[dt], device=re.device)
+    nat.call("jxr_complex_from_parts", _ptr(re), _ptr(im), re.numel(), _FLOAT_CODE[real],
+             math.sqrt(2), _ptr(z), _stream())
     return z.reshape(bshape + shape)
 
 
@@ -1363,8 +1364,9 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
     layout = _layout()
     if replace:
         # cumulative sums in the dtype, left to right (jnp_cumsum)
-        cuml_h = np.cumsum(pt.detach().cpu().numpy().astype(pdt), dtype=pdt)
-        cuml = torch.from_numpy(cuml_h).to(kd.device)
+        pd = pt.to(device=kd.device, dtype=_TORCH[pdt]).contiguous()
+        cuml = torch.empty_like(pd)
+        nat.call("jxr_cumsum", _ptr(pd), n_inputs, _FLOAT_CODE[pdt], _ptr(cuml), _stream())
         unit = _k_uniform(kd, n_draws, pdt, 0.0, 1.0, layout)
         ind = torch.empty(n_draws, dtype=_TORCH[dint], device=kd.device)
         nat.call("jxr_choice_p_from_unit", _ptr(unit), n_draws, _FLOAT_CODE[pdt], _ptr(cuml),

@@ -165,6 +165,23 @@ def normal(key, dtype, size, partitionable=True, fma=True, begin=0, count=None):
     return out
 
 
+def complex_normal(key, dtype, size, partitionable=True):
+    """Complex normals (R/random.R:489-499): the key split in two, a real normal of the
+    component dtype from each half (real part from the first), each divided by sqrt(2)
+    rounded to the component dtype.  XLA divides (re + i im) by (sqrt2 + 0i) with Smith's
+    method, whose ratio 0 / sqrt2 = 0 leaves re / sqrt2 and im / sqrt2."""
+    real = {"complex64": "float32", "complex128": "float64"}[dtype]
+    rdt = np.float32 if real == "float32" else np.float64
+    ks = split(key, 2, partitionable)
+    s2 = rdt(np.sqrt(2.0))
+    re = (normal(ks[0], real, size, partitionable) / s2).astype(rdt)
+    im = (normal(ks[1], real, size, partitionable) / s2).astype(rdt)
+    out = np.empty(int(size), dtype=np.complex64 if real == "float32" else np.complex128)
+    out.real = re
+    out.imag = im
+    return out
+
+
 def bernoulli(key, p_dtype, p, size, partitionable=True, begin=0, count=None):
     code = DTYPE_CODE[p_dtype]
     count = size - begin if count is None else count

@@ -187,6 +187,14 @@ def _enc(v, dtype):
 def case(name, source, op, args, dtype, shape, values, compare, **extra):
     if isinstance(shape, int):
         shape = [shape]
+    if dtype.startswith("complex"):
+        # list(re = c(...), im = c(...)) -> re0, im0, re1, im1, ... as component floats
+        real = "float32" if dtype == "complex64" else "float64"
+        values = [_enc(v, real) for pair in zip(values["re"], values["im"]) for v in pair]
+        d = {"name": name, "source": source, "op": op, "args": args, "dtype": dtype,
+             "shape": list(shape), "values": values, "compare": compare}
+        d.update(extra)
+        return d
     d = {"name": name, "source": source, "op": op, "args": args, "dtype": dtype,
          "shape": list(shape), "values": [_enc(v, dtype) for v in values], "compare": compare}
     d.update(extra)
@@ -298,6 +306,7 @@ def build(ref):
                                          "maxval": 5}),
         "normal_0_5": ("normal", {"seed": 0, "shape": [5]}),
         "normal_42_23": ("normal", {"seed": 42, "shape": [2, 3]}),
+        "normal_0_c64": ("normal", {"seed": 0, "shape": [3], "dtype": "complex64"}),
         "unif_bf16": ("uniform", {"seed": 0, "shape": [4], "dtype": "bfloat16"}),
         "unif_f16": ("uniform", {"seed": 0, "shape": [4], "dtype": "float16"}),
         # vmap(function(k) random_uniform(k, 3))(random_split(rr_k0(), 4))
@@ -338,6 +347,8 @@ def build(ref):
         (shape, vals, dt), line = rr[name]
         shape = [shape] if isinstance(shape, int) else shape
         cmp = "ulp16" if dt.startswith("float") else "exact"
+        if dt.startswith("complex"):
+            cmp = "rel:1e-6"  # test-random.R:131-132 compares complex normals to 1e-6
         if name.startswith("unif_"):
             args["result_as"] = "float32"  # the test compares jnp_astype(..., "float32")
         cases.append(case(name, src(rand, line), op, args, dt, shape, vals, cmp,
@@ -357,6 +368,7 @@ def build(ref):
         "uniform_0_5": ("uniform", {"seed": 0, "shape": [5]}),
         "uniform_42_23_m": ("uniform", {"seed": 42, "shape": [2, 3], "minval": -2, "maxval": 3}),
         "normal_0_5": ("normal", {"seed": 0, "shape": [5]}),
+        "normal_0_c128": ("normal", {"seed": 0, "shape": [3], "dtype": "complex128"}),
         "np_uniform_0_5": ("uniform", {"seed": 0, "shape": [5], "partitionable": False}),
         "randint_0_6": ("randint", {"seed": 0, "shape": [6], "minval": 0, "maxval": 10}),
         "randint_42_neg": ("randint", {"seed": 42, "shape": [5], "minval": -5, "maxval": 5}),
@@ -369,6 +381,7 @@ def build(ref):
         shape = [shape] if isinstance(shape, int) else shape
         args = dict(args, x64=True)
         # the reference holds its float64 truncated normal to 1e-14 relative (test-random.R:193)
+        # complex128 normals are compared exactly (test-random.R:185, tol = 0)
         cmp = ("exact" if not dt.startswith("float") else
                "rel:1e-14" if name == "truncnorm" else "ulp16")
         cases.append(case(f"x64_{name}", src(rand, line), op, args, dt, shape, vals, cmp,

@@ -38,7 +38,11 @@ def expected(case):
     dt = case["dtype"]
     vals = case["values"]
     shape = tuple(case["shape"])
-    if dt.startswith("float"):
+    if dt.startswith("complex"):
+        # values interleaved re, im
+        real = "float32" if dt == "complex64" else "float64"
+        a = np.array([_f(v) for v in vals], dtype=np.float64).astype(real).view(dt)
+    elif dt.startswith("float"):
         a = np.array([_f(v) for v in vals], dtype=np.float64).astype(dt)
     elif dt == "bool":
         a = np.array(vals, dtype=bool)
@@ -82,6 +86,10 @@ def check(case, got):
     if tuple(got.shape) != tuple(want.shape):
         return False, f"shape {got.shape} != {want.shape}"
     cmp = case["compare"]
+    if want.dtype.kind == "c":
+        # compared component by component
+        got = np.ascontiguousarray(got.astype(want.dtype)).view(want.real.dtype)
+        want = np.ascontiguousarray(want).view(want.real.dtype)
     if want.dtype.kind in "uib":
         ok = np.array_equal(got.astype(want.dtype), want)
         return ok, "exact" if ok else f"got {got.ravel().tolist()} want {want.ravel().tolist()}"
@@ -209,6 +217,11 @@ def evaluate(case, be):
         if dt in ("float16", "bfloat16"):
             out = bits_to_float32(out, dt)
         return out
+    if op == "normal" and float_dtype(a).startswith("complex"):
+        dt = float_dtype(a)
+        shape = tuple(a["shape"])
+        return np.asarray(be.complex_normal(key_of(a["seed"]), dt, shape_size(shape),
+                                            part)).reshape(shape)
     if op in ("normal", "vmap_normal"):
         dt = float_dtype(a)
         shape = tuple(a["shape"])
@@ -321,6 +334,9 @@ class OracleBackend:
 
     def normal(self, key, dt, n, part):
         return self.o.normal(key, dt, n, part, fma=self.erfinv_fma)
+
+    def complex_normal(self, key, dt, n, part):
+        return self.o.complex_normal(key, dt, n, part)
 
     def bernoulli(self, key, dt, p, n, part):
         return self.o.bernoulli(key, dt, p, n, part)

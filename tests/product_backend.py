@@ -98,6 +98,10 @@ class ProductBackend:
             out = jr.random_normal(torch.tensor(np.asarray(key, np.uint32)), (n,), dt)
         return _raw(out, dt)
 
+    def complex_normal(self, key, dt, n, part):
+        with flags(dt == "complex128" or self.x64, part):
+            return to_np(jr.random_normal(torch.tensor(np.asarray(key, np.uint32)), (n,), dt))
+
     def bernoulli(self, key, dt, p, n, part):
         with flags(dt == "float64" or self.x64, part):
             pt = torch.tensor(p, dtype=jrr._TORCH[dt])
