@@ -169,3 +169,17 @@ def test_choice_key_batches():
     assert tuple(out.shape) == (3, 4)
     for r in range(3):
         assert np.array_equal(to_np(out[r]), orc.choice(keys[r], 20, (4,), False))
+
+
+@pytest.mark.parametrize("dt", ["float32", "float64"])
+def test_choice_p_long_vector(dt):
+    """Choice with replacement from 100003 unnormalised probabilities: the device cumulative
+    sum is taken left to right in the dtype, so every draw matches the oracle's."""
+    rng = np.random.default_rng(4)
+    p = rng.random(100003).astype(dt)
+    p[rng.integers(0, p.size, 1000)] = 0
+    key = orc.seed(12)
+    with flags(dt == "float64"):
+        got = to_np(jr.random_choice(dev_key(key), p.size, (50000,), True, p))
+    assert np.array_equal(got, orc.choice(key, p.size, (50000,), True, p, x64=dt == "float64"))
+    assert not np.any(p[got] == 0)

@@ -286,3 +286,27 @@ def test_samplers_inside_a_cuda_graph():
     r = subprocess.run([sys.executable, "-c", _GRAPH_CHILD, root], capture_output=True,
                        text=True, timeout=300)
     assert r.returncode == 0 and "graph ok" in r.stdout, r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("dt", ["complex64", "complex128"])
+@pytest.mark.parametrize("part", [True, False])
+def test_complex_normal_exact(dt, part):
+    """Complex normals (R/random.R:489-499): both components bit-exact against the oracle's
+    split-then-divide-by-sqrt(2), at an odd size with a ragged tail (and the f32 size above
+    the sampler table's threshold, so the real parts come from the table path)."""
+    key = orc.seed(31)
+    for n in (1, 7, 1001, (1 << 22) + 5):
+        with flags(dt == "complex128", part):
+            got = to_np(jr.random_normal(dev_key(key), (n,), dt))
+        want = orc.complex_normal(key, dt, n, part)
+        assert got.dtype == want.dtype
+        assert np.array_equal(got.view(got.real.dtype), want.view(want.real.dtype)), (dt, n)
+
+
+def test_complex_normal_key_batches():
+    keys = np.stack([orc.seed(s) for s in range(4)])
+    out = to_np(jr.vmap(lambda k: jr.random_normal(k, (2, 3), "complex64"))(dev_key(keys)))
+    assert out.shape == (4, 2, 3)
+    for r in range(4):
+        want = orc.complex_normal(keys[r], "complex64", 6).reshape(2, 3)
+        assert np.array_equal(out[r].view(np.float32), want.view(np.float32))
