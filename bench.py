@@ -296,7 +296,7 @@ def sampler_cpu_baseline(c, min_seconds=2.0):
         if c in _SAMPLER_WORKLOADS:
             lib.orc_sample(k, orc.SAMPLE_KIND[_SAMPLER_WORKLOADS[c]], orc.F32, size, 1, 0, n, optr)
         elif c == "truncnorm":
-            lib.orc_truncated_normal(k, orc.F32, size, 1, -1.0, 2.0, 0, n, optr)
+            lib.orc_truncated_normal(k, orc.F32, size, 1, -1.0, 2.0, 1, 0, n, optr)
         else:
             ks = orc.split(key, 2, True)
             hi = orc.random_bits(ks[0], 32, size, True, 0, n).astype(np.uint64)

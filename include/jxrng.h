@@ -70,6 +70,15 @@ enum { JXR_F32 = 0, JXR_F64 = 1, JXR_F16 = 2, JXR_BF16 = 3 };
  * this flag asks for a separately rounded multiply and add instead. */
 enum { JXR_FLAG_UNFUSED_MUL_ADD = 1 };
 
+/* jax_accurate_erf_inv (R/config.R:18; R/lax_special.R:1326-1331 lowers erf_inv to JAX's
+ * erf_inv_core, R/lax_special.R:1022-1082, when it is set): for the calling host thread,
+ * selects the erf_inv that jxr_normal, jxr_normal_from_bits, jxr_normal_bernoulli, the
+ * jxr_truncated_normal family and jxr_erf_inv evaluate.  Off (0) by default, as in the
+ * reference; the setter returns the previous value.  The choice is made when a call
+ * launches its kernels. */
+int jxr_set_accurate_erf_inv(int enable);
+int jxr_get_accurate_erf_inv(void);
+
 /* ABI version (JXR_ABI_VERSION) and the last error of this host thread. */
 int jxr_abi_version(void);
 const char* jxr_last_error(void);

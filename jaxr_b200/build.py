@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libjxrng.so")
 SOURCES = [os.path.join(CSRC, "jxrng.cu")]
 # every header the library includes: a change to any of them rebuilds it
-HEADERS = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")) + [
+HEADERS = sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))) + [
     os.path.join(ROOT, "include", "jxrng.h")]
 
 NVCC_FLAGS = [

@@ -4,8 +4,8 @@ Only the options this path reads are kept: jax_enable_x64 (default dtypes and se
 width), jax_threefry_partitionable (counter layout), jax_default_prng_impl and
 jax_random_seed_offset; jax_legacy_prng_key governs raw uint32 keys;
 jax_use_high_dynamic_range_gumbel picks random_gumbel's default mode;
-jax_accurate_erf_inv (JAX's alternative erf_inv, R/lax_special.R:1324-1331) is recognised
-and refused by the functions that would use it.
+jax_accurate_erf_inv (R/lax_special.R:1324-1331) selects JAX's erf_inv_core for the normal
+and truncated-normal samplers and lax_erf_inv.
 """
 
 from __future__ import annotations

@@ -26,6 +26,7 @@
 #include <limits>
 #include <mutex>
 #include <type_traits>
+#include <type_traits>
 #include <string>
 #include <vector>
 
@@ -42,6 +43,18 @@ const PipeConsts kPipe = make_pipe_consts();
 
 
 thread_local std::string g_error;
+
+// jax_accurate_erf_inv for this host thread (jxr_set_accurate_erf_inv): which erf_inv the
+// normal and truncated-normal samplers and jxr_erf_inv evaluate.
+thread_local int g_accurate_erf_inv = 0;
+
+// f(std::true_type{}) under the accurate erf_inv, else f(std::false_type{}): the variant
+// becomes a compile-time constant of the kernel that f launches.
+template <class F>
+int with_erfinv(F&& f) {
+  if (g_accurate_erf_inv) return f(std::true_type{});
+  return f(std::false_type{});
+}
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -401,7 +414,9 @@ __global__ void k_build_table(Op op, float* __restrict__ table) {
 // Requests of at least this many float32 samples use (and, the first time, build) the
 // sampler's table.
 constexpr uint64_t kTableMin = 1ull << 22;
-constexpr int kTables = 8;  // 0: normal, 1 + kind: the log-transform samplers
+constexpr int kTables = 8;  // 0: normal, 1 + kind: the log-transform samplers, 5: normal
+                            // with the accurate erf_inv
+constexpr int kTableNormalAccurate = 5;
 std::mutex g_tab_mu;
 float* g_tables[64][kTables];
 
@@ -542,15 +557,17 @@ int launch_from_bits(const void* bits, int64_t n, const Op& op, void* out, cudaS
   return JXR_OK;
 }
 
+template <bool kAcc>
 __global__ void k_erfinv_f32(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = erfinv_f32(x[i]);
+    out[i] = erfinv32<kAcc>(x[i]);
 }
+template <bool kAcc>
 __global__ void k_erfinv_f64(const double* __restrict__ x, int64_t n, double* __restrict__ out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = erfinv_f64(x[i]);
+    out[i] = erfinv64<kAcc>(x[i]);
 }
 
 // ---- element-wise helpers for array-valued parameters ------------------------------------
@@ -695,7 +712,7 @@ __global__ void k_add_log(T* __restrict__ x, const T* __restrict__ p, int64_t n)
 // f = uniform(0, 1): a = erf(lower / sqrt2), b = erf(upper / sqrt2) (CUDA's erf in double,
 // rounded to the dtype), u = max(a, f (b - a) + a), sqrt2 erf_inv(u), clipped to
 // [nextafter(lower, inf), nextafter(upper, -inf)].  Bounds have stride 0 or 1.
-template <int D>
+template <int D, bool kAcc>
 __global__ void k_trunc_unit(const void* __restrict__ unit, const void* __restrict__ lower,
                              int64_t ls, const void* __restrict__ upper, int64_t us, int64_t n,
                              void* __restrict__ out) {
@@ -707,7 +724,7 @@ __global__ void k_trunc_unit(const void* __restrict__ unit, const void* __restri
       const float a = __double2float_rn(erf((double)__fdiv_rn(lo, s2)));
       const float b = __double2float_rn(erf((double)__fdiv_rn(hi, s2)));
       const float u = xla_max(a, __fmaf_rn(((const float*)unit)[i], __fsub_rn(b, a), a));
-      const float x = __fmul_rn(s2, erfinv_f32(u));
+      const float x = __fmul_rn(s2, erfinv32<kAcc>(u));
       const float cl = nextafterf(lo, __int_as_float(0x7F800000)),
                   ch = nextafterf(hi, __int_as_float(0xFF800000));
       ((float*)out)[i] = xla_min(ch, xla_max(cl, x));
@@ -716,7 +733,7 @@ __global__ void k_trunc_unit(const void* __restrict__ unit, const void* __restri
       const double lo = ((const double*)lower)[i * ls], hi = ((const double*)upper)[i * us];
       const double a = erf(__ddiv_rn(lo, s2)), b = erf(__ddiv_rn(hi, s2));
       const double u = xla_max(a, __fma_rn(((const double*)unit)[i], __dsub_rn(b, a), a));
-      const double x = __dmul_rn(s2, erfinv_f64(u));
+      const double x = __dmul_rn(s2, erfinv64<kAcc>(u));
       const double inf = __longlong_as_double(0x7FF0000000000000ll);
       ((double*)out)[i] = xla_min(nextafter(hi, -inf), xla_max(nextafter(lo, inf), x));
     } else {
@@ -729,7 +746,7 @@ __global__ void k_trunc_unit(const void* __restrict__ unit, const void* __restri
       const float d = rh<BF>(__fsub_rn(b, a));
       const float f = h2f<BF>(((const uint16_t*)unit)[i]);
       const float u = xla_max(a, h2f<BF>(d2h<BF>(__fma_rn((double)f, (double)d, (double)a))));
-      const float x = rh<BF>(__fmul_rn(s2, rh<BF>(erfinv_f32(u))));
+      const float x = rh<BF>(__fmul_rn(s2, rh<BF>(erfinv32<kAcc>(u))));
       ((uint16_t*)out)[i] = f2h<BF>(xla_min(h2f<BF>(half_next(hi, false, BF)),
                                             xla_max(h2f<BF>(half_next(lo, true, BF)), x)));
     }
@@ -1201,17 +1218,20 @@ int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
   int rc = check_dtype(dtype);
   if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  switch (dtype) {
-    case JXR_F32: {
-      if (count * (uint64_t)nkeys >= kTableMin)
-        if (const float* t = f32_table(0, OpNormalF32{}, st))
-          return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{t}, out, st);
-      return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32{}, out, st);
+  return with_erfinv([&](auto acc) -> int {
+    constexpr bool A = decltype(acc)::value;
+    switch (dtype) {
+      case JXR_F32: {
+        if (count * (uint64_t)nkeys >= kTableMin)
+          if (const float* t = f32_table(A ? kTableNormalAccurate : 0, OpNormalF32T<A>{}, st))
+            return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{t}, out, st);
+        return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32T<A>{}, out, st);
+      }
+      case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF64T<A>{}, out, st);
+      case JXR_F16: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<false, A>{}, out, st);
+      default: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<true, A>{}, out, st);
     }
-    case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF64{}, out, st);
-    case JXR_F16: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<false>{}, out, st);
-    default: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<true>{}, out, st);
-  }
+  });
 }
 
 int jxr_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
@@ -1235,12 +1255,18 @@ int jxr_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, uin
   if (count && nkeys && !bern_out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == JXR_F64 && !(layout == JXR_LAYOUT_ORIGINAL && size >= 0x7FFFFFFFull)) {
-    return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout, OpNormalF64{},
-                                   OpBernoulliF64{p}, normal_out, bern_out, st);
+    return with_erfinv([&](auto acc) -> int {
+      return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout,
+                                     OpNormalF64T<decltype(acc)::value>{}, OpBernoulliF64{p},
+                                     normal_out, bern_out, st);
+    });
   }
   if (dtype == JXR_F32 && layout == JXR_LAYOUT_PARTITIONABLE)
-    return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout, OpNormalF32{},
-                                   OpBernoulliF32{(float)p}, normal_out, bern_out, st);
+    return with_erfinv([&](auto acc) -> int {
+      return launch_normal_bernoulli(keys, nkeys, size, begin, count, layout,
+                                     OpNormalF32T<decltype(acc)::value>{},
+                                     OpBernoulliF32{(float)p}, normal_out, bern_out, st);
+    });
   // other dtypes and layouts: the two samplers one after the other (same results)
   if ((rc = jxr_normal(keys, nkeys, size, begin, count, layout, dtype, normal_out, stream))) return rc;
   return jxr_bernoulli(keys, nkeys, size, begin, count, layout, dtype, p, bern_out, stream);
@@ -1287,12 +1313,15 @@ int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void
   int grid;
   if ((rc = small_grid(n, &grid))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  switch (dtype) {
-    case JXR_F32: return launch_from_bits(bits, n, OpNormalF32{}, out, st, grid);
-    case JXR_F64: return launch_from_bits(bits, n, OpNormalF64{}, out, st, grid);
-    case JXR_F16: return launch_from_bits(bits, n, OpNormalH<false>{}, out, st, grid);
-    default: return launch_from_bits(bits, n, OpNormalH<true>{}, out, st, grid);
-  }
+  return with_erfinv([&](auto acc) -> int {
+    constexpr bool A = decltype(acc)::value;
+    switch (dtype) {
+      case JXR_F32: return launch_from_bits(bits, n, OpNormalF32T<A>{}, out, st, grid);
+      case JXR_F64: return launch_from_bits(bits, n, OpNormalF64T<A>{}, out, st, grid);
+      case JXR_F16: return launch_from_bits(bits, n, OpNormalH<false, A>{}, out, st, grid);
+      default: return launch_from_bits(bits, n, OpNormalH<true, A>{}, out, st, grid);
+    }
+  });
 }
 
 int jxr_uniform_affine(const void* unit, const void* minval, const void* maxval, int64_t n,
@@ -1575,20 +1604,20 @@ float half_step(float x, bool up, bool bf) {
 namespace {
 // Calls f(op) with the fused truncated-normal op of dtype for scalar bounds: a, b =
 // erf(lower / sqrt2), erf(upper / sqrt2) and the clip bounds, computed here once.
-template <class F>
-int visit_trunc_op(int dtype, double lower, double upper, F&& f) {
+template <bool A, class F>
+int visit_trunc_op_as(int dtype, double lower, double upper, F&& f) {
   const double inf = std::numeric_limits<double>::infinity();
   switch (dtype) {
     case JXR_F32: {
       const float s2 = 1.41421354f, lo = (float)lower, hi = (float)upper;
       const float a = (float)std::erf((double)(lo / s2)), b = (float)std::erf((double)(hi / s2));
       const float cl = std::nextafter(lo, (float)inf), ch = std::nextafter(hi, (float)-inf);
-      return f(OpTruncNormal<0>{{a, b - a}, cl, ch});
+      return f(OpTruncNormal<0, A>{{a, b - a}, cl, ch});
     }
     case JXR_F64: {
       const double s2 = 1.4142135623730951;
       const double a = std::erf(lower / s2), b = std::erf(upper / s2);
-      return f(OpTruncNormal<1>{{a, b - a}, std::nextafter(lower, inf), std::nextafter(upper, -inf)});
+      return f(OpTruncNormal<1, A>{{a, b - a}, std::nextafter(lower, inf), std::nextafter(upper, -inf)});
     }
     default: {
       const bool bf = dtype == JXR_BF16;
@@ -1600,10 +1629,17 @@ int visit_trunc_op(int dtype, double lower, double upper, F&& f) {
       const float b = to_half_value((double)(float)std::erf((double)qh), bf);
       const float d = to_half_value((double)b - (double)a, bf);
       const float cl = half_step(lo, true, bf), ch = half_step(hi, false, bf);
-      if (bf) return f(OpTruncNormal<3>{{{a, d}, cl, ch}});
-      return f(OpTruncNormal<2>{{{a, d}, cl, ch}});
+      if (bf) return f(OpTruncNormal<3, A>{{{a, d}, cl, ch}});
+      return f(OpTruncNormal<2, A>{{{a, d}, cl, ch}});
     }
   }
+}
+
+template <class F>
+int visit_trunc_op(int dtype, double lower, double upper, F&& f) {
+  return with_erfinv([&](auto acc) -> int {
+    return visit_trunc_op_as<decltype(acc)::value>(dtype, lower, upper, f);
+  });
 }
 }  // namespace
 
@@ -1648,14 +1684,17 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
   int grid;
   if ((rc = small_grid(n, &grid))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
-  switch (dtype) {
-    case JXR_F32: k_trunc_unit<JXR_F32><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
-    case JXR_F64: k_trunc_unit<JXR_F64><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
-    case JXR_F16: k_trunc_unit<JXR_F16><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
-    default: k_trunc_unit<JXR_BF16><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out);
-  }
-  JXR_CUDA(cudaGetLastError());
-  return JXR_OK;
+  return with_erfinv([&](auto acc) -> int {
+    constexpr bool A = decltype(acc)::value;
+    switch (dtype) {
+      case JXR_F32: k_trunc_unit<JXR_F32, A><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
+      case JXR_F64: k_trunc_unit<JXR_F64, A><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
+      case JXR_F16: k_trunc_unit<JXR_F16, A><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out); break;
+      default: k_trunc_unit<JXR_BF16, A><<<grid, 256, 0, st>>>(unit, lower, lower_stride, upper, upper_stride, n, out);
+    }
+    JXR_CUDA(cudaGetLastError());
+    return JXR_OK;
+  });
 }
 
 // ---- permutation: stable radix sort of (random key, position) pairs ----------------------
@@ -2058,13 +2097,24 @@ int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream) {
   if (!x || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
   int grid, rc;
   if ((rc = small_grid(n, &grid))) return rc;
-  if (dtype == JXR_F32)
-    k_erfinv_f32<<<grid, 256, 0, (cudaStream_t)stream>>>((const float*)x, n, (float*)out);
-  else
-    k_erfinv_f64<<<grid, 256, 0, (cudaStream_t)stream>>>((const double*)x, n, (double*)out);
-  JXR_CUDA(cudaGetLastError());
-  return JXR_OK;
+  return with_erfinv([&](auto acc) -> int {
+    constexpr bool A = decltype(acc)::value;
+    if (dtype == JXR_F32)
+      k_erfinv_f32<A><<<grid, 256, 0, (cudaStream_t)stream>>>((const float*)x, n, (float*)out);
+    else
+      k_erfinv_f64<A><<<grid, 256, 0, (cudaStream_t)stream>>>((const double*)x, n, (double*)out);
+    JXR_CUDA(cudaGetLastError());
+    return JXR_OK;
+  });
 }
+
+int jxr_set_accurate_erf_inv(int enable) {
+  const int prev = g_accurate_erf_inv;
+  g_accurate_erf_inv = enable ? 1 : 0;
+  return prev;
+}
+
+int jxr_get_accurate_erf_inv(void) { return g_accurate_erf_inv; }
 
 int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size, uint64_t begin,
                          uint64_t count, int layout, int bit_width, void* host_out) {

@@ -21,6 +21,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "erfinv_tables.h"
+
 namespace jxr {
 
 // lax_max(a, b) as XLA's CPU code computes it: NaN-propagating, `a` on ties.
@@ -197,6 +199,79 @@ __device__ __forceinline__ double erfinv_f64(double x) {
   return __dmul_rn(p, x);
 }
 
+// ---- accurate erf_inv (jax_accurate_erf_inv; R/lax_special.R:1022-1082) -----------------
+//
+// JAX's erf_inv_core(x, q = 1 - |x|) without its far-tail pieces: w = -log(q (1 + |x|)),
+// which has no cancellation near |x| = 1.  Below the first split (float32 w < 3.5, float64
+// w < 4.5) the result is x * P(w - c1); above it z = sqrt(w) is carried as z_h (the top
+// half of its mantissa, so that z_h^2 is exact) plus z_l = (w - z_h^2) / (z + z_h), and
+// the result is sign(x) (z_h + (z_l + P(z - shift))).  Each piece's coefficients are
+// selected per element, as the reference selects them, and P is a fused Horner
+// evaluation from the highest coefficient down.  The float32 logarithm is taken in double
+// and rounded once.  |x| > 1 or NaN gives NaN, |x| = 1 gives x * inf.
+
+__device__ __forceinline__ float erfinv_acc_f32(float x) {
+  constexpr float P1[JXR_ERFINV32_P1_N] = {JXR_ERFINV32_P1};
+  constexpr float P2[JXR_ERFINV32_P2_N] = {JXR_ERFINV32_P2};
+  static_assert(JXR_ERFINV32_P1_N == JXR_ERFINV32_P2_N, "equal-length pieces");
+  const float ax = fabsf(x);
+  const float q = __fsub_rn(1.0f, ax);
+  const float w = -__double2float_rn(log_pos((double)__fmul_rn(q, __fadd_rn(1.0f, ax))));
+  const bool first = w < 3.5f;
+  const float w_safe = first ? 1.0f : w;
+  const float z = __fsqrt_rn(w_safe);
+  const float z_h = __uint_as_float(__float_as_uint(z) & 0xFFFFF000u);
+  const float z_l = __fdiv_rn(__fsub_rn(w_safe, __fmul_rn(z_h, z_h)), __fadd_rn(z, z_h));
+  const float t = first ? __fsub_rn(w, 1.75f) : __fsub_rn(z, 3.0f);
+  float p = first ? P1[JXR_ERFINV32_P1_N - 1] : P2[JXR_ERFINV32_P1_N - 1];
+#pragma unroll
+  for (int i = JXR_ERFINV32_P1_N - 2; i >= 0; --i) p = __fmaf_rn(p, t, first ? P1[i] : P2[i]);
+  const float mag = __fadd_rn(z_h, __fadd_rn(z_l, p));
+  const float r = first ? __fmul_rn(x, p) : (x < 0.0f ? -mag : mag);
+  if (!(ax <= 1.0f)) return __int_as_float(0x7FC00000);
+  if (ax == 1.0f) return __fmul_rn(x, __int_as_float(0x7F800000));
+  return r;
+}
+
+__device__ __forceinline__ double erfinv_acc_f64(double x) {
+  constexpr double P1[JXR_ERFINV64_P1_N] = {JXR_ERFINV64_P1};
+  constexpr double P2[JXR_ERFINV64_P2_N] = {JXR_ERFINV64_P2};
+  constexpr double P3[JXR_ERFINV64_P3_N] = {JXR_ERFINV64_P3};
+  static_assert(JXR_ERFINV64_P1_N == JXR_ERFINV64_P2_N && JXR_ERFINV64_P1_N == JXR_ERFINV64_P3_N,
+                "equal-length pieces");
+  const double ax = fabs(x);
+  const double q = __dsub_rn(1.0, ax);
+  const double w = -log_pos(__dmul_rn(q, __dadd_rn(1.0, ax)));
+  const int piece = w < 4.5 ? 0 : (w < 16.0 ? 1 : 2);
+  const double w_safe = piece == 0 ? 1.0 : w;
+  const double z = __dsqrt_rn(w_safe);
+  const double z_h = __longlong_as_double(__double_as_longlong(z) & (long long)0xFFFFFFFFF8000000ull);
+  const double z_l = __ddiv_rn(__dsub_rn(w_safe, __dmul_rn(z_h, z_h)), __dadd_rn(z, z_h));
+  const double t = piece == 0 ? __dsub_rn(w, 2.25) : __dsub_rn(z, piece == 1 ? 3.0 : 5.0);
+  constexpr int N = JXR_ERFINV64_P1_N;
+  double p = piece == 0 ? P1[N - 1] : (piece == 1 ? P2[N - 1] : P3[N - 1]);
+#pragma unroll
+  for (int i = N - 2; i >= 0; --i)
+    p = __fma_rn(p, t, piece == 0 ? P1[i] : (piece == 1 ? P2[i] : P3[i]));
+  const double mag = __dadd_rn(z_h, __dadd_rn(z_l, p));
+  const double r = piece == 0 ? __dmul_rn(x, p) : (x < 0.0 ? -mag : mag);
+  if (!(ax <= 1.0)) return __longlong_as_double(0x7FF8000000000000ll);
+  if (ax == 1.0) return __dmul_rn(x, __longlong_as_double(0x7FF0000000000000ll));
+  return r;
+}
+
+// erf_inv of the reference's default lowering, or (kAcc) of jax_accurate_erf_inv's
+template <bool kAcc>
+__device__ __forceinline__ float erfinv32(float x) {
+  if constexpr (kAcc) return erfinv_acc_f32(x);
+  else return erfinv_f32(x);
+}
+template <bool kAcc>
+__device__ __forceinline__ double erfinv64(double x) {
+  if constexpr (kAcc) return erfinv_acc_f64(x);
+  else return erfinv_f64(x);
+}
+
 // ---- 16-bit float helpers (raw bits in, raw bits out, arithmetic exact then rounded once) -
 
 template <bool BF>
@@ -293,7 +368,8 @@ struct OpUniformH {
 
 // u = uniform(nextafter(-1, 0), 1): maxval - minval rounds to exactly 2 in every dtype,
 // so u = 2 f + lo is exact and the fused and unfused forms agree.
-struct OpNormalF32 {
+template <bool kAcc = false>
+struct OpNormalF32T {
   static constexpr int kBits = 32;
   static constexpr int kGroups = 1;  // 4 blocks per thread: the transform needs the registers
   using Bits = uint32_t;
@@ -301,9 +377,10 @@ struct OpNormalF32 {
   __device__ __forceinline__ Out operator()(Bits b) const {
     const float lo = -0x1.fffffep-1f;  // -1 + 2^-24
     const float u = xla_max(lo, __fmaf_rn(unit_f32(b), 2.0f, lo));
-    return __fmul_rn(1.41421354f, erfinv_f32(u));
+    return __fmul_rn(1.41421354f, erfinv32<kAcc>(u));
   }
 };
+using OpNormalF32 = OpNormalF32T<false>;
 
 // A float32 sampler whose output depends only on bits >> 9 (the 23 mantissa bits of its
 // unit float), read back from the table of its 2^23 results (32 MiB, built on the device by
@@ -316,7 +393,8 @@ struct OpTableF32 {
   __device__ __forceinline__ Out operator()(Bits b) const { return __ldg(table + (b >> 9)); }
 };
 
-struct OpNormalF64 {
+template <bool kAcc = false>
+struct OpNormalF64T {
   static constexpr int kBits = 64;
   static constexpr int kGroups = 2;
   using Bits = uint64_t;
@@ -324,12 +402,13 @@ struct OpNormalF64 {
   __device__ __forceinline__ Out operator()(Bits b) const {
     const double lo = -0x1.fffffffffffffp-1;  // -1 + 2^-53
     const double u = xla_max(lo, __fma_rn(unit_f64(b), 2.0, lo));
-    return __dmul_rn(1.4142135623730951, erfinv_f64(u));
+    return __dmul_rn(1.4142135623730951, erfinv64<kAcc>(u));
   }
 };
+using OpNormalF64 = OpNormalF64T<false>;
 
 // erf_inv of a 16-bit float is evaluated in float32 and rounded back.
-template <bool BF>
+template <bool BF, bool kAcc = false>
 struct OpNormalH {
   static constexpr int kBits = BF ? 8 : 16;
   static constexpr int kGroups = 1;
@@ -338,7 +417,7 @@ struct OpNormalH {
   __device__ __forceinline__ Out operator()(Bits b) const {
     const float lo = BF ? -0x1.fep-1f : -0x1.ffcp-1f;  // -1 + 2^-8, -1 + 2^-11
     const float u = xla_max(lo, rh<BF>(__fmaf_rn(unit_h<BF>(b), 2.0f, lo)));
-    const float e = rh<BF>(erfinv_f32(u));
+    const float e = rh<BF>(erfinv32<kAcc>(u));
     return f2h<BF>(__fmul_rn(rh<BF>(1.41421354f), e));
   }
 };
@@ -475,11 +554,11 @@ __device__ __forceinline__ U randint_offset(U hi, U lo, U span) {
 // sqrt(2) erf_inv(u) clipped to [nextafter(lower, inf), nextafter(upper, -inf)].  a, b and
 // the clip bounds are parameters (computed once per call on the host).
 
-template <int D>
+template <int D, bool kAcc = false>
 struct OpTruncNormal;
 
-template <>
-struct OpTruncNormal<0> {  // float32
+template <bool kAcc>
+struct OpTruncNormal<0, kAcc> {  // float32
   static constexpr int kBits = 32;
   static constexpr int kGroups = 1;
   using Bits = uint32_t;
@@ -487,13 +566,13 @@ struct OpTruncNormal<0> {  // float32
   OpUniformF32<true> uni;
   float lo, hi;
   __device__ __forceinline__ Out operator()(Bits b) const {
-    const float x = __fmul_rn(1.41421354f, erfinv_f32(uni(b)));
+    const float x = __fmul_rn(1.41421354f, erfinv32<kAcc>(uni(b)));
     return xla_min(hi, xla_max(lo, x));
   }
 };
 
-template <>
-struct OpTruncNormal<1> {  // float64
+template <bool kAcc>
+struct OpTruncNormal<1, kAcc> {  // float64
   static constexpr int kBits = 64;
   static constexpr int kGroups = 2;
   using Bits = uint64_t;
@@ -501,12 +580,12 @@ struct OpTruncNormal<1> {  // float64
   OpUniformF64<true> uni;
   double lo, hi;
   __device__ __forceinline__ Out operator()(Bits b) const {
-    const double x = __dmul_rn(1.4142135623730951, erfinv_f64(uni(b)));
+    const double x = __dmul_rn(1.4142135623730951, erfinv64<kAcc>(uni(b)));
     return xla_min(hi, xla_max(lo, x));
   }
 };
 
-template <bool BF>
+template <bool BF, bool kAcc>
 struct OpTruncNormalH {
   static constexpr int kBits = BF ? 8 : 16;
   static constexpr int kGroups = 1;
@@ -515,15 +594,15 @@ struct OpTruncNormalH {
   OpUniformH<BF, true> uni;
   float lo, hi;  // values of 16-bit floats
   __device__ __forceinline__ Out operator()(Bits b) const {
-    const float e = rh<BF>(erfinv_f32(h2f<BF>(uni(b))));
+    const float e = rh<BF>(erfinv32<kAcc>(h2f<BF>(uni(b))));
     const float x = rh<BF>(__fmul_rn(rh<BF>(1.41421354f), e));
     return f2h<BF>(xla_min(hi, xla_max(lo, x)));
   }
 };
-template <>
-struct OpTruncNormal<2> : OpTruncNormalH<false> {};
-template <>
-struct OpTruncNormal<3> : OpTruncNormalH<true> {};
+template <bool kAcc>
+struct OpTruncNormal<2, kAcc> : OpTruncNormalH<false, kAcc> {};
+template <bool kAcc>
+struct OpTruncNormal<3, kAcc> : OpTruncNormalH<true, kAcc> {};
 
 // ---- gumbel modes "high" and "highest" (R/random.R:1465-1489) ----------------------------
 //

@@ -758,12 +758,11 @@ def random_bits(key, shape=(), dtype=None):
 
 # ---- uniform / normal / bernoulli (R/random.R:278-304, :466-508, :643-666) -------------------
 
-def _default_erf_inv():
-    """The samplers evaluate erf_inv as chlo.erf_inv (R/lax_special.R:1324-1331);
-    jax_accurate_erf_inv selects another approximation, which is not provided."""
-    if cfg.jax_config("jax_accurate_erf_inv"):
-        raise JaxNotImplementedError("jax_accurate_erf_inv: only the default erf_inv "
-                                     "(chlo.erf_inv) is provided")
+def _select_erf_inv():
+    """Sets, for this thread's library calls, the erf_inv that jax_accurate_erf_inv names
+    (R/lax_special.R:1324-1331): chlo.erf_inv by default, JAX's erf_inv_core
+    (R/lax_special.R:1022-1082) when the option is set."""
+    nat.lib().jxr_set_accurate_erf_inv(1 if cfg.jax_config("jax_accurate_erf_inv") else 0)
 
 
 def _float_dtype(name, dt, kind="a float"):
@@ -834,7 +833,7 @@ def random_uniform(key, shape=(), dtype=None, minval=0.0, maxval=1.0):
 def random_normal(key, shape=(), dtype=None):
     """Standard normal floats: sqrt(2) * erf_inv(u), u uniform in (-1, 1)
     (R/random.R:482-508)."""
-    _default_erf_inv()
+    _select_erf_inv()
     k, _, nb = _check_key("normal", key)
     dt = _float_dtype("normal", dtype, kind="a float or complex")
     shape = canon_shape(shape)
@@ -914,7 +913,7 @@ def random_bernoulli(key, p=0.5, shape=None, mode="low"):
 def random_normal_bernoulli(key, p=0.5, shape=(), dtype=None):
     """(random_normal(key, shape, dtype), random_bernoulli(key, p, shape)) of one key in a
     single cipher pass; p is a Python float converted to dtype."""
-    _default_erf_inv()
+    _select_erf_inv()
     k, _, nb = _check_key("normal", key)
     dt = _float_dtype("normal", dtype)
     shape = canon_shape(shape)
@@ -1015,7 +1014,7 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
     [erf(lower / sqrt 2), erf(upper / sqrt 2)), clipped to the open interval
     (R/random.R:576-603).  Scalar bounds run in one fused kernel; array bounds
     (broadcast to `shape`) take the unit draw and a per-element transform."""
-    _default_erf_inv()
+    _select_erf_inv()
     if shape is not None:
         shape = canon_shape(shape)
     k, _, nb = _check_key("truncated_normal", key)
@@ -1421,7 +1420,7 @@ def lax_rng_bit_generator(key, shape, dtype="uint32", algorithm=0):
 
 def lax_erf_inv(x):
     """Element-wise inverse error function for float32/float64 arrays."""
-    _default_erf_inv()
+    _select_erf_inv()
     t = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x, dtype=default_float()))
     dt = _NAME[t.dtype]
     if dt not in ("float32", "float64"):

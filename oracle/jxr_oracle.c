@@ -10,6 +10,7 @@
  * Reference lines cited are paths within the jaxR project.
  */
 #include "jxr_oracle.h"
+#include "erfinv_tables.h"
 
 #include <math.h>
 #include <string.h>
@@ -334,7 +335,73 @@ static const float GS_GE5[9] = {-0.000200214257f, 0.000100950558f, 0.00134934322
                                 -0.00367342844f, 0.00573950773f, -0.0076224613f,
                                 0.00943887047f, 1.00167406f, 2.83297682f};
 
+/* ---- accurate erf_inv (jax_accurate_erf_inv; R/lax_special.R:1022-1082) ---------------
+ *
+ * erf_inv_core(x, q = 1 - |x|) without the far-tail pieces: w = -log(q (1 + |x|)).  Below
+ * the first split (float32 w < 3.5, float64 w < 4.5) the result is x * P(w - c1); above
+ * it z = sqrt(w) is carried as z_h (the top half of its mantissa, so z_h^2 is exact) plus
+ * z_l = (w - z_h^2) / (z + z_h), and the result is sign(x) (z_h + (z_l + P(z - shift))).
+ * The polynomials are JAX's Sollya fits as the reference holds them (erfinv_tables.h),
+ * evaluated by Horner from the highest coefficient down.  |x| > 1 or NaN gives NaN,
+ * |x| = 1 gives x * inf. */
+static const float EA32_P1[JXR_ERFINV32_P1_N] = {JXR_ERFINV32_P1};
+static const float EA32_P2[JXR_ERFINV32_P2_N] = {JXR_ERFINV32_P2};
+static const double EA64_P1[JXR_ERFINV64_P1_N] = {JXR_ERFINV64_P1};
+static const double EA64_P2[JXR_ERFINV64_P2_N] = {JXR_ERFINV64_P2};
+static const double EA64_P3[JXR_ERFINV64_P3_N] = {JXR_ERFINV64_P3};
+
+static float erfinv_accurate_f32(float x, int fused) {
+  const float ax = fabsf(x);
+  if (!(ax <= 1.0f)) return NAN;
+  if (ax == 1.0f) return x * INFINITY;
+  const float q = 1.0f - ax;
+  const float arg = q * (1.0f + ax);
+  const float w = -(float)log_pos((double)arg); /* the logarithm rounded once */
+  const int first = w < 3.5f;
+  const float w_safe = first ? 1.0f : w;
+  const float z = sqrtf(w_safe);
+  uint32_t zb;
+  memcpy(&zb, &z, 4);
+  zb &= 0xFFFFF000u;
+  float z_h;
+  memcpy(&z_h, &zb, 4);
+  const float z_l = (w_safe - z_h * z_h) / (z + z_h);
+  const float t = first ? w - 1.75f : z - 3.0f;
+  const float* c = first ? EA32_P1 : EA32_P2;
+  float p = c[JXR_ERFINV32_P1_N - 1];
+  for (int i = JXR_ERFINV32_P1_N - 2; i >= 0; --i) p = fused ? fmaf(p, t, c[i]) : p * t + c[i];
+  if (first) return x * p;
+  const float mag = z_h + (z_l + p);
+  return x < 0.0f ? -mag : mag;
+}
+
+static double erfinv_accurate_f64(double x, int fused) {
+  const double ax = fabs(x);
+  if (!(ax <= 1.0)) return NAN;
+  if (ax == 1.0) return x * INFINITY;
+  const double q = 1.0 - ax;
+  const double w = -log_pos(q * (1.0 + ax));
+  const int piece = (w < 4.5) ? 0 : (w < 16.0) ? 1 : 2;
+  const double w_safe = piece == 0 ? 1.0 : w;
+  const double z = sqrt(w_safe);
+  uint64_t zb;
+  memcpy(&zb, &z, 8);
+  zb &= 0xFFFFFFFFF8000000ull;
+  double z_h;
+  memcpy(&z_h, &zb, 8);
+  const double z_l = (w_safe - z_h * z_h) / (z + z_h);
+  const double shift = piece == 1 ? 3.0 : 5.0;
+  const double t = piece == 0 ? w - 2.25 : z - shift;
+  const double* c = piece == 0 ? EA64_P1 : piece == 1 ? EA64_P2 : EA64_P3;
+  double p = c[JXR_ERFINV64_P1_N - 1];
+  for (int i = JXR_ERFINV64_P1_N - 2; i >= 0; --i) p = fused ? fma(p, t, c[i]) : p * t + c[i];
+  if (piece == 0) return x * p;
+  const double mag = z_h + (z_l + p);
+  return x < 0.0 ? -mag : mag;
+}
+
 float orc_erfinv_f32(float x, int fma) {
+  if (fma & ORC_ERFINV_ACCURATE) return erfinv_accurate_f32(x, fma & 1);
   /* log1p of the rounded float -(x*x), evaluated in double and rounded once */
   const float w0 = -(float)log1p_neg((double)(-(x * x)));
   const int lt = w0 < 5.0f;
@@ -373,6 +440,7 @@ static const double GD_GE16[17] = {
     1.0103004648645343977,      4.8499064014085844221};
 
 double orc_erfinv_f64(double x, int fma_) {
+  if (fma_ & ORC_ERFINV_ACCURATE) return erfinv_accurate_f64(x, fma_ & 1);
   const double w0 = -log1p_neg(-(x * x));
   const double* c;
   int n;
@@ -680,13 +748,14 @@ static float half_step(float x, int up, int bf) {
  * u = uniform(a, b) (fused multiply-add), sqrt2 * erf_inv(u) (fused Horner), clipped to
  * [nextafter(lower, inf), nextafter(upper, -inf)]. */
 double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
-                               int partitionable, double lower, double upper, uint64_t i) {
+                               int partitionable, double lower, double upper, int erfinv_mode,
+                               uint64_t i) {
   switch (dtype) {
     case ORC_F32: {
       const float s2 = 1.41421356237309504880f, lo = (float)lower, hi = (float)upper;
       const float a = (float)erf((double)(lo / s2)), b = (float)erf((double)(hi / s2));
       const float u = (float)orc_uniform_at(key, ORC_F32, size, partitionable, a, b, 1, i);
-      const float x = s2 * orc_erfinv_f32(u, 1);
+      const float x = s2 * orc_erfinv_f32(u, erfinv_mode);
       const float cl = nextafterf(lo, INFINITY), ch = nextafterf(hi, -INFINITY);
       const float m = isnan(x) ? x : (cl >= x ? cl : x);
       return isnan(m) ? m : (ch <= m ? ch : m);
@@ -695,7 +764,7 @@ double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
       const double s2 = 1.41421356237309504880;
       const double a = erf(lower / s2), b = erf(upper / s2);
       const double u = orc_uniform_at(key, ORC_F64, size, partitionable, a, b, 1, i);
-      const double x = s2 * orc_erfinv_f64(u, 1);
+      const double x = s2 * orc_erfinv_f64(u, erfinv_mode);
       const double cl = nextafter(lower, INFINITY), ch = nextafter(upper, -INFINITY);
       const double m = isnan(x) ? x : (cl >= x ? cl : x);
       return isnan(m) ? m : (ch <= m ? ch : m);
@@ -707,7 +776,7 @@ double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
       const float a = rh((float)erf((double)rh(lo / s2, bf)), bf);
       const float b = rh((float)erf((double)rh(hi / s2, bf)), bf);
       const float u = (float)orc_uniform_at(key, dtype, size, partitionable, a, b, 1, i);
-      const float e = rh(orc_erfinv_f32(u, 1), bf);
+      const float e = rh(orc_erfinv_f32(u, erfinv_mode), bf);
       const float x = rh(s2 * e, bf);
       const float cl = half_step(lo, 1, bf), ch = half_step(hi, 0, bf);
       const float m = isnan(x) ? x : (cl >= x ? cl : x);
@@ -726,14 +795,15 @@ int orc_gumbel_mode(const uint32_t key[2], int mode, int dtype, uint64_t size,
 }
 
 int orc_truncated_normal(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
-                         double lower, double upper, uint64_t begin, uint64_t count, void* out) {
+                         double lower, double upper, int erfinv_mode, uint64_t begin,
+                         uint64_t count, void* out) {
   if (dtype < ORC_F32 || dtype > ORC_BF16) return 1;
   if (begin > size || count > size - begin) return 2;
   ORC_PAR_FOR
   for (int64_t t = 0; t < (int64_t)count; ++t)
     store_float(out, dtype, t,
                 orc_truncated_normal_at(key, dtype, size, partitionable, lower, upper,
-                                        begin + (uint64_t)t));
+                                        erfinv_mode, begin + (uint64_t)t));
   return 0;
 }
 

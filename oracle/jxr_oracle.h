@@ -60,6 +60,10 @@ int orc_random_bits(const uint32_t key[2], int bit_width, uint64_t size, int par
  * taken as -log1p(-x*x) and erf_inv(+-1) = +-inf (R/lax_special.R:1327-1331
  * emits chlo.erf_inv).  fma selects a fused Horner evaluation.  The logarithm is
  * log1p_neg below, evaluated in double (and, for float32, rounded once). */
+/* mode bit 1 (ORC_ERFINV_ACCURATE): the accurate erf_inv of jax_accurate_erf_inv instead
+ * (R/lax_special.R:1022-1082, JAX's erf_inv_core without the far-tail pieces); bit 0
+ * still selects fused Horner steps. */
+enum { ORC_ERFINV_ACCURATE = 2 };
 float orc_erfinv_f32(float x, int fma);
 double orc_erfinv_f64(double x, int fma);
 void orc_erfinv_arr(const void* x, int64_t n, int dtype, int fma, void* out);
@@ -105,9 +109,11 @@ int orc_gumbel_mode(const uint32_t key[2], int mode, int dtype, uint64_t size,
 double orc_gumbel_mode_at(const uint32_t key[2], int mode, int dtype, uint64_t size,
                           int partitionable, uint64_t i);
 int orc_truncated_normal(const uint32_t key[2], int dtype, uint64_t size, int partitionable,
-                         double lower, double upper, uint64_t begin, uint64_t count, void* out);
+                         double lower, double upper, int erfinv_mode, uint64_t begin,
+                         uint64_t count, void* out);
 double orc_truncated_normal_at(const uint32_t key[2], int dtype, uint64_t size,
-                               int partitionable, double lower, double upper, uint64_t i);
+                               int partitionable, double lower, double upper, int erfinv_mode,
+                               uint64_t i);
 
 /* rbg / unsafe_rbg (R/prng.R:264-426): XLA's RngBitGenerator as Philox4x32-10 with key
  * (q0, q1) and the key q as 128-bit counter, advanced per block of four 32-bit outputs. */

@@ -65,7 +65,7 @@ def lib():
         L.orc_sample_at.argtypes = [u32p, i32, i32, u64, i32, u64]
         L.orc_sample_at.restype = dbl
         L.orc_gumbel_mode.argtypes = [u32p, i32, i32, u64, i32, vp]
-        L.orc_truncated_normal.argtypes = [u32p, i32, u64, i32, dbl, dbl, u64, u64, vp]
+        L.orc_truncated_normal.argtypes = [u32p, i32, u64, i32, dbl, dbl, i32, u64, u64, vp]
         L.orc_philox4x32.argtypes = [u32p, u32p, u32p]
         L.orc_rbg_bits.argtypes = [u32p, i32, u64, u64, u64, vp]
         L.orc_rbg_unsafe_split.argtypes = [u32p, i64, u32p]
@@ -135,10 +135,18 @@ def bits_at(key, bit_width, size, partitionable, idx):
                      for i in idx], dtype=NP_BITS[bit_width])
 
 
-def erfinv(x, dtype="float32", fma=True):
+ERFINV_ACCURATE = 2  # ORC_ERFINV_ACCURATE: jax_accurate_erf_inv's erf_inv
+
+
+def _erfinv_mode(fma, accurate):
+    return int(bool(fma)) | (ERFINV_ACCURATE if accurate else 0)
+
+
+def erfinv(x, dtype="float32", fma=True, accurate=False):
     a = np.ascontiguousarray(np.asarray(x, dtype=np.float32 if dtype == "float32" else np.float64))
     out = np.empty_like(a)
-    lib().orc_erfinv_arr(_ptr(a), a.size, F32 if dtype == "float32" else F64, int(fma), _ptr(out))
+    lib().orc_erfinv_arr(_ptr(a), a.size, F32 if dtype == "float32" else F64,
+                         _erfinv_mode(fma, accurate), _ptr(out))
     return out.ravel()
 
 
@@ -154,18 +162,18 @@ def uniform(key, dtype, size, partitionable=True, minval=0.0, maxval=1.0, fma=Tr
     return out
 
 
-def normal(key, dtype, size, partitionable=True, fma=True, begin=0, count=None):
+def normal(key, dtype, size, partitionable=True, fma=True, begin=0, count=None, accurate=False):
     code = DTYPE_CODE[dtype]
     count = size - begin if count is None else count
     out = np.empty(int(count), dtype=NP_FLOAT[code])
-    rc = lib().orc_normal(_key(key), code, int(size), int(bool(partitionable)), int(fma),
-                          int(begin), int(count), _ptr(out))
+    rc = lib().orc_normal(_key(key), code, int(size), int(bool(partitionable)),
+                          _erfinv_mode(fma, accurate), int(begin), int(count), _ptr(out))
     if rc:
         raise ValueError(f"orc_normal failed ({rc})")
     return out
 
 
-def complex_normal(key, dtype, size, partitionable=True):
+def complex_normal(key, dtype, size, partitionable=True, accurate=False):
     """Complex normals (R/random.R:489-499): the key split in two, a real normal of the
     component dtype from each half (real part from the first), each divided by sqrt(2)
     rounded to the component dtype.  XLA divides (re + i im) by (sqrt2 + 0i) with Smith's
@@ -174,8 +182,8 @@ def complex_normal(key, dtype, size, partitionable=True):
     rdt = np.float32 if real == "float32" else np.float64
     ks = split(key, 2, partitionable)
     s2 = rdt(np.sqrt(2.0))
-    re = (normal(ks[0], real, size, partitionable) / s2).astype(rdt)
-    im = (normal(ks[1], real, size, partitionable) / s2).astype(rdt)
+    re = (normal(ks[0], real, size, partitionable, accurate=accurate) / s2).astype(rdt)
+    im = (normal(ks[1], real, size, partitionable, accurate=accurate) / s2).astype(rdt)
     out = np.empty(int(size), dtype=np.complex64 if real == "float32" else np.complex128)
     out.real = re
     out.imag = im
@@ -244,12 +252,14 @@ def gumbel_mode(key, mode, dtype, size, partitionable=True):
     return out
 
 
-def truncated_normal(key, dtype, size, lower, upper, partitionable=True, begin=0, count=None):
+def truncated_normal(key, dtype, size, lower, upper, partitionable=True, begin=0, count=None,
+                     accurate=False):
     code = DTYPE_CODE[dtype]
     count = size - begin if count is None else count
     out = np.empty(int(count), dtype=NP_FLOAT[code])
     rc = lib().orc_truncated_normal(_key(key), code, int(size), int(bool(partitionable)),
-                                    float(lower), float(upper), int(begin), int(count), _ptr(out))
+                                    float(lower), float(upper), _erfinv_mode(True, accurate),
+                                    int(begin), int(count), _ptr(out))
     if rc:
         raise ValueError(f"orc_truncated_normal failed ({rc})")
     return out

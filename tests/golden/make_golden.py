@@ -459,6 +459,17 @@ def build(ref):
                           {"x": [float(v) if not isinstance(v, str) else v for v in xs],
                            "dtype": dt}, dt, lst[1] if isinstance(lst[1], list) else [lst[1]],
                           lst[2], "rel:1e-12" if dt == "float64" else "rel:1e-5"))
+    # the accurate erf_inv of jax_accurate_erf_inv (test-lax-special.R:204-212); the oracle
+    # reproduces every recorded value bit for bit, so the comparison is exact
+    lsp = os.path.join(tt, "test-lax-special.R")
+    for dt, pat in (("float32", r"sp_erf_inv_impl\(as_jax\(array\((?=c\(0, 0.300000012)"),
+                    ("float64", r"sp_erf_inv_impl\(as_jax\(array\((?=c\(0, 0x1.3333333333333p-2)")):
+        xs, line = c_vector_at(lsp, pat)
+        lst, _ = literal_at(lsp, pat, which=0)
+        cases.append(case(f"erf_inv_accurate_{dt}", src(lsp, line), "erf_inv",
+                          {"x": [float(v) if not isinstance(v, str) else v for v in xs],
+                           "dtype": dt, "accurate": True}, dt,
+                          lst[1] if isinstance(lst[1], list) else [lst[1]], lst[2], "exact"))
     return cases
 
 

@@ -284,7 +284,7 @@ def evaluate(case, be):
     if op == "erf_inv":
         dt = a["dtype"]
         xs = np.array([_f(v) for v in a["x"]], dtype=np.float64).astype(dt)
-        return be.erfinv(xs, dt)
+        return be.erfinv(xs, dt, bool(a.get("accurate", False)))
     raise ValueError(f"unknown op {op}")
 
 
@@ -341,8 +341,8 @@ class OracleBackend:
     def bernoulli(self, key, dt, p, n, part):
         return self.o.bernoulli(key, dt, p, n, part)
 
-    def erfinv(self, xs, dt):
-        return self.o.erfinv(xs, dt, fma=self.erfinv_fma)
+    def erfinv(self, xs, dt, accurate=False):
+        return self.o.erfinv(xs, dt, fma=self.erfinv_fma, accurate=accurate)
 
     def randint(self, key, shape, mn, mx, dt, part):
         return self.o.randint(key, shape, mn, mx, dt, part)

@@ -107,8 +107,9 @@ class ProductBackend:
             pt = torch.tensor(p, dtype=jrr._TORCH[dt])
             return to_np(jr.random_bernoulli(torch.tensor(np.asarray(key, np.uint32)), pt, (n,)))
 
-    def erfinv(self, xs, dt):
-        with flags(dt == "float64", self.part):
+    def erfinv(self, xs, dt, accurate=False):
+        with flags(dt == "float64", self.part), \
+                jr.with_jax_config("jax_accurate_erf_inv", accurate):
             return to_np(jr.lax_erf_inv(torch.tensor(np.asarray(xs))))
 
 

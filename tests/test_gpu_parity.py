@@ -265,6 +265,25 @@ def test_erf_inv_edges():
     assert np.isnan(y[6]) and np.isnan(y[7]) and np.isnan(y[8])
 
 
+@pytest.mark.parametrize("dt", ["float32", "float64"])
+def test_erf_inv_bit_exact_with_oracle(oracle, dt):
+    """lax_erf_inv on 2^20 + tail values: uniform in (-1, 1), within 1e-3..1e-15 of +-1,
+    tiny and subnormal magnitudes, the exact ends and zeros; every result bit-identical
+    with the oracle's."""
+    npdt = np.float32 if dt == "float32" else np.float64
+    rng = np.random.default_rng(3)
+    digits = 7 if dt == "float32" else 15
+    tail = 1 - 10.0 ** -rng.uniform(3, digits, 1 << 16)
+    tiny = 10.0 ** -rng.uniform(5, 300 if dt == "float64" else 40, 1 << 12)
+    x = np.concatenate([rng.uniform(-1, 1, 1 << 20), tail, -tail, tiny, -tiny,
+                        [0.0, -0.0, 1.0, -1.0, np.finfo(npdt).tiny, np.finfo(npdt).eps]])
+    x = x.astype(npdt)
+    with flags(dt == "float64"):
+        got = to_np(jr.lax_erf_inv(torch.from_numpy(x).cuda()))
+    want = oracle.erfinv(x, dt)
+    assert np.array_equal(got.view(f"u{npdt().itemsize}"), want.view(f"u{npdt().itemsize}"))
+
+
 @pytest.mark.parametrize("part", [True, False], ids=["partitionable", "original"])
 @pytest.mark.parametrize("dt", ["float32", "float64", "float16", "bfloat16"])
 def test_bernoulli_exact(oracle, part, dt):

@@ -217,11 +217,15 @@ def test_randint_bounds_follow_reference(monkeypatch):
         assert bounds(6, 0, 10, "uint64") == (64, 0, [0], [10], [0], 64)
 
 
-def test_accurate_erf_inv_option_is_refused():
-    k = raw(2)
+def test_accurate_erf_inv_option_selects_the_library_variant():
+    """jax_accurate_erf_inv reaches the library as its per-thread erf_inv setting, which
+    every sampler that evaluates erf_inv reads when it launches (no GPU call here)."""
+    from jaxr_b200 import _native as nat
+    lib = nat.lib()
     with jr.with_jax_config("jax_accurate_erf_inv", True):
-        for call in (lambda: jr.random_normal(k, 3), lambda: jr.lax_erf_inv(np.zeros(3)),
-                     lambda: jr.random_truncated_normal(k, -1, 1, 3)):
-            with pytest.raises(jr.JaxNotImplementedError, match="jax_accurate_erf_inv"):
-                call()
+        jrr._select_erf_inv()
+        assert lib.jxr_get_accurate_erf_inv() == 1
+    jrr._select_erf_inv()
+    assert lib.jxr_get_accurate_erf_inv() == 0
+    assert lib.jxr_set_accurate_erf_inv(7) == 0 and lib.jxr_set_accurate_erf_inv(0) == 1
     assert jr.jax_config("jax_accurate_erf_inv") is False
