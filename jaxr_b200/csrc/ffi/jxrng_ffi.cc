@@ -9,14 +9,15 @@
 //                                             through jxr_random_bits_host_static, which
 //                                             allocates nothing
 //   jxr_ffi_uniform          platform "cuda"  float result, attributes minval, maxval
-//   jxr_ffi_normal           platform "cuda"  float result
+//   jxr_ffi_normal           platform "cuda"  float result, attribute accurate_erf_inv
 //
 // One argument, the key buffer (threefry2x32 data, u32[*batch, 2]: one key per batch row,
 // as ffi_call's vmap methods deliver them); one result, whose dtype gives the bit width
 // or the float type and whose element count divided by the number of keys gives each
 // key's request.  Attribute "partitionable" (a bool scalar; the value of
-// jax_threefry_partitionable, default true) selects the counter layout.  Errors come back
-// as XLA FFI errors carrying the library's message.
+// jax_threefry_partitionable, default true) selects the counter layout, and
+// "accurate_erf_inv" (a bool scalar; jax_accurate_erf_inv, default false) the normal's
+// erf_inv.  Errors come back as XLA FFI errors carrying the library's message.
 
 #include <cstring>
 
@@ -50,6 +51,7 @@ struct Frame {
   const XLA_FFI_Buffer* out = nullptr;
   int64_t nkeys = 0, out_elems = 0;
   int layout = JXR_LAYOUT_PARTITIONABLE;
+  int accurate_erf_inv = 0;
   double minval = 0.0, maxval = 1.0;
 };
 
@@ -99,6 +101,7 @@ XLA_FFI_Error* decode(XLA_FFI_CallFrame* cf, Frame* f) {
     const XLA_FFI_ByteSpan* name = cf->attrs.names[i];
     if (name_is(name, "partitionable"))
       f->layout = scalar_value(sc) != 0.0 ? JXR_LAYOUT_PARTITIONABLE : JXR_LAYOUT_ORIGINAL;
+    else if (name_is(name, "accurate_erf_inv")) f->accurate_erf_inv = scalar_value(sc) != 0.0;
     else if (name_is(name, "minval")) f->minval = scalar_value(sc);
     else if (name_is(name, "maxval")) f->maxval = scalar_value(sc);
   }
@@ -178,7 +181,11 @@ XLA_FFI_Error* handle(XLA_FFI_CallFrame* cf, Kind kind) {
   if (kind == kUniform)
     return status(cf->api, jxr_uniform(keys, f.nkeys, size, 0, size, f.layout, dt, f.minval,
                                        f.maxval, 0, out, stream));
-  return status(cf->api, jxr_normal(keys, f.nkeys, size, 0, size, f.layout, dt, out, stream));
+  // the library's erf_inv setting is per host thread: set for this call, then restored
+  const int prev = jxr_set_accurate_erf_inv(f.accurate_erf_inv);
+  const int rc = jxr_normal(keys, f.nkeys, size, 0, size, f.layout, dt, out, stream);
+  jxr_set_accurate_erf_inv(prev);
+  return status(cf->api, rc);
 }
 
 }  // namespace

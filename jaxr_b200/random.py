@@ -12,6 +12,7 @@ torch.uint64 tensors, bool results torch.bool.
 
 from __future__ import annotations
 
+import functools
 import math
 import numbers
 import warnings
@@ -758,11 +759,20 @@ def random_bits(key, shape=(), dtype=None):
 
 # ---- uniform / normal / bernoulli (R/random.R:278-304, :466-508, :643-666) -------------------
 
-def _select_erf_inv():
-    """Sets, for this thread's library calls, the erf_inv that jax_accurate_erf_inv names
-    (R/lax_special.R:1324-1331): chlo.erf_inv by default, JAX's erf_inv_core
-    (R/lax_special.R:1022-1082) when the option is set."""
-    nat.lib().jxr_set_accurate_erf_inv(1 if cfg.jax_config("jax_accurate_erf_inv") else 0)
+def _uses_erf_inv(fn):
+    """Runs `fn` with the library's erf_inv (a per-thread setting) set to the one that
+    jax_accurate_erf_inv names (R/lax_special.R:1324-1331): chlo.erf_inv by default, JAX's
+    erf_inv_core (R/lax_special.R:1022-1082) when the option is set.  The previous setting
+    is restored on return, so other callers of the library on this thread see theirs."""
+    @functools.wraps(fn)
+    def wrapped(*args, **kwargs):
+        lib = nat.lib()
+        prev = lib.jxr_set_accurate_erf_inv(1 if cfg.jax_config("jax_accurate_erf_inv") else 0)
+        try:
+            return fn(*args, **kwargs)
+        finally:
+            lib.jxr_set_accurate_erf_inv(prev)
+    return wrapped
 
 
 def _float_dtype(name, dt, kind="a float"):
@@ -830,10 +840,10 @@ def random_uniform(key, shape=(), dtype=None, minval=0.0, maxval=1.0):
     return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
 
 
+@_uses_erf_inv
 def random_normal(key, shape=(), dtype=None):
     """Standard normal floats: sqrt(2) * erf_inv(u), u uniform in (-1, 1)
     (R/random.R:482-508)."""
-    _select_erf_inv()
     k, _, nb = _check_key("normal", key)
     dt = _float_dtype("normal", dtype, kind="a float or complex")
     shape = canon_shape(shape)
@@ -910,10 +920,10 @@ def random_bernoulli(key, p=0.5, shape=None, mode="low"):
     return _rebatch(out.view(torch.bool).reshape(bshape + shape), nb)
 
 
+@_uses_erf_inv
 def random_normal_bernoulli(key, p=0.5, shape=(), dtype=None):
     """(random_normal(key, shape, dtype), random_bernoulli(key, p, shape)) of one key in a
     single cipher pass; p is a Python float converted to dtype."""
-    _select_erf_inv()
     k, _, nb = _check_key("normal", key)
     dt = _float_dtype("normal", dtype)
     shape = canon_shape(shape)
@@ -1009,12 +1019,12 @@ def random_gumbel(key, shape=(), dtype=None, mode=None):
 
 # ---- truncated normal (R/random.R:576-603) ---------------------------------------------------
 
+@_uses_erf_inv
 def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
     """Normal samples truncated to (lower, upper): sqrt(2) erf_inv(u) with u uniform in
     [erf(lower / sqrt 2), erf(upper / sqrt 2)), clipped to the open interval
     (R/random.R:576-603).  Scalar bounds run in one fused kernel; array bounds
     (broadcast to `shape`) take the unit draw and a per-element transform."""
-    _select_erf_inv()
     if shape is not None:
         shape = canon_shape(shape)
     k, _, nb = _check_key("truncated_normal", key)
@@ -1418,9 +1428,9 @@ def lax_rng_bit_generator(key, shape, dtype="uint32", algorithm=0):
 
 # ---- erf_inv (R/lax.R:222) ---------------------------------------------------------------------
 
+@_uses_erf_inv
 def lax_erf_inv(x):
     """Element-wise inverse error function for float32/float64 arrays."""
-    _select_erf_inv()
     t = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x, dtype=default_float()))
     dt = _NAME[t.dtype]
     if dt not in ("float32", "float64"):

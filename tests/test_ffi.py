@@ -90,7 +90,18 @@ def test_cuda_handlers_match_the_oracle(lib):
         want = orc.uniform(keys[r], "float32", 500, True, -2.0, 3.0)
         assert np.array_equal(u[r].cpu().numpy().view(np.uint32), want.view(np.uint32))
         wn = orc.normal(keys[r], "float64", 500, True)
-        assert np.allclose(n[r].cpu().numpy(), wn, rtol=1e-12, atol=0)
+        assert np.array_equal(n[r].cpu().numpy().view(np.uint64), wn.view(np.uint64))
+    # attribute accurate_erf_inv: the accurate erf_inv for this call only
+    from jaxr_b200 import _native as nat
+    na = torch.empty((3, 500), dtype=torch.float32, device="cuda")
+    before = nat.lib().jxr_get_accurate_erf_inv()
+    rt.call(lib.jxr_ffi_normal, (ff.U32, kd.data_ptr(), [3, 2]), (ff.F32, na.data_ptr(), [3, 500]),
+            [("accurate_erf_inv", ff.PRED, C.c_uint8(1))])
+    torch.cuda.synchronize()
+    assert nat.lib().jxr_get_accurate_erf_inv() == before == 0
+    for r in range(3):
+        wa = orc.normal(keys[r], "float32", 500, True, accurate=True)
+        assert np.array_equal(na[r].cpu().numpy().view(np.uint32), wa.view(np.uint32))
 
 
 @pytest.mark.gpu

@@ -217,15 +217,23 @@ def test_randint_bounds_follow_reference(monkeypatch):
         assert bounds(6, 0, 10, "uint64") == (64, 0, [0], [10], [0], 64)
 
 
-def test_accurate_erf_inv_option_selects_the_library_variant():
-    """jax_accurate_erf_inv reaches the library as its per-thread erf_inv setting, which
-    every sampler that evaluates erf_inv reads when it launches (no GPU call here)."""
+def test_accurate_erf_inv_option_selects_the_library_variant(monkeypatch):
+    """jax_accurate_erf_inv reaches the library as its per-thread erf_inv setting for the
+    duration of each sampler call, and the previous setting comes back afterwards (no GPU
+    call here: the sampler body is a stub that records the setting it sees)."""
     from jaxr_b200 import _native as nat
     lib = nat.lib()
+    seen = []
+    f = jrr._uses_erf_inv(lambda: seen.append(lib.jxr_get_accurate_erf_inv()))
     with jr.with_jax_config("jax_accurate_erf_inv", True):
-        jrr._select_erf_inv()
-        assert lib.jxr_get_accurate_erf_inv() == 1
-    jrr._select_erf_inv()
-    assert lib.jxr_get_accurate_erf_inv() == 0
-    assert lib.jxr_set_accurate_erf_inv(7) == 0 and lib.jxr_set_accurate_erf_inv(0) == 1
+        f()
+    f()
+    assert seen == [1, 0] and lib.jxr_get_accurate_erf_inv() == 0
+    lib.jxr_set_accurate_erf_inv(1)
+    f()
+    assert seen[-1] == 0 and lib.jxr_get_accurate_erf_inv() == 1
+    assert lib.jxr_set_accurate_erf_inv(7) == 1 and lib.jxr_set_accurate_erf_inv(0) == 1
+    for fn in (jr.random_normal, jr.random_normal_bernoulli, jr.random_truncated_normal,
+               jr.lax_erf_inv):
+        assert getattr(fn, "__wrapped__", None) is not None, fn.__name__
     assert jr.jax_config("jax_accurate_erf_inv") is False
