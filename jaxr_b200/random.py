@@ -100,14 +100,26 @@ def _is_float(dt):
     return dt in _FLOAT_CODE
 
 
+_cuda_ready = False
+
+
 def _device():
-    if not torch.cuda.is_available():
-        raise RuntimeError("no CUDA device: the threefry kernels run on an sm_100 GPU and "
-                           "there is no CPU path")
+    global _cuda_ready
+    if not _cuda_ready:
+        if not torch.cuda.is_available():
+            raise RuntimeError("no CUDA device: the threefry kernels run on an sm_100 GPU and "
+                               "there is no CPU path")
+        _cuda_ready = True
     return torch.device("cuda", torch.cuda.current_device())
 
 
+# the current stream's handle without building a torch.cuda.Stream object per call
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream():
+    if _raw_stream is not None:
+        return _raw_stream(torch.cuda.current_device())
     return ctypes_stream(torch.cuda.current_stream())
 
 
@@ -129,6 +141,8 @@ def shape_str(s):
 
 def canon_shape(shape):
     """Shape argument to a tuple of non-negative ints (R/lax_shape.R:16-28)."""
+    if type(shape) is tuple and all(type(v) is int and v >= 0 for v in shape):
+        return shape
     if shape is None:
         return ()
     if isinstance(shape, torch.Tensor):
@@ -520,7 +534,10 @@ def random_Key(x):
 def _flat_keys(k):
     """Key data as a contiguous (nkeys, 2) (threefry2x32) or (nkeys, 4) (rbg, unsafe_rbg)
     uint32 tensor on the current device."""
-    return k.data.to(_device()).reshape(-1, _KEY_WORDS[k.impl]).contiguous()
+    d = k.data
+    if d.is_cuda and d.is_contiguous() and d.get_device() == torch.cuda.current_device():
+        return d.view(-1, _KEY_WORDS[k.impl])
+    return d.to(_device()).reshape(-1, _KEY_WORDS[k.impl]).contiguous()
 
 
 def _is_rbg(kd):
@@ -578,12 +595,14 @@ def _check_size(size, layout):
         raise JaxNotImplementedError("random bits array of size exceeding 2 ** 64")
 
 
-def _k_bits(kd, size, bit_width, layout):
-    """(nkeys, size) random bits.  rbg / unsafe_rbg keys draw from XLA's RngBitGenerator;
-    batched keys of those all draw from the first key, (nkeys, size) of its stream (the
-    primitive's batching rule, R/prng.R:309-320)."""
+def _k_bits(kd, size, bit_width, layout, shape=None):
+    """(nkeys, size) random bits (allocated as `shape`, of as many elements, when given).
+    rbg / unsafe_rbg keys draw from XLA's RngBitGenerator; batched keys of those all draw
+    from the first key, (nkeys, size) of its stream (the primitive's batching rule,
+    R/prng.R:309-320)."""
     _check_size(size, layout)
-    out = torch.empty((kd.shape[0], size), dtype=_TORCH[f"uint{bit_width}"], device=kd.device)
+    out = torch.empty(shape if shape is not None else (kd.shape[0], size),
+                      dtype=_TORCH[f"uint{bit_width}"], device=kd.device)
     if _is_rbg(kd):
         total = kd.shape[0] * size
         nat.call("jxr_rbg_bits", _ptr(kd[0]), total, 0, total, bit_width, _ptr(out), None,
@@ -606,9 +625,10 @@ def _as_float_view(t, dt):
     return t.view(_TORCH[dt]) if dt in ("float16", "bfloat16") else t
 
 
-def _k_uniform(kd, size, dt, mn, mx, layout, flags=0):
+def _k_uniform(kd, size, dt, mn, mx, layout, flags=0, shape=None):
     _check_size(size, layout)
-    out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    out = torch.empty(shape if shape is not None else (kd.shape[0], size),
+                      dtype=_float_storage(dt), device=kd.device)
     if _is_rbg(kd):
         bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
         nat.call("jxr_uniform_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt], float(mn),
@@ -619,9 +639,10 @@ def _k_uniform(kd, size, dt, mn, mx, layout, flags=0):
     return _as_float_view(out, dt)
 
 
-def _k_normal(kd, size, dt, layout):
+def _k_normal(kd, size, dt, layout, shape=None):
     _check_size(size, layout)
-    out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    out = torch.empty(shape if shape is not None else (kd.shape[0], size),
+                      dtype=_float_storage(dt), device=kd.device)
     if _is_rbg(kd):
         bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
         nat.call("jxr_normal_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt], _ptr(out),
@@ -753,8 +774,8 @@ def random_bits(key, shape=(), dtype=None):
     if not _is_unsigned(dt):
         raise JaxValueError(f"dtype argument to `bits` must be an unsigned int dtype, got {dt}")
     shape = canon_shape(shape)
-    out = _k_bits(_flat_keys(k), _size(shape), _BITS[dt], _layout())
-    return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
+    out = _k_bits(_flat_keys(k), _size(shape), _BITS[dt], _layout(), k.shape[:nb] + shape)
+    return _rebatch(out, nb)
 
 
 # ---- uniform / normal / bernoulli (R/random.R:278-304, :466-508, :643-666) -------------------
@@ -826,7 +847,8 @@ def random_uniform(key, shape=(), dtype=None, minval=0.0, maxval=1.0):
     mn_s, mn_t = _param(minval, dt)
     mx_s, mx_t = _param(maxval, dt)
     if mn_t is None and mx_t is None:
-        out = _k_uniform(kd, size, dt, mn_s, mx_s, _layout())
+        return _rebatch(_k_uniform(kd, size, dt, mn_s, mx_s, _layout(), shape=k.shape[:nb] + shape),
+                        nb)
     else:
         unit = _k_uniform(kd, size, dt, 0.0, 1.0, _layout())
         mn = _broadcast_param(mn_t if mn_t is not None else torch.tensor(mn_s), shape, dt, "uniform")
@@ -851,8 +873,7 @@ def random_normal(key, shape=(), dtype=None):
     bshape = k.shape[:nb]
     if dt.startswith("complex"):
         return _rebatch(_complex_normal(k, bshape, shape, dt), nb)
-    out = _k_normal(_flat_keys(k), size, dt, _layout())
-    return _rebatch(out.reshape(bshape + shape), nb)
+    return _rebatch(_k_normal(_flat_keys(k), size, dt, _layout(), bshape + shape), nb)
 
 
 def _complex_normal(k, bshape, shape, dt):
