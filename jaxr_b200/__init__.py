@@ -9,7 +9,7 @@ from . import config
 from .config import enable_x64, jax_config, jax_config_update, with_jax_config
 from .errors import (JaxError, JaxNotImplementedError, JaxOverflowError, JaxTypeError,
                      JaxValueError)
-from .random import (PRNGKeyArray, canonicalize_dtype, dtype, lax_erf_inv, lax_RandomAlgorithm,
+from .random import (PRNGKeyArray, canonicalize_dtype, dtype, free_caches, lax_erf_inv, lax_RandomAlgorithm,
                      lax_rng_bit_generator, random_bernoulli,
                      random_bits, random_choice, random_clone, random_exponential,
                      random_fold_in, random_gumbel, random_Key, random_key, random_key_data,
@@ -21,7 +21,7 @@ from .random import (PRNGKeyArray, canonicalize_dtype, dtype, lax_erf_inv, lax_R
 __all__ = [
     "config", "enable_x64", "jax_config", "jax_config_update", "with_jax_config", "JaxError",
     "JaxNotImplementedError", "JaxOverflowError", "JaxTypeError", "JaxValueError",
-    "PRNGKeyArray", "canonicalize_dtype", "dtype", "lax_erf_inv", "lax_RandomAlgorithm",
+    "PRNGKeyArray", "canonicalize_dtype", "dtype", "free_caches", "lax_erf_inv", "lax_RandomAlgorithm",
     "lax_rng_bit_generator", "random_bernoulli",
     "random_bits", "random_choice", "random_clone", "random_exponential", "random_fold_in",
     "random_gumbel", "random_Key", "random_key", "random_key_data", "random_key_dtype",

@@ -74,6 +74,7 @@ SIGNATURES = {
     "jxr_cumsum": [_vp, _i64, _int, _vp, _vp],
     "jxr_erf_inv": [_vp, _i64, _int, _vp, _vp],
     "jxr_set_accurate_erf_inv": [_int],
+    "jxr_free_caches": [],
     "jxr_get_accurate_erf_inv": [],
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],

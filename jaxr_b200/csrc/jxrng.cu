@@ -110,24 +110,45 @@ struct HostCopyCtx {
   uint32_t* dkeys = nullptr;
   size_t key_cap = 0;
 
+  // Creates what is missing (a failed call leaves what it made for the next one to reuse).
   int ensure(size_t nkeys) {
     if (!ready) {
-      JXR_CUDA(cudaStreamCreateWithFlags(&gen, cudaStreamNonBlocking));
-      JXR_CUDA(cudaStreamCreateWithFlags(&cpy, cudaStreamNonBlocking));
+      if (!gen) JXR_CUDA(cudaStreamCreateWithFlags(&gen, cudaStreamNonBlocking));
+      if (!cpy) JXR_CUDA(cudaStreamCreateWithFlags(&cpy, cudaStreamNonBlocking));
       for (int b = 0; b < 2; ++b) {
-        JXR_CUDA(cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming));
-        JXR_CUDA(cudaEventCreateWithFlags(&freed[b], cudaEventDisableTiming));
-        JXR_CUDA(cudaMalloc(&stage[b], kStageBytes));
+        if (!done[b]) JXR_CUDA(cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming));
+        if (!freed[b]) JXR_CUDA(cudaEventCreateWithFlags(&freed[b], cudaEventDisableTiming));
+        if (!stage[b]) JXR_CUDA(cudaMalloc(&stage[b], kStageBytes));
       }
       ready = true;
     }
     if (key_cap < nkeys) {
+      if (nkeys > (SIZE_MAX >> 3)) return fail(JXR_ERR_INVALID_ARGUMENT, "too many keys");
       if (dkeys) JXR_CUDA(cudaFree(dkeys));
       dkeys = nullptr;
+      key_cap = 0;
       JXR_CUDA(cudaMalloc(&dkeys, 8 * nkeys));
       key_cap = nkeys;
     }
     return JXR_OK;
+  }
+
+  // Releases everything (the caller holds mu and the current device is this context's).
+  void release() {
+    for (int b = 0; b < 2; ++b) {
+      if (stage[b]) cudaFree(stage[b]);
+      if (done[b]) cudaEventDestroy(done[b]);
+      if (freed[b]) cudaEventDestroy(freed[b]);
+      stage[b] = nullptr;
+      done[b] = freed[b] = nullptr;
+    }
+    if (dkeys) cudaFree(dkeys);
+    if (gen) cudaStreamDestroy(gen);
+    if (cpy) cudaStreamDestroy(cpy);
+    dkeys = nullptr;
+    gen = cpy = nullptr;
+    key_cap = 0;
+    ready = false;
   }
 };
 
@@ -2106,6 +2127,26 @@ int jxr_erf_inv(const void* x, int64_t n, int dtype, void* out, void* stream) {
     JXR_CUDA(cudaGetLastError());
     return JXR_OK;
   });
+}
+
+int jxr_free_caches(void) {
+  int dev = 0;
+  JXR_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(JXR_ERR_NO_DEVICE, "device index %d out of range", dev);
+  // tables may still be read by kernels in flight on any stream of this device
+  JXR_CUDA(cudaDeviceSynchronize());
+  {
+    std::lock_guard<std::mutex> lock(g_tab_mu);
+    for (int id = 0; id < kTables; ++id) {
+      if (g_tables[dev][id]) cudaFree(g_tables[dev][id]);
+      g_tables[dev][id] = nullptr;
+    }
+  }
+  HostCopyCtx& cx = g_host_ctx[dev];
+  std::lock_guard<std::mutex> lock(cx.mu);
+  cx.release();
+  JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
 }
 
 int jxr_set_accurate_erf_inv(int enable) {

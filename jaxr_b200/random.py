@@ -780,6 +780,12 @@ def random_bits(key, shape=(), dtype=None):
 
 # ---- uniform / normal / bernoulli (R/random.R:278-304, :466-508, :643-666) -------------------
 
+def free_caches():
+    """Frees the current device's library caches (the float32 samplers' 32 MiB tables and
+    the host-copy staging buffers); later calls rebuild what they need."""
+    nat.call("jxr_free_caches")
+
+
 def _uses_erf_inv(fn):
     """Runs `fn` with the library's erf_inv (a per-thread setting) set to the one that
     jax_accurate_erf_inv names (R/lax_special.R:1324-1331): chlo.erf_inv by default, JAX's

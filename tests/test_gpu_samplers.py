@@ -310,3 +310,20 @@ def test_complex_normal_key_batches():
     for r in range(4):
         want = orc.complex_normal(keys[r], "complex64", 6).reshape(2, 3)
         assert np.array_equal(out[r].view(np.float32), want.view(np.float32))
+
+
+def test_free_caches_then_rebuild():
+    """jxr_free_caches releases the sampler tables and the host-copy buffers; the next
+    calls rebuild them and give the same results."""
+    from jaxr_b200.shard import random_bits_to_host
+    key = orc.seed(5)
+    n = 1 << 22
+    a = to_np(jr.random_normal(dev_key(key), (n,)))
+    h1 = random_bits_to_host(jr.random_key(3), (1 << 20,)).numpy().copy()
+    jr.free_caches()
+    jr.free_caches()  # idempotent
+    b = to_np(jr.random_normal(dev_key(key), (n,)))
+    h2 = random_bits_to_host(jr.random_key(3), (1 << 20,)).numpy()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert np.array_equal(h1, h2)
+    assert np.array_equal(a[:4096], orc.normal(key, "float32", n, True, count=4096))
