@@ -1864,6 +1864,11 @@ int jxr_take(const void* src, int64_t outer, int64_t n_src, const uint32_t* idx,
              int64_t row_bytes, void* out, int* err, void* stream) {
   if (outer < 0 || n_src < 0 || n_idx < 0 || row_bytes < 0)
     return fail(JXR_ERR_INVALID_ARGUMENT, "sizes must be >= 0");
+  if ((n_idx && outer > INT64_MAX / n_idx) ||
+      (n_idx && outer && row_bytes > INT64_MAX / (outer * n_idx)) ||
+      (n_src && outer > INT64_MAX / n_src) ||
+      (n_src && outer && row_bytes > INT64_MAX / (outer * n_src)))
+    return fail(JXR_ERR_INVALID_ARGUMENT, "outer * n * row_bytes overflows");
   const int64_t total_bytes = outer * n_idx * row_bytes;
   if (!total_bytes) return JXR_OK;
   if (!src || !idx || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");

@@ -267,20 +267,7 @@ __global__ void k_take_rows(const W* __restrict__ src, int64_t outer, int64_t n_
     const int64_t i = oi % n_idx, o = oi / n_idx;
     const uint32_t s = idx[i];
     if ((int64_t)s < n_src) out[t] = src[(o * n_src + s) * row + u];
-    else atomicExch(err, 4);
-  }
-}
-
-// out[f] = src[idx[f]] for elements of W bytes
-template <class W>
-__global__ void k_take_flat(const W* __restrict__ src, int64_t total,
-                            const uint32_t* __restrict__ idx, W* __restrict__ out,
-                            int* __restrict__ err) {
-  for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < total;
-       f += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t s = idx[f];
-    if ((int64_t)s < total) out[f] = src[s];
-    else atomicExch(err, 4);
+    else if (err) atomicExch(err, 4);
   }
 }
 
