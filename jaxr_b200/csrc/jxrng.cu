@@ -2050,8 +2050,9 @@ int jxr_random_bits_multi(const int* devices, int ndev, const uint32_t* const* k
   JXR_CUDA(cudaGetDevice(&prev));
   int rc = JXR_OK;
   for (int i = 0; i < ndev && rc == JXR_OK; ++i) {
-    const uint64_t lo = size * (uint64_t)i / (uint64_t)ndev;
-    const uint64_t hi = size * (uint64_t)(i + 1) / (uint64_t)ndev;
+    // slab bounds in 128 bits: size * i overflows 64 bits for requests above 2^61
+    const uint64_t lo = (uint64_t)((unsigned __int128)size * (unsigned)i / (unsigned)ndev);
+    const uint64_t hi = (uint64_t)((unsigned __int128)size * (unsigned)(i + 1) / (unsigned)ndev);
     if (cudaSetDevice(devices[i]) != cudaSuccess) {
       rc = fail(JXR_ERR_CUDA, "cannot select device %d", devices[i]);
       break;
