@@ -90,6 +90,24 @@ struct GroupsOf<Op, std::void_t<decltype(Op::kGroups)>> {
 
 __host__ __device__ __forceinline__ uint64_t umin(uint64_t a, uint64_t b) { return a < b ? a : b; }
 
+// Ops with kDirect > 0 (OpTableHybridF32) evaluate the last kDirect of a thread's outputs
+// per tile with op.direct and gather the rest from their table; others evaluate every
+// output alike.
+template <class Op, class = void>
+struct DirectOutputsOf {
+  static constexpr int value = 0;
+};
+template <class Op>
+struct DirectOutputsOf<Op, std::void_t<decltype(Op::kDirect)>> {
+  static constexpr int value = Op::kDirect;
+};
+
+template <class Op>
+__device__ __forceinline__ typename Op::Out apply_direct(const Op& op, uint32_t x0, uint32_t x1) {
+  if constexpr (DirectOutputsOf<Op>::value > 0) return op.direct(Draw<Op::kBits>::get(x0, x1));
+  else return apply(op, x0, x1);
+}
+
 // ---- single key ---------------------------------------------------------------------------
 
 template <class Op, int kCtr, class Mix = ProductMix, int G = GroupsOf<Op>::value>
@@ -141,7 +159,19 @@ __global__ void __launch_bounds__(kThreads)
     }
     threefry20<N, Mix>(s, x0, x1, pc);
     Out* dst = out + p0 + toff;
-    if (vec_ok && p0 + TILE <= count) {
+    constexpr int D = DirectOutputsOf<Op>::value;
+    static_assert(D <= N, "direct outputs per thread");
+    if (D > 0 && vec_ok && p0 + TILE <= count) {
+      // the table gathers of outputs 0 .. N - D are issued first, the last D outputs are
+      // computed while they are in flight, then all groups are stored
+      Vec16<Out> r[G];
+#pragma unroll
+      for (int k = 0; k < N - D; ++k) r[k / V].v[k % V] = apply(op, x0[k], x1[k]);
+#pragma unroll
+      for (int k = N - D; k < N; ++k) r[k / V].v[k % V] = apply_direct(op, x0[k], x1[k]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) *reinterpret_cast<uint4*>(dst + g * kThreads * V) = r[g].u;
+    } else if (vec_ok && p0 + TILE <= count) {
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         Vec16<Out> r;

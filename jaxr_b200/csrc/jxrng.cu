@@ -471,6 +471,37 @@ const float* f32_table(int id, const Op& op, cudaStream_t st) {
   return t;
 }
 
+// Outputs per thread (of 16) that a table-backed sampler evaluates directly: where the
+// integer pipe's time for the cipher plus those evaluations meets the L1TEX time of the
+// remaining gathers.  Measured on B200 (2^26 outputs, one key): 4 for the samplers with one
+// logarithm or an erf_inv (normal 0.283 -> 0.243 ms, exponential 0.283 -> 0.233 ms), 3 for
+// gumbel and logistic, which take two logarithms (0.283 -> 0.248 / 0.251 ms).
+template <class Op>
+struct DirectShare {
+  static constexpr int value = 4;
+};
+template <>
+struct DirectShare<OpLogSampler<kGumbel, 0>> {
+  static constexpr int value = 3;
+};
+template <>
+struct DirectShare<OpLogSampler<kLogistic, 0>> {
+  static constexpr int value = 3;
+};
+
+// A float32 sampler through its table: one key in the partitionable layout evaluates part
+// of the outputs directly and gathers the rest (OpTableHybridF32); other requests gather
+// every output.
+template <class Op>
+int launch_table(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
+                 uint64_t count, int layout, const float* table, const Op& op, void* out,
+                 cudaStream_t st) {
+  using H = OpTableHybridF32<Op, DirectShare<Op>::value>;
+  if (nkeys == 1 && layout == JXR_LAYOUT_PARTITIONABLE)
+    return launch_blocks<H, kCtrIndex>(keys, 1, size, begin, count, H{table, op}, out, st);
+  return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{table}, out, st);
+}
+
 int check_request(const void* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
                   int layout, const void* out) {
   if (nkeys < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "nkeys must be >= 0, got %lld", (long long)nkeys);
@@ -1245,7 +1276,8 @@ int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
       case JXR_F32: {
         if (count * (uint64_t)nkeys >= kTableMin)
           if (const float* t = f32_table(A ? kTableNormalAccurate : 0, OpNormalF32T<A>{}, st))
-            return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{t}, out, st);
+            return launch_table(keys, nkeys, size, begin, count, layout, t, OpNormalF32T<A>{},
+                                out, st);
         return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32T<A>{}, out, st);
       }
       case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF64T<A>{}, out, st);
@@ -1464,7 +1496,7 @@ int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
     if constexpr (std::is_same_v<typename O::Out, float>) {
       if (big)
         if (const float* t = f32_table(1 + kind, op, st))
-          return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{t}, out, st);
+          return launch_table(keys, nkeys, size, begin, count, layout, t, op, out, st);
     }
     return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
   });

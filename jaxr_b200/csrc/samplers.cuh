@@ -393,6 +393,24 @@ struct OpTableF32 {
   __device__ __forceinline__ Out operator()(Bits b) const { return __ldg(table + (b >> 9)); }
 };
 
+// The table gathers are bound by L1TEX throughput while the integer pipe has room, and
+// evaluating an op directly is bound by the integer pipe: the single-key kernel evaluates
+// kDirect of a thread's 16 outputs directly (op.direct, the op the table was built from,
+// so the values are identical) and gathers the others.  Other kernels use the
+// table for every element.
+template <class Op, int kDirectOutputs = 4>
+struct OpTableHybridF32 {
+  static constexpr int kBits = 32;
+  static constexpr int kGroups = 4;                    // 16 outputs per thread and tile
+  static constexpr int kDirect = kDirectOutputs;       // of which evaluated directly
+  using Bits = uint32_t;
+  using Out = float;
+  const float* __restrict__ table;
+  Op op;
+  __device__ __forceinline__ Out operator()(Bits b) const { return __ldg(table + (b >> 9)); }
+  __device__ __forceinline__ Out direct(Bits b) const { return op(b); }
+};
+
 template <bool kAcc = false>
 struct OpNormalF64T {
   static constexpr int kBits = 64;
