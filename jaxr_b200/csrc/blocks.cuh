@@ -250,7 +250,19 @@ __global__ void __launch_bounds__(kThreads)
     }
     threefry20<N, Mix>(s, x0, x1, pc);
     Out* orow = out + row * count;
-    if (vec_ok && p0 + WT <= count) {
+    constexpr int D = DirectOutputsOf<Op>::value;
+    static_assert(D <= N, "direct outputs per thread");
+    if (D > 0 && vec_ok && p0 + WT <= count) {
+      // as in k_blocks_1key: gathers first, the last D outputs computed meanwhile
+      Vec16<Out> r[G];
+#pragma unroll
+      for (int k = 0; k < N - D; ++k) r[k / V].v[k % V] = apply(op, x0[k], x1[k]);
+#pragma unroll
+      for (int k = N - D; k < N; ++k) r[k / V].v[k % V] = apply_direct(op, x0[k], x1[k]);
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        *reinterpret_cast<uint4*>(orow + p0 + loff + g * 32 * V) = r[g].u;
+    } else if (vec_ok && p0 + WT <= count) {
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         Vec16<Out> r;

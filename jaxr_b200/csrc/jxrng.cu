@@ -247,35 +247,69 @@ __global__ void __launch_bounds__(kThreads)
     }
     threefry20<B, ProductMix>(s, x0, x1, pc);
     Out* orow = out + row * count;
+    // table-backed samplers (32-bit words, one output each): both slabs' values first,
+    // the table gathers before the directly evaluated share (the op's kDirect per 16
+    // outputs, rounded down), then the stores
+    constexpr int kDirectWords = DirectOutputsOf<Op>::value * 2 * B / 16;
+    if constexpr (kDirectWords > 0 && W == 32) {
+      Vec16<Out> r[2][(B + Vec16<Out>::N - 1) / Vec16<Out>::N];
 #pragma unroll
-    for (int slab = 0; slab < 2; ++slab) {
-      const uint64_t w0 = slab == 0 ? j0 : half + j0;  // first word of this slab chunk
-      // words of this slab that exist: slab 0 needs j < half, slab 1 half + j < nwords
-      const uint64_t wlim = slab == 0 ? umin(half, jhi) : umin(nwords, half + jhi);
-      const uint64_t e0 = w0 * per;  // first element
-      Vec16<Out> r[(B * per + Vec16<Out>::N - 1) / Vec16<Out>::N];
-      Out* rv = &r[0].v[0];
+      for (int k = 0; k < 2 * B; ++k) {
+        const uint32_t word = k < B ? x0[k] : x1[k - B];
+        Out* rv = &r[k / B][0].v[0];
+        if (k < 2 * B - kDirectWords) rv[k % B] = op(word);
+        else rv[k % B] = op.direct(word);
+      }
 #pragma unroll
-      for (int b = 0; b < B; ++b) {
-        const uint32_t word = slab == 0 ? x0[b] : x1[b];
+      for (int slab = 0; slab < 2; ++slab) {
+        const uint64_t w0 = slab == 0 ? j0 : half + j0;
+        const uint64_t wlim = slab == 0 ? umin(half, jhi) : umin(nwords, half + jhi);
+        const bool all_in = w0 + B <= wlim && w0 >= begin && w0 + B <= end;
+        Out* dst = orow + (w0 - begin);
+        const Out* rv = &r[slab][0].v[0];
+        if (all_in && ((uintptr_t)dst % 16) == 0) {
 #pragma unroll
-        for (int q = 0; q < per; ++q) {
-          if constexpr (W == 32) rv[b * per + q] = op(word);
-          else rv[b * per + q] = op((typename Op::Bits)(word >> (W * q)));
+          for (int k = 0; k < (B * (int)sizeof(Out)) / 16; ++k)
+            reinterpret_cast<uint4*>(dst)[k] = r[slab][k].u;
+        } else {
+#pragma unroll
+          for (int k = 0; k < B; ++k) {
+            const uint64_t e = w0 + k;
+            if (e < wlim && e >= begin && e < end) orow[e - begin] = rv[k];
+          }
         }
       }
-      constexpr int NE = B * per;
-      const bool all_in = w0 + B <= wlim && e0 >= begin && e0 + NE <= end;
-      Out* dst = orow + (e0 - begin);
-      if (all_in && ((uintptr_t)dst % 16) == 0) {
+    } else {
 #pragma unroll
-        for (int k = 0; k < (NE * (int)sizeof(Out)) / 16; ++k)
-          reinterpret_cast<uint4*>(dst)[k] = r[k].u;
-      } else {
+      for (int slab = 0; slab < 2; ++slab) {
+        const uint64_t w0 = slab == 0 ? j0 : half + j0;  // first word of this slab chunk
+        // words of this slab that exist: slab 0 needs j < half, slab 1 half + j < nwords
+        const uint64_t wlim = slab == 0 ? umin(half, jhi) : umin(nwords, half + jhi);
+        const uint64_t e0 = w0 * per;  // first element
+        Vec16<Out> r[(B * per + Vec16<Out>::N - 1) / Vec16<Out>::N];
+        Out* rv = &r[0].v[0];
 #pragma unroll
-        for (int k = 0; k < NE; ++k) {
-          const uint64_t e = e0 + k;
-          if (w0 + k / per < wlim && e >= begin && e < end) orow[e - begin] = rv[k];
+        for (int b = 0; b < B; ++b) {
+          const uint32_t word = slab == 0 ? x0[b] : x1[b];
+#pragma unroll
+          for (int q = 0; q < per; ++q) {
+            if constexpr (W == 32) rv[b * per + q] = op(word);
+            else rv[b * per + q] = op((typename Op::Bits)(word >> (W * q)));
+          }
+        }
+        constexpr int NE = B * per;
+        const bool all_in = w0 + B <= wlim && e0 >= begin && e0 + NE <= end;
+        Out* dst = orow + (e0 - begin);
+        if (all_in && ((uintptr_t)dst % 16) == 0) {
+#pragma unroll
+          for (int k = 0; k < (NE * (int)sizeof(Out)) / 16; ++k)
+            reinterpret_cast<uint4*>(dst)[k] = r[k].u;
+        } else {
+#pragma unroll
+          for (int k = 0; k < NE; ++k) {
+            const uint64_t e = e0 + k;
+            if (w0 + k / per < wlim && e >= begin && e < end) orow[e - begin] = rv[k];
+          }
         }
       }
     }
@@ -489,17 +523,15 @@ struct DirectShare<OpLogSampler<kLogistic, 0>> {
   static constexpr int value = 3;
 };
 
-// A float32 sampler through its table: one key in the partitionable layout evaluates part
-// of the outputs directly and gathers the rest (OpTableHybridF32); other requests gather
-// every output.
+// A float32 sampler through its table: part of every thread's outputs are evaluated
+// directly while the rest are gathered (OpTableHybridF32), in the bulk kernels of both
+// layouts and of key batches.
 template <class Op>
 int launch_table(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
                  uint64_t count, int layout, const float* table, const Op& op, void* out,
                  cudaStream_t st) {
   using H = OpTableHybridF32<Op, DirectShare<Op>::value>;
-  if (nkeys == 1 && layout == JXR_LAYOUT_PARTITIONABLE)
-    return launch_blocks<H, kCtrIndex>(keys, 1, size, begin, count, H{table, op}, out, st);
-  return launch_op(keys, nkeys, size, begin, count, layout, OpTableF32{table}, out, st);
+  return launch_op(keys, nkeys, size, begin, count, layout, H{table, op}, out, st);
 }
 
 int check_request(const void* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,

@@ -327,3 +327,29 @@ def test_free_caches_then_rebuild():
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
     assert np.array_equal(h1, h2)
     assert np.array_equal(a[:4096], orc.normal(key, "float32", n, True, count=4096))
+
+
+@pytest.mark.parametrize("kind", ["normal"] + KINDS)
+def test_table_samplers_every_output(kind):
+    """Requests of 2^22 or more float32 samples read the sampler's table for most outputs
+    and evaluate a share of each thread's outputs directly (fixed positions in every
+    tile): every output compared with the oracle, for one key in both layouts (a ragged
+    tail past the last full tile) and for a batch of four keys."""
+    fn = jr.random_normal if kind == "normal" else FN[kind]
+
+    def want(k, n, part):
+        if kind == "normal":
+            return orc.normal(k, "float32", n, part)
+        return orc.sample(k, kind, "float32", n, part)
+
+    key = orc.seed(123)
+    n = (1 << 22) + 777
+    for part in (True, False):
+        with flags(False, part):
+            got = to_np(fn(dev_key(key), (n,)))
+        assert same_bits(got, want(key, n, part), "float32"), (kind, part)
+    keys = np.stack([orc.seed(s) for s in range(4)])
+    m = (1 << 20) + 3
+    got = to_np(jr.vmap(lambda k: fn(k, (m,)))(dev_key(keys)))
+    for r in range(4):
+        assert same_bits(got[r], want(keys[r], m, True), "float32"), (kind, r)
