@@ -19,7 +19,6 @@ import ctypes
 import torch
 
 from . import _native as nat
-from . import config as cfg
 from .random import (_TORCH, _BITS, _KEY_WORDS, _check_key, _flat_keys, _layout, _ptr, _size,
                      _stream, canon_shape, canonicalize_dtype, default_uint)
 from .errors import JaxValueError
