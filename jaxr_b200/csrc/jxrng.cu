@@ -967,18 +967,24 @@ __global__ void k_rbg_advance(const uint32_t* __restrict__ key, uint64_t nblocks
 // randint with scalar bounds in one pass (partitionable layout): element c of key row r
 // draws hi and lo from the two halves (kh, kl) of split(key) at counter c and writes the
 // low out_bits of a + offset (randint_offset with the span's multiplier precomputed).
-// Each thread takes 4 consecutive elements of one row.
+// Each thread takes kRandintV consecutive elements of one row; rows and columns advance
+// by a fixed stride (one division per thread, not one per unit).
+constexpr int kRandintV = 8;
 template <class U, class OutT>
 __global__ void __launch_bounds__(256)
 k_randint_fused(const uint32_t* __restrict__ kh, const uint32_t* __restrict__ kl, int64_t nkeys,
                 uint64_t begin, uint64_t count, U a, U span, U mult, PipeConsts pc,
                 OutT* __restrict__ out) {
-  constexpr int V = 4;
+  constexpr int V = kRandintV;
   const uint64_t per_row = (count + V - 1) / V;
   const uint64_t units = per_row * (uint64_t)nkeys;
-  for (uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units;
-       u += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t r = u / per_row, j0 = (u % per_row) * V;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  uint64_t u = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (u >= units) return;
+  uint64_t r = u / per_row, col = u - r * per_row;
+  const uint64_t dr = stride / per_row, dc = stride - dr * per_row;
+  for (; u < units; u += stride) {
+    const uint64_t j0 = col * V;
     const KeySchedule sh = make_schedule(kh[2 * r], kh[2 * r + 1]);
     const KeySchedule sl = make_schedule(kl[2 * r], kl[2 * r + 1]);
     uint32_t h0[V], h1[V], l0[V], l1[V];
@@ -991,9 +997,12 @@ k_randint_fused(const uint32_t* __restrict__ kh, const uint32_t* __restrict__ kl
     threefry20<V, ProductMix>(sh, h0, h1, pc);
     threefry20<V, ProductMix>(sl, l0, l1, pc);
     OutT* dst = out + r * count + j0;
+    union {
+      OutT v[V];
+      uint4 q[(V * sizeof(OutT) + 15) / 16];
+    } res;
 #pragma unroll
     for (int t = 0; t < V; ++t) {
-      if (j0 + t >= count) break;
       U hi, lo;
       if constexpr (sizeof(U) == 4) {
         hi = h0[t] ^ h1[t];
@@ -1003,7 +1012,23 @@ k_randint_fused(const uint32_t* __restrict__ kh, const uint32_t* __restrict__ kl
         lo = (uint64_t)l0[t] << 32 | l1[t];
       }
       const U off = span == 0 ? lo : (U)((U)((hi % span) * mult) + lo % span) % span;
-      dst[t] = (OutT)(U)(a + off);
+      res.v[t] = (OutT)(U)(a + off);
+    }
+    constexpr bool kVec = (V * sizeof(OutT)) % 16 == 0;
+    if (kVec && j0 + V <= count && ((uintptr_t)dst % 16) == 0) {
+#pragma unroll
+      for (int k = 0; k < (int)(V * sizeof(OutT)) / 16; ++k)
+        reinterpret_cast<uint4*>(dst)[k] = res.q[k];
+    } else {
+#pragma unroll
+      for (int t = 0; t < V; ++t)
+        if (j0 + t < count) dst[t] = res.v[t];
+    }
+    col += dc;
+    r += dr;
+    if (col >= per_row) {
+      col -= per_row;
+      ++r;
     }
   }
 }
@@ -1581,7 +1606,7 @@ int jxr_randint(const uint32_t* keys_hi, const uint32_t* keys_lo, int64_t nkeys,
       mult = (m * m) % span;
     }
   }
-  const uint64_t units = (count + 3) / 4 * (uint64_t)nkeys;
+  const uint64_t units = (count + kRandintV - 1) / kRandintV * (uint64_t)nkeys;
   int grid;
   if ((rc = resident_grid(k_randint_fused<uint32_t, uint32_t>, (units + 255) / 256, &grid)))
     return rc;
