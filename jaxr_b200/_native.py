@@ -32,6 +32,7 @@ _u64 = ctypes.c_uint64
 _int = ctypes.c_int
 _dbl = ctypes.c_double
 _u32 = ctypes.c_uint32
+_sz = ctypes.c_size_t
 
 # name -> argument types; every entry point returns int status
 SIGNATURES = {
@@ -68,6 +69,8 @@ SIGNATURES = {
     "jxr_rbg_blocks": [_vp, _u64, _u64, _i64, _vp, _vp],
     "jxr_rbg_unsafe_fold_in": [_vp, _i64, _vp, _i64, _int, _vp, _vp],
     "jxr_sample_from_bits": [_vp, _i64, _int, _int, _vp, _vp],
+    "jxr_truncated_normal_scratch": [_vp, _i64, _u64, _u64, _u64, _int, _int, _dbl, _dbl, _vp,
+                                     _sz, _vp, _vp],
     "jxr_truncated_normal_from_bits": [_vp, _i64, _int, _dbl, _dbl, _vp, _vp],
     "jxr_random_bits_multi": [_vp, _int, _vp, _u64, _int, _int, _vp, _int, _vp, _vp],
     "jxr_complex_from_parts": [_vp, _vp, _i64, _int, _dbl, _vp, _vp],

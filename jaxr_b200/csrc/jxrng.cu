@@ -469,6 +469,9 @@ __global__ void k_build_table(Op op, float* __restrict__ table) {
 // Requests of at least this many float32 samples use (and, the first time, build) the
 // sampler's table.
 constexpr uint64_t kTableMin = 1ull << 22;
+// A truncated normal builds its table in the call (it depends on the bounds): worth it from
+// 2^25 samples, where the 2^23 evaluations of the build are under a quarter of the request.
+constexpr uint64_t kTruncTableMin = 1ull << 25;
 constexpr int kTables = 8;  // 0: normal, 1 + kind: the log-transform samplers, 5: normal
                             // with the accurate erf_inv
 constexpr int kTableNormalAccurate = 5;
@@ -1763,6 +1766,32 @@ int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uin
   cudaStream_t st = (cudaStream_t)stream;
   return visit_trunc_op(dtype, lower, upper, [&](const auto& op) {
     return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
+  });
+}
+
+int jxr_truncated_normal_scratch(const uint32_t* keys, int64_t nkeys, uint64_t size,
+                                 uint64_t begin, uint64_t count, int layout, int dtype,
+                                 double lower, double upper, void* scratch, size_t scratch_bytes,
+                                 void* out, void* stream) {
+  int rc = check_dtype(dtype);
+  if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
+  const bool table = dtype == JXR_F32 && count * (uint64_t)nkeys >= kTruncTableMin && scratch &&
+                     scratch_bytes >= (sizeof(float) << 23) && (uintptr_t)scratch % 16 == 0;
+  if (!table)
+    return jxr_truncated_normal(keys, nkeys, size, begin, count, layout, dtype, lower, upper,
+                                out, stream);
+  cudaStream_t st = (cudaStream_t)stream;
+  return visit_trunc_op(dtype, lower, upper, [&](const auto& op) -> int {
+    using O = std::decay_t<decltype(op)>;
+    if constexpr (std::is_same_v<typename O::Out, float>) {
+      // this call's table: the op at all 2^23 values of bits >> 9
+      k_build_table<O><<<1024, 256, 0, st>>>(op, (float*)scratch);
+      JXR_CUDA(cudaGetLastError());
+      return launch_table(keys, nkeys, size, begin, count, layout, (const float*)scratch, op,
+                          out, st);
+    } else {
+      return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
+    }
   });
 }
 

@@ -1074,8 +1074,13 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
             nat.call("jxr_truncated_normal_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt],
                      float(lo_s), float(hi_s), _ptr(out), _stream())
         else:
-            nat.call("jxr_truncated_normal", _ptr(kd), kd.shape[0], size, 0, size, layout,
-                     _FLOAT_CODE[dt], float(lo_s), float(hi_s), _ptr(out), _stream())
+            # large float32 requests build the sampler's table for these bounds in the call
+            # (2^23 floats of scratch from torch's allocator)
+            big = dt == "float32" and kd.shape[0] * size >= _TRUNC_TABLE_MIN
+            scratch = torch.empty(1 << 23 if big else 0, dtype=torch.float32, device=kd.device)
+            nat.call("jxr_truncated_normal_scratch", _ptr(kd), kd.shape[0], size, 0, size, layout,
+                     _FLOAT_CODE[dt], float(lo_s), float(hi_s),
+                     _ptr(scratch) if big else None, scratch.numel() * 4, _ptr(out), _stream())
         return _rebatch(_as_float_view(out, dt).reshape(bshape + shape), nb)
     lo = _broadcast_param(lo_t if lo_t is not None else torch.tensor(lo_s), shape, dt,
                           "truncated_normal")
@@ -1088,6 +1093,11 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
                  _ptr(_raw16(lo, dt)), 1, _ptr(_raw16(hi, dt)), 1, size, _FLOAT_CODE[dt],
                  _ptr(_raw16(out[r], dt)), _stream())
     return _rebatch(out.reshape(bshape + shape), nb)
+
+
+# float32 truncated normals of at least this many samples read a table built in the call
+# (jxr_truncated_normal_scratch's own threshold)
+_TRUNC_TABLE_MIN = 1 << 25
 
 
 # ---- randint (R/random.R:306-359) -------------------------------------------------------------

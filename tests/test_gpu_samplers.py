@@ -353,3 +353,26 @@ def test_table_samplers_every_output(kind):
     got = to_np(jr.vmap(lambda k: fn(k, (m,)))(dev_key(keys)))
     for r in range(4):
         assert same_bits(got[r], want(keys[r], m, True), "float32"), (kind, r)
+
+
+def test_truncated_normal_table_in_the_call():
+    """float32 truncated normals of 2^25 or more samples build the table for their bounds in
+    the call and read most samples from it: every output against the oracle, one key in
+    both layouts (a ragged tail), a batch of two keys, and with the accurate erf_inv."""
+    key = orc.seed(31)
+    n = (1 << 25) + 777
+    for part in (True, False):
+        with flags(False, part):
+            got = to_np(jr.random_truncated_normal(dev_key(key), -0.7, 2.25, (n,)))
+        assert same_bits(got, orc.truncated_normal(key, "float32", n, -0.7, 2.25, part),
+                         "float32"), part
+    keys = np.stack([orc.seed(s) for s in (4, 5)])
+    m = (1 << 24) + 5
+    got = to_np(jr.vmap(lambda k: jr.random_truncated_normal(k, -3.0, 1.5, (m,)))(dev_key(keys)))
+    for r in range(2):
+        assert same_bits(got[r], orc.truncated_normal(keys[r], "float32", m, -3.0, 1.5),
+                         "float32"), r
+    with jr.with_jax_config("jax_accurate_erf_inv", True):
+        got = to_np(jr.random_truncated_normal(dev_key(key), -0.7, 2.25, (n,)))
+    assert same_bits(got, orc.truncated_normal(key, "float32", n, -0.7, 2.25, accurate=True),
+                     "float32")
