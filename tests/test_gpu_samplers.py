@@ -376,3 +376,21 @@ def test_truncated_normal_table_in_the_call():
         got = to_np(jr.random_truncated_normal(dev_key(key), -0.7, 2.25, (n,)))
     assert same_bits(got, orc.truncated_normal(key, "float32", n, -0.7, 2.25, accurate=True),
                      "float32")
+
+
+def test_truncated_normal_scratch_entry_point():
+    """jxr_truncated_normal_scratch through the C ABI: with a table-sized scratch, with one
+    too small (it falls back to jxr_truncated_normal) and below the size threshold, the
+    same samples as jxr_truncated_normal."""
+    from jaxr_b200 import _native as nat
+    kd = dev_key(orc.seed(8)).view(1, 2)
+    st = torch.cuda.current_stream().cuda_stream
+    for n, scratch_words in (((1 << 25) + 3, 1 << 23), ((1 << 25) + 3, 1000), (4097, 1 << 23)):
+        ref = torch.empty(n, dtype=torch.float32, device="cuda")
+        nat.call("jxr_truncated_normal", kd.data_ptr(), 1, n, 0, n, 1, nat.F32, -1.0, 2.0,
+                 ref.data_ptr(), st)
+        got = torch.empty_like(ref)
+        scratch = torch.empty(scratch_words, dtype=torch.float32, device="cuda")
+        nat.call("jxr_truncated_normal_scratch", kd.data_ptr(), 1, n, 0, n, 1, nat.F32, -1.0, 2.0,
+                 scratch.data_ptr(), scratch_words * 4, got.data_ptr(), st)
+        assert torch.equal(got.view(torch.int32), ref.view(torch.int32)), (n, scratch_words)
