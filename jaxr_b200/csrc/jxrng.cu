@@ -537,6 +537,58 @@ int launch_table(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t be
   return launch_op(keys, nkeys, size, begin, count, layout, H{table, op}, out, st);
 }
 
+// The 16-bit samplers' tables (OpTableH): slot 2 * sampler + (bfloat16), sampler 0..3 the
+// log-transform kinds, 4 the normal, 5 the normal with the accurate erf_inv.  Requests of
+// at least kTable16Min samples use them.
+constexpr uint64_t kTable16Min = 1ull << 16;
+constexpr int kTables16 = 12;
+uint16_t* g_tables16[64][kTables16];
+
+template <class Op, class T>
+__global__ void k_build_table16(Op op, uint16_t* __restrict__ table) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < (uint32_t)T::kEntries) table[i] = op((typename Op::Bits)(i << T::kShift));
+}
+
+// The table of the 16-bit op on the current device, as f32_table (nullptr while st is
+// being captured into a CUDA graph, or when it cannot be built; the caller evaluates).
+template <class Op>
+const uint16_t* h16_table(int slot, const Op& op, cudaStream_t st) {
+  using T = OpTableH<Op::kBits>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_tab_mu);
+  if (g_tables16[dev][slot]) return g_tables16[dev][slot];
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  uint16_t* t = nullptr;
+  if (cudaMalloc(&t, sizeof(uint16_t) * T::kEntries) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  k_build_table16<Op, T><<<(T::kEntries + 255) / 256, 256, 0, st>>>(op, t);
+  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+    cudaFree(t);
+    return nullptr;
+  }
+  g_tables16[dev][slot] = t;
+  return t;
+}
+
+// A 16-bit sampler: through its table (OpTableH) for requests of kTable16Min or more
+// samples, else evaluated.
+template <class Op>
+int launch_h(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
+             int layout, int slot, const Op& op, void* out, cudaStream_t st) {
+  if (count * (uint64_t)nkeys >= kTable16Min)
+    if (const uint16_t* t = h16_table(slot, op, st))
+      return launch_op(keys, nkeys, size, begin, count, layout, OpTableH<Op::kBits>{t}, out, st);
+  return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
+}
+
 int check_request(const void* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
                   int layout, const void* out) {
   if (nkeys < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "nkeys must be >= 0, got %lld", (long long)nkeys);
@@ -1341,8 +1393,10 @@ int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
         return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32T<A>{}, out, st);
       }
       case JXR_F64: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF64T<A>{}, out, st);
-      case JXR_F16: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<false, A>{}, out, st);
-      default: return launch_op(keys, nkeys, size, begin, count, layout, OpNormalH<true, A>{}, out, st);
+      case JXR_F16: return launch_h(keys, nkeys, size, begin, count, layout, 2 * (A ? 5 : 4),
+                                    OpNormalH<false, A>{}, out, st);
+      default: return launch_h(keys, nkeys, size, begin, count, layout, 2 * (A ? 5 : 4) + 1,
+                               OpNormalH<true, A>{}, out, st);
     }
   });
 }
@@ -1557,6 +1611,9 @@ int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
       if (big)
         if (const float* t = f32_table(1 + kind, op, st))
           return launch_table(keys, nkeys, size, begin, count, layout, t, op, out, st);
+    } else if constexpr (std::is_same_v<typename O::Out, uint16_t>) {
+      return launch_h(keys, nkeys, size, begin, count, layout,
+                      2 * kind + (dtype == JXR_BF16 ? 1 : 0), op, out, st);
     }
     return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
   });
@@ -2264,6 +2321,10 @@ int jxr_free_caches(void) {
     for (int id = 0; id < kTables; ++id) {
       if (g_tables[dev][id]) cudaFree(g_tables[dev][id]);
       g_tables[dev][id] = nullptr;
+    }
+    for (int id = 0; id < kTables16; ++id) {
+      if (g_tables16[dev][id]) cudaFree(g_tables16[dev][id]);
+      g_tables16[dev][id] = nullptr;
     }
   }
   HostCopyCtx& cx = g_host_ctx[dev];

@@ -393,6 +393,21 @@ struct OpTableF32 {
   __device__ __forceinline__ Out operator()(Bits b) const { return __ldg(table + (b >> 9)); }
 };
 
+// A float16 (bfloat16) sampler whose output depends only on the top 10 (7) bits of its
+// 16-bit (8-bit) draw -- every op built on unit_h -- read back from the table of its
+// 1024 (128) results, built on the device by the op itself: 2 KiB at most, so the
+// gathers hit L1.
+template <int kDrawBits>
+struct OpTableH {
+  static constexpr int kBits = kDrawBits;
+  static constexpr int kShift = kDrawBits == 16 ? 6 : 1;
+  static constexpr int kEntries = 1 << (kDrawBits - kShift);
+  using Bits = typename UintOf<kBits>::T;
+  using Out = uint16_t;
+  const uint16_t* __restrict__ table;
+  __device__ __forceinline__ Out operator()(Bits b) const { return __ldg(table + (b >> kShift)); }
+};
+
 // The table gathers are bound by L1TEX throughput while the integer pipe has room, and
 // evaluating an op directly is bound by the integer pipe: the single-key kernel evaluates
 // kDirect of a thread's 16 outputs directly (op.direct, the op the table was built from,

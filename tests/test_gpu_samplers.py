@@ -394,3 +394,42 @@ def test_truncated_normal_scratch_entry_point():
         nat.call("jxr_truncated_normal_scratch", kd.data_ptr(), 1, n, 0, n, 1, nat.F32, -1.0, 2.0,
                  scratch.data_ptr(), scratch_words * 4, got.data_ptr(), st)
         assert torch.equal(got.view(torch.int32), ref.view(torch.int32)), (n, scratch_words)
+
+
+@pytest.mark.parametrize("dt", ["float16", "bfloat16"])
+@pytest.mark.parametrize("kind", ["normal", "normal_accurate"] + KINDS)
+def test_16bit_table_samplers_every_output(kind, dt):
+    """16-bit samplers of 2^16 or more samples read the table of their 1024 (float16) or
+    128 (bfloat16) possible results: every output against the oracle, one key in both
+    layouts and a batch of three keys."""
+    def sample(k, shape):
+        if kind.startswith("normal"):
+            return jr.random_normal(k, shape, dt)
+        return FN[kind](k, shape, dt)
+
+    def want(k, n, part):
+        if kind.startswith("normal"):
+            return orc.normal(k, dt, n, part, accurate=kind == "normal_accurate")
+        return orc.sample(k, kind, dt, n, part)
+
+    acc = jr.with_jax_config("jax_accurate_erf_inv", kind == "normal_accurate")
+    key = orc.seed(64)
+    n = (1 << 17) + 5
+    for part in (True, False):
+        with flags(False, part), acc:
+            got = to_np(sample(dev_key(key), (n,)))
+        assert same_bits_h(got, want(key, n, part), dt), part
+    keys = np.stack([orc.seed(s) for s in range(3)])
+    m = (1 << 16) + 1
+    with jr.with_jax_config("jax_accurate_erf_inv", kind == "normal_accurate"):
+        got = to_np(jr.vmap(lambda k: sample(k, (m,)))(dev_key(keys)))
+    for r in range(3):
+        assert same_bits_h(got[r], want(keys[r], m, True), dt), r
+
+
+def same_bits_h(got_values, want_bits, dt):
+    """16-bit results (as float32 values) against the oracle's raw 16-bit patterns."""
+    g = np.asarray(got_values, dtype=np.float32)
+    w = np.asarray(as_float(np.asarray(want_bits), dt), dtype=np.float32)
+    gn, wn = np.isnan(g), np.isnan(w)
+    return np.array_equal(gn, wn) and np.array_equal(g[~gn].view(np.uint32), w[~wn].view(np.uint32))
