@@ -412,16 +412,18 @@ def test_16bit_table_samplers_every_output(kind, dt):
             return orc.normal(k, dt, n, part, accurate=kind == "normal_accurate")
         return orc.sample(k, kind, dt, n, part)
 
-    acc = jr.with_jax_config("jax_accurate_erf_inv", kind == "normal_accurate")
+    def acc():
+        return jr.with_jax_config("jax_accurate_erf_inv", kind == "normal_accurate")
+
     key = orc.seed(64)
     n = (1 << 17) + 5
     for part in (True, False):
-        with flags(False, part), acc:
+        with flags(False, part), acc():
             got = to_np(sample(dev_key(key), (n,)))
         assert same_bits_h(got, want(key, n, part), dt), part
     keys = np.stack([orc.seed(s) for s in range(3)])
     m = (1 << 16) + 1
-    with jr.with_jax_config("jax_accurate_erf_inv", kind == "normal_accurate"):
+    with acc():
         got = to_np(jr.vmap(lambda k: sample(k, (m,)))(dev_key(keys)))
     for r in range(3):
         assert same_bits_h(got[r], want(keys[r], m, True), dt), r
