@@ -80,7 +80,8 @@ int jxr_set_accurate_erf_inv(int enable);
 int jxr_get_accurate_erf_inv(void);
 
 /* Frees the current device's caches: the float32 samplers' tables (32 MiB each, built on
- * first use by requests of 2^22 or more samples) and jxr_random_bits_host's staging
+ * first use by requests of 2^22 or more samples), the 16-bit samplers' tables (2 KiB at
+ * most, from 2^16 samples) and jxr_random_bits_host's staging
  * buffers, streams and events.  Waits for the device first; later calls rebuild what they
  * need.  Call it before cudaDeviceReset or to return the memory. */
 int jxr_free_caches(void);
