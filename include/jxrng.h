@@ -212,8 +212,10 @@ int jxr_truncated_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uin
 /* jxr_truncated_normal with caller-provided scratch (device memory, 16-byte aligned):
  * float32 requests of 2^25 or more samples with at least 32 MiB of scratch build, in the
  * call, the table of the sampler at all 2^23 values it can take (each sample depends
- * only on bits >> 9 of its draw) and read most samples from it; the results are those of
- * jxr_truncated_normal, which every other request calls. */
+ * only on bits >> 9 of its draw) and read most samples from it; float16 / bfloat16
+ * requests of 2^16 or more samples with at least 2 KiB of scratch do the same with their
+ * 1024 / 128 possible results.  The results are those of jxr_truncated_normal, which
+ * every other request calls. */
 int jxr_truncated_normal_scratch(const uint32_t* keys, int64_t nkeys, uint64_t size,
                                  uint64_t begin, uint64_t count, int layout, int dtype,
                                  double lower, double upper, void* scratch, size_t scratch_bytes,

@@ -1834,6 +1834,25 @@ int jxr_truncated_normal_scratch(const uint32_t* keys, int64_t nkeys, uint64_t s
   if (rc || (rc = check_request(keys, nkeys, size, begin, count, layout, out))) return rc;
   const bool table = dtype == JXR_F32 && count * (uint64_t)nkeys >= kTruncTableMin && scratch &&
                      scratch_bytes >= (sizeof(float) << 23) && (uintptr_t)scratch % 16 == 0;
+  const bool table16 = (dtype == JXR_F16 || dtype == JXR_BF16) &&
+                       count * (uint64_t)nkeys >= kTable16Min && scratch &&
+                       scratch_bytes >= 2048 && (uintptr_t)scratch % 16 == 0;
+  if (table16) {
+    cudaStream_t st = (cudaStream_t)stream;
+    return visit_trunc_op(dtype, lower, upper, [&](const auto& op) -> int {
+      using O = std::decay_t<decltype(op)>;
+      if constexpr (std::is_same_v<typename O::Out, uint16_t>) {
+        // this call's table: the op at all 1024 (float16) / 128 (bfloat16) draws it tells apart
+        using T = OpTableH<O::kBits>;
+        k_build_table16<O, T><<<(T::kEntries + 255) / 256, 256, 0, st>>>(op, (uint16_t*)scratch);
+        JXR_CUDA(cudaGetLastError());
+        return launch_op(keys, nkeys, size, begin, count, layout, T{(const uint16_t*)scratch}, out,
+                         st);
+      } else {
+        return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
+      }
+    });
+  }
   if (!table)
     return jxr_truncated_normal(keys, nkeys, size, begin, count, layout, dtype, lower, upper,
                                 out, stream);

@@ -1074,10 +1074,13 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
             nat.call("jxr_truncated_normal_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt],
                      float(lo_s), float(hi_s), _ptr(out), _stream())
         else:
-            # large float32 requests build the sampler's table for these bounds in the call
-            # (2^23 floats of scratch from torch's allocator)
-            big = dt == "float32" and kd.shape[0] * size >= _TRUNC_TABLE_MIN
-            scratch = torch.empty(1 << 23 if big else 0, dtype=torch.float32, device=kd.device)
+            # large requests build the sampler's table for these bounds in the call (float32:
+            # 2^23 floats of scratch from torch's allocator; 16-bit: 2 KiB)
+            total = kd.shape[0] * size
+            words = (1 << 23 if dt == "float32" and total >= _TRUNC_TABLE_MIN else
+                     512 if dt in ("float16", "bfloat16") and total >= 1 << 16 else 0)
+            big = words > 0
+            scratch = torch.empty(words, dtype=torch.float32, device=kd.device)
             nat.call("jxr_truncated_normal_scratch", _ptr(kd), kd.shape[0], size, 0, size, layout,
                      _FLOAT_CODE[dt], float(lo_s), float(hi_s),
                      _ptr(scratch) if big else None, scratch.numel() * 4, _ptr(out), _stream())

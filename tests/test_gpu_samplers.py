@@ -435,3 +435,15 @@ def same_bits_h(got_values, want_bits, dt):
     w = np.asarray(as_float(np.asarray(want_bits), dt), dtype=np.float32)
     gn, wn = np.isnan(g), np.isnan(w)
     return np.array_equal(gn, wn) and np.array_equal(g[~gn].view(np.uint32), w[~wn].view(np.uint32))
+
+
+@pytest.mark.parametrize("dt", ["float16", "bfloat16"])
+def test_16bit_truncated_normal_table_in_the_call(dt):
+    """16-bit truncated normals of 2^16 or more samples build the table of their bounds
+    (1024 / 128 entries) in the call: every output against the oracle in both layouts."""
+    key = orc.seed(65)
+    n = (1 << 17) + 5
+    for part in (True, False):
+        with flags(False, part):
+            got = to_np(jr.random_truncated_normal(dev_key(key), -0.5, 3.0, (n,), dt))
+        assert same_bits_h(got, orc.truncated_normal(key, dt, n, -0.5, 3.0, part), dt), part
