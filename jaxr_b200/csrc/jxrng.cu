@@ -696,6 +696,24 @@ int launch_from_bits(const void* bits, int64_t n, const Op& op, void* out, cudaS
   return JXR_OK;
 }
 
+// A sampler's transform of given draws through its table (float32: 2^22 or more draws,
+// 16-bit: 2^16 or more), else evaluated; slot32 / slot16 are the op's table slots.
+template <class Op>
+int launch_from_bits_table(const void* bits, int64_t n, int slot32, int slot16, const Op& op,
+                           void* out, cudaStream_t st, int grid) {
+  using Out = typename Op::Out;
+  if constexpr (std::is_same_v<Out, float> && Op::kBits == 32) {
+    if ((uint64_t)n >= kTableMin)
+      if (const float* t = f32_table(slot32, op, st))
+        return launch_from_bits(bits, n, OpTableF32{t}, out, st, grid);
+  } else if constexpr (std::is_same_v<Out, uint16_t>) {
+    if ((uint64_t)n >= kTable16Min)
+      if (const uint16_t* t = h16_table(slot16, op, st))
+        return launch_from_bits(bits, n, OpTableH<Op::kBits>{t}, out, st, grid);
+  }
+  return launch_from_bits(bits, n, op, out, st, grid);
+}
+
 template <bool kAcc>
 __global__ void k_erfinv_f32(const float* __restrict__ x, int64_t n, float* __restrict__ out) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -1483,10 +1501,16 @@ int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void
   return with_erfinv([&](auto acc) -> int {
     constexpr bool A = decltype(acc)::value;
     switch (dtype) {
-      case JXR_F32: return launch_from_bits(bits, n, OpNormalF32T<A>{}, out, st, grid);
+      case JXR_F32:
+        return launch_from_bits_table(bits, n, A ? kTableNormalAccurate : 0, 0,
+                                      OpNormalF32T<A>{}, out, st, grid);
       case JXR_F64: return launch_from_bits(bits, n, OpNormalF64T<A>{}, out, st, grid);
-      case JXR_F16: return launch_from_bits(bits, n, OpNormalH<false, A>{}, out, st, grid);
-      default: return launch_from_bits(bits, n, OpNormalH<true, A>{}, out, st, grid);
+      case JXR_F16:
+        return launch_from_bits_table(bits, n, 0, 2 * (A ? 5 : 4), OpNormalH<false, A>{}, out,
+                                      st, grid);
+      default:
+        return launch_from_bits_table(bits, n, 0, 2 * (A ? 5 : 4) + 1, OpNormalH<true, A>{},
+                                      out, st, grid);
     }
   });
 }
@@ -1630,7 +1654,8 @@ int jxr_sample_from_bits(const void* bits, int64_t n, int kind, int dtype, void*
   if ((rc = small_grid(n, &grid))) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   return visit_sample_op(kind, dtype, [&](const auto& op) {
-    return launch_from_bits(bits, n, op, out, st, grid);
+    return launch_from_bits_table(bits, n, 1 + kind, 2 * kind + (dtype == JXR_BF16 ? 1 : 0), op,
+                                  out, st, grid);
   });
 }
 

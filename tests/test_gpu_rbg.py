@@ -153,3 +153,45 @@ def test_rbg_shards_cover_the_request():
     size = 100003
     slabs = [to_np(random_bits_shard(k, (size,), r, 3)) for r in range(3)]
     assert np.array_equal(np.concatenate(slabs), orc.rbg_bits(KEYS[3], 32, size))
+
+
+@pytest.mark.parametrize("dt", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("kind", ["normal", "normal_accurate", "exponential", "gumbel",
+                                  "logistic", "laplace"])
+def test_from_bits_tables_match_direct(kind, dt):
+    """The from-bits transforms (how rbg keys sample) read the sampler's table for 2^22 or
+    more float32 draws and 2^16 or more 16-bit draws: the same draws transformed in one
+    call (table) and in chunks below the threshold (evaluated directly) agree bit for bit."""
+    from jaxr_b200 import _native as nat
+    code = {"float32": nat.F32, "float16": nat.F16, "bfloat16": nat.BF16}[dt]
+    bits_dt = {"float32": torch.int32, "float16": torch.int16, "bfloat16": torch.uint8}[dt]
+    out_dt = torch.float32 if dt == "float32" else torch.int16
+    n = (1 << 22) + 3 if dt == "float32" else (1 << 16) + 3
+    chunk = (1 << 21) if dt == "float32" else (1 << 15)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    bits = torch.randint(-2**31 if bits_dt != torch.uint8 else 0,
+                         2**31 - 1 if bits_dt != torch.uint8 else 256, (n,),
+                         generator=g, device="cuda", dtype=torch.int64).to(bits_dt)
+    st = torch.cuda.current_stream().cuda_stream
+    kinds = {"exponential": 0, "gumbel": 1, "logistic": 2, "laplace": 3}
+
+    def transform(b, out):
+        if kind.startswith("normal"):
+            nat.call("jxr_normal_from_bits", b.data_ptr(), b.numel(), code, out.data_ptr(), st)
+        else:
+            nat.call("jxr_sample_from_bits", b.data_ptr(), b.numel(), kinds[kind], code,
+                     out.data_ptr(), st)
+
+    prev = nat.lib().jxr_set_accurate_erf_inv(1 if kind == "normal_accurate" else 0)
+    try:
+        whole = torch.empty(n, dtype=out_dt, device="cuda")
+        transform(bits, whole)
+        parts = torch.empty_like(whole)
+        for s in range(0, n, chunk):
+            transform(bits[s:s + chunk], parts[s:s + chunk])
+        torch.cuda.synchronize()
+    finally:
+        nat.lib().jxr_set_accurate_erf_inv(prev)
+    wi = whole.view(torch.int32 if dt == "float32" else torch.int16)
+    pi = parts.view(torch.int32 if dt == "float32" else torch.int16)
+    assert torch.equal(wi, pi)
