@@ -21,6 +21,11 @@
  *    device writes its own slab; begin = 0, count = size is the whole request.
  *  - layout selects jax_threefry_partitionable: JXR_LAYOUT_PARTITIONABLE (the
  *    reference's default) or JXR_LAYOUT_ORIGINAL.
+ *  - Entry points allocate no device memory and do not wait for the stream unless
+ *    their comment says so: jxr_prepare_device (set-up), jxr_free_caches, the HOST-memory
+ *    entry points jxr_random_bits_host / _host_static, and jxr_shuffle /
+ *    jxr_argsort_float, which synchronise to read a bounds-check flag (their scratch
+ *    comes from the caller).
  *
  * Reference interfaces replaced (paths within the jaxR project):
  *  - threefry2x32_p and its lowering           R/prng.R:48-99
@@ -79,11 +84,37 @@ enum { JXR_FLAG_UNFUSED_MUL_ADD = 1 };
 int jxr_set_accurate_erf_inv(int enable);
 int jxr_get_accurate_erf_inv(void);
 
-/* Frees the current device's caches: the float32 samplers' tables (32 MiB each, built on
- * first use by requests of 2^22 or more samples), the 16-bit samplers' tables (2 KiB at
- * most, from 2^16 samples) and jxr_random_bits_host's staging
- * buffers, streams and events.  Waits for the device first; later calls rebuild what they
- * need.  Call it before cudaDeviceReset or to return the memory. */
+/* Set-up of the current device, the one call that allocates on purpose; do it once per
+ * device, before any stream capture and before a host framework reserves the GPU for its
+ * own memory pool.  Synchronous: waits for `stream`; refused (JXR_ERR_INVALID_ARGUMENT)
+ * while `stream` is being captured into a CUDA graph.
+ *  - Every call loads this library's module on the device (CUDA loads modules lazily,
+ *    on first use) and looks up the array of jxr_random_bits_host_static: the module's
+ *    code and its fixed 16 MiB + 32 KiB array are created then, not inside a later call.
+ *  - `what` (JXR_PREPARE_* bits, 0 for none) names the samplers whose lookup tables to
+ *    build: per sampler a float32 table of its 2^23 possible results (32 MiB) and the
+ *    float16 / bfloat16 tables of its 1024 / 128 results (2 KiB + 256 B).  Every float32
+ *    sample depends only on bits >> 9 of its draw, every 16-bit one on the top 10 / 7
+ *    bits, so a table holds the sampler's exact results.
+ * Sampling entry points never allocate, build a table or wait: a prepared table is read
+ * by requests of 2^22 or more float32 samples (jxr_normal, jxr_sample and their _from_bits
+ * forms) or 2^16 or more 16-bit samples, which then run about twice as fast; without it
+ * every sample is evaluated directly, with identical results. */
+enum {
+  JXR_PREPARE_TABLE_NORMAL = 1u << 0,          /* normal, default erf_inv */
+  JXR_PREPARE_TABLE_NORMAL_ACCURATE = 1u << 1, /* normal under jax_accurate_erf_inv */
+  JXR_PREPARE_TABLE_EXPONENTIAL = 1u << 2,     /* jxr_sample kinds 0..3, in order */
+  JXR_PREPARE_TABLE_GUMBEL = 1u << 3,
+  JXR_PREPARE_TABLE_LOGISTIC = 1u << 4,
+  JXR_PREPARE_TABLE_LAPLACE = 1u << 5,
+  JXR_PREPARE_ALL = 0x3F
+};
+int jxr_prepare_device(uint32_t what, void* stream);
+
+/* Frees the current device's caches: the samplers' tables that jxr_prepare_device built,
+ * jxr_random_bits_host's staging buffers, streams and events, and the cached address of
+ * jxr_random_bits_host_static's array (looked up again by the next call).  Waits for the
+ * device first.  Call it before cudaDeviceReset or to return the memory. */
 int jxr_free_caches(void);
 
 /* ABI version (JXR_ABI_VERSION) and the last error of this host thread. */
@@ -129,7 +160,8 @@ int jxr_uniform(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t beg
                 uint32_t flags, void* out, void* stream);
 
 /* random_normal for a real dtype (R/random.R:501-508): sqrt(2) * erf_inv(u) with u
- * uniform on [nextafter(-1, 0), 1). out: dtype[nkeys][count]. */
+ * uniform on [nextafter(-1, 0), 1). out: dtype[nkeys][count].  Large float32 / 16-bit
+ * requests read the sampler's table when jxr_prepare_device has built it (same results). */
 int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
                uint64_t count, int layout, int dtype, void* out, void* stream);
 
@@ -163,13 +195,20 @@ int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void
  *    u_hi are the two halves of uniform(key, (2, shape)).  out: uint8 0/1. */
 int jxr_uniform_affine(const void* unit, const void* minval, const void* maxval, int64_t n,
                        int dtype, uint32_t flags, void* out, void* stream);
+/* jxr_uniform_affine over nrows rows of n unit draws (unit, out: dtype[nrows][n], a key
+ * batch's rows) with one row of bounds (minval, maxval: dtype[n]) for every row, in one
+ * launch. */
+int jxr_uniform_affine_rows(const void* unit, const void* minval, const void* maxval,
+                            int64_t nrows, int64_t n, int dtype, uint32_t flags, void* out,
+                            void* stream);
 int jxr_bernoulli_from_uniform(const void* u_lo, const void* u_hi, const void* p, int64_t n,
                                int dtype, uint8_t* out, void* stream);
 
 /* The log-transform samplers (R/random.R:1422-1516) fused like jxr_uniform, kind:
  * 0 exponential -log1p(-u); 1 gumbel (mode "low") -log(-log(u)), u from (tiny, 1);
  * 2 logistic log(x) - log1p(-x), x from (tiny, 1); 3 laplace sign(u) log1p(-|u|),
- * u from (-1 + 2^-(nmant+1), 1).  out: dtype[nkeys][count]. */
+ * u from (-1 + 2^-(nmant+1), 1).  out: dtype[nkeys][count].  Large float32 / 16-bit
+ * requests read the sampler's table when jxr_prepare_device has built it (same results). */
 int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin,
                uint64_t count, int layout, int kind, int dtype, void* out, void* stream);
 /* The same transforms of n random_bits values (the dtype's draw width: 32/64/16/8 bits for
@@ -345,13 +384,19 @@ int jxr_ipc_close(void* base);
  *  - nkeys may be at most 4096; larger batches are rejected with
  *    JXR_ERR_INVALID_ARGUMENT.  count is produced in 16 MiB chunks, any length.
  *  - Work is ordered on `stream` (NULL = legacy default stream) and the call returns
- *    when host_out holds the result.  The first call on a device looks up the array's
- *    device address (cudaGetSymbolAddress); make that first call before any stream
- *    capture on that device.
+ *    when host_out holds the result, also when it fails part way.
+ *  - Set-up: the array exists once the library's module is loaded on the device, and
+ *    CUDA loads modules lazily, on the library's first use there.  If a call of this
+ *    entry point is that first use, the module (its code and this array) is created
+ *    inside the call, i.e. allocated.  So call jxr_prepare_device once per device at
+ *    set-up, before the framework reserves its memory pool and before any stream capture:
+ *    it loads the module and looks up the array's device address
+ *    (cudaGetSymbolAddress).  Otherwise the first call on a device does that look-up.
  *  - Every call on a device shares the one array, which keeps the last call's contents
  *    (nothing in it needs to start at zero: keys and staging are rewritten before they
- *    are read).  Calls that overlap on the GPU -- e.g. from two host threads at once on
- *    the same device -- race on it: serialise them. */
+ *    are read).  Calls that overlap on the GPU would race on it; the library holds a lock
+ *    per device for the whole of each call (which ends with its stream synchronised), so
+ *    calls from several host threads of one process take turns. */
 int jxr_random_bits_host_static(const uint32_t* keys_host, int64_t nkeys, uint64_t size,
                                 uint64_t begin, uint64_t count, int layout, int bit_width,
                                 void* host_out, void* stream);

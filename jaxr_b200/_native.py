@@ -49,6 +49,7 @@ SIGNATURES = {
     "jxr_uniform_from_bits": [_vp, _i64, _int, _dbl, _dbl, _u32, _vp, _vp],
     "jxr_normal_from_bits": [_vp, _i64, _int, _vp, _vp],
     "jxr_uniform_affine": [_vp, _vp, _vp, _i64, _int, _u32, _vp, _vp],
+    "jxr_uniform_affine_rows": [_vp, _vp, _vp, _i64, _i64, _int, _u32, _vp, _vp],
     "jxr_bernoulli_from_uniform": [_vp, _vp, _vp, _i64, _int, _vp, _vp],
     "jxr_sample": [_vp, _i64, _u64, _u64, _u64, _int, _int, _int, _vp, _vp],
     "jxr_randint": [_vp, _vp, _i64, _u64, _u64, _u64, _int, _int, _i64, _i64, _int, _int, _vp,
@@ -78,6 +79,7 @@ SIGNATURES = {
     "jxr_erf_inv": [_vp, _i64, _int, _vp, _vp],
     "jxr_set_accurate_erf_inv": [_int],
     "jxr_free_caches": [],
+    "jxr_prepare_device": [_u32, _vp],
     "jxr_get_accurate_erf_inv": [],
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],

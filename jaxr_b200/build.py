@@ -56,30 +56,35 @@ FFI_SOURCE = os.path.join(CSRC, "ffi", "jxrng_ffi.cc")
 FFI_OUT = os.path.join(HERE, "libjxrng_ffi.so")
 
 
+FFI_HEADERS = [os.path.join(CSRC, "ffi", "xla_ffi_abi.h"), os.path.join(ROOT, "include", "jxrng.h"),
+               os.path.join(ROOT, "include", "jxrng_ffi.h")]
+
+
 def xla_ffi_include_dir():
-    """A directory holding xla/ffi/api/c_api.h: $XLA_FFI_INCLUDE_DIR, else the copy jaxR
-    vendors for ffi_include_dir() (its inst/include), where that tree is present."""
-    for cand in (os.environ.get("XLA_FFI_INCLUDE_DIR"), "/root/reference/inst/include"):
-        if cand and os.path.exists(os.path.join(cand, "xla", "ffi", "api", "c_api.h")):
-            return cand
+    """$XLA_FFI_INCLUDE_DIR when it holds xla/ffi/api/c_api.h (XLA's own FFI header, e.g.
+    the copy jaxR vendors for ffi_include_dir()), else None."""
+    cand = os.environ.get("XLA_FFI_INCLUDE_DIR")
+    if cand and os.path.exists(os.path.join(cand, "xla", "ffi", "api", "c_api.h")):
+        return cand
     return None
 
 
 def build_ffi(force=False, verbose=False):
-    """Builds libjxrng_ffi.so (host C++, linked to libjxrng.so) when XLA's FFI headers are
-    available; returns its path, or None when they are not (a prebuilt library is kept)."""
+    """Builds libjxrng_ffi.so (host C++, linked to libjxrng.so) and returns its path.  The
+    handlers compile against csrc/ffi/xla_ffi_abi.h, the part of XLA's FFI C API they use;
+    with $XLA_FFI_INCLUDE_DIR set they compile against XLA's own c_api.h instead."""
     inc = xla_ffi_include_dir()
-    if inc is None:
-        return FFI_OUT if os.path.exists(FFI_OUT) else None
     lib = build(verbose=verbose)
     if (not force and os.path.exists(FFI_OUT) and
             all(os.path.getmtime(q) <= os.path.getmtime(FFI_OUT)
-                for q in (FFI_SOURCE, lib, __file__, os.path.join(ROOT, "include", "jxrng.h")))):
+                for q in [FFI_SOURCE, lib, __file__] + FFI_HEADERS)):
         return FFI_OUT
     cxx = os.environ.get("CXX_FOR_FFI") or shutil.which("g++") or "g++"
-    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-I" + inc,
-           "-I" + os.path.join(ROOT, "include"), FFI_SOURCE, "-L" + HERE, "-ljxrng",
-           "-Wl,-rpath,$ORIGIN", "-o", FFI_OUT + ".tmp"]
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall",
+           "-I" + os.path.join(CSRC, "ffi"), "-I" + os.path.join(ROOT, "include")]
+    if inc is not None:
+        cmd += ["-DJXR_FFI_XLA_HEADER", "-I" + inc]
+    cmd += [FFI_SOURCE, "-L" + HERE, "-ljxrng", "-Wl,-rpath,$ORIGIN", "-o", FFI_OUT + ".tmp"]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

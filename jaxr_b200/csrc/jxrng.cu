@@ -478,34 +478,35 @@ constexpr int kTableNormalAccurate = 5;
 std::mutex g_tab_mu;
 float* g_tables[64][kTables];
 
-// The table of `op` on the current device (built on stream st and waited for once), or
-// nullptr when it cannot be built now (no device memory, or st is being captured into a
-// CUDA graph); the caller then evaluates the op.
-template <class Op>
-const float* f32_table(int id, const Op& op, cudaStream_t st) {
+// The current device's table in slot `id` once jxr_prepare_device has built it, else
+// nullptr: the caller then evaluates the op.  Sampling entry points only look tables up;
+// they never allocate, build or wait for one.
+const float* f32_table(int id) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
   std::lock_guard<std::mutex> lock(g_tab_mu);
-  if (g_tables[dev][id]) return g_tables[dev][id];
-  // building allocates and waits for the stream, which a CUDA graph capture forbids: the
-  // caller then evaluates the op directly
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return nullptr;
-  }
+  return g_tables[dev][id];
+}
+
+// Builds the table of `op` in slot `id` of device `dev` (current), on stream st, and waits
+// for it (jxr_prepare_device; the caller holds g_tab_mu).
+template <class Op>
+int build_f32_table(int dev, int id, const Op& op, cudaStream_t st) {
+  if (g_tables[dev][id]) return JXR_OK;
   float* t = nullptr;
-  if (cudaMalloc(&t, sizeof(float) << 23) != cudaSuccess) {
-    cudaGetLastError();
-    return nullptr;
-  }
+  JXR_CUDA(cudaMalloc(&t, sizeof(float) << 23));
   k_build_table<Op><<<1024, 256, 0, st>>>(op, t);
-  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
     cudaFree(t);
-    return nullptr;
+    return fail(JXR_ERR_CUDA, "building a float32 sampler table: %s", cudaGetErrorString(e));
   }
   g_tables[dev][id] = t;
-  return t;
+  return JXR_OK;
 }
 
 // Outputs per thread (of 16) that a table-backed sampler evaluates directly: where the
@@ -550,41 +551,44 @@ __global__ void k_build_table16(Op op, uint16_t* __restrict__ table) {
   if (i < (uint32_t)T::kEntries) table[i] = op((typename Op::Bits)(i << T::kShift));
 }
 
-// The table of the 16-bit op on the current device, as f32_table (nullptr while st is
-// being captured into a CUDA graph, or when it cannot be built; the caller evaluates).
-template <class Op>
-const uint16_t* h16_table(int slot, const Op& op, cudaStream_t st) {
-  using T = OpTableH<Op::kBits>;
+// The current device's 16-bit table in `slot` once jxr_prepare_device has built it, else
+// nullptr (the caller evaluates), as f32_table.
+const uint16_t* h16_table(int slot) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return nullptr;
+  }
   std::lock_guard<std::mutex> lock(g_tab_mu);
-  if (g_tables16[dev][slot]) return g_tables16[dev][slot];
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return nullptr;
-  }
+  return g_tables16[dev][slot];
+}
+
+// Builds the 16-bit op's table in `slot` of device `dev` (current) and waits for it
+// (jxr_prepare_device; the caller holds g_tab_mu).
+template <class Op>
+int build_h16_table(int dev, int slot, const Op& op, cudaStream_t st) {
+  using T = OpTableH<Op::kBits>;
+  if (g_tables16[dev][slot]) return JXR_OK;
   uint16_t* t = nullptr;
-  if (cudaMalloc(&t, sizeof(uint16_t) * T::kEntries) != cudaSuccess) {
-    cudaGetLastError();
-    return nullptr;
-  }
+  JXR_CUDA(cudaMalloc(&t, sizeof(uint16_t) * T::kEntries));
   k_build_table16<Op, T><<<(T::kEntries + 255) / 256, 256, 0, st>>>(op, t);
-  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
     cudaFree(t);
-    return nullptr;
+    return fail(JXR_ERR_CUDA, "building a 16-bit sampler table: %s", cudaGetErrorString(e));
   }
   g_tables16[dev][slot] = t;
-  return t;
+  return JXR_OK;
 }
 
 // A 16-bit sampler: through its table (OpTableH) for requests of kTable16Min or more
-// samples, else evaluated.
+// samples once the table is prepared, else evaluated.
 template <class Op>
 int launch_h(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begin, uint64_t count,
              int layout, int slot, const Op& op, void* out, cudaStream_t st) {
   if (count * (uint64_t)nkeys >= kTable16Min)
-    if (const uint16_t* t = h16_table(slot, op, st))
+    if (const uint16_t* t = h16_table(slot))
       return launch_op(keys, nkeys, size, begin, count, layout, OpTableH<Op::kBits>{t}, out, st);
   return launch_op(keys, nkeys, size, begin, count, layout, op, out, st);
 }
@@ -697,18 +701,18 @@ int launch_from_bits(const void* bits, int64_t n, const Op& op, void* out, cudaS
 }
 
 // A sampler's transform of given draws through its table (float32: 2^22 or more draws,
-// 16-bit: 2^16 or more), else evaluated; slot32 / slot16 are the op's table slots.
+// 16-bit: 2^16 or more) once prepared, else evaluated; slot32 / slot16 are the op's slots.
 template <class Op>
 int launch_from_bits_table(const void* bits, int64_t n, int slot32, int slot16, const Op& op,
                            void* out, cudaStream_t st, int grid) {
   using Out = typename Op::Out;
   if constexpr (std::is_same_v<Out, float> && Op::kBits == 32) {
     if ((uint64_t)n >= kTableMin)
-      if (const float* t = f32_table(slot32, op, st))
+      if (const float* t = f32_table(slot32))
         return launch_from_bits(bits, n, OpTableF32{t}, out, st, grid);
   } else if constexpr (std::is_same_v<Out, uint16_t>) {
     if ((uint64_t)n >= kTable16Min)
-      if (const uint16_t* t = h16_table(slot16, op, st))
+      if (const uint16_t* t = h16_table(slot16))
         return launch_from_bits(bits, n, OpTableH<Op::kBits>{t}, out, st, grid);
   }
   return launch_from_bits(bits, n, op, out, st, grid);
@@ -733,33 +737,42 @@ __global__ void k_erfinv_f64(const double* __restrict__ x, int64_t n, double* __
 // float itself): max(minval, u * (maxval - minval) + minval), R/random.R:297-303.
 template <class T, bool kFused>
 __global__ void k_affine(const T* __restrict__ u, const T* __restrict__ mn, const T* __restrict__ mx,
-                         int64_t n, T* __restrict__ out) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const T lo = mn[i];
-    T r;
-    if constexpr (sizeof(T) == 4) {
-      const T d = __fsub_rn(mx[i], lo);
-      r = kFused ? __fmaf_rn(u[i], d, lo) : __fadd_rn(__fmul_rn(u[i], d), lo);
-    } else {
-      const T d = __dsub_rn(mx[i], lo);
-      r = kFused ? __fma_rn(u[i], d, lo) : __dadd_rn(__dmul_rn(u[i], d), lo);
+                         int64_t nrows, int64_t n, T* __restrict__ out) {
+  for (int64_t r = blockIdx.y; r < nrows; r += gridDim.y) {
+    const T* ur = u + r * n;
+    T* outr = out + r * n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const T lo = mn[i];
+      T res;
+      if constexpr (sizeof(T) == 4) {
+        const T d = __fsub_rn(mx[i], lo);
+        res = kFused ? __fmaf_rn(ur[i], d, lo) : __fadd_rn(__fmul_rn(ur[i], d), lo);
+      } else {
+        const T d = __dsub_rn(mx[i], lo);
+        res = kFused ? __fma_rn(ur[i], d, lo) : __dadd_rn(__dmul_rn(ur[i], d), lo);
+      }
+      outr[i] = xla_max(lo, res);
     }
-    out[i] = xla_max(lo, r);
   }
 }
 
 template <bool BF, bool kFused>
 __global__ void k_affine_h(const uint16_t* __restrict__ u, const uint16_t* __restrict__ mn,
-                           const uint16_t* __restrict__ mx, int64_t n, uint16_t* __restrict__ out) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const float f = h2f<BF>(u[i]), lo = h2f<BF>(mn[i]);
-    const float d = rh<BF>(__fsub_rn(h2f<BF>(mx[i]), lo));
-    float r;
-    if (kFused) r = h2f<BF>(d2h<BF>(__fma_rn((double)f, (double)d, (double)lo)));
-    else r = rh<BF>(__fadd_rn(rh<BF>(__fmul_rn(f, d)), lo));
-    out[i] = f2h<BF>(xla_max(lo, r));
+                           const uint16_t* __restrict__ mx, int64_t nrows, int64_t n,
+                           uint16_t* __restrict__ out) {
+  for (int64_t r = blockIdx.y; r < nrows; r += gridDim.y) {
+    const uint16_t* ur = u + r * n;
+    uint16_t* outr = out + r * n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const float f = h2f<BF>(ur[i]), lo = h2f<BF>(mn[i]);
+      const float d = rh<BF>(__fsub_rn(h2f<BF>(mx[i]), lo));
+      float res;
+      if (kFused) res = h2f<BF>(d2h<BF>(__fma_rn((double)f, (double)d, (double)lo)));
+      else res = rh<BF>(__fadd_rn(rh<BF>(__fmul_rn(f, d)), lo));
+      outr[i] = f2h<BF>(xla_max(lo, res));
+    }
   }
 }
 
@@ -1260,9 +1273,13 @@ constexpr size_t kStaticStageBytes = 16ull << 20;                // 16 MiB
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticKeyBytes + kStaticStageBytes];
 
 // Device address of g_static_scratch per device, looked up once with that device current
-// (the name is only a host-side stand-in for the array; host code must not pass it).
+// (the name is only a host-side stand-in for the array; host code must not pass it), and
+// cleared by jxr_free_caches (after a device reset the module, and the array, may move).
 static void* g_static_scratch_addr[64] = {};
 static std::mutex g_static_scratch_mu;
+// Held for the whole of a jxr_random_bits_host_static call on that device: calls from
+// several host threads take turns, so they cannot overlap on the GPU through the array.
+static std::mutex g_static_call_mu[64];
 
 static int static_scratch(int dev, unsigned char** out) {
   std::lock_guard<std::mutex> lock(g_static_scratch_mu);
@@ -1405,7 +1422,7 @@ int jxr_normal(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
     switch (dtype) {
       case JXR_F32: {
         if (count * (uint64_t)nkeys >= kTableMin)
-          if (const float* t = f32_table(A ? kTableNormalAccurate : 0, OpNormalF32T<A>{}, st))
+          if (const float* t = f32_table(A ? kTableNormalAccurate : 0))
             return launch_table(keys, nkeys, size, begin, count, layout, t, OpNormalF32T<A>{},
                                 out, st);
         return launch_op(keys, nkeys, size, begin, count, layout, OpNormalF32T<A>{}, out, st);
@@ -1517,32 +1534,44 @@ int jxr_normal_from_bits(const void* bits, int64_t n, int dtype, void* out, void
 
 int jxr_uniform_affine(const void* unit, const void* minval, const void* maxval, int64_t n,
                        int dtype, uint32_t flags, void* out, void* stream) {
+  return jxr_uniform_affine_rows(unit, minval, maxval, 1, n, dtype, flags, out, stream);
+}
+
+int jxr_uniform_affine_rows(const void* unit, const void* minval, const void* maxval,
+                            int64_t nrows, int64_t n, int dtype, uint32_t flags, void* out,
+                            void* stream) {
   int rc;
   if ((rc = check_dtype(dtype))) return rc;
-  if (n < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n must be >= 0");
-  if (!n) return JXR_OK;
+  if (n < 0 || nrows < 0) return fail(JXR_ERR_INVALID_ARGUMENT, "n and nrows must be >= 0");
+  if (!n || !nrows) return JXR_OK;
   if (!unit || !minval || !maxval || !out) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
-  int grid;
-  if ((rc = small_grid(n, &grid))) return rc;
+  if (nrows > INT64_MAX / n) return fail(JXR_ERR_INVALID_ARGUMENT, "nrows * n overflows");
+  // columns of 256-thread CTAs over a row, rows over grid.y: one wave of 8 CTAs per SM
+  DeviceInfo di;
+  if ((rc = device_info(&di))) return rc;
+  const int64_t wave = (int64_t)di.sms * 8;
+  const int64_t gx = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, wave));
+  const int64_t gy = std::max<int64_t>(1, std::min<int64_t>({nrows, std::max<int64_t>(1, wave / gx), 65535}));
+  const dim3 grid((unsigned)gx, (unsigned)gy);
   cudaStream_t st = (cudaStream_t)stream;
   const bool f = !(flags & JXR_FLAG_UNFUSED_MUL_ADD);
   using U16 = const uint16_t*;
   switch (dtype) {
     case JXR_F32:
-      if (f) k_affine<float, true><<<grid, 256, 0, st>>>((const float*)unit, (const float*)minval, (const float*)maxval, n, (float*)out);
-      else k_affine<float, false><<<grid, 256, 0, st>>>((const float*)unit, (const float*)minval, (const float*)maxval, n, (float*)out);
+      if (f) k_affine<float, true><<<grid, 256, 0, st>>>((const float*)unit, (const float*)minval, (const float*)maxval, nrows, n, (float*)out);
+      else k_affine<float, false><<<grid, 256, 0, st>>>((const float*)unit, (const float*)minval, (const float*)maxval, nrows, n, (float*)out);
       break;
     case JXR_F64:
-      if (f) k_affine<double, true><<<grid, 256, 0, st>>>((const double*)unit, (const double*)minval, (const double*)maxval, n, (double*)out);
-      else k_affine<double, false><<<grid, 256, 0, st>>>((const double*)unit, (const double*)minval, (const double*)maxval, n, (double*)out);
+      if (f) k_affine<double, true><<<grid, 256, 0, st>>>((const double*)unit, (const double*)minval, (const double*)maxval, nrows, n, (double*)out);
+      else k_affine<double, false><<<grid, 256, 0, st>>>((const double*)unit, (const double*)minval, (const double*)maxval, nrows, n, (double*)out);
       break;
     case JXR_F16:
-      if (f) k_affine_h<false, true><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
-      else k_affine_h<false, false><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
+      if (f) k_affine_h<false, true><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, nrows, n, (uint16_t*)out);
+      else k_affine_h<false, false><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, nrows, n, (uint16_t*)out);
       break;
     default:
-      if (f) k_affine_h<true, true><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
-      else k_affine_h<true, false><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, n, (uint16_t*)out);
+      if (f) k_affine_h<true, true><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, nrows, n, (uint16_t*)out);
+      else k_affine_h<true, false><<<grid, 256, 0, st>>>((U16)unit, (U16)minval, (U16)maxval, nrows, n, (uint16_t*)out);
   }
   JXR_CUDA(cudaGetLastError());
   return JXR_OK;
@@ -1633,7 +1662,7 @@ int jxr_sample(const uint32_t* keys, int64_t nkeys, uint64_t size, uint64_t begi
     using O = std::decay_t<decltype(op)>;
     if constexpr (std::is_same_v<typename O::Out, float>) {
       if (big)
-        if (const float* t = f32_table(1 + kind, op, st))
+        if (const float* t = f32_table(1 + kind))
           return launch_table(keys, nkeys, size, begin, count, layout, t, op, out, st);
     } else if constexpr (std::is_same_v<typename O::Out, uint16_t>) {
       return launch_h(keys, nkeys, size, begin, count, layout,
@@ -2371,10 +2400,66 @@ int jxr_free_caches(void) {
       g_tables16[dev][id] = nullptr;
     }
   }
+  {
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    g_static_scratch_addr[dev] = nullptr;
+  }
   HostCopyCtx& cx = g_host_ctx[dev];
   std::lock_guard<std::mutex> lock(cx.mu);
   cx.release();
   JXR_CUDA(cudaGetLastError());
+  return JXR_OK;
+}
+
+int jxr_prepare_device(uint32_t what, void* stream) {
+  if (what & ~(uint32_t)JXR_PREPARE_ALL)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "unknown bits 0x%x in what (JXR_PREPARE_ALL is 0x%x)",
+                what & ~(uint32_t)JXR_PREPARE_ALL, (unsigned)JXR_PREPARE_ALL);
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int dev = 0;
+  JXR_CUDA(cudaGetDevice(&dev));
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  JXR_CUDA(cudaStreamIsCapturing(st, &cap));
+  if (cap != cudaStreamCaptureStatusNone)
+    return fail(JXR_ERR_INVALID_ARGUMENT,
+                "jxr_prepare_device allocates and waits for its stream: call it outside stream "
+                "capture");
+  // Looking the array up makes the runtime load this library's module on the device now
+  // (CUDA loads modules lazily), which is when the module's fixed arrays are created; every
+  // call does this, whatever `what` asks for.
+  unsigned char* scratch = nullptr;
+  if ((rc = static_scratch(dev, &scratch))) return rc;
+  std::lock_guard<std::mutex> lock(g_tab_mu);
+  if (what & JXR_PREPARE_TABLE_NORMAL) {
+    if ((rc = build_f32_table(dev, 0, OpNormalF32T<false>{}, st)) ||
+        (rc = build_h16_table(dev, 2 * 4, OpNormalH<false, false>{}, st)) ||
+        (rc = build_h16_table(dev, 2 * 4 + 1, OpNormalH<true, false>{}, st)))
+      return rc;
+  }
+  if (what & JXR_PREPARE_TABLE_NORMAL_ACCURATE) {
+    if ((rc = build_f32_table(dev, kTableNormalAccurate, OpNormalF32T<true>{}, st)) ||
+        (rc = build_h16_table(dev, 2 * 5, OpNormalH<false, true>{}, st)) ||
+        (rc = build_h16_table(dev, 2 * 5 + 1, OpNormalH<true, true>{}, st)))
+      return rc;
+  }
+  for (int kind = 0; kind < 4; ++kind) {
+    if (!(what & ((uint32_t)JXR_PREPARE_TABLE_EXPONENTIAL << kind))) continue;
+    for (int dtype : {JXR_F32, JXR_F16, JXR_BF16}) {
+      rc = visit_sample_op(kind, dtype, [&](const auto& op) -> int {
+        using O = std::decay_t<decltype(op)>;
+        if constexpr (std::is_same_v<typename O::Out, float>)
+          return build_f32_table(dev, 1 + kind, op, st);
+        else if constexpr (std::is_same_v<typename O::Out, uint16_t>)
+          return build_h16_table(dev, 2 * kind + (dtype == JXR_BF16 ? 1 : 0), op, st);
+        else
+          return JXR_OK;
+      });
+      if (rc) return rc;
+    }
+  }
   return JXR_OK;
 }
 
@@ -2463,6 +2548,7 @@ int jxr_random_bits_host_static(const uint32_t* keys_host, int64_t nkeys, uint64
   int dev = 0;
   JXR_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(JXR_ERR_NO_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> call_lock(g_static_call_mu[dev]);
   unsigned char* scratch = nullptr;
   if ((rc = static_scratch(dev, &scratch))) return rc;
   uint32_t* dkeys = (uint32_t*)scratch;
@@ -2473,18 +2559,25 @@ int jxr_random_bits_host_static(const uint32_t* keys_host, int64_t nkeys, uint64
   // Everything is ordered on the caller's stream: the staging buffer is regenerated only
   // after the copy of the previous chunk out of it has run.
   JXR_CUDA(cudaMemcpyAsync(dkeys, keys_host, 8 * (size_t)nkeys, cudaMemcpyHostToDevice, st));
-  for (int64_t r = 0; r < nkeys; ++r) {
+  for (int64_t r = 0; r < nkeys && rc == JXR_OK; ++r) {
     for (uint64_t off = 0; off < count; off += chunk) {
       const uint64_t n = std::min(chunk, count - off);
       if ((rc = jxr_random_bits(dkeys + 2 * r, 1, size, begin + off, n, layout, bit_width, stage,
                                 stream)))
-        return rc;
+        break;
       char* dst = (char*)host_out + ((uint64_t)r * count + off) * esz;
-      JXR_CUDA(cudaMemcpyAsync(dst, stage, n * esz, cudaMemcpyDeviceToHost, st));
+      cudaError_t e = cudaMemcpyAsync(dst, stage, n * esz, cudaMemcpyDeviceToHost, st);
+      if (e != cudaSuccess) {
+        rc = fail(JXR_ERR_CUDA, "cudaMemcpyAsync: %s", cudaGetErrorString(e));
+        break;
+      }
     }
   }
-  JXR_CUDA(cudaStreamSynchronize(st));
-  return JXR_OK;
+  // also on failure: copies already queued into host_out finish before the call returns
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (rc == JXR_OK && e != cudaSuccess)
+    rc = fail(JXR_ERR_CUDA, "cudaStreamSynchronize: %s", cudaGetErrorString(e));
+  return rc;
 }
 
 // ---- device memory shared between the processes of one node (CUDA IPC) -------------------

@@ -9,7 +9,7 @@ samplers has no far-tail pieces, so the others are not used.  Results match the
 reference's only with these exact values, so they are read from its source as text, as
 tests/golden/make_golden.py reads the recorded samples; the header is committed.
 
-    python jaxr_b200/csrc/make_erfinv_tables.py [/root/reference]
+    python jaxr_b200/csrc/make_erfinv_tables.py JAXR_SOURCE_DIR   # or $JAXR_REFERENCE_DIR
 """
 
 from __future__ import annotations
@@ -48,7 +48,10 @@ def literal(v, single):
 
 
 def main(argv):
-    ref = argv[1] if len(argv) > 1 else "/root/reference"
+    ref = argv[1] if len(argv) > 1 else os.environ.get("JAXR_REFERENCE_DIR")
+    if not ref:
+        sys.exit(f"usage: {argv[0]} JAXR_SOURCE_DIR (or set $JAXR_REFERENCE_DIR): the root "
+                 "of the jaxR source tree to read")
     tables = read_tables(ref)
     lines = [
         "/* Coefficients of the accurate erf_inv (jax_accurate_erf_inv), lowest degree first:",

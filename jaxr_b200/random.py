@@ -131,6 +131,29 @@ def _ptr(t):
     return t.data_ptr()
 
 
+# Lookup tables that jxr_prepare_device has built in this process, per device index (bit
+# masks of JXR_PREPARE_TABLE_*).  The library's sampling entry points only read tables; this
+# host layer builds a sampler's tables the first time a request large enough to read them
+# comes, outside CUDA graph capture (building allocates and waits for the stream).
+_PREPARED = {}
+_TABLE_MIN = {"float32": 1 << 22, "float16": 1 << 16, "bfloat16": 1 << 16}
+_TABLE_BIT = {"normal": 1, "normal_accurate": 2, "exponential": 4, "gumbel": 8,
+              "logistic": 16, "laplace": 32}
+
+
+def _prepare_table(device, sampler, dt, n):
+    if n < _TABLE_MIN.get(dt, 1 << 63):
+        return
+    if sampler == "normal" and cfg.jax_config("jax_accurate_erf_inv"):
+        sampler = "normal_accurate"
+    bit = _TABLE_BIT[sampler]
+    done = _PREPARED.get(device.index, 0)
+    if done & bit or torch.cuda.is_current_stream_capturing():
+        return
+    nat.call("jxr_prepare_device", bit, _stream())
+    _PREPARED[device.index] = done | bit
+
+
 def shape_str(s):
     """The reference's prng_shape_str: (5,), (2, 3), ()."""
     s = tuple(int(v) for v in s)
@@ -643,6 +666,7 @@ def _k_normal(kd, size, dt, layout, shape=None):
     _check_size(size, layout)
     out = torch.empty(shape if shape is not None else (kd.shape[0], size),
                       dtype=_float_storage(dt), device=kd.device)
+    _prepare_table(kd.device, "normal", dt, kd.shape[0] * size)
     if _is_rbg(kd):
         bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
         nat.call("jxr_normal_from_bits", _ptr(bits), bits.numel(), _FLOAT_CODE[dt], _ptr(out),
@@ -659,9 +683,9 @@ def _k_bernoulli(kd, size, dt, p, layout):
     if _is_rbg(kd):
         u = _k_uniform(kd, size, dt, 0.0, 1.0, layout)
         pt = _broadcast_param(torch.tensor(float(p), dtype=torch.float64), (size,), dt, "bernoulli")
-        for r in range(kd.shape[0] if size else 0):
-            nat.call("jxr_bernoulli_from_uniform", _ptr(_raw16(u[r].contiguous(), dt)), None,
-                     _ptr(_raw16(pt, dt)), size, _FLOAT_CODE[dt], _ptr(out[r]), _stream())
+        pt = pt.expand(kd.shape[0], size).contiguous()  # every key row in one launch
+        nat.call("jxr_bernoulli_from_uniform", _ptr(_raw16(u.contiguous(), dt)), None,
+                 _ptr(_raw16(pt, dt)), kd.shape[0] * size, _FLOAT_CODE[dt], _ptr(out), _stream())
         return out.view(torch.bool)
     nat.call("jxr_bernoulli", _ptr(kd), kd.shape[0], size, 0, size, layout, _FLOAT_CODE[dt],
              float(p), _ptr(out), _stream())
@@ -781,9 +805,10 @@ def random_bits(key, shape=(), dtype=None):
 # ---- uniform / normal / bernoulli (R/random.R:278-304, :466-508, :643-666) -------------------
 
 def free_caches():
-    """Frees the current device's library caches (the float32 samplers' 32 MiB tables and
-    the host-copy staging buffers); later calls rebuild what they need."""
+    """Frees the current device's library caches (the samplers' tables, 32 MiB each for
+    float32, and the host-copy staging buffers); later calls rebuild what they need."""
     nat.call("jxr_free_caches")
+    _PREPARED.pop(torch.cuda.current_device(), None)
 
 
 def _uses_erf_inv(fn):
@@ -860,11 +885,10 @@ def random_uniform(key, shape=(), dtype=None, minval=0.0, maxval=1.0):
         mn = _broadcast_param(mn_t if mn_t is not None else torch.tensor(mn_s), shape, dt, "uniform")
         mx = _broadcast_param(mx_t if mx_t is not None else torch.tensor(mx_s), shape, dt, "uniform")
         out = torch.empty_like(unit)
-        n = size
-        for r in range(unit.shape[0] if n else 0):
-            nat.call("jxr_uniform_affine", _ptr(_raw16(unit[r], dt)), _ptr(_raw16(mn, dt)),
-                     _ptr(_raw16(mx, dt)), n, _FLOAT_CODE[dt], 0, _ptr(_raw16(out[r], dt)),
-                     _stream())
+        # one launch for every key row, each with the same row of bounds
+        nat.call("jxr_uniform_affine_rows", _ptr(_raw16(unit, dt)), _ptr(_raw16(mn, dt)),
+                 _ptr(_raw16(mx, dt)), unit.shape[0], size, _FLOAT_CODE[dt], 0,
+                 _ptr(_raw16(out, dt)), _stream())
     return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
 
 
@@ -939,11 +963,12 @@ def random_bernoulli(key, p=0.5, shape=None, mode="low"):
         u = _k_uniform(kd, 2 * size, dt, 0.0, 1.0, layout).reshape(kd.shape[0], 2, size)
         lo, hi = u[:, 0], u[:, 1]
     out = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
-    for r in range(kd.shape[0] if n else 0):
-        lo_r = _raw16(lo[r].contiguous(), dt)
-        hi_r = _raw16(hi[r].contiguous(), dt) if hi is not None else None
-        nat.call("jxr_bernoulli_from_uniform", _ptr(lo_r), _ptr(hi_r) if hi_r is not None else None,
-                 _ptr(_raw16(pt, dt)), n, _FLOAT_CODE[dt], _ptr(out[r]), _stream())
+    # every key row in one launch: p repeated per row, the draws' rows made contiguous
+    pt = pt.reshape(-1).expand(kd.shape[0], n).contiguous()
+    lo_c = _raw16(lo.contiguous(), dt)
+    hi_c = _raw16(hi.contiguous(), dt) if hi is not None else None
+    nat.call("jxr_bernoulli_from_uniform", _ptr(lo_c), _ptr(hi_c) if hi_c is not None else None,
+             _ptr(_raw16(pt, dt)), kd.shape[0] * n, _FLOAT_CODE[dt], _ptr(out), _stream())
     return _rebatch(out.view(torch.bool).reshape(bshape + shape), nb)
 
 
@@ -963,6 +988,7 @@ def random_normal_bernoulli(key, p=0.5, shape=(), dtype=None):
             key, torch.tensor(float(p), dtype=_TORCH[dt]), shape)
     nout = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
     bout = torch.empty((kd.shape[0], size), dtype=torch.uint8, device=kd.device)
+    _prepare_table(kd.device, "normal", dt, kd.shape[0] * size)
     nat.call("jxr_normal_bernoulli", _ptr(kd), kd.shape[0], size, 0, size, layout,
              _FLOAT_CODE[dt], float(p), _ptr(nout), _ptr(bout), _stream())
     bshape = k.shape[:nb]
@@ -978,6 +1004,7 @@ _SAMPLE_KIND = {"exponential": 0, "gumbel": 1, "logistic": 2, "laplace": 3}
 def _k_sample(kd, size, dt, kind, layout):
     _check_size(size, layout)
     out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
+    _prepare_table(kd.device, kind, dt, kd.shape[0] * size)
     if _is_rbg(kd):
         bits = _k_bits(kd, size, _DRAW_BITS[dt], layout)
         nat.call("jxr_sample_from_bits", _ptr(bits), bits.numel(), _SAMPLE_KIND[kind],
@@ -1038,9 +1065,12 @@ def random_gumbel(key, shape=(), dtype=None, mode=None):
             kd.shape[0], 2, size)
         code = 0
     out = torch.empty((kd.shape[0], size), dtype=_float_storage(dt), device=kd.device)
-    for r in range(kd.shape[0] if size else 0):
-        nat.call("jxr_gumbel_rows", _ptr(rows[r, 0]), _ptr(rows[r, 1]), size, code,
-                 _FLOAT_CODE[dt], _ptr(out[r]), _stream())
+    if kd.shape[0] == 1:
+        r0, r1 = rows[0, 0], rows[0, 1]
+    else:  # every key row in one launch: the two draws of each row gathered
+        r0, r1 = rows[:, 0].contiguous(), rows[:, 1].contiguous()
+    nat.call("jxr_gumbel_rows", _ptr(r0), _ptr(r1), kd.shape[0] * size, code, _FLOAT_CODE[dt],
+             _ptr(out), _stream())
     return _rebatch(_as_float_view(out, dt).reshape(k.shape[:nb] + shape), nb)
 
 
@@ -1091,10 +1121,12 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
                           "truncated_normal")
     unit = _k_uniform(kd, size, dt, 0.0, 1.0, layout)
     out = torch.empty_like(unit)
-    for r in range(kd.shape[0] if size else 0):
-        nat.call("jxr_truncated_normal_from_unit", _ptr(_raw16(unit[r], dt)),
-                 _ptr(_raw16(lo, dt)), 1, _ptr(_raw16(hi, dt)), 1, size, _FLOAT_CODE[dt],
-                 _ptr(_raw16(out[r], dt)), _stream())
+    if kd.shape[0] > 1:  # every key row in one launch: the bounds repeated per row
+        lo = lo.reshape(-1).expand(kd.shape[0], size).contiguous()
+        hi = hi.reshape(-1).expand(kd.shape[0], size).contiguous()
+    nat.call("jxr_truncated_normal_from_unit", _ptr(_raw16(unit, dt)), _ptr(_raw16(lo, dt)), 1,
+             _ptr(_raw16(hi, dt)), 1, kd.shape[0] * size, _FLOAT_CODE[dt], _ptr(_raw16(out, dt)),
+             _stream())
     return _rebatch(out.reshape(bshape + shape), nb)
 
 
@@ -1231,11 +1263,17 @@ def random_randint(key, shape, minval, maxval, dtype=None):
             nat.call("jxr_randint_combine", _ptr(hi), _ptr(lo), kd.shape[0] * size, sbits,
                      int(ssigned), _ptr(mn_t), 0, _ptr(mx_t), 0, _ptr(oor_t), 0, dbits,
                      _ptr(out), _stream())
-        else:
-            for r in range(kd.shape[0]):
-                nat.call("jxr_randint_combine", _ptr(hi[r]), _ptr(lo[r]), size, sbits,
-                         int(ssigned), _ptr(mn_t), mn_s, _ptr(mx_t), mx_s, _ptr(oor_t),
-                         int(oor_t.numel() != 1), dbits, _ptr(out[r]), _stream())
+        else:  # every key row in one launch: per-element parameters repeated per row
+            nrows = kd.shape[0]
+            oor_s = int(oor_t.numel() != 1)
+
+            def rows(t, stride):
+                return t.reshape(-1).expand(nrows, size).contiguous() if stride and nrows > 1 else t
+
+            mn_r, mx_r, oor_r = rows(mn_t, mn_s), rows(mx_t, mx_s), rows(oor_t, oor_s)
+            nat.call("jxr_randint_combine", _ptr(hi), _ptr(lo), nrows * size, sbits,
+                     int(ssigned), _ptr(mn_r), mn_s, _ptr(mx_r), mx_s, _ptr(oor_r), oor_s, dbits,
+                     _ptr(out), _stream())
     return _rebatch(out.reshape(k.shape[:nb] + shape), nb)
 
 

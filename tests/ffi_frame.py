@@ -128,9 +128,10 @@ class Runtime:
         self.api.Stream_Get = C.cast(stream_get, C.c_void_p)
 
     def call(self, handler, key, out, attrs=(), stage=STAGE_EXECUTE, metadata=None):
-        """Call `handler` with one argument buffer and one result buffer, each a tuple
-        (dtype, data pointer, dims), and scalar attributes [(name, dtype, ctypes value)]
-        sorted by name as XLA sorts them."""
+        """Call `handler` with one argument buffer and the result buffer(s) `out` (one
+        tuple, or a list of tuples for several results), each a tuple (dtype, data
+        pointer, dims), and scalar attributes [(name, dtype, ctypes value)] sorted by name
+        as XLA sorts them."""
         keep = []
 
         def buf(spec):
@@ -146,10 +147,11 @@ class Runtime:
         f.stage = stage
         at = (C.c_int * 1)(ARG_BUFFER)
         av = (C.c_void_p * 1)(buf(key))
-        rt = (C.c_int * 1)(RET_BUFFER)
-        rv = (C.c_void_p * 1)(buf(out))
+        outs = out if isinstance(out, list) else [out]
+        rt = (C.c_int * len(outs))(*([RET_BUFFER] * len(outs)))
+        rv = (C.c_void_p * len(outs))(*[buf(o) for o in outs])
         f.args = Args(C.sizeof(Args), None, 1, at, av)
-        f.rets = Args(C.sizeof(Args), None, 1, rt, rv)
+        f.rets = Args(C.sizeof(Args), None, len(outs), rt, rv)
         attrs = sorted(attrs)
         n = len(attrs)
         tt = (C.c_int * max(n, 1))(*([ATTR_SCALAR] * n))
@@ -175,10 +177,13 @@ class Runtime:
             raise FfiError(code, msg)
 
 
+HANDLERS = ("jxr_ffi_random_bits", "jxr_ffi_random_bits_cpu", "jxr_ffi_uniform", "jxr_ffi_normal",
+            "jxr_ffi_bernoulli", "jxr_ffi_normal_bernoulli")
+
+
 def load():
     lib = C.CDLL(FFI_LIB)
-    for name in ("jxr_ffi_random_bits", "jxr_ffi_random_bits_cpu", "jxr_ffi_uniform",
-                 "jxr_ffi_normal"):
+    for name in HANDLERS:
         fn = getattr(lib, name)
         fn.argtypes = [C.c_void_p]
         fn.restype = C.c_void_p

@@ -1,9 +1,9 @@
 """Extract the reference's golden vectors for the threefry path into a JSON fixture.
 
-Run in a container that has the jaxR sources at /root/reference (the GPU box does
-not; the fixture this writes is committed):
+Run where the jaxR sources are available (the fixture this writes is committed, so the
+tests do not need them):
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py JAXR_SOURCE_DIR   # or $JAXR_REFERENCE_DIR
 
 The expected values are read from the reference's own tests as text (they were
 produced there by jax 0.12.0.1 on CPU): tests/testthat/test-prng.R,
@@ -490,7 +490,10 @@ def _normalise_specials(cases):
 
 
 def main(argv):
-    ref = argv[1] if len(argv) > 1 else "/root/reference"
+    ref = argv[1] if len(argv) > 1 else os.environ.get("JAXR_REFERENCE_DIR")
+    if not ref:
+        sys.exit(f"usage: {argv[0]} JAXR_SOURCE_DIR (or set $JAXR_REFERENCE_DIR): the root "
+                 "of the jaxR source tree to read")
     cases = _normalise_specials(build(ref))
     meta = {"generated_by": "tests/golden/make_golden.py",
             "reference": "jaxR (adamrsophie/jaxR); values produced there by jax 0.12.0.1 on CPU",
