@@ -88,9 +88,10 @@ int jxr_get_accurate_erf_inv(void);
  * device, before any stream capture and before a host framework reserves the GPU for its
  * own memory pool.  Synchronous: waits for `stream`; refused (JXR_ERR_INVALID_ARGUMENT)
  * while `stream` is being captured into a CUDA graph.
- *  - Every call loads this library's module on the device (CUDA loads modules lazily,
- *    on first use) and looks up the array of jxr_random_bits_host_static: the module's
- *    code and its fixed 16 MiB + 32 KiB array are created then, not inside a later call.
+ *  - Every call loads this library's module on the device (CUDA loads modules and their
+ *    kernels lazily, on first use), looks up the array of jxr_random_bits_host_static and
+ *    loads every kernel that entry point launches: the module's fixed 16 MiB + 32 KiB
+ *    array and that code are created then, not inside a later call.
  *  - `what` (JXR_PREPARE_* bits, 0 for none) names the samplers whose lookup tables to
  *    build: per sampler a float32 table of its 2^23 possible results (32 MiB) and the
  *    float16 / bfloat16 tables of its 1024 / 128 results (2 KiB + 256 B).  Every float32
@@ -390,8 +391,8 @@ int jxr_ipc_close(void* base);
  *    entry point is that first use, the module (its code and this array) is created
  *    inside the call, i.e. allocated.  So call jxr_prepare_device once per device at
  *    set-up, before the framework reserves its memory pool and before any stream capture:
- *    it loads the module and looks up the array's device address
- *    (cudaGetSymbolAddress).  Otherwise the first call on a device does that look-up.
+ *    it loads the module and this entry point's kernels and looks up the array's device
+ *    address (cudaGetSymbolAddress).  Otherwise the first call on a device does that.
  *  - Every call on a device shares the one array, which keeps the last call's contents
  *    (nothing in it needs to start at zero: keys and staging are rewritten before they
  *    are read).  Calls that overlap on the GPU would race on it; the library holds a lock

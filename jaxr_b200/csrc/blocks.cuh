@@ -102,6 +102,32 @@ struct DirectOutputsOf<Op, std::void_t<decltype(Op::kDirect)>> {
   static constexpr int value = Op::kDirect;
 };
 
+// Ops with kBatch (the float64 normal) transform a thread's N draws at once (op.batch<N>)
+// in the bulk kernels' full tiles; others one draw at a time.
+template <class Op, class = void>
+struct BatchOf {
+  static constexpr bool value = false;
+};
+template <class Op>
+struct BatchOf<Op, std::void_t<decltype(Op::kBatch)>> {
+  static constexpr bool value = Op::kBatch;
+};
+
+// out[k] = the op's value of draw k, k < N, through op.batch where the op has it
+template <int N, class Op>
+__device__ __forceinline__ void apply_all(const Op& op, const uint32_t* x0, const uint32_t* x1,
+                                          typename Op::Out* out) {
+  if constexpr (BatchOf<Op>::value) {
+    typename Op::Bits b[N];
+#pragma unroll
+    for (int k = 0; k < N; ++k) b[k] = Draw<Op::kBits>::get(x0[k], x1[k]);
+    op.template batch<N>(b, out);
+  } else {
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[k] = apply(op, x0[k], x1[k]);
+  }
+}
+
 template <class Op>
 __device__ __forceinline__ typename Op::Out apply_direct(const Op& op, uint32_t x0, uint32_t x1) {
   if constexpr (DirectOutputsOf<Op>::value > 0) return op.direct(Draw<Op::kBits>::get(x0, x1));
@@ -172,11 +198,13 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
       for (int g = 0; g < G; ++g) *reinterpret_cast<uint4*>(dst + g * kThreads * V) = r[g].u;
     } else if (vec_ok && p0 + TILE <= count) {
+      Out o[N];
+      apply_all<N>(op, x0, x1, o);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         Vec16<Out> r;
 #pragma unroll
-        for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g * V + v], x1[g * V + v]);
+        for (int v = 0; v < V; ++v) r.v[v] = o[g * V + v];
         *reinterpret_cast<uint4*>(dst + g * kThreads * V) = r.u;
       }
     } else {
@@ -263,11 +291,13 @@ __global__ void __launch_bounds__(kThreads)
       for (int g = 0; g < G; ++g)
         *reinterpret_cast<uint4*>(orow + p0 + loff + g * 32 * V) = r[g].u;
     } else if (vec_ok && p0 + WT <= count) {
+      Out o[N];
+      apply_all<N>(op, x0, x1, o);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         Vec16<Out> r;
 #pragma unroll
-        for (int v = 0; v < V; ++v) r.v[v] = apply(op, x0[g * V + v], x1[g * V + v]);
+        for (int v = 0; v < V; ++v) r.v[v] = o[g * V + v];
         *reinterpret_cast<uint4*>(orow + p0 + loff + g * 32 * V) = r.u;
       }
     } else {

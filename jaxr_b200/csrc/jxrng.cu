@@ -1163,7 +1163,7 @@ int small_grid(int64_t n, int* grid) {
 constexpr int kNBBytes = 32;  // normal bytes per thread and iteration of k_normal_bernoulli
 
 template <class OpN, class OpB, int kCtr, bool kOneKey>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 6)
     k_normal_bernoulli(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
                        uint64_t count, uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, OpN opn,
                        OpB opb, PipeConsts pc, typename OpN::Out* __restrict__ nout,
@@ -1185,19 +1185,30 @@ __global__ void __launch_bounds__(kThreads)
     threefry20<V, ProductMix>(s, x0, x1, pc);
     Vec16<Out> r[2];
     uint8_t bb[V];
+    Out o[V];
+    apply_all<V>(opn, x0, x1, o);  // every draw's normal (OpN::batch where it has one)
 #pragma unroll
     for (int v = 0; v < V; ++v) {
-      const auto bits = Draw<OpN::kBits>::get(x0[v], x1[v]);
-      r[v / (V / 2)].v[v % (V / 2)] = opn(bits);
-      bb[v] = opb(bits);
+      r[v / (V / 2)].v[v % (V / 2)] = o[v];
+      bb[v] = opb(Draw<OpB::kBits>::get(x0[v], x1[v]));
     }
     Out* dst = nout + row * count + pos;
     uint8_t* bdst = bout + row * count + pos;
     if (vec_ok && pos + V <= count) {
       reinterpret_cast<uint4*>(dst)[0] = r[0].u;
       reinterpret_cast<uint4*>(dst)[1] = r[1].u;
+      if (vec_ok & 2) {  // the V flags as one V-byte store
+        uint32_t w[V / 4];
 #pragma unroll
-      for (int v = 0; v < V; ++v) bdst[v] = bb[v];
+        for (int q = 0; q < V / 4; ++q)
+          w[q] = bb[4 * q] | (bb[4 * q + 1] << 8) | (bb[4 * q + 2] << 16) |
+                 ((uint32_t)bb[4 * q + 3] << 24);
+        if constexpr (V == 4) *reinterpret_cast<uint32_t*>(bdst) = w[0];
+        else *reinterpret_cast<uint2*>(bdst) = make_uint2(w[0], w[1]);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v) bdst[v] = bb[v];
+      }
     } else {
 #pragma unroll
       for (int v = 0; v < V; ++v)
@@ -1215,7 +1226,11 @@ int launch_normal_bernoulli(const uint32_t* keys, int64_t nkeys, uint64_t size, 
   if (count == 0 || nkeys == 0) return JXR_OK;
   const uint64_t cpr = (count + V - 1) / V;
   const uint64_t nchunks = cpr * (uint64_t)nkeys;
-  const int vec_ok = ((uintptr_t)nout % 16 == 0) && (nkeys == 1 || (count * sizeof(Out)) % 16 == 0);
+  // a chunk is two 16-byte stores of normals (the kernel writes r[0] and r[1])
+  static_assert(kNBBytes == 32 && (V == 4 || V == 8), "32-byte chunks of 4 or 8 outputs");
+  // bit 0: 16-byte normal stores; bit 1: also the V flag bytes as one store
+  int vec_ok = ((uintptr_t)nout % 16 == 0) && (nkeys == 1 || (count * sizeof(Out)) % 16 == 0);
+  if (vec_ok && (uintptr_t)bout % V == 0 && (nkeys == 1 || count % V == 0)) vec_ok |= 2;
   const uint64_t ctas = (nchunks + kThreads - 1) / kThreads;
   int grid = 0, rc;
 #define JXR_NB_LAUNCH(CTR, ONE)                                                              \
@@ -1280,6 +1295,20 @@ static std::mutex g_static_scratch_mu;
 // Held for the whole of a jxr_random_bits_host_static call on that device: calls from
 // several host threads take turns, so they cannot overlap on the GPU through the array.
 static std::mutex g_static_call_mu[64];
+
+// Loads, on the current device, every kernel that jxr_random_bits_host_static can launch
+// for bit width W: CUDA loads a module's functions lazily, on first use, which allocates
+// their code on the device; querying a function's attributes loads it now.
+template <int W>
+static int preload_bits_kernels() {
+  using Op = OpBits<W>;
+  cudaFuncAttributes a;
+  JXR_CUDA(cudaFuncGetAttributes(&a, (const void*)k_blocks_1key<Op, kCtrIndex>));
+  JXR_CUDA(cudaFuncGetAttributes(&a, (const void*)k_original_segmented<Op>));
+  if constexpr (W == 64) JXR_CUDA(cudaFuncGetAttributes(&a, (const void*)k_blocks_1key<Op, kCtrPair>));
+  else JXR_CUDA(cudaFuncGetAttributes(&a, (const void*)k_words<Op>));
+  return JXR_OK;
+}
 
 static int static_scratch(int dev, unsigned char** out) {
   std::lock_guard<std::mutex> lock(g_static_scratch_mu);
@@ -2428,10 +2457,14 @@ int jxr_prepare_device(uint32_t what, void* stream) {
                 "jxr_prepare_device allocates and waits for its stream: call it outside stream "
                 "capture");
   // Looking the array up makes the runtime load this library's module on the device now
-  // (CUDA loads modules lazily), which is when the module's fixed arrays are created; every
-  // call does this, whatever `what` asks for.
+  // (CUDA loads modules lazily), which is when the module's fixed arrays are created, and
+  // the kernels of jxr_random_bits_host_static are loaded too; every call does this,
+  // whatever `what` asks for.
   unsigned char* scratch = nullptr;
-  if ((rc = static_scratch(dev, &scratch))) return rc;
+  if ((rc = static_scratch(dev, &scratch)) || (rc = preload_bits_kernels<8>()) ||
+      (rc = preload_bits_kernels<16>()) || (rc = preload_bits_kernels<32>()) ||
+      (rc = preload_bits_kernels<64>()))
+    return rc;
   std::lock_guard<std::mutex> lock(g_tab_mu);
   if (what & JXR_PREPARE_TABLE_NORMAL) {
     if ((rc = build_f32_table(dev, 0, OpNormalF32T<false>{}, st)) ||

@@ -22,6 +22,7 @@
 #include <cuda_fp16.h>
 
 #include "erfinv_tables.h"
+#include "log_table.h"
 
 namespace jxr {
 
@@ -126,35 +127,42 @@ __device__ __forceinline__ float erfinv_f32(float x) {
   return __fmul_rn(p, x);
 }
 
-__device__ __forceinline__ double erfinv_f64(double x) {
-  const double w0 = -log1p_neg(-__dmul_rn(x, x));
+// Giles' float64 erf_inv: p(w0) with erf_inv(x) = p x, for w0 = -log1p(-x*x).  The central
+// piece (w0 < 6.25, i.e. |x| < 0.99903: all but about 1e-3 of a normal sampler's draws) and
+// the two tail pieces are separate functions so that a kernel can evaluate several draws'
+// central pieces in one branch-free stretch and the tails only where needed.
+__device__ __forceinline__ double giles_f64_central(double w0) {
+  double p;
+  const double w = __dsub_rn(w0, 3.125);
+  p = -3.6444120640178196996e-21;
+  p = __fma_rn(p, w, -1.685059138182016589e-19);
+  p = __fma_rn(p, w, 1.2858480715256400167e-18);
+  p = __fma_rn(p, w, 1.115787767802518096e-17);
+  p = __fma_rn(p, w, -1.333171662854620906e-16);
+  p = __fma_rn(p, w, 2.0972767875968561637e-17);
+  p = __fma_rn(p, w, 6.6376381343583238325e-15);
+  p = __fma_rn(p, w, -4.0545662729752068639e-14);
+  p = __fma_rn(p, w, -8.1519341976054721522e-14);
+  p = __fma_rn(p, w, 2.6335093153082322977e-12);
+  p = __fma_rn(p, w, -1.2975133253453532498e-11);
+  p = __fma_rn(p, w, -5.4154120542946279317e-11);
+  p = __fma_rn(p, w, 1.051212273321532285e-09);
+  p = __fma_rn(p, w, -4.1126339803469836976e-09);
+  p = __fma_rn(p, w, -2.9070369957882005086e-08);
+  p = __fma_rn(p, w, 4.2347877827932403518e-07);
+  p = __fma_rn(p, w, -1.3654692000834678645e-06);
+  p = __fma_rn(p, w, -1.3882523362786468719e-05);
+  p = __fma_rn(p, w, 0.0001867342080340571352);
+  p = __fma_rn(p, w, -0.00074070253416626697512);
+  p = __fma_rn(p, w, -0.0060336708714301490533);
+  p = __fma_rn(p, w, 0.24015818242558961693);
+  p = __fma_rn(p, w, 1.6536545626831027356);
+  return p;
+}
+
+__device__ __forceinline__ double giles_f64_tail(double w0) {
   double p, w;
-  if (w0 < 6.25) {
-    w = __dsub_rn(w0, 3.125);
-    p = -3.6444120640178196996e-21;
-    p = __fma_rn(p, w, -1.685059138182016589e-19);
-    p = __fma_rn(p, w, 1.2858480715256400167e-18);
-    p = __fma_rn(p, w, 1.115787767802518096e-17);
-    p = __fma_rn(p, w, -1.333171662854620906e-16);
-    p = __fma_rn(p, w, 2.0972767875968561637e-17);
-    p = __fma_rn(p, w, 6.6376381343583238325e-15);
-    p = __fma_rn(p, w, -4.0545662729752068639e-14);
-    p = __fma_rn(p, w, -8.1519341976054721522e-14);
-    p = __fma_rn(p, w, 2.6335093153082322977e-12);
-    p = __fma_rn(p, w, -1.2975133253453532498e-11);
-    p = __fma_rn(p, w, -5.4154120542946279317e-11);
-    p = __fma_rn(p, w, 1.051212273321532285e-09);
-    p = __fma_rn(p, w, -4.1126339803469836976e-09);
-    p = __fma_rn(p, w, -2.9070369957882005086e-08);
-    p = __fma_rn(p, w, 4.2347877827932403518e-07);
-    p = __fma_rn(p, w, -1.3654692000834678645e-06);
-    p = __fma_rn(p, w, -1.3882523362786468719e-05);
-    p = __fma_rn(p, w, 0.0001867342080340571352);
-    p = __fma_rn(p, w, -0.00074070253416626697512);
-    p = __fma_rn(p, w, -0.0060336708714301490533);
-    p = __fma_rn(p, w, 0.24015818242558961693);
-    p = __fma_rn(p, w, 1.6536545626831027356);
-  } else if (w0 < 16.0) {
+  if (w0 < 16.0) {
     w = __dsub_rn(__dsqrt_rn(w0), 3.25);
     p = 2.2137376921775787049e-09;
     p = __fma_rn(p, w, 9.0756561938885390979e-08);
@@ -195,8 +203,62 @@ __device__ __forceinline__ double erfinv_f64(double x) {
     p = __fma_rn(p, w, 1.0103004648645343977);
     p = __fma_rn(p, w, 4.8499064014085844221);
   }
-  if (fabs(x) == 1.0) return __dmul_rn(x, __longlong_as_double(0x7FF0000000000000ll));
+  return p;
+}
+
+__device__ __forceinline__ double erfinv_f64_w(double x, double w0) {
+  double p;
+  if (w0 < 6.25) p = giles_f64_central(w0);
+  else p = giles_f64_tail(w0);
   return __dmul_rn(p, x);
+}
+
+__device__ __forceinline__ double erfinv_f64(double x) {
+  const double w0 = -log1p_neg(-__dmul_rn(x, x));
+  if (fabs(x) == 1.0) return __dmul_rn(x, __longlong_as_double(0x7FF0000000000000ll));
+  return erfinv_f64_w(x, w0);
+}
+
+// ---- the float64 normal sampler's logarithm ----------------------------------------------
+//
+// -log(t) for a normal number t in (0, 1], table-driven (P. T. P. Tang, "Table-driven
+// implementation of the logarithm function in IEEE floating-point arithmetic", ACM TOMS
+// 16(4), 1990): t = 2^k z with z in [0.75, 1.5), the top 7 bits of z above 0.75 pick
+// (inv, -log inv) with inv ~ 1 / z (log_table.h, made by make_log_table.py), and
+// log t = k log 2 - log inv + log1p(z inv - 1), |z inv - 1| < 2^-8, the log1p a degree-7
+// Taylor polynomial.  Integer work, one 16-byte L1-resident load and 11 float64
+// operations, against ~27 float64 operations and 6 conversions or reciprocals of
+// log1p_neg: the float64 normal sampler spends most of its time here.  Its absolute error
+// is below 4e-16 (1 + |log t|), which moves a float64 normal by far less than the 1e-12
+// relative that normals are held to; it is not bit-identical with log1p_neg.
+__device__ const double2 kLogTabF64[JXR_LOG_TABLE_N] = {JXR_LOG_TABLE};
+
+__device__ __forceinline__ double neg_log_tab(double t) {
+  const uint32_t hi = (uint32_t)__double2hiint(t), lo = (uint32_t)__double2loint(t);
+  const int k = (int)(hi - 0x3FE80000u) >> 20;  // arithmetic shift: z = t 2^-k in [0.75, 1.5)
+  const uint32_t zhi = hi - ((uint32_t)k << 20);
+  const double z = __hiloint2double((int)zhi, (int)lo);
+  const double2 e = __ldg(&kLogTabF64[(zhi - 0x3FE80000u) >> 13]);
+  const double r = __fma_rn(z, e.x, -1.0);
+  double p = 0x1.2492492492492p-3;            //  1/7
+  p = __fma_rn(p, r, -0x1.5555555555555p-3);  // -1/6
+  p = __fma_rn(p, r, 0x1.999999999999ap-3);   //  1/5
+  p = __fma_rn(p, r, -0.25);
+  p = __fma_rn(p, r, 0x1.5555555555555p-2);   //  1/3
+  p = __fma_rn(p, r, -0.5);
+  const double l1p = __fma_rn(__dmul_rn(r, r), p, r);
+  // k as a double without a conversion instruction: (2^52 + 2^31 + k) - (2^52 + 2^31)
+  const double kd =
+      __dsub_rn(__hiloint2double(0x43300000, (int)(0x80000000u + (uint32_t)k)), 0x1.000008p52);
+  const double LN2_HI = 0x1.62e42fefa3800p-1, LN2_LO = 0x1.ef35793c76730p-45;
+  return -__fma_rn(kd, LN2_HI, __fma_rn(kd, LN2_LO, __dadd_rn(e.y, l1p)));
+}
+
+// erf_inv of the default lowering for |x| < 1 (the normal sampler's open interval), with
+// w = -log(1 - x*x) from neg_log_tab: x*x is rounded as the reference rounds it, and
+// 1 - x*x is exact where it matters (x*x >= 1/2).
+__device__ __forceinline__ double erfinv_f64_open(double x) {
+  return erfinv_f64_w(x, neg_log_tab(__dsub_rn(1.0, __dmul_rn(x, x))));
 }
 
 // ---- accurate erf_inv (jax_accurate_erf_inv; R/lax_special.R:1022-1082) -----------------
@@ -435,7 +497,36 @@ struct OpNormalF64T {
   __device__ __forceinline__ Out operator()(Bits b) const {
     const double lo = -0x1.fffffffffffffp-1;  // -1 + 2^-53
     const double u = xla_max(lo, __fma_rn(unit_f64(b), 2.0, lo));
-    return __dmul_rn(1.4142135623730951, erfinv64<kAcc>(u));
+    // |u| < 1: the default erf_inv takes its logarithm from neg_log_tab
+    if constexpr (kAcc) return __dmul_rn(1.4142135623730951, erfinv_acc_f64(u));
+    else return __dmul_rn(1.4142135623730951, erfinv_f64_open(u));
+  }
+  // N draws at once (default erf_inv): the uniforms and logarithms, then every draw's
+  // central piece in one branch-free stretch -- N independent polynomial chains that the
+  // scheduler interleaves, where one branch per draw would run them one after another --
+  // and the tail piece only where a draw needs it.  The same operations as operator(),
+  // so the same results.
+  static constexpr bool kBatch = !kAcc;
+  template <int N>
+  __device__ __forceinline__ void batch(const Bits* b, Out* out) const {
+    const double lo = -0x1.fffffffffffffp-1;
+    double u[N], w[N];
+    bool tail = false;
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      u[k] = xla_max(lo, __fma_rn(unit_f64(b[k]), 2.0, lo));
+      w[k] = neg_log_tab(__dsub_rn(1.0, __dmul_rn(u[k], u[k])));
+      tail |= !(w[k] < 6.25);
+    }
+#pragma unroll
+    for (int k = 0; k < N; ++k)
+      out[k] = __dmul_rn(1.4142135623730951, __dmul_rn(giles_f64_central(w[k]), u[k]));
+    if (tail) {
+#pragma unroll
+      for (int k = 0; k < N; ++k)
+        if (!(w[k] < 6.25))
+          out[k] = __dmul_rn(1.4142135623730951, __dmul_rn(giles_f64_tail(w[k]), u[k]));
+    }
   }
 };
 using OpNormalF64 = OpNormalF64T<false>;

@@ -291,16 +291,21 @@ def test_samplers_inside_a_cuda_graph():
 @pytest.mark.parametrize("dt", ["complex64", "complex128"])
 @pytest.mark.parametrize("part", [True, False])
 def test_complex_normal_exact(dt, part):
-    """Complex normals (R/random.R:489-499): both components bit-exact against the oracle's
-    split-then-divide-by-sqrt(2), at an odd size with a ragged tail (and the f32 size above
-    the sampler table's threshold, so the real parts come from the table path)."""
+    """Complex normals (R/random.R:489-499) against the oracle's split-then-divide-by-
+    sqrt(2), at an odd size with a ragged tail (and the f32 size above the sampler table's
+    threshold, so the real parts come from the table path): complex64 components
+    bit-exact, complex128 ones within the float64 normal's 1e-12 relative."""
     key = orc.seed(31)
     for n in (1, 7, 1001, (1 << 22) + 5):
         with flags(dt == "complex128", part):
             got = to_np(jr.random_normal(dev_key(key), (n,), dt))
         want = orc.complex_normal(key, dt, n, part)
         assert got.dtype == want.dtype
-        assert np.array_equal(got.view(got.real.dtype), want.view(want.real.dtype)), (dt, n)
+        g, w = got.view(got.real.dtype), want.view(want.real.dtype)
+        if dt == "complex64":
+            assert np.array_equal(g, w), (dt, n)
+        else:
+            assert np.all(np.abs(g - w) <= 1e-12 * np.abs(w)), (dt, n)
 
 
 def test_complex_normal_key_batches():
