@@ -529,6 +529,10 @@ def run_ours(args):
     ms = e0.elapsed_time(e1) / args.steps
     ms_max = max_over_ranks(ms)
     value = TOTAL / (ms_max * 1e-3)
+    per_rank = None
+    if world > 1:  # every rank's step time and clocks, for the line (rank 0 prints)
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, {"rank": rank, "ms_per_step": ms, "clocks": clocks})
 
     # roofline of the kernel on this GPU: cipher blocks/s against the register-resident
     # cipher's ceiling, and output bytes/s against measured HBM bandwidth
@@ -539,10 +543,11 @@ def run_ours(args):
         hbm_peak = json.load(open(PEAKS))["hbm_gbs"]
     except (OSError, ValueError, KeyError):
         pass
-    traffic = None
+    traffic, evidence = None, None
     try:
         tr = json.load(open(TRAFFIC))["bits_u32"]
         traffic = tr["dram_bytes_per_word"] * (hi - lo)
+        evidence = tr.get("ncu")
     except (OSError, ValueError, KeyError):
         pass
     roofline = {
@@ -553,6 +558,9 @@ def run_ours(args):
         "ops_per_block": OPS_PER_BLOCK,
         "peak_source": "measured: jxr_probe_cipher (threefry20 in registers, no memory), this GPU",
         "traffic": traffic,
+        # why frac is a true fraction of the integer pipes, independent of the probe: the
+        # kernel's own ncu counters (ALU pipe, issue slots, instructions per word)
+        "ncu_evidence": evidence,
         "hbm": {"achieved": my_blocks * 4 / 1e9, "peak": hbm_peak, "unit": "GB/s",
                 "frac": (my_blocks * 4 / 1e9 / hbm_peak) if hbm_peak else None,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
@@ -648,6 +656,14 @@ def run_ours(args):
         }
         if gather is not None:
             line["gather"] = gather
+        if per_rank is not None:
+            line["nranks"] = world
+            line["per_rank"] = per_rank
+            # the run's clocks: every rank's sampled median, and every reason any rank saw
+            line["clocks"] = dict(clocks or {}, sm_mhz_per_rank=[(r["clocks"] or {}).get("sm_mhz")
+                                                                 for r in per_rank],
+                                  reasons=sorted({x for r in per_rank
+                                                  for x in ((r["clocks"] or {}).get("reasons") or [])}))
         emit(line)
     del out
     if world > 1:

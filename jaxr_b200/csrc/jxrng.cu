@@ -1163,7 +1163,7 @@ int small_grid(int64_t n, int* grid) {
 constexpr int kNBBytes = 32;  // normal bytes per thread and iteration of k_normal_bernoulli
 
 template <class OpN, class OpB, int kCtr, bool kOneKey>
-__global__ void __launch_bounds__(kThreads, 6)
+__global__ void __launch_bounds__(kThreads)
     k_normal_bernoulli(const uint32_t* __restrict__ keys, uint64_t size, uint64_t begin,
                        uint64_t count, uint64_t chunks_per_row, uint64_t nchunks, int vec_ok, OpN opn,
                        OpB opb, PipeConsts pc, typename OpN::Out* __restrict__ nout,
