@@ -848,16 +848,46 @@ def _param(x, dt):
     return None, t
 
 
-def _broadcast_param(t, shape, dt, name):
+def _batch_rows(nb, kbshape, params, shape, dt, name):
+    """Sampler parameters batched under vmap (the reference's vmap batches every primitive
+    argument, R/batching.R:22-50): params are (value, batch axes) pairs.  Every batched
+    value must carry the key's batch axes (or, with an unbatched key, all the same ones),
+    which give the batch shape B.  Returns (levels, B, rows) with rows the parameters, each
+    broadcast per lane to `shape` and laid out as a contiguous (prod(B), size) tensor of
+    dt."""
+    levels = max([nb] + [pb for _, pb in params])
+    if any(pb not in (0, levels) for _, pb in params) or (nb not in (0, levels)):
+        raise JaxNotImplementedError("vmap: sampler parameters batched at other levels than the key")
+    bshapes = [tuple(v.shape[:pb]) for v, pb in params if pb]
+    B = tuple(kbshape) if nb else bshapes[0]
+    if any(b != B for b in bshapes):
+        raise JaxValueError(f"vmap got inconsistent sizes for the mapped axis: {sorted(set(bshapes))}")
+    nrows, size = _size(B), _size(shape)
+    rows = []
+    for v, pb in params:
+        t = v if isinstance(v, torch.Tensor) else torch.as_tensor(np.asarray(v, dtype=np.float64))
+        lane = tuple(t.shape[pb:])
+        _check_param_shape(lane, shape, name)  # the per-lane shape rule
+        t = t.to(torch.float64).to(_device()).to(_TORCH[dt])
+        t = t.reshape((B if pb else ()) + (1,) * (len(shape) - len(lane)) + lane)
+        rows.append(t.expand(B + tuple(shape)).reshape(nrows, size).contiguous())
+    return levels, B, rows
+
+
+def _check_param_shape(pshape, shape, name):
     try:
-        b = torch.broadcast_shapes(tuple(t.shape), shape)
+        b = torch.broadcast_shapes(tuple(pshape), shape)
     except RuntimeError:
         b = None
     if b != tuple(shape):
         raise JaxValueError(
             f"{name} parameter shapes must be broadcast-compatible with shape argument, and the "
             "result of broadcasting the shapes must equal the shape argument, but got result "
-            f"{shape_str(b or t.shape)} for shape argument {shape_str(shape)}.")
+            f"{shape_str(b or tuple(pshape))} for shape argument {shape_str(shape)}.")
+
+
+def _broadcast_param(t, shape, dt, name):
+    _check_param_shape(t.shape, shape, name)
     # convert in double then to the dtype (one rounding), as lax_convert_element_type
     t64 = t.to(torch.float64).to(_device())
     conv = t64.to(_TORCH[dt])
@@ -875,6 +905,18 @@ def random_uniform(key, shape=(), dtype=None, minval=0.0, maxval=1.0):
     shape = canon_shape(shape)
     size = _size(shape)
     kd = _flat_keys(k)
+    (mnv, mnb), (mxv, mxb) = _unbatch(minval), _unbatch(maxval)
+    if mnb or mxb:  # bounds batched under vmap: one row of bounds per lane
+        levels, B, (mn, mx) = _batch_rows(nb, k.shape[:nb], [(mnv, mnb), (mxv, mxb)], shape, dt,
+                                          "uniform")
+        unit = _k_uniform(kd, size, dt, 0.0, 1.0, _layout())
+        if unit.shape[0] != mn.shape[0]:  # an unbatched key: every lane draws the same
+            unit = unit.expand(mn.shape[0], size).contiguous()
+        out = torch.empty_like(unit)
+        nat.call("jxr_uniform_affine", _ptr(_raw16(unit, dt)), _ptr(_raw16(mn, dt)),
+                 _ptr(_raw16(mx, dt)), unit.numel(), _FLOAT_CODE[dt], 0, _ptr(_raw16(out, dt)),
+                 _stream())
+        return _rebatch(out.reshape(B + shape), levels)
     mn_s, mn_t = _param(minval, dt)
     mx_s, mx_t = _param(maxval, dt)
     if mn_t is None and mx_t is None:
@@ -944,6 +986,29 @@ def random_bernoulli(key, p=0.5, shape=None, mode="low"):
         dt = default_float()  # an R number: weak float of the default width
     if not _is_float(dt):
         raise JaxTypeError(f"bernoulli probability `p` must have a floating dtype, got {dt}.")
+    if pnb:  # p batched under vmap: one row of p per lane
+        dt = canonicalize_dtype(dt)  # an array of R numbers is float32 unless x64 is on
+        if shape is None:
+            shape = tuple(pv.shape[pnb:])
+        size = _size(shape)
+        kd = _flat_keys(k)
+        levels, B, (pr,) = _batch_rows(nb, k.shape[:nb], [(pv, pnb)], shape, dt, "bernoulli")
+        nrows = pr.shape[0]
+        if mode == "low":
+            lo = _k_uniform(kd, size, dt, 0.0, 1.0, _layout())
+            hi = None
+        else:
+            u = _k_uniform(kd, 2 * size, dt, 0.0, 1.0, _layout()).reshape(kd.shape[0], 2, size)
+            lo, hi = u[:, 0], u[:, 1]
+        if lo.shape[0] != nrows:  # an unbatched key: every lane draws the same
+            lo = lo.expand(nrows, size)
+            hi = hi.expand(nrows, size) if hi is not None else None
+        lo = _raw16(lo.contiguous(), dt)
+        hi = _raw16(hi.contiguous(), dt) if hi is not None else None
+        out = torch.empty((nrows, size), dtype=torch.uint8, device=kd.device)
+        nat.call("jxr_bernoulli_from_uniform", _ptr(lo), _ptr(hi) if hi is not None else None,
+                 _ptr(_raw16(pr, dt)), nrows * size, _FLOAT_CODE[dt], _ptr(out), _stream())
+        return _rebatch(out.view(torch.bool).reshape(B + shape), levels)
     p_s, p_t = _param(p, dt)
     if shape is None:
         shape = () if p_t is None else tuple(p_t.shape)

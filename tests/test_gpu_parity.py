@@ -507,3 +507,35 @@ def test_bits_fuzz_ranges_and_batches(oracle):
         for r in range(nkeys):
             want = oracle.random_bits(keys[r], bw, size, part, begin, count)
             assert np.array_equal(got[r], want), (nkeys, size, begin, count, part, bw, r)
+
+
+def test_vmap_batched_sampler_parameters():
+    """vmap over (key, bound) and (key, p) pairs, and over p alone with one key, equals the
+    loop over the lanes (the reference's vmap batches every primitive argument,
+    R/batching.R:22-50)."""
+    keys = jr.random_split(jr.random_key(11), 4)
+    mins = torch.tensor([-2.0, 0.0, 1.5, -0.25])
+    for dt in ("float32", "float16"):
+        out = jr.vmap(lambda k, m: jr.random_uniform(k, (5,), dt, minval=m, maxval=3))(keys, mins)
+        assert tuple(out.shape) == (4, 5)
+        for i in range(4):
+            want = jr.random_uniform(keys[i], (5,), dt, minval=float(mins[i]), maxval=3)
+            assert np.array_equal(to_np(out)[i], to_np(want)), (dt, i)
+    # array bounds per lane, broadcast along the shape
+    rows = torch.tensor([[0.0, 1.0, 2.0], [5.0, 6.0, 7.0]])
+    k2 = jr.random_split(jr.random_key(12), 2)
+    out = jr.vmap(lambda k, m: jr.random_uniform(k, (4, 3), minval=m, maxval=10))(k2, rows)
+    for i in range(2):
+        want = jr.random_uniform(k2[i], (4, 3), minval=rows[i], maxval=10)
+        assert np.array_equal(to_np(out)[i], to_np(want))
+    # one key for every lane: every lane draws the same unit floats
+    out = jr.vmap(lambda m: jr.random_uniform(jr.random_key(3), (6,), minval=m), in_axes=0)(mins)
+    for i in range(4):
+        want = jr.random_uniform(jr.random_key(3), (6,), minval=float(mins[i]))
+        assert np.array_equal(to_np(out)[i], to_np(want))
+    ps = torch.tensor([0.1, 0.5, 0.9, 0.3], dtype=torch.float32)
+    for mode in ("low", "high"):
+        out = jr.vmap(lambda k, p: jr.random_bernoulli(k, p, (64,), mode=mode))(keys, ps)
+        for i in range(4):
+            want = jr.random_bernoulli(keys[i], ps[i], (64,), mode=mode)
+            assert np.array_equal(to_np(out)[i], to_np(want)), (mode, i)
