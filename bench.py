@@ -422,6 +422,23 @@ def run_workload(args):
         roofline = {"bound": "int", "unit": "Tops/s", "achieved": bps * OPS_PER_BLOCK / 1e12,
                     "peak": peak_blocks * OPS_PER_BLOCK / 1e12, "frac": bps / peak_blocks,
                     "ops_per_block": OPS_PER_BLOCK, "hbm": hbm}
+    library = None
+    if c == "perm":  # NVIDIA's radix sort on the same pairs: CUB through torch.sort(stable)
+        keys = jr.random_bits(jr.random_key(7), (1 << 26,)).view(torch.int32)
+        for _ in range(args.warmup):
+            torch.sort(keys, stable=True)
+        torch.cuda.synchronize()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for _ in range(args.steps):
+            torch.sort(keys, stable=True)
+        g1.record()
+        g1.synchronize()
+        cub_ms = g0.elapsed_time(g1) / args.steps
+        library = {"what": "torch.sort(2^26 int32 keys, stable=True): CUB's radix sort of the "
+                           "same (32-bit key, position) pairs, one sort", "ms": cub_ms,
+                   "per_round_ms_here": ms / 3, "round_vs_library": ms / 3 / cub_ms}
+        del keys
     cpu = None if args.no_cpu_baseline else workload_cpu_baseline(c)
     line = {
         "metric": "threefry 32-bit words/s (device-timed), secondary workload", "value": words / (ms * 1e-3),
@@ -436,6 +453,8 @@ def run_workload(args):
         "gpu_launches": args.steps * LAUNCHES_PER_CALL.get(c, 1), "clocks": clocks,
         "cpu_baseline": cpu,
     }
+    if library is not None:
+        line["library_baseline"] = library
     jr.enable_x64(old[0])
     jr.jax_config_update("jax_threefry_partitionable", old[1])
     emit(line)

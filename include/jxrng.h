@@ -353,7 +353,8 @@ int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size
                          uint64_t begin, uint64_t count, int layout, int bit_width,
                          void* host_out);
 
-/* Throughput probe: launches (number of SMs) x ctas_per_sm CTAs of 256 threads that
+/* ---- measurement hook (for bench.py's roofline; not part of the sampling API) ----
+ * Throughput probe: launches (number of SMs) x ctas_per_sm CTAs of 256 threads that
  * each push 8 register-resident blocks through `iters` threefry20 passes (no counters,
  * loads or stores) and returns in *blocks_out the number of cipher blocks that launch
  * computes; sink needs (number of SMs) x ctas_per_sm x 256 uint32.  Timing it gives the

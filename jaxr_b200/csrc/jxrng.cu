@@ -511,12 +511,17 @@ int build_f32_table(int dev, int id, const Op& op, cudaStream_t st) {
 
 // Outputs per thread (of 16) that a table-backed sampler evaluates directly: where the
 // integer pipe's time for the cipher plus those evaluations meets the L1TEX time of the
-// remaining gathers.  Measured on B200 (2^26 outputs, one key): 4 for the samplers with one
-// logarithm or an erf_inv (normal 0.283 -> 0.243 ms, exponential 0.283 -> 0.233 ms), 3 for
-// gumbel and logistic, which take two logarithms (0.283 -> 0.248 / 0.251 ms).
+// remaining gathers.  Measured on B200 (2^26 outputs, one key): 4 for the normal (0.283
+// -> 0.245 ms), 6 for the exponential, whose one table-driven logarithm is cheapest
+// (0.283 -> 0.229 ms; 4: 0.239 ms), 3 for gumbel and logistic, which take two logarithms
+// (0.283 -> 0.256 / 0.258 ms).
 template <class Op>
 struct DirectShare {
   static constexpr int value = 4;
+};
+template <>
+struct DirectShare<OpLogSampler<kExponential, 0>> {
+  static constexpr int value = 6;
 };
 template <>
 struct DirectShare<OpLogSampler<kGumbel, 0>> {

@@ -670,6 +670,48 @@ int orc_sample(const uint32_t key[2], int kind, int dtype, uint64_t size, int pa
   return 0;
 }
 
+/* The float32 samplers of given 32-bit draws (each float32 sample depends only on
+ * bits >> 9), for exhaustive checks over all 2^23 draws: kind 0..3 the log-transform
+ * samplers as orc_sample_at evaluates them (R/random.R:1428-1516), 4 the normal as
+ * orc_normal_at does (R/random.R:501-508, fused Horner steps). */
+static float unit_f32_of(uint32_t b) { return bits_f32((b >> 9) | 0x3F800000u) - 1.0f; }
+
+void orc_sample_f32_from_bits(const uint32_t* bits, int64_t n, int kind, float* out) {
+  ORC_PAR_FOR
+  for (int64_t t = 0; t < n; ++t) {
+    const float f = unit_f32_of(bits[t]);
+    if (kind == 4) {
+      const float lo = (float)(-1.0 + 0x1p-24);
+      const float u = (float)xla_max(lo, f * 2.0f + lo);
+      out[t] = (float)1.41421356237309504880 * orc_erfinv_f32(u, 1);
+      continue;
+    }
+    const float mn = kind == ORC_EXPONENTIAL ? 0.0f
+                     : kind == ORC_LAPLACE   ? (float)(-1.0 + 0x1p-24)
+                                             : 0x1p-126f;
+    const float d = 1.0f - mn;
+    const float u = (float)xla_max(mn, fmaf(f, d, mn));
+    switch (kind) {
+      case ORC_EXPONENTIAL: out[t] = -(float)log1p_neg(-(double)u); break;
+      case ORC_GUMBEL: {
+        const float a = (float)log_pos((double)u);
+        out[t] = -(float)log_pos(-(double)a);
+        break;
+      }
+      case ORC_LOGISTIC: {
+        const float a = (float)log_pos((double)u);
+        const float c = (float)log1p_neg(-(double)u);
+        out[t] = a - c;
+        break;
+      }
+      default: {
+        const float l = (float)log1p_neg(-(double)fabsf(u));
+        out[t] = u < 0.0f ? -l : l;
+      }
+    }
+  }
+}
+
 /* ---- gumbel modes "high" and "highest" (R/random.R:1465-1489) ------------------------- */
 
 /* XLA shifts: amounts of 32 or more give 0. */

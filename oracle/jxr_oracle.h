@@ -104,6 +104,9 @@ double orc_sample_at(const uint32_t key[2], int kind, int dtype, uint64_t size,
 
 /* random_gumbel modes "high" (0) and "highest" (1, float32) (R/random.R:1465-1489) and
  * random_truncated_normal with scalar bounds (R/random.R:586-603). */
+/* The float32 samplers of n given 32-bit draws: kind 0..3 exponential, gumbel (mode
+ * "low"), logistic, laplace; 4 the normal (fused Horner steps). */
+void orc_sample_f32_from_bits(const uint32_t* bits, int64_t n, int kind, float* out);
 int orc_gumbel_mode(const uint32_t key[2], int mode, int dtype, uint64_t size,
                     int partitionable, void* out);
 double orc_gumbel_mode_at(const uint32_t key[2], int mode, int dtype, uint64_t size,

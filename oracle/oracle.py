@@ -61,6 +61,7 @@ def lib():
         L.orc_normal_at.restype = dbl
         L.orc_log_pos.argtypes = [dbl]
         L.orc_log_pos.restype = dbl
+        L.orc_sample_f32_from_bits.argtypes = [vp, i64, i32, vp]
         L.orc_sample.argtypes = [u32p, i32, i32, u64, i32, u64, u64, vp]
         L.orc_sample_at.argtypes = [u32p, i32, i32, u64, i32, u64]
         L.orc_sample_at.restype = dbl
@@ -219,6 +220,16 @@ def normal_at(key, dtype, size, partitionable, fma, idx):
 
 
 SAMPLE_KIND = {"exponential": 0, "gumbel": 1, "logistic": 2, "laplace": 3}
+
+
+def sample_f32_from_bits(bits, kind):
+    """float32 samples of given uint32 draws: kind "exponential" / "gumbel" / "logistic" /
+    "laplace" (mode "low" gumbel), or "normal" (fused Horner steps)."""
+    bits = np.ascontiguousarray(bits, dtype=np.uint32)
+    out = np.empty(bits.shape[0], dtype=np.float32)
+    code = 4 if kind == "normal" else SAMPLE_KIND[kind]
+    lib().orc_sample_f32_from_bits(_ptr(bits), bits.shape[0], code, _ptr(out))
+    return out
 
 
 def sample(key, kind, dtype, size, partitionable=True, begin=0, count=None):

@@ -71,8 +71,8 @@ def _gpu():
 # ---- golden vectors of the reference ---------------------------------------------------------
 
 def _f64_normal(case):
-    """A float64 (or complex128) normal: held to north_star's 1e-12 relative and the
-    reference's own 16 ulp (test-random.R:10-27), since its logarithm is not the oracle's."""
+    """A float64 (or complex128) normal: held to 1e-12 relative (the float64 normal's bar)
+    and the reference's own 16 ulp (test-random.R:10-27), since its logarithm is not the oracle's."""
     return case["op"] in ("normal", "vmap_normal") and float_dtype(case["args"]) in (
         "float64", "complex128")
 
