@@ -190,19 +190,22 @@ WORKLOADS = {
     "randint": "random_randint(random_key(7L), (8192, 8192), 0L, 1000L) int32 "
                "(split, then both 32-bit draws and the combine in one kernel)",
     "perm": "random_permutation(random_key(7L), 2^26) int32: 3 shuffle rounds, each 2^26 "
-            "32-bit sort keys and a 4-pass stable radix sort of (key, position) pairs",
+            "32-bit sort keys, 2 stable radix passes over their top 16 bits and the span sort "
+            "of every run of equal top bits in shared memory",
     "rbg": "random_bits(random_key(0L, impl = \"rbg\"), 2^30) uint32: XLA RngBitGenerator "
            "(Philox4x32-10), 4 words per block",
 }
 
 # Kernels of this library one call launches (1 unless listed): randint = split and the
-# fused draws + combine; perm = iota, then per round split, bits and 4 x (histogram,
-# scan, scatter).
-LAUNCHES_PER_CALL = {"randint": 2, "perm": 1 + 3 * 14}
+# fused draws + combine; perm = iota, then per round the key split, the sort keys with the
+# first pass's counts, the second pass's counts, 2 x (scan, scatter) and the span sort.
+LAUNCHES_PER_CALL = {"randint": 2, "perm": 1 + 3 * 8}
 
 # Algorithmic HBM bytes per element of one shuffle round: the 32-bit sort keys written
-# once, then per 8-bit pass one read and one write of the (key, position) pair.
-PERM_BYTES_PER_ROUND = 4 + 4 * 16
+# once (their first-pass counts taken on the way); per radix pass the (key, position) pair
+# read and written, the second pass also reading the keys for its counts; the span sort
+# reads the pair and writes the position.
+PERM_BYTES_PER_ROUND = 4 + 16 + (4 + 16) + 8 + 4
 
 _SAMPLER_WORKLOADS = {"exp": "exponential", "gumbel": "gumbel", "logistic": "logistic"}
 

@@ -274,13 +274,23 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
  * shape (outer, n, inner), shuffling each 1-D slice along the middle axis (outer = inner = 1
  * for a vector).  Writes perm[f] = the flat index of the source element that lands at flat
  * position f (total = outer * n * inner < 2^31).  Each of the ceil(3 log(total) /
- * log(2^32 - 1)) rounds splits the key, draws 32-bit sort keys and sorts stably.  scratch
- * (256-byte aligned) holds jxr_shuffle_scratch_bytes(total) bytes.  Synchronises `stream`
- * to read back the sort's bounds-check flag.  impl: the key's implementation (JXR_IMPL_*;
- * key is u32[2] for threefry2x32, u32[4] for rbg and unsafe_rbg). */
+ * log(2^32 - 1)) rounds splits the key, draws 32-bit sort keys and sorts stably: radix
+ * passes over the keys' top bits, then every run of equal top bits sorted in shared memory
+ * (the span sort).  scratch (256-byte aligned) holds jxr_shuffle_scratch_bytes(total)
+ * bytes.  Synchronises `stream` to read back the sort's flags; if a run was longer than
+ * the span sort takes (which uniformly random keys make vanishingly unlikely), the shuffle
+ * is repeated with radix passes alone before the call returns.  impl: the key's
+ * implementation (JXR_IMPL_*; key is u32[2] for threefry2x32, u32[4] for rbg and
+ * unsafe_rbg). */
 size_t jxr_shuffle_scratch_bytes(int64_t total);
 int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t inner,
                 int layout, uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream);
+/* The longest span (elements) the span sort of jxr_shuffle takes, for the calling host
+ * thread: 4096 by default, 0 = radix passes only, anything in [0, 4096] accepted; returns
+ * the previous value, or -1 (and the message for jxr_last_error) for a value outside that
+ * range.  Shorter caps exercise the repeat by radix passes; the results are identical
+ * either way. */
+int jxr_set_shuffle_span_cap(int cap);
 
 /* jnp_take along the middle axis: out[o][i][:] = src[o][idx[i]][:], rows of row_bytes bytes,
  * src of shape (outer, n_src, row), out (outer, n_idx, row).  An index >= n_src is skipped

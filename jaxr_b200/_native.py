@@ -81,6 +81,7 @@ SIGNATURES = {
     "jxr_free_caches": [],
     "jxr_prepare_device": [_u32, _vp],
     "jxr_get_accurate_erf_inv": [],
+    "jxr_set_shuffle_span_cap": [_int],
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],
     "jxr_random_bits_host_static": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp, _vp],

@@ -2002,6 +2002,61 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
 
 // ---- permutation: stable radix sort of (random key, position) pairs ----------------------
 
+namespace jxr {
+// A shuffle round's sort keys as random_bits(key, 32, n) draws them in the partitionable
+// layout (element e < 2^31 hashes the counters (0, e); the key is x0 ^ x1, R/prng.R:212-226),
+// and each sort tile's digit counts at `shift` for the first radix pass, in one pass: one CTA
+// per tile of kSortTile keys, 16 cipher blocks in flight per thread, 16-byte stores.
+__global__ void __launch_bounds__(kSortThreads)
+k_sort_keys_hist(const uint32_t* __restrict__ key, int64_t n, int shift, int64_t ntiles,
+                 PipeConsts pc, uint32_t* __restrict__ keys_out, uint32_t* __restrict__ counts) {
+  constexpr int G = 4, V = 4, N = G * V;
+  constexpr int kRound = kSortThreads * N;  // keys per round of the CTA
+  static_assert(kSortThreads == 256 && kSortTile % kRound == 0, "one digit per thread");
+  __shared__ uint32_t h[256];
+  h[threadIdx.x] = 0;
+  const KeySchedule ks = make_schedule(__ldg(key), __ldg(key + 1));
+  const int64_t base = (int64_t)blockIdx.x * kSortTile;
+  __syncthreads();
+  for (int r = 0; r < kSortTile / kRound; ++r) {
+    const int64_t p0 = base + (int64_t)r * kRound + threadIdx.x * V;
+    // n < 2^31: the high counter word is 0
+    uint32_t x0[N], x1[N];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        x0[g * V + v] = 0u;
+        x1[g * V + v] = (uint32_t)p0 + (uint32_t)(g * kSortThreads * V + v);
+      }
+    threefry20<N, ProductMix>(ks, x0, x1, pc);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int64_t q = p0 + g * kSortThreads * V;
+      uint32_t w[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) w[v] = x0[g * V + v] ^ x1[g * V + v];
+      if (q + V <= n) {
+        *reinterpret_cast<uint4*>(keys_out + q) = make_uint4(w[0], w[1], w[2], w[3]);
+#pragma unroll
+        for (int v = 0; v < V; ++v) atomicAdd(&h[(w[v] >> shift) & 255u], 1u);
+      } else {
+#pragma unroll
+        for (int v = 0; v < V; ++v)
+          if (q + v < n) {
+            keys_out[q + v] = w[v];
+            atomicAdd(&h[(w[v] >> shift) & 255u], 1u);
+          }
+      }
+    }
+  }
+  __syncthreads();
+  counts[(int64_t)threadIdx.x * ntiles + blockIdx.x] = h[threadIdx.x];
+}
+
+}  // namespace jxr
+
+
 namespace {
 int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
 
@@ -2036,25 +2091,81 @@ size_t shuffle_scratch(int64_t total, char* base, SortScratch* s) {
   return off;
 }
 
+// One stable 8-bit radix pass of (k, v) by the digit at `shift` into (k2, v2); the pointers
+// are swapped, so k / v hold the result.
+int radix_pass(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n, int shift,
+               const SortScratch& s, cudaStream_t st, bool counted = false) {
+  const int64_t nt = sort_tiles(n);
+  JXR_CUDA(cudaFuncSetAttribute(k_sort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kSortScatterSmem));
+  // the scatter's CTAs are persistent: as many as are resident at once, or one per tile
+  static int per_sm = 0;
+  if (!per_sm) {
+    JXR_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_sort_scatter,
+                                                           kScatterThreads, kSortScatterSmem));
+    per_sm = std::max(per_sm, 1);
+  }
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const int64_t grid = std::min<int64_t>(nt, (int64_t)di.sms * per_sm);
+  if (!counted) k_sort_hist<<<(unsigned)nt, kSortThreads, 0, st>>>(k, n, shift, nt, s.counts);
+  k_sort_scan_rows<<<256, 1024, 0, st>>>(s.counts, nt, s.totals);
+  k_sort_scatter<<<(unsigned)grid, kScatterThreads, kSortScatterSmem, st>>>(
+      k, v, n, shift, nt, s.counts, s.totals, k2, v2, s.err);
+  JXR_CUDA(cudaGetLastError());
+  std::swap(k, k2);
+  std::swap(v, v2);
+  return JXR_OK;
+}
+
 // Sorts (k, v) by the low `bits` bits of k (a multiple of 8), stably; k2 / v2 are scratch
 // of the same size.  On return k / v point at the sorted pairs, k2 / v2 at free buffers.
 int sort_pairs(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n, int bits,
                const SortScratch& s, cudaStream_t st) {
-  const int64_t nt = sort_tiles(n);
-  JXR_CUDA(cudaFuncSetAttribute(k_sort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kSortScatterSmem));
-  for (int shift = 0; shift < bits; shift += 8) {
-    k_sort_hist<<<(unsigned)nt, kSortThreads, 0, st>>>(k, n, shift, nt, s.counts);
-    k_sort_scan_rows<<<256, 1024, 0, st>>>(s.counts, nt, s.totals);
-    k_sort_scatter<<<(unsigned)nt, kScatterThreads, kSortScatterSmem, st>>>(
-        k, v, n, shift, nt, s.counts, s.totals, k2, v2, s.err);
-    JXR_CUDA(cudaGetLastError());
-    std::swap(k, k2);
-    std::swap(v, v2);
-  }
+  int rc;
+  for (int shift = 0; shift < bits; shift += 8)
+    if ((rc = radix_pass(k, v, k2, v2, n, shift, s, st))) return rc;
+  return JXR_OK;
+}
+
+// Mean bucket size (elements of equal top bits) that the span sort is given at most: a
+// span is kSpanOwn positions plus the rest of the bucket running past them, so buckets well
+// below kSpanCap - kSpanOwn keep every span within kSpanCap.
+constexpr int64_t kSpanBucketMean = 1536;
+
+// Radix passes over the top 8 g bits of the keys, the fewest that leave buckets of at most
+// kSpanBucketMean elements on average (none when the whole array fits one span).
+int span_sort_passes(int64_t n, int cap) {
+  if (n <= cap) return 0;
+  int g = 1;
+  while (g < 3 && (n >> (8 * g)) > kSpanBucketMean) ++g;
+  return g;
+}
+
+// The stable sort of a shuffle round, whose keys are uniformly random 32-bit words: radix
+// passes over the top 8 g bits, then k_sort_spans sorts every bucket in shared memory.
+// On return v holds the values in sorted order (k is not sorted).  A span longer than
+// `cap` sets s.err[1]; the caller then repeats the shuffle with the radix passes alone.
+int sort_random_keys(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n,
+                     int cap, const SortScratch& s, cudaStream_t st, bool first_counted = false) {
+  const int g = span_sort_passes(n, cap);
+  int rc;
+  for (int p = g; p >= 1; --p)
+    if ((rc = radix_pass(k, v, k2, v2, n, 32 - 8 * p, s, st, first_counted && p == g))) return rc;
+  JXR_CUDA(cudaFuncSetAttribute(k_sort_spans, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kSpanSmem));
+  const int64_t ctas = (n + kSpanOwn - 1) / kSpanOwn;
+  k_sort_spans<<<(unsigned)ctas, kSpanThreads, kSpanSmem, st>>>(k, v, n, 32 - 8 * g, cap, v2,
+                                                                s.err + 1, s.err);
+  JXR_CUDA(cudaGetLastError());
+  std::swap(v, v2);
   return JXR_OK;
 }
 }  // namespace
+
+// Longest span k_sort_spans sorts for this host thread's shuffles (0: radix passes only).
+thread_local int g_shuffle_span_cap = kSpanCap;
 
 size_t jxr_shuffle_scratch_bytes(int64_t total) {
   if (total < 0) return 0;
@@ -2093,51 +2204,72 @@ int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t
       (int)std::ceil(3.0 * std::log(std::max(1.0, (double)total)) / std::log(4294967295.0));
   int segbits = 0;
   for (int64_t nseg = outer * inner; nseg > 1 && ((int64_t)1 << segbits) < nseg;) ++segbits;
-  JXR_CUDA(cudaMemsetAsync(s.err, 0, sizeof(int), st));
-  // keys12: the running key (words 0..3), ks[0] (4..7), ks[1] (8..11); threefry keys use
-  // the first two words of each
-  const size_t kw = impl == JXR_IMPL_THREEFRY ? 8 : 16;
-  JXR_CUDA(cudaMemcpyAsync(s.keys12, key, kw, cudaMemcpyDeviceToDevice, st));
-  // values are original flat indices: v[f] = index of the element now at position f
-  uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
-  k_iota_u32<<<grid, 256, 0, st>>>(v, total);
-  for (int r = 0; r < rounds; ++r) {
-    // ks = split(key); key = ks[0]; sort keys = random_bits(ks[1], 32, shape)
-    uint32_t* ks0 = s.keys12 + 4;
-    uint32_t* ks1 = s.keys12 + 8;
-    if (impl == JXR_IMPL_THREEFRY) {
-      if ((rc = jxr_split(s.keys12, 1, 2, layout, ks0, stream))) return rc;  // ks0, then ks1
-      ks1 = ks0 + 2;
-    } else if (impl == JXR_IMPL_RBG) {
-      // each half split as a threefry key: (h0 ks0, h0 ks1, h1 ks0, h1 ks1) in tmp
-      uint32_t* tmp = s.keys12 + 12;
-      if ((rc = jxr_split(s.keys12, 2, 2, layout, tmp, stream))) return rc;
-      JXR_CUDA(cudaMemcpyAsync(ks0, tmp, 8, cudaMemcpyDeviceToDevice, st));
-      JXR_CUDA(cudaMemcpyAsync(ks0 + 2, tmp + 4, 8, cudaMemcpyDeviceToDevice, st));
-      JXR_CUDA(cudaMemcpyAsync(ks1, tmp + 2, 8, cudaMemcpyDeviceToDevice, st));
-      JXR_CUDA(cudaMemcpyAsync(ks1 + 2, tmp + 6, 8, cudaMemcpyDeviceToDevice, st));
-    } else {  // unsafe_rbg: rows 0 and 10 of the key's (20, 4) request
-      if ((rc = jxr_rbg_blocks(s.keys12, 0, 10, 2, ks0, stream))) return rc;
+  // every round: the 32-bit sort by span sort (cap > 0) or by radix passes alone (cap == 0)
+  auto run = [&](int cap) -> int {
+    JXR_CUDA(cudaMemsetAsync(s.err, 0, 2 * sizeof(int), st));
+    // keys12: the running key (words 0..3), ks[0] (4..7), ks[1] (8..11); threefry keys use
+    // the first two words of each
+    const size_t kw = impl == JXR_IMPL_THREEFRY ? 8 : 16;
+    JXR_CUDA(cudaMemcpyAsync(s.keys12, key, kw, cudaMemcpyDeviceToDevice, st));
+    // values are original flat indices: v[f] = index of the element now at position f
+    uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
+    k_iota_u32<<<grid, 256, 0, st>>>(v, total);
+    for (int r = 0; r < rounds; ++r) {
+      // ks = split(key); key = ks[0]; sort keys = random_bits(ks[1], 32, shape)
+      uint32_t* ks0 = s.keys12 + 4;
+      uint32_t* ks1 = s.keys12 + 8;
+      if (impl == JXR_IMPL_THREEFRY) {
+        if ((rc = jxr_split(s.keys12, 1, 2, layout, ks0, stream))) return rc;  // ks0, then ks1
+        ks1 = ks0 + 2;
+      } else if (impl == JXR_IMPL_RBG) {
+        // each half split as a threefry key: (h0 ks0, h0 ks1, h1 ks0, h1 ks1) in tmp
+        uint32_t* tmp = s.keys12 + 12;
+        if ((rc = jxr_split(s.keys12, 2, 2, layout, tmp, stream))) return rc;
+        JXR_CUDA(cudaMemcpyAsync(ks0, tmp, 8, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(ks0 + 2, tmp + 4, 8, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(ks1, tmp + 2, 8, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(ks1 + 2, tmp + 6, 8, cudaMemcpyDeviceToDevice, st));
+      } else {  // unsafe_rbg: rows 0 and 10 of the key's (20, 4) request
+        if ((rc = jxr_rbg_blocks(s.keys12, 0, 10, 2, ks0, stream))) return rc;
+      }
+      JXR_CUDA(cudaMemcpyAsync(s.keys12, ks0, kw, cudaMemcpyDeviceToDevice, st));
+      // the default keys (threefry, partitionable) are drawn together with the counts of
+      // the first radix pass
+      const int g = span_sort_passes(total, cap);
+      const bool fused = cap && g && impl == JXR_IMPL_THREEFRY && layout == JXR_LAYOUT_PARTITIONABLE;
+      if (fused)
+        k_sort_keys_hist<<<(unsigned)sort_tiles(total), kSortThreads, 0, st>>>(
+            ks1, total, 32 - 8 * g, sort_tiles(total), kPipe, k, s.counts);
+      else if (impl == JXR_IMPL_THREEFRY)
+        rc = jxr_random_bits(ks1, 1, (uint64_t)total, 0, (uint64_t)total, layout, 32, k, stream);
+      else
+        rc = jxr_rbg_bits(ks1, (uint64_t)total, 0, (uint64_t)total, 32, k, nullptr, stream);
+      if (rc) return rc;
+      if (cap) rc = sort_random_keys(k, v, k2, v2, total, cap, s, st, fused);
+      else rc = sort_pairs(k, v, k2, v2, total, 32, s, st);
+      if (rc) return rc;
+      if (segbits) {  // then by segment (the slice along the middle axis), stably
+        k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
+        if ((rc = sort_pairs(k, v, k2, v2, total, (segbits + 7) / 8 * 8, s, st))) return rc;
+        k_shuffle_place<<<grid, 256, 0, st>>>(v, total, n, inner, v2, s.err);
+        std::swap(v, v2);
+      }
     }
-    JXR_CUDA(cudaMemcpyAsync(s.keys12, ks0, kw, cudaMemcpyDeviceToDevice, st));
-    if (impl == JXR_IMPL_THREEFRY)
-      rc = jxr_random_bits(ks1, 1, (uint64_t)total, 0, (uint64_t)total, layout, 32, k, stream);
-    else
-      rc = jxr_rbg_bits(ks1, (uint64_t)total, 0, (uint64_t)total, 32, k, nullptr, stream);
-    if (rc) return rc;
-    if ((rc = sort_pairs(k, v, k2, v2, total, 32, s, st))) return rc;
-    if (segbits) {  // then by segment (the slice along the middle axis), stably
-      k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
-      if ((rc = sort_pairs(k, v, k2, v2, total, (segbits + 7) / 8 * 8, s, st))) return rc;
-      k_shuffle_place<<<grid, 256, 0, st>>>(v, total, n, inner, v2, s.err);
-      std::swap(v, v2);
-    }
-  }
-  JXR_CUDA(cudaMemcpyAsync(perm, v, (size_t)total * 4, cudaMemcpyDeviceToDevice, st));
-  JXR_CUDA(cudaGetLastError());
-  int err = 0;
-  JXR_CUDA(cudaMemcpyAsync(&err, s.err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    JXR_CUDA(cudaMemcpyAsync(perm, v, (size_t)total * 4, cudaMemcpyDeviceToDevice, st));
+    JXR_CUDA(cudaGetLastError());
+    return JXR_OK;
+  };
+  int flags[2] = {0, 0};
+  const int cap = std::min(g_shuffle_span_cap, kSpanCap);
+  if ((rc = run(cap))) return rc;
+  JXR_CUDA(cudaMemcpyAsync(flags, s.err, sizeof flags, cudaMemcpyDeviceToHost, st));
   JXR_CUDA(cudaStreamSynchronize(st));
+  if (flags[1] && !flags[0]) {  // a span over the cap: the whole shuffle by radix passes
+    if ((rc = run(0))) return rc;
+    JXR_CUDA(cudaMemcpyAsync(flags, s.err, sizeof flags, cudaMemcpyDeviceToHost, st));
+    JXR_CUDA(cudaStreamSynchronize(st));
+  }
+  const int err = flags[0];
   if (err) return fail(JXR_ERR_CUDA, "shuffle: a bounds check in the sort failed (code %d)", err);
   return JXR_OK;
 }
@@ -2508,6 +2640,16 @@ int jxr_set_accurate_erf_inv(int enable) {
 }
 
 int jxr_get_accurate_erf_inv(void) { return g_accurate_erf_inv; }
+
+int jxr_set_shuffle_span_cap(int cap) {
+  if (cap < 0 || cap > kSpanCap) {
+    fail(JXR_ERR_INVALID_ARGUMENT, "span cap must be in [0, %d], got %d", kSpanCap, cap);
+    return -1;
+  }
+  const int prev = g_shuffle_span_cap;
+  g_shuffle_span_cap = cap;
+  return prev;
+}
 
 int jxr_random_bits_host(const uint32_t* keys_host, int64_t nkeys, uint64_t size, uint64_t begin,
                          uint64_t count, int layout, int bit_width, void* host_out) {

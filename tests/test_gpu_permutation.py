@@ -183,3 +183,55 @@ def test_choice_p_long_vector(dt):
         got = to_np(jr.random_choice(dev_key(key), p.size, (50000,), True, p))
     assert np.array_equal(got, orc.choice(key, p.size, (50000,), True, p, x64=dt == "float64"))
     assert not np.any(p[got] == 0)
+
+
+def _span_cap(cap):
+    from jaxr_b200 import _native as nat
+    prev = nat.lib().jxr_set_shuffle_span_cap(cap)
+    assert prev >= 0
+    return prev
+
+
+@pytest.mark.parametrize("n", [4096, 4097, 393216, 393217, (1 << 20) + 7, (1 << 27) + 5])
+def test_span_sort_matches_radix_passes(n):
+    """The span sort (radix passes over the top 0, 8, 16 or 24 bits, then every run of
+    equal top bits in shared memory) against the radix passes over all four digits, at the
+    sizes where the number of top-bit passes changes; the result is a permutation."""
+    key = dev_key(orc.seed(31))
+    got = jr.random_permutation(key, n)
+    prev = _span_cap(0)
+    try:
+        want = jr.random_permutation(key, n)
+    finally:
+        _span_cap(prev)
+    assert torch.equal(got, want), n
+    srt = torch.sort(got.to(torch.int64))[0]
+    assert torch.equal(srt, torch.arange(n, dtype=torch.int64, device=srt.device))
+
+
+def test_span_sort_overflow_repeats_with_radix_passes():
+    """A span longer than the cap (forced here with a cap of 64) makes the shuffle repeat
+    with radix passes alone: the results stay exact against the oracle, for vectors and
+    for independent slices."""
+    key = orc.seed(2718)
+    prev = _span_cap(64)
+    try:
+        for n in (50, 64, 65, 8193, 100003):
+            got = to_np(jr.random_permutation(dev_key(key), n))
+            assert np.array_equal(got, orc.permutation(key, n)), n
+        x = torch.arange(300 * 40, dtype=torch.int32).reshape(300, 40)
+        got = to_np(jr.random_permutation(dev_key(key), x, axis=1, independent=True))
+        assert np.array_equal(got, orc.permutation(key, x.numpy(), axis=1, independent=True))
+    finally:
+        _span_cap(prev)
+
+
+def test_span_cap_setter():
+    from jaxr_b200 import _native as nat
+    L = nat.lib()
+    prev = L.jxr_set_shuffle_span_cap(4096)
+    assert prev == 4096
+    assert L.jxr_set_shuffle_span_cap(4097) == -1
+    assert b"span cap" in L.jxr_last_error()
+    assert L.jxr_set_shuffle_span_cap(-1) == -1
+    assert L.jxr_set_shuffle_span_cap(prev) == 4096
