@@ -1151,6 +1151,21 @@ def random_truncated_normal(key, lower, upper, shape=None, dtype=None):
         shape = canon_shape(shape)
     k, _, nb = _check_key("truncated_normal", key)
     dt = _float_dtype("truncated_normal", dtype)
+    (lov, lob), (hiv, hib) = _unbatch(lower), _unbatch(upper)
+    if lob or hib:  # bounds batched under vmap: one row of bounds per lane
+        if shape is None:
+            lane = lambda v, pb: tuple(np.shape(v))[pb:]  # noqa: E731
+            shape = tuple(torch.broadcast_shapes(lane(lov, lob), lane(hiv, hib)))
+        levels, B, (lo, hi) = _batch_rows(nb, k.shape[:nb], [(lov, lob), (hiv, hib)], shape, dt,
+                                          "truncated_normal")
+        unit = _k_uniform(_flat_keys(k), _size(shape), dt, 0.0, 1.0, _layout())
+        if unit.shape[0] != lo.shape[0]:  # an unbatched key: every lane draws the same
+            unit = unit.expand(lo.shape[0], unit.shape[1]).contiguous()
+        out = torch.empty_like(unit)
+        nat.call("jxr_truncated_normal_from_unit", _ptr(_raw16(unit, dt)), _ptr(_raw16(lo, dt)), 1,
+                 _ptr(_raw16(hi, dt)), 1, unit.numel(), _FLOAT_CODE[dt], _ptr(_raw16(out, dt)),
+                 _stream())
+        return _rebatch(out.reshape(B + shape), levels)
     lo_s, lo_t = _param(lower, dt)
     hi_s, hi_t = _param(upper, dt)
     if shape is None:
@@ -1268,8 +1283,41 @@ def random_randint(key, shape, minval, maxval, dtype=None):
     shape = canon_shape(shape)
     if dt not in _INT_INFO:
         raise JaxTypeError(f"randint only accepts integer dtypes, got {dt}")
-    mn, mn_dt = _int_bound(minval, "minval")
-    mx, mx_dt = _int_bound(maxval, "maxval")
+    (mnv, mnb), (mxv, mxb) = _unbatch(minval), _unbatch(maxval)
+    levels, bshape = nb, tuple(k.shape[:nb])
+    if mnb or mxb:  # bounds batched under vmap: every lane its own bounds, one launch
+        levels = max(nb, mnb, mxb)
+        if any(b not in (0, levels) for b in (nb, mnb, mxb)):
+            raise JaxNotImplementedError("vmap: sampler parameters batched at other levels than "
+                                         "the key")
+        bs = [tuple(np.shape(v))[:b] for v, b in ((mnv, mnb), (mxv, mxb)) if b]
+        if not nb:
+            bshape = bs[0]
+        if any(b != bshape for b in bs):
+            raise JaxValueError(f"vmap got inconsistent sizes for the mapped axis: "
+                                f"{sorted(set(bs + [bshape]))}")
+    mn, mn_dt = _int_bound(mnv, "minval")
+    mx, mx_dt = _int_bound(mxv, "maxval")
+    nlead = len(bshape) if (mnb or mxb) else 0
+    if nlead:  # per-lane bounds: B + (1,) * pad + lane shape, broadcast to B + shape
+        def per_lane(vals, pb):
+            lane = tuple(vals.shape[pb:])
+            if len(lane) > len(shape):
+                lane_b = None
+            else:
+                try:
+                    lane_b = tuple(np.broadcast_shapes(shape, lane))
+                except ValueError:
+                    lane_b = None
+            if lane_b != tuple(shape):
+                raise JaxValueError(
+                    "randint parameter shapes must be broadcast-compatible with shape argument, "
+                    "and the result of broadcasting the shapes must equal the shape argument, "
+                    f"but got result {shape_str(lane_b or lane)} for shape argument "
+                    f"{shape_str(shape)}.")
+            full = vals.reshape((bshape if pb else ()) + (1,) * (len(shape) - len(lane)) + lane)
+            return np.broadcast_to(full, bshape + tuple(shape))
+        mn, mx = per_lane(mn, mnb), per_lane(mx, mxb)
     dbits, dsigned = _INT_INFO[dt]
     if dbits < 32:  # sample in int32, bounds wrapped to int32 and clipped (:320-325)
         lo_d, hi_d = _int_range(dbits, dsigned)
@@ -1281,7 +1329,7 @@ def random_randint(key, shape, minval, maxval, dtype=None):
     else:
         sbits, ssigned = dbits, dsigned
     try:
-        b = tuple(np.broadcast_shapes(shape, mn.shape, mx.shape))
+        b = tuple(np.broadcast_shapes(bshape[:nlead] + tuple(shape), mn.shape, mx.shape))[nlead:]
     except ValueError:
         b = None
     if b != tuple(shape):
@@ -1299,14 +1347,30 @@ def random_randint(key, shape, minval, maxval, dtype=None):
 
     def as_param(vals, f):
         flat = [f(int(v)) for v in np.asarray(vals, dtype=object).ravel()]
-        if len(flat) != 1:
+        if len(flat) != 1 or nlead:
             flat = [f(int(v)) for v in np.broadcast_to(np.asarray(vals, dtype=object),
-                                                       shape).ravel()]
+                                                       bshape[:nlead] + tuple(shape)).ravel()]
         t = torch.tensor([_wrap_int(v, 64, True) for v in flat], dtype=torch.int64)
         return t.to(dev), (0 if len(flat) == 1 else 1)
 
     clip = lambda v: min(max(v, smin), smax)  # noqa: E731 - convert_and_clip_integer
     halves = _k_split(kd, (2,), layout, k.impl)
+    if nlead:  # every lane a row of draws (an unbatched key: the same draws in every lane)
+        nrows = _size(bshape)
+        hi = _k_bits(halves[:, 0].contiguous(), size, sbits, layout)
+        lo = _k_bits(halves[:, 1].contiguous(), size, sbits, layout)
+        if hi.shape[0] != nrows:
+            hi = hi.expand(nrows, size).contiguous()
+            lo = lo.expand(nrows, size).contiguous()
+        oor_t, _ = as_param(mx, lambda v: int(v > smax))
+        mn_t, _ = as_param(mn, clip)
+        mx_t, _ = as_param(mx, clip)
+        oor_t = oor_t.to(torch.uint8)
+        out = torch.empty((nrows, size), dtype=_TORCH[dt], device=dev)
+        if size:
+            nat.call("jxr_randint_combine", _ptr(hi), _ptr(lo), nrows * size, sbits, int(ssigned),
+                     _ptr(mn_t), 1, _ptr(mx_t), 1, _ptr(oor_t), 1, dbits, _ptr(out), _stream())
+        return _rebatch(out.reshape(bshape + shape), levels)
     out = torch.empty((kd.shape[0], size), dtype=_TORCH[dt], device=dev)
     if (mn.size == 1 and mx.size == 1 and k.impl == "threefry2x32"
             and layout == nat.LAYOUT_PARTITIONABLE):
@@ -1404,8 +1468,8 @@ def random_permutation(key, x, axis=0, independent=False):
     on the device."""
     k, _, nb = _check_key("permutation", key)
     xv, xnb = _unbatch(x)
-    if xnb:
-        raise JaxNotImplementedError("batched permutation arguments are not supported")
+    if xnb:  # x batched under vmap: each lane shuffles its own array with its own key
+        return _permutation_lanes(k, nb, xv, xnb, axis, independent)
     ndim = xv.ndim if isinstance(xv, (torch.Tensor, np.ndarray)) else np.ndim(xv)
     axis = _norm_axis(axis, max(ndim, 1))
     kd = _flat_keys(k)
@@ -1430,17 +1494,48 @@ def random_permutation(key, x, axis=0, independent=False):
         return _rebatch(out.reshape(bshape + (n,)), nb)
     xt = _as_device_array(xv)
     shape = tuple(xt.shape)
-    outer, n, inner = _size(shape[:axis]), shape[axis], _size(shape[axis + 1:])
-    outs = []
-    for r in range(kd.shape[0]):
-        if independent or xt.ndim == 1:
-            perm = _k_shuffle(kd[r], k.impl, outer, n, inner, layout)
-            outs.append(_take(xt.reshape(-1), perm, 0).reshape(shape))
-        else:
-            ind = _k_shuffle(kd[r], k.impl, 1, n, 1, layout)
-            outs.append(_take(xt, ind, axis))
+    outs = [_permute_array(kd[r], k.impl, xt, axis, independent, layout)
+            for r in range(kd.shape[0])]
     out = torch.stack(outs) if outs else torch.empty((0,) + shape, dtype=xt.dtype)
     return _rebatch(out.reshape(bshape + shape), nb)
+
+
+def _permute_array(kd_row, impl, xt, axis, independent, layout):
+    """One key's shuffle of the device array xt along `axis` (rnd_permutation's array
+    branch, R/random.R:388-400)."""
+    shape = tuple(xt.shape)
+    outer, n, inner = _size(shape[:axis]), shape[axis], _size(shape[axis + 1:])
+    if independent or xt.ndim == 1:
+        perm = _k_shuffle(kd_row, impl, outer, n, inner, layout)
+        return _take(xt.reshape(-1), perm, 0).reshape(shape)
+    ind = _k_shuffle(kd_row, impl, 1, n, 1, layout)
+    return _take(xt, ind, axis)
+
+
+def _permutation_lanes(k, nb, xv, xnb, axis, independent):
+    """random_permutation with x batched under vmap (the reference's vmap batches every
+    argument, R/batching.R:22-50): lane i shuffles x's i-th array with key i (or with the
+    one key when only x is batched), as the loop over the lanes would."""
+    levels = max(nb, xnb)
+    if nb not in (0, levels):
+        raise JaxNotImplementedError("vmap: sampler parameters batched at other levels than the key")
+    if nb and k.impl != "threefry2x32":
+        raise JaxNotImplementedError("random_permutation under vmap with rbg keys")
+    xt = _as_device_array(xv)
+    B = tuple(xt.shape[:xnb])
+    if nb and tuple(k.shape[:nb]) != B:
+        raise JaxValueError(f"vmap got inconsistent sizes for the mapped axis: "
+                            f"{sorted({tuple(k.shape[:nb]), B})}")
+    lane = tuple(xt.shape[xnb:])
+    if not lane:  # an integer n per lane would give lanes of different lengths
+        raise JaxTypeError("x must be an integer or at least 1-dimensional")
+    axis = _norm_axis(axis, len(lane))
+    kd = _flat_keys(k)
+    rows = xt.reshape((-1,) + lane)
+    outs = [_permute_array(kd[i] if kd.shape[0] > 1 else kd[0], k.impl, rows[i].contiguous(),
+                           axis, independent, _layout()) for i in range(rows.shape[0])]
+    out = torch.stack(outs) if outs else torch.empty((0,) + lane, dtype=xt.dtype)
+    return _rebatch(out.reshape(B + lane), levels)
 
 
 def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
@@ -1448,6 +1543,31 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
     replacement through randint; without, the first draws of a permutation; with p,
     searchsorted of the cumulative sums (replace) or the top draws of gumbel + log(p)."""
     k, _, nb = _check_key("choice", key)
+    (av0, anb), (pv0, pnb) = _unbatch(a), _unbatch(p)
+    if anb or pnb:  # a or p batched under vmap: each lane's choice, stacked
+        levels = max(nb, anb, pnb)
+        if any(b not in (0, levels) for b in (nb, anb, pnb)):
+            raise JaxNotImplementedError("vmap: sampler parameters batched at other levels than "
+                                         "the key")
+        bs = [tuple(np.shape(v))[:b] for v, b in ((av0, anb), (pv0, pnb)) if b]
+        B = tuple(k.shape[:nb]) if nb else bs[0]
+        if any(b != B for b in bs):
+            raise JaxValueError(f"vmap got inconsistent sizes for the mapped axis: "
+                                f"{sorted(set(bs + [B]))}")
+
+        def lanes(v, b):
+            if not b:
+                return None
+            t = v if isinstance(v, torch.Tensor) else torch.as_tensor(np.asarray(v))
+            return t.reshape((-1,) + tuple(t.shape[b:]))
+        arows, prows = lanes(av0, anb), lanes(pv0, pnb)
+        kw = _KEY_WORDS[k.impl]
+        kdata = k.data.reshape((-1, kw))
+        rows = [random_choice(PRNGKeyArray(kdata[i] if nb else kdata[0], k.impl),
+                              arows[i] if anb else av0, shape, replace,
+                              prows[i] if pnb else pv0, axis, mode) for i in range(_size(B))]
+        out = torch.stack(rows) if rows else torch.empty((0,))
+        return _rebatch(out.reshape(B + tuple(out.shape[1:])), levels)
     if nb:  # vmap over keys: each key's choice, stacked along the batch axes
         rows = [random_choice(PRNGKeyArray(d, k.impl), a, shape, replace, p, axis, mode)
                 for d in k.data.reshape((-1, _KEY_WORDS[k.impl]))]

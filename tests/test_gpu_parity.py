@@ -539,3 +539,39 @@ def test_vmap_batched_sampler_parameters():
         for i in range(4):
             want = jr.random_bernoulli(keys[i], ps[i], (64,), mode=mode)
             assert np.array_equal(to_np(out)[i], to_np(want)), (mode, i)
+
+
+def test_vmap_batched_truncated_normal_and_randint_bounds(oracle):
+    """vmap over (key, bounds) for the truncated normal and randint, and over the bounds
+    alone with one key, equals the loop over the lanes with each lane's bounds given as
+    arrays; randint also against the oracle lane by lane."""
+    keys = jr.random_split(jr.random_key(21), 3)
+    lows = torch.tensor([-1.0, 0.0, -2.5])
+    for dt in ("float32", "float64", "bfloat16"):
+        out = jr.vmap(lambda k, lo: jr.random_truncated_normal(k, lo, 2.0, (40,), dt))(keys, lows)
+        assert tuple(out.shape) == (3, 40)
+        for i in range(3):
+            want = jr.random_truncated_normal(keys[i], torch.full((40,), float(lows[i])), 2.0,
+                                              (40,), dt)
+            assert np.array_equal(to_np(out)[i], to_np(want)), (dt, i)
+    out = jr.vmap(lambda lo: jr.random_truncated_normal(jr.random_key(4), lo, 1.0, (8,)))(lows)
+    for i in range(3):
+        want = jr.random_truncated_normal(jr.random_key(4), torch.full((8,), float(lows[i])), 1.0,
+                                          (8,))
+        assert np.array_equal(to_np(out)[i], to_np(want))
+    mins = torch.tensor([0, -50, 7], dtype=torch.int32)
+    maxs = torch.tensor([10, 50, 1000], dtype=torch.int32)
+    kraw = np.stack([oracle.split(oracle.seed(21), 3, True)[i] for i in range(3)])
+    out = jr.vmap(lambda k, a, b: jr.random_randint(k, (50,), a, b))(keys, mins, maxs)
+    assert tuple(out.shape) == (3, 50) and out.dtype == torch.int32
+    for i in range(3):
+        want = jr.random_randint(keys[i], (50,), int(mins[i]), int(maxs[i]))
+        assert np.array_equal(to_np(out)[i], to_np(want)), i
+        assert np.array_equal(to_np(out)[i], oracle.randint(kraw[i], (50,), int(mins[i]),
+                                                            int(maxs[i]), "int32")), i
+    # per-lane array bounds broadcast along the shape; one key for every lane
+    rows = torch.tensor([[0, 100], [5, 6]], dtype=torch.int32)
+    out = jr.vmap(lambda m: jr.random_randint(jr.random_key(9), (3, 2), m, 200))(rows)
+    for i in range(2):
+        want = jr.random_randint(jr.random_key(9), (3, 2), rows[i], 200)
+        assert np.array_equal(to_np(out)[i], to_np(want)), i

@@ -235,3 +235,35 @@ def test_span_cap_setter():
     assert b"span cap" in L.jxr_last_error()
     assert L.jxr_set_shuffle_span_cap(-1) == -1
     assert L.jxr_set_shuffle_span_cap(prev) == 4096
+
+
+def test_vmap_batched_arrays_and_probabilities():
+    """vmap over (key, x) for the permutation and over (key, a) / (key, p) for choice, and
+    over x, a or p alone with one key, equals the loop over the lanes."""
+    keys = jr.random_split(jr.random_key(17), 3)
+    x = torch.arange(3 * 4 * 5, dtype=torch.int32).reshape(3, 4, 5)
+    for axis, indep in ((0, False), (1, False), (1, True)):
+        out = jr.vmap(lambda k, r: jr.random_permutation(k, r, axis=axis, independent=indep))(keys, x)
+        assert tuple(out.shape) == (3, 4, 5)
+        for i in range(3):
+            want = jr.random_permutation(keys[i], x[i], axis=axis, independent=indep)
+            assert np.array_equal(to_np(out)[i], to_np(want)), (axis, indep, i)
+    out = jr.vmap(lambda r: jr.random_permutation(jr.random_key(5), r))(x[:, 0, :])
+    for i in range(3):
+        assert np.array_equal(to_np(out)[i], to_np(jr.random_permutation(jr.random_key(5), x[i, 0])))
+    a = torch.arange(3 * 7, dtype=torch.int32).reshape(3, 7)
+    for replace in (True, False):
+        out = jr.vmap(lambda k, r: jr.random_choice(k, r, (4,), replace))(keys, a)
+        for i in range(3):
+            want = jr.random_choice(keys[i], a[i], (4,), replace)
+            assert np.array_equal(to_np(out)[i], to_np(want)), (replace, i)
+    ns = torch.tensor([5, 9, 30], dtype=torch.int32)
+    out = jr.vmap(lambda k, n: jr.random_choice(k, n, (6,)))(keys, ns)
+    for i in range(3):
+        assert np.array_equal(to_np(out)[i], to_np(jr.random_choice(keys[i], int(ns[i]), (6,))))
+    ps = torch.tensor([[0.2, 0.3, 0.5, 0.0], [0.25, 0.25, 0.25, 0.25], [0.0, 0.0, 1.0, 0.0]])
+    for replace in (True, False):
+        out = jr.vmap(lambda pr: jr.random_choice(jr.random_key(8), 4, (2,), replace, pr))(ps)
+        for i in range(3):
+            want = jr.random_choice(jr.random_key(8), 4, (2,), replace, ps[i])
+            assert np.array_equal(to_np(out)[i], to_np(want)), (replace, i)
