@@ -197,15 +197,18 @@ WORKLOADS = {
 }
 
 # Kernels of this library one call launches (1 unless listed): randint = split and the
-# fused draws + combine; perm = iota, then per round the key split, the sort keys with the
-# first pass's counts, the second pass's counts, 2 x (scan, scatter) and the span sort.
-LAUNCHES_PER_CALL = {"randint": 2, "perm": 1 + 3 * 8}
+# fused draws + combine; perm = per round the key split, the sort keys with the first
+# pass's counts, the second pass's counts, 2 x (scan, scatter) and the span sort (round 0's
+# first scatter takes the positions as values).
+LAUNCHES_PER_CALL = {"randint": 2, "perm": 3 * 8}
 
 # Algorithmic HBM bytes per element of one shuffle round: the 32-bit sort keys written
 # once (their first-pass counts taken on the way); per radix pass the (key, position) pair
 # read and written, the second pass also reading the keys for its counts; the span sort
 # reads the pair and writes the position.
 PERM_BYTES_PER_ROUND = 4 + 16 + (4 + 16) + 8 + 4
+# three rounds; round 0's first pass takes the positions as values (4 B not read)
+PERM_BYTES_PER_CALL = 3 * PERM_BYTES_PER_ROUND - 4
 
 _SAMPLER_WORKLOADS = {"exp": "exponential", "gumbel": "gumbel", "logistic": "logistic"}
 
@@ -373,8 +376,8 @@ def run_workload(args):
     elif c == "perm":
         key = jr.random_key(7)
         step = lambda: jr.random_permutation(key, 1 << 26)
-        # 3 rounds: 2^26 cipher blocks and PERM_BYTES_PER_ROUND bytes per element each
-        words, blocks, out_bytes, dt = 1 << 26, 3 << 26, 3 * PERM_BYTES_PER_ROUND << 26, "int32"
+        # 3 rounds: 2^26 cipher blocks each, PERM_BYTES_PER_CALL bytes per element in all
+        words, blocks, out_bytes, dt = 1 << 26, 3 << 26, PERM_BYTES_PER_CALL << 26, "int32"
     else:
         raise SystemExit(f"unknown config {c}")
     small = out_bytes < (1 << 30)
@@ -417,7 +420,7 @@ def run_workload(args):
     hbm = {"achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
            "frac": gbs / hbm_peak if hbm_peak else None}
     if c == "perm":  # a sort: memory-bound, the cipher is 3 blocks per element
-        roofline = dict(hbm, bound="hbm", bytes_per_element=3 * PERM_BYTES_PER_ROUND,
+        roofline = dict(hbm, bound="hbm", bytes_per_element=PERM_BYTES_PER_CALL,
                         int_frac=bps / peak_blocks)
     elif c == "rbg":  # Philox: ~40 multiplies per 4 words, below the store bandwidth
         roofline = dict(hbm, bound="hbm", bytes_per_element=4)

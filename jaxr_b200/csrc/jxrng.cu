@@ -2092,9 +2092,10 @@ size_t shuffle_scratch(int64_t total, char* base, SortScratch* s) {
 }
 
 // One stable 8-bit radix pass of (k, v) by the digit at `shift` into (k2, v2); the pointers
-// are swapped, so k / v hold the result.
+// are swapped, so k / v hold the result.  counted: the tile counts are in s.counts already;
+// iota: the values are the positions (v is not read).
 int radix_pass(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n, int shift,
-               const SortScratch& s, cudaStream_t st, bool counted = false) {
+               const SortScratch& s, cudaStream_t st, bool counted = false, bool iota = false) {
   const int64_t nt = sort_tiles(n);
   JXR_CUDA(cudaFuncSetAttribute(k_sort_scatter, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kSortScatterSmem));
@@ -2112,7 +2113,7 @@ int radix_pass(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t
   if (!counted) k_sort_hist<<<(unsigned)nt, kSortThreads, 0, st>>>(k, n, shift, nt, s.counts);
   k_sort_scan_rows<<<256, 1024, 0, st>>>(s.counts, nt, s.totals);
   k_sort_scatter<<<(unsigned)grid, kScatterThreads, kSortScatterSmem, st>>>(
-      k, v, n, shift, nt, s.counts, s.totals, k2, v2, s.err);
+      k, iota ? nullptr : v, n, shift, nt, s.counts, s.totals, k2, v2, s.err);
   JXR_CUDA(cudaGetLastError());
   std::swap(k, k2);
   std::swap(v, v2);
@@ -2122,10 +2123,10 @@ int radix_pass(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t
 // Sorts (k, v) by the low `bits` bits of k (a multiple of 8), stably; k2 / v2 are scratch
 // of the same size.  On return k / v point at the sorted pairs, k2 / v2 at free buffers.
 int sort_pairs(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n, int bits,
-               const SortScratch& s, cudaStream_t st) {
+               const SortScratch& s, cudaStream_t st, bool iota = false) {
   int rc;
   for (int shift = 0; shift < bits; shift += 8)
-    if ((rc = radix_pass(k, v, k2, v2, n, shift, s, st))) return rc;
+    if ((rc = radix_pass(k, v, k2, v2, n, shift, s, st, false, iota && shift == 0))) return rc;
   return JXR_OK;
 }
 
@@ -2148,11 +2149,19 @@ int span_sort_passes(int64_t n, int cap) {
 // On return v holds the values in sorted order (k is not sorted).  A span longer than
 // `cap` sets s.err[1]; the caller then repeats the shuffle with the radix passes alone.
 int sort_random_keys(uint32_t*& k, uint32_t*& v, uint32_t*& k2, uint32_t*& v2, int64_t n,
-                     int cap, const SortScratch& s, cudaStream_t st, bool first_counted = false) {
+                     int cap, const SortScratch& s, cudaStream_t st, bool first_counted = false,
+                     bool iota = false) {
   const int g = span_sort_passes(n, cap);
   int rc;
+  if (iota && !g) {  // the span sort reads the values: write the positions
+    int grid;
+    if ((rc = small_grid(n, &grid))) return rc;
+    k_iota_u32<<<grid, 256, 0, st>>>(v, n);
+  }
   for (int p = g; p >= 1; --p)
-    if ((rc = radix_pass(k, v, k2, v2, n, 32 - 8 * p, s, st, first_counted && p == g))) return rc;
+    if ((rc = radix_pass(k, v, k2, v2, n, 32 - 8 * p, s, st, first_counted && p == g,
+                         iota && p == g)))
+      return rc;
   JXR_CUDA(cudaFuncSetAttribute(k_sort_spans, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 kSpanSmem));
   const int64_t ctas = (n + kSpanOwn - 1) / kSpanOwn;
@@ -2211,9 +2220,10 @@ int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t
     // the first two words of each
     const size_t kw = impl == JXR_IMPL_THREEFRY ? 8 : 16;
     JXR_CUDA(cudaMemcpyAsync(s.keys12, key, kw, cudaMemcpyDeviceToDevice, st));
-    // values are original flat indices: v[f] = index of the element now at position f
+    // values are original flat indices: v[f] = index of the element now at position f;
+    // until the first sort writes them they are the positions themselves (iota)
     uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
-    k_iota_u32<<<grid, 256, 0, st>>>(v, total);
+    bool iota = true;
     for (int r = 0; r < rounds; ++r) {
       // ks = split(key); key = ks[0]; sort keys = random_bits(ks[1], 32, shape)
       uint32_t* ks0 = s.keys12 + 4;
@@ -2245,9 +2255,10 @@ int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t
       else
         rc = jxr_rbg_bits(ks1, (uint64_t)total, 0, (uint64_t)total, 32, k, nullptr, stream);
       if (rc) return rc;
-      if (cap) rc = sort_random_keys(k, v, k2, v2, total, cap, s, st, fused);
-      else rc = sort_pairs(k, v, k2, v2, total, 32, s, st);
+      if (cap) rc = sort_random_keys(k, v, k2, v2, total, cap, s, st, fused, iota);
+      else rc = sort_pairs(k, v, k2, v2, total, 32, s, st, iota);
       if (rc) return rc;
+      iota = false;
       if (segbits) {  // then by segment (the slice along the middle axis), stably
         k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
         if ((rc = sort_pairs(k, v, k2, v2, total, (segbits + 7) / 8 * 8, s, st))) return rc;
@@ -2255,6 +2266,7 @@ int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t
         std::swap(v, v2);
       }
     }
+    if (iota) k_iota_u32<<<grid, 256, 0, st>>>(v, total);  // no rounds (a single element)
     JXR_CUDA(cudaMemcpyAsync(perm, v, (size_t)total * 4, cudaMemcpyDeviceToDevice, st));
     JXR_CUDA(cudaGetLastError());
     return JXR_OK;

@@ -6,10 +6,10 @@
 // pairs: radix passes of 8 bits over the keys' top bits (each pass a histogram kernel, a
 // scan of the per-tile counts and a scatter), then the span sort (k_sort_spans) orders
 // each run of equal top bits in shared memory.  Sorts of other keys (argsort of floats,
-// segment ids) take radix passes over every digit.  The scatter ranks a tile's elements stably (per warp and chunk of 32, the
-// lanes of equal digit from bits ORed into shared memory, running counts per warp),
-// places them by digit in shared memory and writes each digit's run to its global
-// offset, so the global stores are contiguous runs.
+// segment ids) take radix passes over every digit.  The scatter ranks a tile's elements
+// stably (per warp and chunk of 32, the lanes of equal digit from bits ORed into shared
+// memory, running counts per warp), places them by digit in shared memory and writes each
+// digit's run to its global offset, so the global stores are contiguous runs.
 #pragma once
 
 #include <cstdint>
@@ -130,9 +130,9 @@ __device__ __forceinline__ void block256_exclusive2(uint32_t a, uint32_t b, uint
 // shared memory by digit and each digit's run written to its global offset, so the global
 // stores are contiguous runs.  The CTAs are persistent (tiles blockIdx.x, + gridDim.x, ...):
 // once a tile is staged, the next tile's keys and values are loaded into the same
-// registers, so those loads are in flight while the staged tile is written out.  Positions
-// outside [0, n) or a local rank outside the tile (which correct scans never give) are
-// skipped and set *err.
+// registers, so those loads are in flight while the staged tile is written out.  With vals
+// == nullptr the values are the elements' positions.  Positions outside [0, n) or a local
+// rank outside the tile (which correct scans never give) are skipped and set *err.
 __global__ void __launch_bounds__(kScatterThreads, 2)
 k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ vals, int64_t n,
                int shift, int64_t ntiles, const uint32_t* __restrict__ counts,
@@ -167,7 +167,7 @@ k_sort_scatter(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ v
     for (int c = 0; c < kChunks; ++c) {
       const int i = i0 + c * 32;
       kreg[c] = i < cnt ? keys[base + i] : 0u;
-      vreg[c] = i < cnt ? vals[base + i] : 0u;
+      vreg[c] = i < cnt ? (vals ? vals[base + i] : (uint32_t)(base + i)) : 0u;
     }
   };
   if (t < ntiles) load(t);
