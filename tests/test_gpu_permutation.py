@@ -209,6 +209,28 @@ def test_span_sort_matches_radix_passes(n):
     assert torch.equal(srt, torch.arange(n, dtype=torch.int64, device=srt.device))
 
 
+@pytest.mark.parametrize("variant", ["original layout", "rbg key", "unsafe_rbg key"])
+def test_span_sort_other_key_paths(variant):
+    """Sort keys that come from the bits kernels rather than the fused key-and-count kernel
+    (the original counter layout; rbg and unsafe_rbg keys): the span sort against the radix
+    passes over all four digits at 2^20 + 7 elements (two top-bit passes)."""
+    n = (1 << 20) + 7
+    if variant == "original layout":
+        key, part = dev_key(orc.seed(31)), False
+    else:
+        key, part = jr.random_key(31, impl=variant.split()[0]), True
+    with flags(False, part):
+        got = jr.random_permutation(key, n)
+        prev = _span_cap(0)
+        try:
+            want = jr.random_permutation(key, n)
+        finally:
+            _span_cap(prev)
+    assert torch.equal(got, want), variant
+    srt = torch.sort(got.to(torch.int64))[0]
+    assert torch.equal(srt, torch.arange(n, dtype=torch.int64, device=srt.device))
+
+
 def test_span_sort_overflow_repeats_with_radix_passes():
     """A span longer than the cap (forced here with a cap of 64) makes the shuffle repeat
     with radix passes alone: the results stay exact against the oracle, for vectors and
