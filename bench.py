@@ -32,6 +32,17 @@ SEED = 123
 METRIC = "threefry 32-bit words/s (device-timed) at 1/2/4/8 B200; % of INT-pipe roofline"
 OPS_PER_BLOCK = 100      # the metric's integer-op count per 64-bit cipher block
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+# HBM copy bandwidth of this pool's B200s measured earlier, for when the per-pod
+# MEASURED_PEAKS.json is absent
+HBM_FALLBACK_GBS = 6650.0
+
+
+def hbm_peak_gbs():
+    """(peak GB/s, where it comes from): MEASURED_PEAKS.json's hbm_gbs, else the fallback."""
+    try:
+        return float(json.load(open(PEAKS))["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    except (OSError, ValueError, KeyError, TypeError):
+        return HBM_FALLBACK_GBS, "fallback 6650 GB/s (MEASURED_PEAKS.json absent; of fallback)"
 TRAFFIC = os.path.join(ROOT, "profiles", "traffic.json")
 
 
@@ -410,15 +421,11 @@ def run_workload(args):
     clocks = sampler.stop()
     ms = total / args.steps
     peak_blocks = probe_peak(torch, nat, dev)
-    hbm_peak = None
-    try:
-        hbm_peak = json.load(open(PEAKS))["hbm_gbs"]
-    except (OSError, ValueError, KeyError):
-        pass
+    hbm_peak, hbm_src = hbm_peak_gbs()
     bps = blocks / (ms * 1e-3)
     gbs = out_bytes / (ms * 1e-3) / 1e9
-    hbm = {"achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-           "frac": gbs / hbm_peak if hbm_peak else None}
+    hbm = {"achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+           "peak_source": hbm_src}
     if c == "perm":  # a sort: memory-bound, the cipher is 3 blocks per element
         roofline = dict(hbm, bound="hbm", bytes_per_element=PERM_BYTES_PER_CALL,
                         int_frac=bps / peak_blocks)
@@ -563,11 +570,7 @@ def run_ours(args):
     # cipher's ceiling, and output bytes/s against measured HBM bandwidth
     peak_blocks = probe_peak(torch, nat, dev)
     my_blocks = (hi - lo) / (ms * 1e-3)
-    hbm_peak = None
-    try:
-        hbm_peak = json.load(open(PEAKS))["hbm_gbs"]
-    except (OSError, ValueError, KeyError):
-        pass
+    hbm_peak, hbm_src = hbm_peak_gbs()
     traffic, evidence = None, None
     try:
         tr = json.load(open(TRAFFIC))["bits_u32"]
@@ -587,8 +590,7 @@ def run_ours(args):
         # kernel's own ncu counters (ALU pipe, issue slots, instructions per word)
         "ncu_evidence": evidence,
         "hbm": {"achieved": my_blocks * 4 / 1e9, "peak": hbm_peak, "unit": "GB/s",
-                "frac": (my_blocks * 4 / 1e9 / hbm_peak) if hbm_peak else None,
-                "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"},
+                "frac": my_blocks * 4 / 1e9 / hbm_peak, "peak_source": hbm_src},
     }
     # the nominal ceiling too: every SM lane issuing one 32-bit integer op per cycle at the
     # SM clock sampled during the timed region, 100 ops per block
