@@ -37,3 +37,20 @@ def test_reference_arm_other_ranks_do_nothing():
     r = _run({"RANK": "1", "WORLD_SIZE": "2"}, "--steps", "1", "--warmup", "0")
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip() == ""
+
+
+def test_hbm_peak_falls_back_when_the_measured_peaks_are_absent(tmp_path, monkeypatch):
+    """The roofline's HBM peak: MEASURED_PEAKS.json's hbm_gbs when the file is there, the
+    recipe's 6650 GB/s (said so in peak_source) when it is absent or unreadable."""
+    sys.path.insert(0, ROOT)
+    import bench
+    monkeypatch.setattr(bench, "PEAKS", str(tmp_path / "missing.json"))
+    peak, src = bench.hbm_peak_gbs()
+    assert peak == 6650.0 and "fallback" in src
+    f = tmp_path / "peaks.json"
+    f.write_text(json.dumps({"hbm_gbs": 6545.6}))
+    monkeypatch.setattr(bench, "PEAKS", str(f))
+    peak, src = bench.hbm_peak_gbs()
+    assert peak == 6545.6 and "of measured" in src
+    f.write_text("{not json")
+    assert bench.hbm_peak_gbs()[0] == 6650.0
