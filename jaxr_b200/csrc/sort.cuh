@@ -364,10 +364,11 @@ k_sort_spans(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ val
   const uint32_t* s_key = s_wk + a;                 // the span's keys
   const uint32_t* s_val = s_wv + (a - lo_w);        // and values
 
-  // slots: M = the power of two >= S (128 .. kSpanSlots); slot of key k = the monotone map
+  // slots: M = the power of two >= 2 S, at most kSpanSlots (>= S always; fewer slots with
+  // several elements to sort than with M >= S); slot of key k = the monotone map
   // floor((k - base) M / R) of its offset in the span's range of buckets R
   int M = 128;
-  while (M < S) M <<= 1;
+  while (M < 2 * S && M < kSpanSlots) M <<= 1;
   const uint32_t t_first = span_top(s_key[0], top_shift), t_last = span_top(s_key[S - 1], top_shift);
   const uint32_t base = top_shift >= 32 ? 0u : t_first << top_shift;
   const float range = top_shift >= 32 ? 4294967296.0f
