@@ -24,8 +24,8 @@
  *  - Entry points allocate no device memory and do not wait for the stream unless
  *    their comment says so: jxr_prepare_device (set-up), jxr_free_caches, the HOST-memory
  *    entry points jxr_random_bits_host / _host_static, and jxr_shuffle /
- *    jxr_argsort_float, which synchronise to read a bounds-check flag (their scratch
- *    comes from the caller).
+ *    jxr_shuffle_lanes / jxr_argsort_float, which synchronise to read a bounds-check flag
+ *    (their scratch comes from the caller).
  *
  * Reference interfaces replaced (paths within the jaxR project):
  *  - threefry2x32_p and its lowering           R/prng.R:48-99
@@ -285,6 +285,17 @@ int jxr_truncated_normal_from_unit(const void* unit, const void* lower, int64_t 
 size_t jxr_shuffle_scratch_bytes(int64_t total);
 int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t inner,
                 int layout, uint32_t* perm, void* scratch, size_t scratch_bytes, void* stream);
+/* rnd_shuffle under vmap with rbg or unsafe_rbg keys (R/random.R:402-413 with the batching
+ * rule of rng_bit_generator, R/prng.R:300-313: every lane's bits come from the first lane's
+ * key, lane i taking row i of one (nlanes, shape) request).  key is the first lane's u32[4]
+ * key; perm (nlanes x total) gets, per lane, the flat source index of each position of an
+ * (outer, n, inner) array shuffled along the middle axis, as jxr_shuffle does for one key.
+ * scratch (256-byte aligned) holds jxr_shuffle_lanes_scratch_bytes(nlanes, total) bytes.
+ * Synchronises `stream` to read back the sort's flags. */
+size_t jxr_shuffle_lanes_scratch_bytes(int64_t nlanes, int64_t total);
+int jxr_shuffle_lanes(const uint32_t* key, int impl, int64_t nlanes, int64_t outer, int64_t n,
+                      int64_t inner, int layout, uint32_t* perm, void* scratch,
+                      size_t scratch_bytes, void* stream);
 /* The longest span (elements) the span sort of jxr_shuffle takes, for the calling host
  * thread: 4096 by default, 0 = radix passes only, anything in [0, 4096] accepted; returns
  * the previous value, or -1 (and the message for jxr_last_error) for a value outside that

@@ -82,6 +82,8 @@ SIGNATURES = {
     "jxr_prepare_device": [_u32, _vp],
     "jxr_get_accurate_erf_inv": [],
     "jxr_set_shuffle_span_cap": [_int],
+    "jxr_shuffle_lanes_scratch_bytes": [_i64, _i64],
+    "jxr_shuffle_lanes": [_vp, _int, _i64, _i64, _i64, _i64, _int, _vp, _vp, ctypes.c_size_t, _vp],
     "jxr_random_bits_host": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp],
     "jxr_probe_cipher": [_u64, _int, _vp, ctypes.POINTER(ctypes.c_uint64), _vp],
     "jxr_random_bits_host_static": [_vp, _i64, _u64, _u64, _u64, _int, _int, _vp, _vp],
@@ -124,6 +126,7 @@ def lib():
             L.jxr_abi_version.restype = ctypes.c_int
             L.jxr_last_error.restype = ctypes.c_char_p
             L.jxr_shuffle_scratch_bytes.restype = ctypes.c_size_t
+            L.jxr_shuffle_lanes_scratch_bytes.restype = ctypes.c_size_t
             L.jxr_argsort_scratch_bytes.restype = ctypes.c_size_t
             _lib = L
     return _lib

@@ -2286,6 +2286,107 @@ int jxr_shuffle(const uint32_t* key, int impl, int64_t outer, int64_t n, int64_t
   return JXR_OK;
 }
 
+// ---- the shuffle of random_permutation under vmap with rbg / unsafe_rbg keys --------------
+
+size_t jxr_shuffle_lanes_scratch_bytes(int64_t nlanes, int64_t total) {
+  if (nlanes < 0 || total < 0 || (total && nlanes > INT64_MAX / 4 / total)) return 0;
+  const size_t bits = ((size_t)nlanes * (size_t)total * 4 + 255) & ~(size_t)255;
+  return shuffle_scratch(total, nullptr, nullptr) + bits;
+}
+
+int jxr_shuffle_lanes(const uint32_t* key, int impl, int64_t nlanes, int64_t outer, int64_t n,
+                      int64_t inner, int layout, uint32_t* perm, void* scratch,
+                      size_t scratch_bytes, void* stream) {
+  if (impl != JXR_IMPL_RBG && impl != JXR_IMPL_UNSAFE_RBG)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "impl must be 1 (rbg) or 2 (unsafe_rbg), got %d "
+                "(threefry lanes shuffle with their own keys: jxr_shuffle per lane)", impl);
+  if (nlanes < 0 || outer < 0 || n < 0 || inner < 0)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "nlanes, outer, n and inner must be >= 0");
+  if (layout != JXR_LAYOUT_ORIGINAL && layout != JXR_LAYOUT_PARTITIONABLE)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "layout must be 0 or 1, got %d", layout);
+  if ((n && outer > INT64_MAX / n) || (n && outer && inner > INT64_MAX / (outer * n)))
+    return fail(JXR_ERR_INVALID_ARGUMENT, "outer * n * inner overflows");
+  const int64_t total = outer * n * inner;
+  if (total > (int64_t)0x7FFFFFFF)
+    return fail(JXR_ERR_INVALID_ARGUMENT,
+                "shuffle of %lld elements: at most 2^31 - 1 (32-bit positions)", (long long)total);
+  if (!total || !nlanes) return JXR_OK;
+  if (nlanes > INT64_MAX / 4 / total)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "nlanes * total overflows");
+  if (!key || !perm || !scratch) return fail(JXR_ERR_INVALID_ARGUMENT, "null pointer");
+  if ((uintptr_t)scratch % 256)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "scratch must be 256-byte aligned");
+  const size_t need = jxr_shuffle_lanes_scratch_bytes(nlanes, total);
+  if (scratch_bytes < need)
+    return fail(JXR_ERR_INVALID_ARGUMENT, "scratch of %zu bytes, need %zu", scratch_bytes, need);
+  SortScratch s;
+  const size_t sort_bytes = shuffle_scratch(total, (char*)scratch, &s);
+  uint32_t* bits = (uint32_t*)((char*)scratch + sort_bytes);  // [nlanes][total]
+  cudaStream_t st = (cudaStream_t)stream;
+  int grid, rc;
+  if ((rc = small_grid(total, &grid))) return rc;
+  const int rounds =
+      (int)std::ceil(3.0 * std::log(std::max(1.0, (double)total)) / std::log(4294967295.0));
+  int segbits = 0;
+  for (int64_t nseg = outer * inner; nseg > 1 && ((int64_t)1 << segbits) < nseg;) ++segbits;
+  const size_t bytes = (size_t)total * 4;
+  auto run = [&](int cap) -> int {
+    JXR_CUDA(cudaMemsetAsync(s.err, 0, 2 * sizeof(int), st));
+    JXR_CUDA(cudaMemcpyAsync(s.keys12, key, 16, cudaMemcpyDeviceToDevice, st));
+    for (int64_t i = 0; i < nlanes; ++i) k_iota_u32<<<grid, 256, 0, st>>>(perm + i * total, total);
+    for (int r = 0; r < rounds; ++r) {
+      // the first lane's key is split as without vmap (an rbg key splits its halves per
+      // lane, and lane 0's rows of a batched unsafe_rbg split are rows 0 and 10 of its own
+      // request); every lane's sort keys are its row of one (nlanes, shape) request from the
+      // first lane's ks[1]
+      uint32_t* ks0 = s.keys12 + 4;
+      uint32_t* ks1 = s.keys12 + 8;
+      if (impl == JXR_IMPL_RBG) {
+        uint32_t* tmp = s.keys12 + 12;
+        if ((rc = jxr_split(s.keys12, 2, 2, layout, tmp, stream))) return rc;
+        JXR_CUDA(cudaMemcpyAsync(ks0, tmp, 8, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(ks0 + 2, tmp + 4, 8, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(ks1, tmp + 2, 8, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(ks1 + 2, tmp + 6, 8, cudaMemcpyDeviceToDevice, st));
+      } else {
+        if ((rc = jxr_rbg_blocks(s.keys12, 0, 10, 2, ks0, stream))) return rc;
+      }
+      JXR_CUDA(cudaMemcpyAsync(s.keys12, ks0, 16, cudaMemcpyDeviceToDevice, st));
+      const uint64_t req = (uint64_t)nlanes * (uint64_t)total;
+      if ((rc = jxr_rbg_bits(ks1, req, 0, req, 32, bits, nullptr, stream))) return rc;
+      for (int64_t i = 0; i < nlanes; ++i) {
+        uint32_t *k = s.ka, *v = s.va, *k2 = s.kb, *v2 = s.vb;
+        JXR_CUDA(cudaMemcpyAsync(k, bits + i * total, bytes, cudaMemcpyDeviceToDevice, st));
+        JXR_CUDA(cudaMemcpyAsync(v, perm + i * total, bytes, cudaMemcpyDeviceToDevice, st));
+        if (cap) rc = sort_random_keys(k, v, k2, v2, total, cap, s, st);
+        else rc = sort_pairs(k, v, k2, v2, total, 32, s, st);
+        if (rc) return rc;
+        if (segbits) {  // then by segment (the slice along the middle axis), stably
+          k_segment_keys<<<grid, 256, 0, st>>>(v, total, n, inner, k);
+          if ((rc = sort_pairs(k, v, k2, v2, total, (segbits + 7) / 8 * 8, s, st))) return rc;
+          k_shuffle_place<<<grid, 256, 0, st>>>(v, total, n, inner, v2, s.err);
+          std::swap(v, v2);
+        }
+        JXR_CUDA(cudaMemcpyAsync(perm + i * total, v, bytes, cudaMemcpyDeviceToDevice, st));
+      }
+    }
+    JXR_CUDA(cudaGetLastError());
+    return JXR_OK;
+  };
+  int flags[2] = {0, 0};
+  if ((rc = run(std::min(g_shuffle_span_cap, kSpanCap)))) return rc;
+  JXR_CUDA(cudaMemcpyAsync(flags, s.err, sizeof flags, cudaMemcpyDeviceToHost, st));
+  JXR_CUDA(cudaStreamSynchronize(st));
+  if (flags[1] && !flags[0]) {  // a span over the cap: the whole shuffle by radix passes
+    if ((rc = run(0))) return rc;
+    JXR_CUDA(cudaMemcpyAsync(flags, s.err, sizeof flags, cudaMemcpyDeviceToHost, st));
+    JXR_CUDA(cudaStreamSynchronize(st));
+  }
+  if (flags[0])
+    return fail(JXR_ERR_CUDA, "shuffle: a bounds check in the sort failed (code %d)", flags[0]);
+  return JXR_OK;
+}
+
 int jxr_take(const void* src, int64_t outer, int64_t n_src, const uint32_t* idx, int64_t n_idx,
              int64_t row_bytes, void* out, int* err, void* stream) {
   if (outer < 0 || n_src < 0 || n_idx < 0 || row_bytes < 0)

@@ -1445,6 +1445,34 @@ def _k_shuffle(kd_row, impl, outer, n, inner, layout):
     return perm
 
 
+def _k_shuffle_lanes(kd0, impl, nlanes, outer, n, inner, layout):
+    """rnd_shuffle under one vmap level with rbg / unsafe_rbg keys: (nlanes, total) uint32,
+    every lane's sort keys drawn from the first lane's key kd0 (rng_bit_generator's
+    batching rule, R/prng.R:300-313)."""
+    total = outer * n * inner
+    perm = torch.empty((nlanes, total), dtype=torch.uint32, device=kd0.device)
+    if total and nlanes:
+        nbytes = nat.lib().jxr_shuffle_lanes_scratch_bytes(nlanes, total)
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=kd0.device)
+        nat.call("jxr_shuffle_lanes", _ptr(kd0), _IMPL_CODE[impl], nlanes, outer, n, inner,
+                 layout, _ptr(perm), _ptr(scratch), nbytes, _stream())
+    return perm
+
+
+def _permute_rbg_lanes(kd0, impl, rows, axis, independent, layout):
+    """Each lane's array rows[i] shuffled along `axis` by the lanes' permutations of
+    _k_shuffle_lanes (rnd_permutation's array branch per lane, R/random.R:388-400)."""
+    nl = rows.shape[0]
+    shape = tuple(rows.shape[1:])
+    outer, n, inner = _size(shape[:axis]), shape[axis], _size(shape[axis + 1:])
+    if independent or len(shape) == 1:
+        perms = _k_shuffle_lanes(kd0, impl, nl, outer, n, inner, layout)
+        return torch.stack([_take(rows[i].reshape(-1), perms[i], 0).reshape(shape)
+                            for i in range(nl)])
+    inds = _k_shuffle_lanes(kd0, impl, nl, 1, n, 1, layout)
+    return torch.stack([_take(rows[i], inds[i], axis) for i in range(nl)])
+
+
 def _take(x, idx, axis):
     """jnp_take(x, idx, axis) for a device tensor x and uint32 (or non-negative int)
     indices of any shape: result shape x.shape[:axis] + idx.shape + x.shape[axis+1:]."""
@@ -1475,8 +1503,9 @@ def random_permutation(key, x, axis=0, independent=False):
     kd = _flat_keys(k)
     layout = _layout()
     bshape = k.shape[:nb]
-    if nb and k.impl != "threefry2x32":
-        raise JaxNotImplementedError("random_permutation under vmap with rbg keys")
+    rbg_lanes = nb and k.impl != "threefry2x32"  # the lanes' bits from the first key
+    if rbg_lanes and nb > 1:
+        raise JaxNotImplementedError("random_permutation under nested vmap with rbg keys")
     if ndim == 0:
         if isinstance(xv, (torch.Tensor, np.ndarray)):
             t = torch.as_tensor(xv)
@@ -1488,12 +1517,19 @@ def random_permutation(key, x, axis=0, independent=False):
         else:
             n = int(xv)
         n = max(n, 0)
+        if rbg_lanes:
+            out = _k_shuffle_lanes(kd[0], k.impl, kd.shape[0], 1, n, 1, layout).view(torch.int32)
+            return _rebatch(out.reshape(bshape + (n,)), nb)
         outs = [_k_shuffle(kd[r], k.impl, 1, n, 1, layout).view(torch.int32)
                 for r in range(kd.shape[0])]
         out = torch.stack(outs) if outs else torch.empty((0, n), dtype=torch.int32)
         return _rebatch(out.reshape(bshape + (n,)), nb)
     xt = _as_device_array(xv)
     shape = tuple(xt.shape)
+    if rbg_lanes:
+        rows = xt.unsqueeze(0).expand((kd.shape[0],) + shape).contiguous()
+        out = _permute_rbg_lanes(kd[0], k.impl, rows, axis, independent, layout)
+        return _rebatch(out.reshape(bshape + shape), nb)
     outs = [_permute_array(kd[r], k.impl, xt, axis, independent, layout)
             for r in range(kd.shape[0])]
     out = torch.stack(outs) if outs else torch.empty((0,) + shape, dtype=xt.dtype)
@@ -1519,8 +1555,8 @@ def _permutation_lanes(k, nb, xv, xnb, axis, independent):
     levels = max(nb, xnb)
     if nb not in (0, levels):
         raise JaxNotImplementedError("vmap: sampler parameters batched at other levels than the key")
-    if nb and k.impl != "threefry2x32":
-        raise JaxNotImplementedError("random_permutation under vmap with rbg keys")
+    if nb > 1 and k.impl != "threefry2x32":
+        raise JaxNotImplementedError("random_permutation under nested vmap with rbg keys")
     xt = _as_device_array(xv)
     B = tuple(xt.shape[:xnb])
     if nb and tuple(k.shape[:nb]) != B:
@@ -1532,6 +1568,9 @@ def _permutation_lanes(k, nb, xv, xnb, axis, independent):
     axis = _norm_axis(axis, len(lane))
     kd = _flat_keys(k)
     rows = xt.reshape((-1,) + lane)
+    if nb and k.impl != "threefry2x32":  # the lanes' bits from the first key
+        out = _permute_rbg_lanes(kd[0], k.impl, rows.contiguous(), axis, independent, _layout())
+        return _rebatch(out.reshape(B + lane), levels)
     outs = [_permute_array(kd[i] if kd.shape[0] > 1 else kd[0], k.impl, rows[i].contiguous(),
                            axis, independent, _layout()) for i in range(rows.shape[0])]
     out = torch.stack(outs) if outs else torch.empty((0,) + lane, dtype=xt.dtype)
@@ -1544,6 +1583,8 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
     searchsorted of the cumulative sums (replace) or the top draws of gumbel + log(p)."""
     k, _, nb = _check_key("choice", key)
     (av0, anb), (pv0, pnb) = _unbatch(a), _unbatch(p)
+    if (anb or pnb) and k.impl != "threefry2x32" and nb:
+        raise JaxNotImplementedError("random_choice under vmap over rbg keys with batched a or p")
     if anb or pnb:  # a or p batched under vmap: each lane's choice, stacked
         levels = max(nb, anb, pnb)
         if any(b not in (0, levels) for b in (nb, anb, pnb)):
@@ -1568,11 +1609,16 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
                               prows[i] if pnb else pv0, axis, mode) for i in range(_size(B))]
         out = torch.stack(rows) if rows else torch.empty((0,))
         return _rebatch(out.reshape(B + tuple(out.shape[1:])), levels)
-    if nb:  # vmap over keys: each key's choice, stacked along the batch axes
+    if nb and k.impl == "threefry2x32":  # vmap over keys: each key's choice, stacked
         rows = [random_choice(PRNGKeyArray(d, k.impl), a, shape, replace, p, axis, mode)
                 for d in k.data.reshape((-1, _KEY_WORDS[k.impl]))]
         out = torch.stack(rows) if rows else torch.empty((0,))
         return _rebatch(out.reshape(k.shape[:nb] + tuple(out.shape[1:])), nb)
+    if nb > 1:
+        raise JaxNotImplementedError("random_choice under nested vmap with rbg keys")
+    # rbg / unsafe_rbg keys under vmap: the draws follow rng_bit_generator's batching rule
+    # (every lane's bits from the first key, R/prng.R:300-313), lane i taking row i
+    lanes = _size(k.shape[:nb]) if nb else 0
     shape = canon_shape(shape)
     av, anb = _unbatch(a)
     if anb:
@@ -1594,26 +1640,36 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
         n_inputs = int(v)
         adtype = _TORCH[default_int()] if float(v) == int(v) else _TORCH[default_float()]
     n_draws = _size(shape)
+    lshape = ((lanes,) if nb else ()) + tuple(shape)  # the result's shape (before a's axes)
     if n_draws == 0:
-        return torch.zeros(shape, dtype=adtype, device=_device())
+        z = torch.zeros(lshape, dtype=adtype, device=_device())
+        return _rebatch(z, nb) if arr is None else _rebatch(
+            torch.stack([_take(arr, z[i].to(torch.int64), axis) for i in range(lanes)])
+            if nb else _take(arr, z.to(torch.int64), axis), nb)
     if n_inputs <= 0:
         raise JaxValueError("a must be greater than 0 unless no samples are taken")
     if not replace and n_draws > n_inputs:
         raise JaxValueError(f"Cannot take a larger sample (size {n_draws}) than population "
                             f"(size {n_inputs}) when 'replace=False'")
+    def take_lanes(ind):  # ind: lshape indices -> arr's rows (per lane under vmap)
+        if arr is None:
+            return _rebatch(ind, nb)
+        if not nb:
+            return _take(arr, ind, axis)
+        return _rebatch(torch.stack([_take(arr, ind[i], axis) for i in range(lanes)]), nb)
     if p is None:
         if replace:
-            ind = random_randint(key, shape, 0, n_inputs)
-            result = ind if arr is None else _take(arr, ind, axis)
+            ind, _ = _unbatch(random_randint(key, shape, 0, n_inputs))
+            return take_lanes(ind)
+        kd = _flat_keys(k)
+        if nb:
+            perm = _k_shuffle_lanes(kd[0], k.impl, lanes, 1, n_inputs, 1, _layout())
+            ind = perm[:, :n_draws].contiguous()
         else:
-            kd = _flat_keys(k)
-            if arr is None:
-                perm = _k_shuffle(kd[0], k.impl, 1, n_inputs, 1, _layout()).view(torch.int32)
-                result = perm[:n_draws].reshape(shape)
-            else:
-                ind = _k_shuffle(kd[0], k.impl, 1, n_inputs, 1, _layout())[:n_draws]
-                result = _take(arr, ind.reshape(shape), axis)
-        return result
+            ind = _k_shuffle(kd[0], k.impl, 1, n_inputs, 1, _layout())[:n_draws]
+        if arr is None:
+            return _rebatch(ind.view(torch.int32).reshape(lshape), nb)
+        return take_lanes(ind.reshape(lshape))
     # promote_dtypes_inexact: float arrays keep their dtype, everything else is the
     # default float
     if isinstance(p, torch.Tensor):
@@ -1639,22 +1695,25 @@ def random_choice(key, a, shape=(), replace=True, p=None, axis=0, mode=None):
         pd = pt.to(device=kd.device, dtype=_TORCH[pdt]).contiguous()
         cuml = torch.empty_like(pd)
         nat.call("jxr_cumsum", _ptr(pd), n_inputs, _FLOAT_CODE[pdt], _ptr(cuml), _stream())
-        unit = _k_uniform(kd, n_draws, pdt, 0.0, 1.0, layout)
-        ind = torch.empty(n_draws, dtype=_TORCH[dint], device=kd.device)
-        nat.call("jxr_choice_p_from_unit", _ptr(unit), n_draws, _FLOAT_CODE[pdt], _ptr(cuml),
-                 n_inputs, _BITS[dint], _ptr(ind), _stream())
+        unit = _k_uniform(kd, n_draws, pdt, 0.0, 1.0, layout)  # (lanes or 1, n_draws)
+        ind = torch.empty(unit.numel(), dtype=_TORCH[dint], device=kd.device)
+        nat.call("jxr_choice_p_from_unit", _ptr(unit), unit.numel(), _FLOAT_CODE[pdt],
+                 _ptr(cuml), n_inputs, _BITS[dint], _ptr(ind), _stream())
     else:
-        g = random_gumbel(key, (n_inputs,), pdt, mode=mode).reshape(-1).contiguous()
+        gv, _ = _unbatch(random_gumbel(key, (n_inputs,), pdt, mode=mode))
+        g = gv.reshape(-1, n_inputs).contiguous()  # (lanes or 1, n_inputs)
         pd = pt.to(device=kd.device, dtype=_TORCH[pdt]).contiguous()
-        nat.call("jxr_add_log", _ptr(g), _ptr(pd), n_inputs, _FLOAT_CODE[pdt], _stream())
-        order = torch.empty(n_inputs, dtype=torch.uint32, device=kd.device)
         nbytes = nat.lib().jxr_argsort_scratch_bytes(n_inputs)
         scratch = torch.empty(nbytes, dtype=torch.uint8, device=kd.device)
-        nat.call("jxr_argsort_float", _ptr(g), n_inputs, _FLOAT_CODE[pdt], 1, _ptr(order),
-                 _ptr(scratch), nbytes, _stream())
-        ind = order[:n_draws].view(torch.int32).to(_TORCH[dint])
-    ind = ind.reshape(shape)
-    return ind if arr is None else _take(arr, ind, axis)
+        inds = []
+        for r in range(g.shape[0]):
+            nat.call("jxr_add_log", _ptr(g[r]), _ptr(pd), n_inputs, _FLOAT_CODE[pdt], _stream())
+            order = torch.empty(n_inputs, dtype=torch.uint32, device=kd.device)
+            nat.call("jxr_argsort_float", _ptr(g[r]), n_inputs, _FLOAT_CODE[pdt], 1,
+                     _ptr(order), _ptr(scratch), nbytes, _stream())
+            inds.append(order[:n_draws].view(torch.int32).to(_TORCH[dint]))
+        ind = torch.stack(inds)
+    return take_lanes(ind.reshape(lshape))
 
 
 # ---- rng_bit_generator (R/prng.R:264-345) ---------------------------------------------------

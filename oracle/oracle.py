@@ -358,6 +358,29 @@ def shuffle(key, outer, n, inner, partitionable=True):
     return cur
 
 
+def shuffle_rbg_lanes(key, impl, nlanes, outer, n, inner, partitionable=True):
+    """rnd_shuffle (R/random.R:402-413) under vmap over nlanes rbg or unsafe_rbg keys, key
+    being the first lane's u32[4] key.  rng_bit_generator's batching rule (R/prng.R:300-313)
+    draws every lane's bits from the first lane's key, lane i taking row i of one
+    (nlanes, shape) request; the first lane's split is its own (an rbg key splits its halves
+    per lane; lane 0's rows of a batched unsafe_rbg split are rows 0 and 10 of its own
+    request).  Returns cur of shape (nlanes, total): per lane, the flat source index of the
+    element at each flat position, as shuffle() gives for one key."""
+    import math
+    total = outer * n * inner
+    rounds = int(math.ceil(3 * math.log(max(1, total)) / math.log(2 ** 32 - 1)))
+    cur = np.tile(np.arange(total, dtype=np.int64), (nlanes, 1))
+    key = np.asarray(key, dtype=np.uint32)
+    for _ in range(rounds):
+        ks = rbg_split(key, 2, partitionable) if impl == "rbg" else rbg_unsafe_split(key, 2)
+        key = ks[0]
+        sk = rbg_bits(ks[1], 32, nlanes * total).reshape(nlanes, outer, n, inner)
+        for i in range(nlanes):
+            order = np.argsort(sk[i], axis=1, kind="stable")
+            cur[i] = np.take_along_axis(cur[i].reshape(outer, n, inner), order, axis=1).ravel()
+    return cur
+
+
 def permutation(key, x, axis=0, independent=False, partitionable=True):
     """random_permutation (R/random.R:378-400): an integer x permutes arange(x) (int32); an
     array is shuffled along `axis`, slices independently or (the default) all by one

@@ -195,3 +195,44 @@ def test_from_bits_tables_match_direct(kind, dt):
     wi = whole.view(torch.int32 if dt == "float32" else torch.int16)
     pi = parts.view(torch.int32 if dt == "float32" else torch.int16)
     assert torch.equal(wi, pi)
+
+
+@pytest.mark.parametrize("impl", ["rbg", "unsafe_rbg"])
+def test_permutation_and_choice_under_vmap(impl):
+    """random_permutation and random_choice under vmap over rbg / unsafe_rbg keys:
+    rng_bit_generator's batching rule draws every lane's bits from the first lane's key,
+    lane i taking row i of one batched request (R/prng.R:300-313).  Against the oracle's
+    restatement of rnd_shuffle under that rule, and lane 0 against the unbatched call with
+    the first key (row 0 of the batched request is the unbatched request)."""
+    keys = jr.random_split(jr.random_key(5, impl=impl), 3)
+    q0 = to_np(jr.random_key_data(keys))[0]
+    n = 3000
+    got = to_np(jr.vmap(lambda k: jr.random_permutation(k, n))(keys))
+    want = orc.shuffle_rbg_lanes(q0, impl, 3, 1, n, 1)
+    assert np.array_equal(got, want.astype(np.int32)), impl
+    k0 = keys[0]
+    assert np.array_equal(got[0], to_np(jr.random_permutation(k0, n)))
+    # a shared array along axis 1: every lane takes its own index vector
+    x = torch.arange(4 * 50, dtype=torch.int32).reshape(4, 50)
+    got = to_np(jr.vmap(lambda k: jr.random_permutation(k, x, axis=1))(keys))
+    ind = orc.shuffle_rbg_lanes(q0, impl, 3, 1, 50, 1)
+    for i in range(3):
+        assert np.array_equal(got[i], np.take(x.numpy(), ind[i], axis=1)), i
+    # batched arrays, shuffled independently along axis 0
+    xs = torch.arange(3 * 40 * 2, dtype=torch.int32).reshape(3, 40, 2)
+    got = to_np(jr.vmap(lambda k, r: jr.random_permutation(k, r, independent=True))(keys, xs))
+    ind = orc.shuffle_rbg_lanes(q0, impl, 3, 1, 40, 2)
+    for i in range(3):
+        assert np.array_equal(got[i].ravel(), xs[i].numpy().ravel()[ind[i]]), i
+    # choice: without replacement the lanes' permutations' first draws; every branch's
+    # lane 0 as the unbatched choice with the first key
+    got = to_np(jr.vmap(lambda k: jr.random_choice(k, 100, (7,), False))(keys))
+    want = orc.shuffle_rbg_lanes(q0, impl, 3, 1, 100, 1)[:, :7]
+    assert np.array_equal(got, want.astype(np.int32))
+    p = torch.tensor([0.1, 0.2, 0.3, 0.4])
+    for replace in (True, False):
+        for pp in (None, p):
+            out = to_np(jr.vmap(lambda k: jr.random_choice(k, 4, (3,), replace, pp))(keys))
+            assert out.shape == (3, 3)
+            one = to_np(jr.random_choice(k0, 4, (3,), replace, pp))
+            assert np.array_equal(out[0], one), (replace, pp is None)

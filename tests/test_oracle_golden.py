@@ -116,3 +116,22 @@ def test_rbg_stream_layout(oracle):
     assert np.array_equal(oracle.rbg_bits(q, 16, 12), (w & 0xFFFF).astype(np.uint16))
     w64 = oracle.rbg_bits(q, 64, 6)
     assert np.array_equal(w64, w.astype(np.uint64)[0::2] | w.astype(np.uint64)[1::2] << 32)
+
+
+def test_rbg_shuffle_under_vmap_reduces_to_the_key_of_lane_zero(oracle):
+    """The vmap restatement of rnd_shuffle with rbg / unsafe_rbg keys: lane 0 is the
+    unbatched shuffle of the first key (row 0 of the batched request is the unbatched
+    request), every lane is a permutation, and the lanes differ."""
+    import numpy as np
+    q = oracle.rbg_seed(5)
+    for impl in ("rbg", "unsafe_rbg"):
+        lanes = oracle.shuffle_rbg_lanes(q, impl, 3, 1, 3000, 1)
+        key, cur = np.asarray(q, dtype=np.uint32), np.arange(3000)
+        for _ in range(2):  # 3000 elements: two rounds
+            sp = oracle.rbg_split(key, 2) if impl == "rbg" else oracle.rbg_unsafe_split(key, 2)
+            key = sp[0]
+            cur = cur[np.argsort(oracle.rbg_bits(sp[1], 32, 3000), kind="stable")]
+        assert np.array_equal(lanes[0], cur), impl
+        for r in lanes:
+            assert np.array_equal(np.sort(r), np.arange(3000))
+        assert not np.array_equal(lanes[1], lanes[0]) and not np.array_equal(lanes[2], lanes[1])
