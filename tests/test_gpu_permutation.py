@@ -192,7 +192,8 @@ def _span_cap(cap):
     return prev
 
 
-@pytest.mark.parametrize("n", [4096, 4097, 393216, 393217, (1 << 20) + 7, (1 << 27) + 5])
+@pytest.mark.parametrize("n", [4096, 4097, 393216, 393217, (1 << 20) + 7, (1 << 27) + 5,
+                               (1 << 30) + 3])
 def test_span_sort_matches_radix_passes(n):
     """The span sort (radix passes over the top 0, 8, 16 or 24 bits, then every run of
     equal top bits in shared memory) against the radix passes over all four digits, at the
